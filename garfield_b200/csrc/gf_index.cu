@@ -1,0 +1,388 @@
+// Index construction: host arrays in the reference's layout -> device-resident index in
+// cell-major order.  Replaces the loading block of real_dataset_test_multiD
+// (realdataset_search.cu:2118-2393): get_graph_info (check.cu:406-484), get_idx_mapper
+// (tools.cuh:862-915), load_result of the global graph (tools.cuh:205-223), f2h
+// (tools.cuh:308-321), load_clustering (tools.cuh:569-602).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+
+#include "gf_internal.h"
+
+namespace gf {
+
+static thread_local std::string g_err;
+
+void set_error(const std::string& msg) { g_err = msg; }
+
+gf_status fail(gf_status s, const std::string& msg) {
+    g_err = msg;
+    return s;
+}
+
+gf_status cuda_fail(cudaError_t e, const char* what) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? GF_ERR_OOM : GF_ERR_CUDA;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int d) {
+        cudaGetDevice(&prev);
+        cudaSetDevice(d);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+// half(x * alpha) per element, rows padded with zeros to d8 (tools.cuh:308-321).
+__global__ void f2h_kernel(const float* __restrict__ in, uint32_t n, uint32_t dim, uint32_t d8, float alpha,
+                           __half* __restrict__ out) {
+    size_t total = (size_t)n * d8;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        size_t row = i / d8;
+        uint32_t d = (uint32_t)(i - row * d8);
+        float v = d < dim ? __fmul_rn(in[row * dim + d], alpha) : 0.0f;
+        out[i] = __float2half_rn(v);
+    }
+}
+
+void launch_f2h(const float* in, uint32_t n, uint32_t dim, uint32_t d8, float alpha, uint4* out, cudaStream_t s) {
+    size_t total = (size_t)n * d8;
+    unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 148 * 32);
+    if (blocks == 0) return;
+    f2h_kernel<<<blocks, 256, 0, s>>>(in, n, dim, d8, alpha, reinterpret_cast<__half*>(out));
+}
+
+template <typename T>
+static gf_status dalloc(T** p, size_t count, uint64_t* bytes) {
+    size_t b = std::max<size_t>(count, 1) * sizeof(T);
+    cudaError_t e = cudaMalloc((void**)p, b);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+    *bytes += b;
+    return GF_OK;
+}
+
+#define GF_TRY(x)                       \
+    do {                                \
+        gf_status s_ = (x);             \
+        if (s_ != GF_OK) return s_;     \
+    } while (0)
+
+static void free_index(DeviceIndex& d) {
+    void* ptrs[] = {d.vec16, d.vec32, d.attrs, d.graph, d.cross, d.i2g, d.seg, d.grid_d,
+                    d.lq_d,  d.rq_d,  d.centroids, d.hist, d.entry};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+}
+
+// Deterministic entry local ids: std::mt19937 with its default seed (as the reference,
+// gpu_graph.cu:12503-12526), value = draw % range, duplicates skipped, in draw order.
+// The reference further shuffles with std::random_shuffle, whose rand() state carries
+// over between calls; this sequence is fixed instead.
+static std::vector<uint32_t> make_entry(uint32_t count, uint32_t range) {
+    std::vector<uint32_t> out;
+    if (range == 0) return out;
+    count = std::min(count, range);
+    std::mt19937 rng;
+    std::vector<uint8_t> seen(range, 0);
+    while (out.size() < count) {
+        uint32_t t = (uint32_t)(rng() % range);
+        if (!seen[t]) {
+            seen[t] = 1;
+            out.push_back(t);
+        }
+    }
+    return out;
+}
+
+static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
+    if (!ds || !out) return fail(GF_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (ds->n == 0 || ds->dim == 0) return fail(GF_ERR_ARG, "empty index");
+    if (ds->n > kPosMask) return fail(GF_ERR_ARG, "more than 2^30-1 points");
+    if (ds->n_attr == 0 || ds->n_attr > kMaxAttr) return fail(GF_ERR_ARG, "n_attr must be 1..8");
+    if (!ds->vectors || !ds->attrs || !ds->grid || !ds->l_quant || !ds->r_quant || !ds->cell_of || !ds->graphs)
+        return fail(GF_ERR_ARG, "missing array");
+    if (ds->degree == 0 || ds->degree > 256) return fail(GF_ERR_ARG, "degree must be 1..256");
+    if (ds->cross_e > 4) return fail(GF_ERR_ARG, "cross_e must be 0..4");
+    if (ds->cross_e && !ds->cross) return fail(GF_ERR_ARG, "missing cross edges");
+    uint64_t ncells = 1, nq = 0;
+    for (uint32_t j = 0; j < ds->n_attr; ++j) {
+        if (ds->grid[j] == 0) return fail(GF_ERR_ARG, "zero grid size");
+        ncells *= ds->grid[j];
+        nq += ds->grid[j];
+    }
+    if (ncells > 65536) return fail(GF_ERR_ARG, "more than 65536 cells");
+    if (ds->dim > 4096) return fail(GF_ERR_ARG, "dim > 4096");
+
+    gf_index* ix = new gf_index();
+    DeviceIndex& d = ix->d;
+    d.device = device;
+    d.n = ds->n;
+    d.dim = ds->dim;
+    d.d8 = (ds->dim + 7) / 8 * 8;
+    d.d4 = (ds->dim + 3) / 4 * 4;
+    d.a = ds->n_attr;
+    d.ncells = (uint32_t)ncells;
+    d.degree = ds->degree;
+    d.E = ds->cross_e;
+    d.alpha = ds->f2h_factor;
+    d.grid.assign(ds->grid, ds->grid + ds->n_attr);
+    d.lq.assign(ds->l_quant, ds->l_quant + nq);
+    d.rq.assign(ds->r_quant, ds->r_quant + nq);
+
+    const uint32_t n = d.n, P = d.ncells, R = d.degree, E = d.E;
+    // positions (get_idx_mapper, tools.cuh:862-889)
+    d.seg_h.assign(P + 1, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (ds->cell_of[i] >= P) {
+            delete ix;
+            return fail(GF_ERR_FORMAT, "cell id out of range at point " + std::to_string(i));
+        }
+        d.seg_h[ds->cell_of[i] + 1]++;
+    }
+    uint32_t minc = 0xFFFFFFFFu;
+    for (uint32_t c = 0; c < P; ++c) {
+        uint32_t sz = d.seg_h[c + 1];
+        if (sz && sz < minc) minc = sz;
+        d.seg_h[c + 1] += d.seg_h[c];
+    }
+    d.min_cell = minc == 0xFFFFFFFFu ? 0 : minc;
+    std::vector<uint32_t> i2g(n), pos_of(n);
+    {
+        std::vector<uint32_t> fill(P, 0);
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t c = ds->cell_of[i];
+            uint32_t p = d.seg_h[c] + fill[c]++;
+            i2g[p] = i;
+            pos_of[i] = p;
+        }
+    }
+    d.entry_h = make_entry(std::max<uint32_t>(R, 64), d.min_cell);
+
+    // graph rows are already in position order; local ids -> positions
+    std::vector<uint32_t> graph((size_t)n * R);
+    for (uint32_t c = 0; c < P; ++c) {
+        uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
+        for (size_t r = base; r < (size_t)base + sz; ++r)
+            for (uint32_t j = 0; j < R; ++j) {
+                uint32_t loc = ds->graphs[r * R + j];
+                graph[r * R + j] = loc < sz ? base + loc : kEmpty;
+            }
+    }
+    std::vector<uint32_t> cross;
+    if (E) {
+        cross.resize((size_t)n * P * E);
+        const size_t rowlen = (size_t)P * E;
+        for (uint32_t g = 0; g < n; ++g) {
+            const uint32_t* src = ds->cross + (size_t)g * rowlen;
+            uint32_t* dst = cross.data() + (size_t)pos_of[g] * rowlen;
+            for (uint32_t c = 0; c < P; ++c) {
+                uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
+                for (uint32_t j = 0; j < E; ++j) {
+                    uint32_t loc = src[c * E + j];
+                    dst[c * E + j] = loc < sz ? base + loc : kEmpty;
+                }
+            }
+        }
+    }
+    std::vector<float> attrs((size_t)n * d.a);
+    for (uint32_t p = 0; p < n; ++p)
+        std::memcpy(&attrs[(size_t)p * d.a], ds->attrs + (size_t)i2g[p] * d.a, sizeof(float) * d.a);
+
+    // clusters (load_clustering, tools.cuh:569-602): centroid = float mean accumulated in
+    // global point order; hist[cell][label]
+    std::vector<float> centroids;
+    std::vector<uint32_t> hist;
+    if (ds->n_clusters && ds->labels) {
+        int32_t mx = -1;
+        for (uint32_t i = 0; i < n; ++i) {
+            if (ds->labels[i] < 0) {
+                delete ix;
+                return fail(GF_ERR_FORMAT, "negative cluster label");
+            }
+            mx = std::max(mx, ds->labels[i]);
+        }
+        d.C = (uint32_t)(mx + 1);
+        centroids.assign((size_t)d.C * d.dim, 0.0f);
+        hist.assign((size_t)P * d.C, 0);
+        std::vector<uint32_t> num(d.C, 0);
+        for (uint32_t i = 0; i < n; ++i) {
+            uint32_t c = (uint32_t)ds->labels[i];
+            num[c]++;
+            hist[(size_t)ds->cell_of[i] * d.C + c]++;
+            float* cr = &centroids[(size_t)c * d.dim];
+            const float* v = ds->vectors + (size_t)i * d.dim;
+            for (uint32_t k = 0; k < d.dim; ++k) cr[k] += v[k];
+        }
+        for (uint32_t c = 0; c < d.C; ++c)
+            for (uint32_t k = 0; k < d.dim; ++k) centroids[(size_t)c * d.dim + k] /= (float)num[c];
+    }
+
+    DeviceGuard guard(device);
+    gf_status st = GF_OK;
+    auto chk = [&](gf_status s) {
+        if (st == GF_OK && s != GF_OK) st = s;
+        return st == GF_OK;
+    };
+    float* vtmp = nullptr;
+    do {
+        if (!chk(dalloc(&d.vec16, (size_t)n * d.d8 / 8, &d.bytes))) break;
+        if (!chk(dalloc(&d.attrs, (size_t)n * d.a, &d.bytes))) break;
+        if (!chk(dalloc(&d.graph, (size_t)n * R, &d.bytes))) break;
+        if (E && !chk(dalloc(&d.cross, (size_t)n * P * E, &d.bytes))) break;
+        if (!chk(dalloc(&d.i2g, n, &d.bytes))) break;
+        if (!chk(dalloc(&d.seg, P + 1, &d.bytes))) break;
+        if (!chk(dalloc(&d.grid_d, d.a, &d.bytes))) break;
+        if (!chk(dalloc(&d.lq_d, nq, &d.bytes))) break;
+        if (!chk(dalloc(&d.rq_d, nq, &d.bytes))) break;
+        if (!chk(dalloc(&d.entry, d.entry_h.size(), &d.bytes))) break;
+        if (d.C) {
+            if (!chk(dalloc(&d.centroids, (size_t)d.C * d.dim, &d.bytes))) break;
+            if (!chk(dalloc(&d.hist, (size_t)P * d.C, &d.bytes))) break;
+        }
+        // fp32 rows in position order (temporary unless kept)
+        uint64_t dummy = 0;
+        if (ds->keep_fp32) {
+            if (!chk(dalloc(&d.vec32, (size_t)n * d.d4 / 4, &d.bytes))) break;
+        }
+        if (!chk(dalloc(&vtmp, (size_t)n * d.dim, &dummy))) break;
+        std::vector<float> rows((size_t)std::min<uint32_t>(n, 65536) * d.dim);
+        const uint32_t chunk = std::min<uint32_t>(n, 65536);
+        for (uint32_t p0 = 0; p0 < n && st == GF_OK; p0 += chunk) {
+            uint32_t cnt = std::min(chunk, n - p0);
+            for (uint32_t r = 0; r < cnt; ++r)
+                std::memcpy(&rows[(size_t)r * d.dim], ds->vectors + (size_t)i2g[p0 + r] * d.dim,
+                            sizeof(float) * d.dim);
+            cudaError_t e = cudaMemcpy(vtmp + (size_t)p0 * d.dim, rows.data(), sizeof(float) * cnt * d.dim,
+                                       cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) st = cuda_fail(e, "upload vectors");
+        }
+        if (st != GF_OK) break;
+        launch_f2h(vtmp, n, d.dim, d.d8, d.alpha, d.vec16, 0);
+        if (d.vec32) {
+            cudaError_t e = cudaMemset2D(d.vec32, sizeof(float) * d.d4, 0, sizeof(float) * d.d4, n);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2D(d.vec32, sizeof(float) * d.d4, vtmp, sizeof(float) * d.dim, sizeof(float) * d.dim,
+                                 n, cudaMemcpyDeviceToDevice);
+            if (e != cudaSuccess) {
+                st = cuda_fail(e, "fp32 rows");
+                break;
+            }
+        }
+        struct Up {
+            void* dst;
+            const void* src;
+            size_t bytes;
+        } ups[] = {
+            {d.attrs, attrs.data(), attrs.size() * 4},
+            {d.graph, graph.data(), graph.size() * 4},
+            {d.cross, cross.data(), cross.size() * 4},
+            {d.i2g, i2g.data(), i2g.size() * 4},
+            {d.seg, d.seg_h.data(), d.seg_h.size() * 4},
+            {d.grid_d, d.grid.data(), d.grid.size() * 4},
+            {d.lq_d, d.lq.data(), d.lq.size() * 4},
+            {d.rq_d, d.rq.data(), d.rq.size() * 4},
+            {d.entry, d.entry_h.data(), d.entry_h.size() * 4},
+            {d.centroids, centroids.data(), centroids.size() * 4},
+            {d.hist, hist.data(), hist.size() * 4},
+        };
+        for (auto& u : ups) {
+            if (!u.dst || u.bytes == 0) continue;
+            cudaError_t e = cudaMemcpy(u.dst, u.src, u.bytes, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                st = cuda_fail(e, "upload index");
+                break;
+            }
+        }
+        if (st != GF_OK) break;
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) st = cuda_fail(e, "index build");
+    } while (0);
+    if (vtmp) cudaFree(vtmp);
+    if (st != GF_OK) {
+        free_index(d);
+        delete ix;
+        return st;
+    }
+    *out = ix;
+    return GF_OK;
+}
+
+}  // namespace gf
+
+using namespace gf;
+
+extern "C" {
+
+const char* gf_status_string(gf_status s) {
+    switch (s) {
+        case GF_OK: return "ok";
+        case GF_ERR_ARG: return "invalid argument";
+        case GF_ERR_IO: return "i/o error";
+        case GF_ERR_FORMAT: return "format error";
+        case GF_ERR_OOM: return "out of memory";
+        case GF_ERR_CUDA: return "cuda error";
+        case GF_ERR_TIMEOUT: return "timeout";
+        case GF_ERR_STATE: return "bad call order";
+    }
+    return "unknown status";
+}
+
+const char* gf_last_error(void) { return g_err.c_str(); }
+
+const char* gf_version(void) { return "garfield_b200 0.1 (sm_100a)"; }
+
+void gf_search_defaults(gf_search_params* p) {
+    if (!p) return;
+    p->L = 64;
+    p->k = 10;
+    p->width = 1;
+    p->max_iter = 10000;
+    p->n_entry = 0;  // 0 = graph degree
+    p->postfilter = 0xFFFFFFFFu;
+    p->hash_slots = 0;
+    p->reserved = 0;
+}
+
+gf_status gf_index_create(const gf_index_desc* desc, int device, gf_index** out) {
+    return create(desc, device, out);
+}
+
+gf_status gf_index_info_get(const gf_index* idx, gf_index_info* out) {
+    if (!idx || !out) return fail(GF_ERR_ARG, "null argument");
+    const DeviceIndex& d = idx->d;
+    out->n = d.n;
+    out->dim = d.dim;
+    out->n_attr = d.a;
+    out->n_cells = d.ncells;
+    out->degree = d.degree;
+    out->cross_e = d.E;
+    out->n_clusters = d.C;
+    out->d_stored = d.d8;
+    out->min_cell_size = d.min_cell;
+    out->device_bytes = d.bytes;
+    return GF_OK;
+}
+
+gf_status gf_index_entry_points(const gf_index* idx, uint32_t n, uint32_t* out_host) {
+    if (!idx || !out_host) return fail(GF_ERR_ARG, "null argument");
+    if (n > idx->d.entry_h.size()) return fail(GF_ERR_ARG, "more entry points than available");
+    std::memcpy(out_host, idx->d.entry_h.data(), sizeof(uint32_t) * n);
+    return GF_OK;
+}
+
+gf_status gf_index_destroy(gf_index* idx) {
+    if (!idx) return GF_OK;
+    DeviceGuard guard(idx->d.device);
+    free_index(idx->d);
+    delete idx;
+    return GF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// Internal declarations shared by the garfield_b200 translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/garfield.h"
+
+namespace gf {
+
+constexpr uint32_t kEmpty = 0xFFFFFFFFu;
+constexpr uint32_t kExplored = 0x80000000u;  // list entry already expanded
+constexpr uint32_t kInRange = 0x40000000u;   // point satisfies the query box
+constexpr uint32_t kPosMask = 0x3FFFFFFFu;   // cell-major position (< 2^30 points)
+constexpr uint32_t kMaxAttr = 8;
+constexpr uint32_t kHopSlots = 64;  // list entries that seed a cross-cell hop (gpu_graph.cu:3569)
+
+void set_error(const std::string& msg);
+gf_status fail(gf_status s, const std::string& msg);
+gf_status cuda_fail(cudaError_t e, const char* what);
+
+#define GF_CUDA(call)                                    \
+    do {                                                 \
+        cudaError_t e_ = (call);                         \
+        if (e_ != cudaSuccess) return gf::cuda_fail(e_, #call); \
+    } while (0)
+
+// Device-resident index in cell-major order: point positions seg[c] .. seg[c+1]-1
+// belong to cell c, in increasing global id (the reference's "logical position",
+// offset[pid] + local_idx, tools.cuh:862-889).
+struct DeviceIndex {
+    int device = 0;
+    uint32_t n = 0, dim = 0, d8 = 0, d4 = 0, a = 0, ncells = 0, degree = 0, E = 0, C = 0;
+    float alpha = 1.0f;
+    uint32_t min_cell = 0;
+    std::vector<uint32_t> grid;       // a
+    std::vector<float> lq, rq;        // sum(grid)
+    std::vector<uint32_t> seg_h;      // ncells + 1
+    std::vector<uint32_t> entry_h;    // deterministic entry local ids
+    uint64_t bytes = 0;
+    // device arrays
+    uint4* vec16 = nullptr;      // n x d8 halves (alpha-scaled), as 16-byte chunks
+    float4* vec32 = nullptr;     // n x d4 fp32 (optional)
+    float* attrs = nullptr;      // n x a
+    uint32_t* graph = nullptr;   // n x degree positions
+    uint32_t* cross = nullptr;   // n x (ncells*E) positions
+    uint32_t* i2g = nullptr;     // position -> global id
+    uint32_t* seg = nullptr;     // ncells + 1
+    uint32_t* grid_d = nullptr;  // a
+    float* lq_d = nullptr;
+    float* rq_d = nullptr;
+    float* centroids = nullptr;  // C x dim fp32
+    uint32_t* hist = nullptr;    // ncells x C
+    uint32_t* entry = nullptr;   // entry_h on device
+};
+
+struct Plan {
+    gf_index* idx = nullptr;
+    uint32_t max_q = 0, qnum = 0;
+    bool planned = false;
+    float prefilter = 0.0f;
+    cudaStream_t stream = nullptr;
+    // device buffers
+    uint4* q16 = nullptr;        // max_q x d8 halves
+    float* q32 = nullptr;        // max_q x dim (copy of the fp32 queries)
+    float* lb = nullptr;         // max_q x a
+    float* rb = nullptr;
+    uint32_t* counts = nullptr;  // max_q
+    uint32_t* offsets = nullptr; // max_q
+    uint32_t* cells = nullptr;   // max_q x ncells
+    uint32_t* top4 = nullptr;    // max_q x 4
+    uint32_t* box = nullptr;     // max_q (box counts)
+    uint32_t* task = nullptr;    // max_q processing order
+    uint32_t* scratch = nullptr; // small counters: [0] queue head, [1..] histogram
+    unsigned long long* stats = nullptr;  // 8 counters
+    void* scan_tmp = nullptr;
+    size_t scan_tmp_bytes = 0;
+    // host staging for gf_search_host
+    float* h_stage = nullptr;
+};
+
+}  // namespace gf
+
+struct gf_index {
+    gf::DeviceIndex d;
+};
+
+struct gf_plan {
+    gf::Plan p;
+};
+
+namespace gf {
+// gf_plan.cu
+gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
+                       uint32_t qnum, float prefilter, cudaStream_t s);
+// gf_search.cu
+gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
+                 cudaStream_t s);
+// gf_bruteforce.cu
+gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s);
+// gf_index.cu
+void launch_f2h(const float* in, uint32_t n, uint32_t dim, uint32_t d8, float alpha, uint4* out, cudaStream_t s);
+}  // namespace gf

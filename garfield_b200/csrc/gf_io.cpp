@@ -1,0 +1,371 @@
+// Readers and writers for the reference's on-disk formats, and gf_index_open.
+// Every reader checks the file size against its header and returns GF_ERR_IO /
+// GF_ERR_FORMAT instead of exiting (the reference prints and calls exit(-1),
+// tools.cuh:66,207).
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "gf_internal.h"
+
+using gf::fail;
+
+namespace {
+
+struct File {
+    FILE* f = nullptr;
+    ~File() {
+        if (f) fclose(f);
+    }
+};
+
+gf_status open_read(File& fl, const char* path, long long* size) {
+    if (!path) return fail(GF_ERR_ARG, "null path");
+    fl.f = fopen(path, "rb");
+    if (!fl.f) return fail(GF_ERR_IO, std::string("cannot open ") + path);
+    if (fseeko(fl.f, 0, SEEK_END) != 0) return fail(GF_ERR_IO, std::string("cannot seek ") + path);
+    *size = (long long)ftello(fl.f);
+    fseeko(fl.f, 0, SEEK_SET);
+    return GF_OK;
+}
+
+gf_status rd(File& fl, void* dst, size_t bytes, const char* path) {
+    if (bytes && fread(dst, 1, bytes, fl.f) != bytes) return fail(GF_ERR_FORMAT, std::string("short read ") + path);
+    return GF_OK;
+}
+
+gf_status open_write(File& fl, const char* path) {
+    if (!path) return fail(GF_ERR_ARG, "null path");
+    fl.f = fopen(path, "wb");
+    if (!fl.f) return fail(GF_ERR_IO, std::string("cannot create ") + path);
+    return GF_OK;
+}
+
+gf_status wr(File& fl, const void* src, size_t bytes, const char* path) {
+    if (bytes && fwrite(src, 1, bytes, fl.f) != bytes) return fail(GF_ERR_IO, std::string("short write ") + path);
+    return GF_OK;
+}
+
+template <typename T>
+T* xmalloc(size_t count) {
+    return static_cast<T*>(malloc(std::max<size_t>(count, 1) * sizeof(T)));
+}
+
+#define TRY(x)                       \
+    do {                             \
+        gf_status s_ = (x);          \
+        if (s_ != GF_OK) return s_;  \
+    } while (0)
+
+// Frees every malloc'd reader output at scope exit.
+struct Holder {
+    std::vector<void*> v;
+    ~Holder() {
+        for (void* p : v) free(p);
+    }
+    template <typename T>
+    T* keep(T* p) {
+        v.push_back((void*)p);
+        return p;
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+void gf_free(void* p) { free(p); }
+
+gf_status gf_read_fvecs(const char* path, float** data, uint32_t* n, uint32_t* dim) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    int32_t d;
+    if (size < 4) return fail(GF_ERR_FORMAT, "empty fvecs");
+    TRY(rd(fl, &d, 4, path));
+    if (d <= 0) return fail(GF_ERR_FORMAT, "bad fvecs dimension");
+    long long row = 4LL * (d + 1);
+    if (size % row != 0) return fail(GF_ERR_FORMAT, "fvecs size not a multiple of the row size");
+    uint32_t num = (uint32_t)(size / row);
+    float* out = xmalloc<float>((size_t)num * d);
+    if (!out) return fail(GF_ERR_OOM, "host allocation");
+    fseeko(fl.f, 0, SEEK_SET);
+    for (uint32_t i = 0; i < num; ++i) {
+        int32_t di;
+        if (rd(fl, &di, 4, path) != GF_OK || di != d || rd(fl, out + (size_t)i * d, 4ull * d, path) != GF_OK) {
+            free(out);
+            return fail(GF_ERR_FORMAT, "fvecs row dimension mismatch");
+        }
+    }
+    *data = out;
+    *n = num;
+    *dim = (uint32_t)d;
+    return GF_OK;
+}
+
+gf_status gf_write_fvecs(const char* path, const float* data, uint32_t n, uint32_t dim) {
+    File fl;
+    TRY(open_write(fl, path));
+    int32_t d = (int32_t)dim;
+    for (uint32_t i = 0; i < n; ++i) {
+        TRY(wr(fl, &d, 4, path));
+        TRY(wr(fl, data + (size_t)i * dim, 4ull * dim, path));
+    }
+    return GF_OK;
+}
+
+gf_status gf_read_u8bin(const char* path, uint8_t** data, uint32_t* n, uint32_t* dim) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    uint32_t h[2];
+    TRY(rd(fl, h, 8, path));
+    if ((long long)h[0] * h[1] + 8 != size) return fail(GF_ERR_FORMAT, "u8bin size mismatch");
+    uint8_t* out = xmalloc<uint8_t>((size_t)h[0] * h[1]);
+    if (!out) return fail(GF_ERR_OOM, "host allocation");
+    if (rd(fl, out, (size_t)h[0] * h[1], path) != GF_OK) {
+        free(out);
+        return GF_ERR_FORMAT;
+    }
+    *data = out;
+    *n = h[0];
+    *dim = h[1];
+    return GF_OK;
+}
+
+gf_status gf_read_attrs(const char* path, int32_t** attrs, uint32_t* n, uint32_t* a) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    uint32_t h[2];
+    TRY(rd(fl, h, 8, path));
+    if (8 + 4LL * h[0] * h[1] != size) return fail(GF_ERR_FORMAT, "attrs size mismatch");
+    int32_t* out = xmalloc<int32_t>((size_t)h[0] * h[1]);
+    if (!out) return fail(GF_ERR_OOM, "host allocation");
+    if (rd(fl, out, 4ull * h[0] * h[1], path) != GF_OK) {
+        free(out);
+        return GF_ERR_FORMAT;
+    }
+    *attrs = out;
+    *n = h[0];
+    *a = h[1];
+    return GF_OK;
+}
+
+gf_status gf_write_attrs(const char* path, const int32_t* attrs, uint32_t n, uint32_t a) {
+    File fl;
+    TRY(open_write(fl, path));
+    uint32_t h[2] = {n, a};
+    TRY(wr(fl, h, 8, path));
+    return wr(fl, attrs, 4ull * n * a, path);
+}
+
+gf_status gf_read_u32mat(const char* path, uint32_t** data, uint32_t* n, uint32_t* k) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    uint32_t h[2];
+    TRY(rd(fl, h, 8, path));
+    if (8 + 4LL * h[0] * h[1] != size) return fail(GF_ERR_FORMAT, std::string("matrix size mismatch ") + path);
+    uint32_t* out = xmalloc<uint32_t>((size_t)h[0] * h[1]);
+    if (!out) return fail(GF_ERR_OOM, "host allocation");
+    if (rd(fl, out, 4ull * h[0] * h[1], path) != GF_OK) {
+        free(out);
+        return GF_ERR_FORMAT;
+    }
+    *data = out;
+    *n = h[0];
+    *k = h[1];
+    return GF_OK;
+}
+
+gf_status gf_write_u32mat(const char* path, const uint32_t* data, uint32_t n, uint32_t k) {
+    File fl;
+    TRY(open_write(fl, path));
+    uint32_t h[2] = {n, k};
+    TRY(wr(fl, h, 8, path));
+    return wr(fl, data, 4ull * n * k, path);
+}
+
+gf_status gf_read_ranges(const char* path, uint32_t qnum, uint32_t a, int32_t* l_out, int32_t* r_out) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    if (size < 8LL * qnum * a) return fail(GF_ERR_FORMAT, "range file shorter than qnum x attrs");
+    std::vector<int32_t> buf((size_t)qnum * a * 2);
+    TRY(rd(fl, buf.data(), buf.size() * 4, path));
+    for (uint32_t q = 0; q < qnum; ++q)
+        for (uint32_t j = 0; j < a; ++j) {
+            l_out[q * a + j] = buf[(size_t)q * a * 2 + j * 2];
+            r_out[q * a + j] = buf[(size_t)q * a * 2 + j * 2 + 1];
+        }
+    return GF_OK;
+}
+
+gf_status gf_write_ranges(const char* path, const int32_t* l, const int32_t* r, uint32_t qnum, uint32_t a) {
+    File fl;
+    TRY(open_write(fl, path));
+    std::vector<int32_t> buf((size_t)qnum * a * 2);
+    for (uint32_t q = 0; q < qnum; ++q)
+        for (uint32_t j = 0; j < a; ++j) {
+            buf[(size_t)q * a * 2 + j * 2] = l[q * a + j];
+            buf[(size_t)q * a * 2 + j * 2 + 1] = r[q * a + j];
+        }
+    return wr(fl, buf.data(), buf.size() * 4, path);
+}
+
+gf_status gf_read_labels(const char* path, int32_t** labels, uint32_t* n) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    int32_t num;
+    TRY(rd(fl, &num, 4, path));
+    if (num < 0 || 4 + 4LL * num != size) return fail(GF_ERR_FORMAT, "cluster file size mismatch");
+    int32_t* out = xmalloc<int32_t>((size_t)num);
+    if (!out) return fail(GF_ERR_OOM, "host allocation");
+    if (rd(fl, out, 4ull * num, path) != GF_OK) {
+        free(out);
+        return GF_ERR_FORMAT;
+    }
+    *labels = out;
+    *n = (uint32_t)num;
+    return GF_OK;
+}
+
+gf_status gf_read_grid(const char* path, uint32_t* n, uint32_t* a, uint32_t** grid, int32_t** l_quant,
+                       int32_t** r_quant, uint32_t** cell_of) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    int32_t h[2];
+    TRY(rd(fl, h, 8, path));
+    if (h[0] <= 0 || h[1] <= 0 || h[1] > (int32_t)gf::kMaxAttr) return fail(GF_ERR_FORMAT, "bad grid header");
+    uint32_t num = (uint32_t)h[0], dims = (uint32_t)h[1];
+    std::vector<int32_t> g(dims);
+    TRY(rd(fl, g.data(), 4ull * dims, path));
+    long long total = 0, expect = 8 + 4LL * dims;
+    for (uint32_t j = 0; j < dims; ++j) {
+        if (g[j] <= 0) return fail(GF_ERR_FORMAT, "bad grid size");
+        total += g[j];
+        expect += 4LL * (2LL * g[j] + num);
+    }
+    expect += 4LL * num;
+    if (expect != size) return fail(GF_ERR_FORMAT, "grid file size mismatch");
+    uint32_t* go = xmalloc<uint32_t>(dims);
+    int32_t* lo = xmalloc<int32_t>((size_t)total);
+    int32_t* ro = xmalloc<int32_t>((size_t)total);
+    uint32_t* co = xmalloc<uint32_t>(num);
+    std::vector<int32_t> pid(num);
+    gf_status st = GF_OK;
+    size_t off = 0;
+    for (uint32_t j = 0; j < dims && st == GF_OK; ++j) {
+        go[j] = (uint32_t)g[j];
+        st = rd(fl, lo + off, 4ull * g[j], path);
+        if (st == GF_OK) st = rd(fl, ro + off, 4ull * g[j], path);
+        if (st == GF_OK) st = rd(fl, pid.data(), 4ull * num, path);  // per-dim slice ids (unused)
+        off += g[j];
+    }
+    if (st == GF_OK) st = rd(fl, co, 4ull * num, path);
+    if (st != GF_OK) {
+        free(go);
+        free(lo);
+        free(ro);
+        free(co);
+        return st;
+    }
+    *n = num;
+    *a = dims;
+    *grid = go;
+    *l_quant = lo;
+    *r_quant = ro;
+    *cell_of = co;
+    return GF_OK;
+}
+
+// Load the reference's index files (realdataset_search.cu:2118-2393) and build the index.
+gf_status gf_index_open(const gf_index_files* fs, int device, gf_index** out) {
+    if (!fs || !out) return fail(GF_ERR_ARG, "null argument");
+    Holder hold;
+    float* vec = nullptr;
+    uint32_t n = 0, dim = 0;
+    TRY(gf_read_fvecs(fs->data_path, &vec, &n, &dim));
+    hold.keep(vec);
+    uint32_t gn, ga, *grid, *cell_of;
+    int32_t *lq, *rq;
+    TRY(gf_read_grid(fs->grid, &gn, &ga, &grid, &lq, &rq, &cell_of));
+    hold.keep(grid);
+    hold.keep(lq);
+    hold.keep(rq);
+    hold.keep(cell_of);
+    if (gn != n) return fail(GF_ERR_FORMAT, "grid point count differs from the data file");
+    int32_t* attrs_i;
+    uint32_t an, aa;
+    TRY(gf_read_attrs(fs->attrs, &attrs_i, &an, &aa));
+    hold.keep(attrs_i);
+    if (an != n || aa != ga) return fail(GF_ERR_FORMAT, "attrs shape differs from data/grid");
+    uint32_t ncells = 1, nq = 0;
+    for (uint32_t j = 0; j < ga; ++j) {
+        ncells *= grid[j];
+        nq += grid[j];
+    }
+    std::vector<uint32_t> sizes(ncells, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (cell_of[i] >= ncells) return fail(GF_ERR_FORMAT, "grid cell id out of range");
+        sizes[cell_of[i]]++;
+    }
+    // per-cell graphs, concatenated in cell order (check.cu:406-484)
+    std::vector<uint32_t> graphs((size_t)n * fs->degree);
+    size_t row = 0;
+    for (uint32_t c = 0; c < ncells; ++c) {
+        std::string p = std::string(fs->cagra_prefix ? fs->cagra_prefix : "") + std::to_string(c) +
+                        (fs->cagra_suffix ? fs->cagra_suffix : "");
+        uint32_t *gdat, gnum, gdeg;
+        TRY(gf_read_u32mat(p.c_str(), &gdat, &gnum, &gdeg));
+        hold.keep(gdat);
+        if (gnum != sizes[c]) return fail(GF_ERR_FORMAT, "graph " + p + " row count differs from its cell size");
+        if (gdeg != fs->degree) return fail(GF_ERR_FORMAT, "graph " + p + " degree differs from --degree");
+        std::memcpy(&graphs[row * fs->degree], gdat, 4ull * gnum * gdeg);
+        row += gnum;
+    }
+    uint32_t *cross = nullptr, cn = 0, ck = 0;
+    TRY(gf_read_u32mat(fs->global_graph, &cross, &cn, &ck));
+    hold.keep(cross);
+    if (cn != n || ck % ncells != 0) return fail(GF_ERR_FORMAT, "global graph shape differs from n x cells*E");
+    int32_t* labels = nullptr;
+    uint32_t ln = 0;
+    if (fs->cluster && fs->cluster[0]) {
+        TRY(gf_read_labels(fs->cluster, &labels, &ln));
+        hold.keep(labels);
+        if (ln != n) return fail(GF_ERR_FORMAT, "cluster label count differs from the data file");
+    }
+    std::vector<float> attrs((size_t)n * ga), lqf(nq), rqf(nq);
+    for (size_t i = 0; i < attrs.size(); ++i) attrs[i] = (float)attrs_i[i];  // realdataset_search.cu:2185-2190
+    for (uint32_t i = 0; i < nq; ++i) {
+        lqf[i] = (float)lq[i];  // real_dataset_adapter.cuh:604-609
+        rqf[i] = (float)rq[i];
+    }
+    gf_index_desc d;
+    std::memset(&d, 0, sizeof(d));
+    d.n = n;
+    d.dim = dim;
+    d.n_attr = ga;
+    d.vectors = vec;
+    d.attrs = attrs.data();
+    d.grid = grid;
+    d.l_quant = lqf.data();
+    d.r_quant = rqf.data();
+    d.cell_of = cell_of;
+    d.degree = fs->degree;
+    d.graphs = graphs.data();
+    d.cross_e = ck / ncells;
+    d.cross = cross;
+    d.n_clusters = labels ? 1 : 0;
+    d.labels = labels;
+    d.f2h_factor = fs->f2h_factor;
+    d.keep_fp32 = fs->keep_fp32;
+    return gf_index_create(&d, device, out);
+}
+
+}  // extern "C"

@@ -1,0 +1,533 @@
+// Query planning: which grid cells each query box overlaps, in cluster-guided order.
+// Re-design of intersection_area_mark_little_seg_V2 (real_dataset_adapter.cuh:390-519:
+// a marking kernel + copy_if/gather/reduce_by_key/exclusive_scan over a qnum x cells
+// flag matrix + a qnum x N box-count pass) and get_partitions_access_order_V2
+// (gpu_graph.cu:11742-11845: fp16 WMMA query x centroid distances written as a
+// qnum x C matrix, a top-4 selection kernel, a per-query bitonic sort).
+// Here: a count kernel + one scan + a fill kernel write the cell lists directly in
+// increasing cell id; one tiled kernel computes query-centroid distances and keeps
+// the 4 nearest in registers (the distance matrix never reaches HBM); one warp per
+// query scores and sorts its cells.  The box-count pass runs only when --prefilter > 0
+// (with prefilter 0 it can only select queries whose box is empty, whose result is
+// empty on either route).
+#include <cub/cub.cuh>
+
+#include <algorithm>
+#include <cstring>
+
+#include "gf_device.cuh"
+#include "gf_internal.h"
+
+namespace gf {
+namespace {
+
+using namespace dev;
+
+struct Slices {
+    uint32_t lo[kMaxAttr], hi[kMaxAttr];
+    bool empty;
+};
+
+// Slice range of each dimension (real_dataset_adapter.cuh:168-176):
+// lo = first slice whose r_quant >= l, hi = last slice whose l_quant <= r.
+__device__ __forceinline__ Slices slices_of(const float* lb, const float* rb, uint32_t a, const uint32_t* grid,
+                                            const float* lq, const float* rq) {
+    Slices s;
+    s.empty = false;
+    uint32_t off = 0;
+    for (uint32_t j = 0; j < a; ++j) {
+        uint32_t g = grid[j], k;
+        for (k = 0; k < g && rq[off + k] < lb[j]; ++k) {
+        }
+        s.lo[j] = k;
+        for (k = 0; k < g && lq[off + k] <= rb[j]; ++k) {
+        }
+        s.hi[j] = k - 1;
+        if (k == 0 || s.lo[j] >= g || k - 1 < s.lo[j]) s.empty = true;
+        off += g;
+    }
+    return s;
+}
+
+__global__ void plan_count_kernel(const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum,
+                                  uint32_t a, const uint32_t* __restrict__ grid, const float* __restrict__ lq,
+                                  const float* __restrict__ rq, uint32_t* __restrict__ counts) {
+    uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= qnum) return;
+    Slices s = slices_of(lb + (size_t)q * a, rb + (size_t)q * a, a, grid, lq, rq);
+    uint32_t c = 1;
+    for (uint32_t j = 0; j < a; ++j) c *= s.empty ? 0 : (s.hi[j] - s.lo[j] + 1);
+    counts[q] = s.empty ? 0 : c;
+}
+
+// Cells of each query in increasing cell id: cell = sum_j idx_j * prod_{k>j} grid_k
+// (gpu_graph.cu:10965-10973), enumerated with the last dimension fastest.
+__global__ void plan_fill_kernel(const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum,
+                                 uint32_t a, const uint32_t* __restrict__ grid, const float* __restrict__ lq,
+                                 const float* __restrict__ rq, const uint32_t* __restrict__ counts,
+                                 const uint32_t* __restrict__ offsets, uint32_t* __restrict__ cells) {
+    uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= qnum || counts[q] == 0) return;
+    Slices s = slices_of(lb + (size_t)q * a, rb + (size_t)q * a, a, grid, lq, rq);
+    uint32_t idx[kMaxAttr];
+    for (uint32_t j = 0; j < a; ++j) idx[j] = s.lo[j];
+    uint32_t* out = cells + offsets[q];
+    uint32_t n = 0;
+    for (;;) {
+        uint32_t pid = 0, f = 1;
+        for (int j = (int)a - 1; j >= 0; --j) {
+            pid += idx[j] * f;
+            f *= grid[j];
+        }
+        out[n++] = pid;
+        int j = (int)a - 1;
+        while (j >= 0) {
+            if (++idx[j] <= s.hi[j]) break;
+            idx[j] = s.lo[j];
+            --j;
+        }
+        if (j < 0) break;
+    }
+}
+
+// Points inside each query box, over all n points (prefiltering_tag_elements,
+// real_dataset_adapter.cuh:347-387).  Block: 256 threads x 8 queries; each thread
+// tests its points against the 8 boxes held in shared memory.
+constexpr uint32_t kBoxQ = 8;
+__global__ void box_count_kernel(const float* __restrict__ attrs, uint32_t n, uint32_t a,
+                                 const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum,
+                                 uint32_t* __restrict__ box) {
+    __shared__ float sl[kBoxQ * kMaxAttr], sr[kBoxQ * kMaxAttr];
+    __shared__ uint32_t red[kBoxQ];
+    const uint32_t q0 = blockIdx.y * kBoxQ;
+    for (uint32_t i = threadIdx.x; i < kBoxQ * a; i += blockDim.x) {
+        uint32_t q = q0 + i / a;
+        sl[i] = q < qnum ? lb[(size_t)q0 * a + i] : 1.0f;
+        sr[i] = q < qnum ? rb[(size_t)q0 * a + i] : 0.0f;
+    }
+    if (threadIdx.x < kBoxQ) red[threadIdx.x] = 0;
+    __syncthreads();
+    uint32_t cnt[kBoxQ] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const uint32_t chunk = (n + gridDim.x - 1) / gridDim.x;
+    const uint32_t beg = blockIdx.x * chunk, end = min(n, beg + chunk);
+    for (uint32_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+        float v[kMaxAttr];
+        for (uint32_t j = 0; j < a; ++j) v[j] = __ldg(attrs + (size_t)i * a + j);
+#pragma unroll
+        for (uint32_t t = 0; t < kBoxQ; ++t) {
+            bool ok = true;
+            for (uint32_t j = 0; j < a; ++j) ok = ok && v[j] >= sl[t * a + j] && v[j] <= sr[t * a + j];
+            cnt[t] += ok;
+        }
+    }
+#pragma unroll
+    for (uint32_t t = 0; t < kBoxQ; ++t) {
+        uint32_t c = cnt[t];
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_down_sync(kFull, c, o);
+        if ((threadIdx.x & 31) == 0 && c) atomicAdd(&red[t], c);
+    }
+    __syncthreads();
+    if (threadIdx.x < kBoxQ && q0 + threadIdx.x < qnum && red[threadIdx.x])
+        atomicAdd(&box[q0 + threadIdx.x], red[threadIdx.x]);
+}
+
+// Four nearest centroids per query (dis_cal_tensor_core + select_topk_by_reduce_min,
+// tools.cuh:1399-1537), distances by one fma chain over d (oracle orc_dist_seq), ties
+// by centroid id.  Block: 32 queries x 64-centroid tiles; thread t owns queries
+// 4*(t%8)..+3 and centroids 4*(t/8)..+3 of the tile; both tiles are stored
+// dimension-major in shared memory so each step reads two float4.
+constexpr uint32_t kTQ = 32, kTC = 64, kTD = 32;
+__global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restrict__ queries, uint32_t qnum,
+                                                            uint32_t dim, const float* __restrict__ cent,
+                                                            uint32_t C, uint32_t* __restrict__ top4) {
+    __shared__ __align__(16) float qt[kTD][kTQ];
+    __shared__ __align__(16) float ct[kTD][kTC];
+    __shared__ float md[kTQ][16][4];
+    __shared__ uint32_t mi[kTQ][16][4];
+    const uint32_t t = threadIdx.x, qg = t & 7, cg = t >> 3;
+    const uint32_t q0 = blockIdx.x * kTQ;
+    float bd[4][4];
+    uint32_t bi[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            bd[i][r] = __int_as_float(0x7f800000);
+            bi[i][r] = kEmpty;
+        }
+    for (uint32_t c0 = 0; c0 < C; c0 += kTC) {
+        float acc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+        for (uint32_t d0 = 0; d0 < dim; d0 += kTD) {
+            __syncthreads();
+            for (uint32_t e = t; e < kTQ * kTD; e += blockDim.x) {
+                uint32_t r = e / kTD, dd = e % kTD;
+                uint32_t q = q0 + r, d = d0 + dd;
+                qt[dd][r] = (q < qnum && d < dim) ? queries[(size_t)q * dim + d] : 0.0f;
+            }
+            for (uint32_t e = t; e < kTC * kTD; e += blockDim.x) {
+                uint32_t r = e / kTD, dd = e % kTD;
+                uint32_t c = c0 + r, d = d0 + dd;
+                ct[dd][r] = (c < C && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
+            }
+            __syncthreads();
+            const uint32_t dn = min(kTD, dim - d0);
+            for (uint32_t dd = 0; dd < dn; ++dd) {
+                float4 qv = *reinterpret_cast<const float4*>(&qt[dd][qg * 4]);
+                float4 cv = *reinterpret_cast<const float4*>(&ct[dd][cg * 4]);
+                float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ca[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float df = __fsub_rn(qa[i], ca[j]);
+                        acc[i][j] = __fmaf_rn(df, df, acc[i][j]);
+                    }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t c = c0 + cg * 4 + j;
+            if (c >= C) continue;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float dv = acc[i][j];
+                // insert (dv, c) into the sorted 4-list of query i
+                if (mkkey(dv, c) < mkkey(bd[i][3], bi[i][3])) {
+                    bd[i][3] = dv;
+                    bi[i][3] = c;
+#pragma unroll
+                    for (int r = 3; r > 0; --r) {
+                        if (mkkey(bd[i][r], bi[i][r]) < mkkey(bd[i][r - 1], bi[i][r - 1])) {
+                            float td = bd[i][r];
+                            bd[i][r] = bd[i][r - 1];
+                            bd[i][r - 1] = td;
+                            uint32_t ti = bi[i][r];
+                            bi[i][r] = bi[i][r - 1];
+                            bi[i][r - 1] = ti;
+                        }
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            md[qg * 4 + i][cg][r] = bd[i][r];
+            mi[qg * 4 + i][cg][r] = bi[i][r];
+        }
+    __syncthreads();
+    if (t < kTQ && q0 + t < qnum) {
+        float fd[4];
+        uint32_t fi[4];
+        for (int r = 0; r < 4; ++r) {
+            fd[r] = __int_as_float(0x7f800000);
+            fi[r] = kEmpty;
+        }
+        for (uint32_t g = 0; g < 16; ++g)
+            for (int r = 0; r < 4; ++r) {
+                float dv = md[t][g][r];
+                uint32_t c = mi[t][g][r];
+                if (c == kEmpty) continue;
+                if (mkkey(dv, c) < mkkey(fd[3], fi[3])) {
+                    fd[3] = dv;
+                    fi[3] = c;
+                    for (int k = 3; k > 0 && mkkey(fd[k], fi[k]) < mkkey(fd[k - 1], fi[k - 1]); --k) {
+                        float td = fd[k];
+                        fd[k] = fd[k - 1];
+                        fd[k - 1] = td;
+                        uint32_t ti = fi[k];
+                        fi[k] = fi[k - 1];
+                        fi[k - 1] = ti;
+                    }
+                }
+            }
+        for (int r = 0; r < 4; ++r) top4[(size_t)(q0 + t) * 4 + r] = fi[r];
+    }
+}
+
+// Score = sum over the 4 nearest centroids of hist[cell][centroid]; cells ordered by
+// decreasing score, ties by increasing cell id (sort_by_clustering_info_weighted,
+// gpu_graph.cu:11344-11396).  One warp per query; rank sort over the query's cells.
+constexpr uint32_t kMaxSortCells = 1024;
+__global__ void order_cells_kernel(uint32_t qnum, const uint32_t* __restrict__ counts,
+                                   const uint32_t* __restrict__ offsets, uint32_t* __restrict__ cells,
+                                   const uint32_t* __restrict__ top4, const uint32_t* __restrict__ hist, uint32_t C) {
+    __shared__ uint64_t keys[4][kMaxSortCells];
+    const uint32_t w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t q = blockIdx.x * 4 + w;
+    if (q >= qnum) return;
+    const uint32_t m = counts[q];
+    if (m <= 1) return;
+    uint32_t* cl = cells + offsets[q];
+    uint32_t t4[4];
+    for (int r = 0; r < 4; ++r) t4[r] = top4[(size_t)q * 4 + r];
+    for (uint32_t i = lane; i < m; i += 32) {
+        uint32_t c = cl[i];
+        uint32_t sc = 0;
+        for (int r = 0; r < 4; ++r)
+            if (t4[r] != kEmpty) sc += hist[(size_t)c * C + t4[r]];
+        keys[w][i] = ((uint64_t)(0xFFFFFFFFu - sc) << 32) | c;
+    }
+    __syncwarp();
+    for (uint32_t i = lane; i < m; i += 32) {
+        uint64_t k = keys[w][i];
+        uint32_t rank = 0;
+        for (uint32_t j = 0; j < m; ++j) rank += keys[w][j] < k;
+        cl[rank] = (uint32_t)k;
+    }
+}
+
+// Task order: queries with more cells first (gpu_graph.cu:12485-12493).
+__global__ void iota_kernel(uint32_t* v, uint32_t n) {
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) v[i] = i;
+}
+
+}  // namespace
+
+gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
+                       uint32_t qnum, float prefilter, cudaStream_t s) {
+    DeviceIndex& d = idx->d;
+    Plan& p = plan->p;
+    if (qnum > p.max_q) return fail(GF_ERR_ARG, "more queries than the plan was created for");
+    if (qnum && (!queries || !lb || !rb)) return fail(GF_ERR_ARG, "null query arrays");
+    p.planned = false;
+    p.qnum = qnum;
+    p.prefilter = prefilter;
+    p.stream = s;
+    if (qnum == 0) {
+        p.planned = true;
+        return GF_OK;
+    }
+    const uint32_t a = d.a;
+    GF_CUDA(cudaMemcpyAsync(p.lb, lb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
+    GF_CUDA(cudaMemcpyAsync(p.rb, rb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
+    GF_CUDA(cudaMemcpyAsync(p.q32, queries, sizeof(float) * qnum * d.dim, cudaMemcpyDeviceToDevice, s));
+    launch_f2h(p.q32, qnum, d.dim, d.d8, d.alpha, p.q16, s);
+    const uint32_t tb = 128, nb = (qnum + tb - 1) / tb;
+    plan_count_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts);
+    size_t tmp = p.scan_tmp_bytes;
+    GF_CUDA(cub::DeviceScan::ExclusiveSum(p.scan_tmp, tmp, p.counts, p.offsets, (int)qnum, s));
+    plan_fill_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts, p.offsets,
+                                       p.cells);
+    if (d.C) {
+        centroid_top4_kernel<<<(qnum + kTQ - 1) / kTQ, 128, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, p.top4);
+        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
+    } else {
+        GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
+    }
+    if (prefilter > 0.0f) {
+        GF_CUDA(cudaMemsetAsync(p.box, 0, sizeof(uint32_t) * qnum, s));
+        dim3 grid(std::min<uint32_t>((d.n + 256 * 64 - 1) / (256 * 64), 1024), (qnum + kBoxQ - 1) / kBoxQ);
+        box_count_kernel<<<grid, 256, 0, s>>>(d.attrs, d.n, a, p.lb, p.rb, qnum, p.box);
+    }
+    // processing order: most cells first
+    iota_kernel<<<nb, tb, 0, s>>>(p.task + p.max_q, qnum);
+    size_t tmp2 = p.scan_tmp_bytes;
+    GF_CUDA(cub::DeviceRadixSort::SortPairsDescending(p.scan_tmp, tmp2, p.counts, p.task + 2 * p.max_q,
+                                                      p.task + p.max_q, p.task, (int)qnum, 0, 32, s));
+    GF_CUDA(cudaGetLastError());
+    p.planned = true;
+    return GF_OK;
+}
+
+}  // namespace gf
+
+using namespace gf;
+
+namespace {
+struct DeviceGuard2 {
+    int prev = -1;
+    explicit DeviceGuard2(int d) {
+        cudaGetDevice(&prev);
+        cudaSetDevice(d);
+    }
+    ~DeviceGuard2() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+void free_plan(Plan& p) {
+    void* ptrs[] = {p.q16, p.q32, p.lb, p.rb, p.counts, p.offsets, p.cells, p.top4, p.box, p.task, p.scratch,
+                    p.stats, p.scan_tmp};
+    for (void* x : ptrs)
+        if (x) cudaFree(x);
+    if (p.h_stage) cudaFreeHost(p.h_stage);
+}
+}  // namespace
+
+extern "C" {
+
+gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
+    if (!idx || !out) return fail(GF_ERR_ARG, "null argument");
+    if (max_queries == 0) return fail(GF_ERR_ARG, "max_queries must be > 0");
+    *out = nullptr;
+    DeviceIndex& d = idx->d;
+    DeviceGuard2 guard(d.device);
+    gf_plan* pl = new gf_plan();
+    Plan& p = pl->p;
+    p.idx = idx;
+    p.max_q = max_queries;
+    const size_t Q = max_queries;
+    cudaError_t e = cudaSuccess;
+    auto A = [&](void** ptr, size_t bytes) {
+        if (e == cudaSuccess) e = cudaMalloc(ptr, std::max<size_t>(bytes, 16));
+    };
+    A((void**)&p.q16, Q * d.d8 * 2);
+    A((void**)&p.q32, Q * d.dim * 4);
+    A((void**)&p.lb, Q * d.a * 4);
+    A((void**)&p.rb, Q * d.a * 4);
+    A((void**)&p.counts, Q * 4);
+    A((void**)&p.offsets, Q * 4);
+    A((void**)&p.cells, Q * d.ncells * 4);
+    A((void**)&p.top4, Q * 16);
+    A((void**)&p.box, Q * 4);
+    A((void**)&p.task, Q * 3 * 4);
+    A((void**)&p.scratch, 64);
+    A((void**)&p.stats, 8 * sizeof(unsigned long long));
+    if (e == cudaSuccess) {
+        size_t t1 = 0, t2 = 0;
+        cub::DeviceScan::ExclusiveSum(nullptr, t1, p.counts, p.offsets, (int)Q);
+        cub::DeviceRadixSort::SortPairsDescending(nullptr, t2, p.counts, p.task, p.task, p.task, (int)Q, 0, 32);
+        p.scan_tmp_bytes = std::max(t1, t2);
+        A(&p.scan_tmp, p.scan_tmp_bytes);
+    }
+    if (e != cudaSuccess) {
+        gf_status st = cuda_fail(e, "plan buffers");
+        free_plan(p);
+        delete pl;
+        return st;
+    }
+    if (d.ncells > kMaxSortCells) {
+        free_plan(p);
+        delete pl;
+        return fail(GF_ERR_ARG, "more than 1024 cells per index are not supported by the planner");
+    }
+    *out = pl;
+    return GF_OK;
+}
+
+gf_status gf_plan_destroy(gf_plan* plan) {
+    if (!plan) return GF_OK;
+    DeviceGuard2 guard(plan->p.idx->d.device);
+    free_plan(plan->p);
+    delete plan;
+    return GF_OK;
+}
+
+gf_status gf_plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
+                          uint32_t qnum, float prefilter, void* stream) {
+    if (!idx || !plan || plan->p.idx != idx) return fail(GF_ERR_ARG, "plan does not belong to this index");
+    DeviceGuard2 guard(idx->d.device);
+    return plan_queries(idx, plan, queries, lb, rb, qnum, prefilter, (cudaStream_t)stream);
+}
+
+gf_status gf_plan_read(gf_plan* plan, uint32_t* counts, uint32_t* offsets, uint32_t* cells, uint64_t cap,
+                       uint32_t* top4, uint32_t* box_counts) {
+    if (!plan) return fail(GF_ERR_ARG, "null plan");
+    Plan& p = plan->p;
+    if (!p.planned) return fail(GF_ERR_STATE, "plan not built");
+    DeviceGuard2 guard(p.idx->d.device);
+    GF_CUDA(cudaStreamSynchronize(p.stream));
+    const uint32_t q = p.qnum;
+    if (q == 0) return GF_OK;
+    std::vector<uint32_t> c(q), o(q);
+    GF_CUDA(cudaMemcpy(c.data(), p.counts, 4ull * q, cudaMemcpyDeviceToHost));
+    GF_CUDA(cudaMemcpy(o.data(), p.offsets, 4ull * q, cudaMemcpyDeviceToHost));
+    uint64_t total = (uint64_t)o[q - 1] + c[q - 1];
+    if (counts) std::memcpy(counts, c.data(), 4ull * q);
+    if (offsets) std::memcpy(offsets, o.data(), 4ull * q);
+    if (cells) {
+        if (total > cap) return fail(GF_ERR_ARG, "cells buffer too small");
+        GF_CUDA(cudaMemcpy(cells, p.cells, 4ull * total, cudaMemcpyDeviceToHost));
+    }
+    if (top4) GF_CUDA(cudaMemcpy(top4, p.top4, 16ull * q, cudaMemcpyDeviceToHost));
+    if (box_counts) GF_CUDA(cudaMemcpy(box_counts, p.box, 4ull * q, cudaMemcpyDeviceToHost));
+    return GF_OK;
+}
+
+gf_status gf_search(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint32_t* ids_out,
+                    float* dist_out, void* stream) {
+    if (!idx || !plan || plan->p.idx != idx) return fail(GF_ERR_ARG, "plan does not belong to this index");
+    DeviceGuard2 guard(idx->d.device);
+    return gf::search(idx, plan, params, ids_out, dist_out, (cudaStream_t)stream);
+}
+
+gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out) {
+    if (!plan || !out) return fail(GF_ERR_ARG, "null argument");
+    Plan& p = plan->p;
+    DeviceGuard2 guard(p.idx->d.device);
+    unsigned long long v[8];
+    GF_CUDA(cudaStreamSynchronize(p.stream));
+    GF_CUDA(cudaMemcpy(v, p.stats, sizeof(v), cudaMemcpyDeviceToHost));
+    out->n_dist = v[0];
+    out->n_exp = v[1];
+    out->n_cross = v[2];
+    out->n_hops = v[3];
+    out->n_exact = v[4];
+    out->n_queries = v[5];
+    return GF_OK;
+}
+
+gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* params, const float* queries_host,
+                         const float* lb_host, const float* rb_host, uint32_t qnum, float prefilter,
+                         uint32_t* ids_host, float* dist_host, void* stream) {
+    if (!idx || !plan || plan->p.idx != idx) return fail(GF_ERR_ARG, "plan does not belong to this index");
+    if (qnum > plan->p.max_q) return fail(GF_ERR_ARG, "more queries than the plan was created for");
+    if (qnum && (!queries_host || !lb_host || !rb_host || !ids_host)) return fail(GF_ERR_ARG, "null host array");
+    DeviceGuard2 guard(idx->d.device);
+    DeviceIndex& d = idx->d;
+    Plan& p = plan->p;
+    cudaStream_t s = (cudaStream_t)stream;
+    gf_search_params P;
+    gf_search_defaults(&P);
+    if (params) P = *params;
+    // device staging: the plan's own buffers are the copy targets; outputs go to the
+    // tail of the cells buffer is not safe, so use dedicated scratch carved from q32 of
+    // the next queries is not possible either: allocate once, lazily.
+    static_assert(sizeof(float) == 4, "");
+    float *dq = nullptr, *dl = nullptr, *dr = nullptr;
+    uint32_t* dids = nullptr;
+    float* ddist = nullptr;
+    size_t need = (size_t)qnum * (d.dim + 2 * d.a + 2 * P.k);
+    cudaError_t e = cudaMallocAsync((void**)&dq, std::max<size_t>(need, 1) * 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "staging buffer");
+    dl = dq + (size_t)qnum * d.dim;
+    dr = dl + (size_t)qnum * d.a;
+    dids = reinterpret_cast<uint32_t*>(dr + (size_t)qnum * d.a);
+    ddist = reinterpret_cast<float*>(dids + (size_t)qnum * P.k);
+    gf_status st = GF_OK;
+    do {
+        if ((e = cudaMemcpyAsync(dq, queries_host, 4ull * qnum * d.dim, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(dl, lb_host, 4ull * qnum * d.a, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(dr, rb_host, 4ull * qnum * d.a, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
+        st = plan_queries(idx, plan, dq, dl, dr, qnum, prefilter, s);
+        if (st != GF_OK) break;
+        st = gf::search(idx, plan, &P, dids, dist_host ? ddist : nullptr, s);
+        if (st != GF_OK) break;
+        if ((e = cudaMemcpyAsync(ids_host, dids, 4ull * qnum * P.k, cudaMemcpyDeviceToHost, s)) != cudaSuccess) break;
+        if (dist_host &&
+            (e = cudaMemcpyAsync(dist_host, ddist, 4ull * qnum * P.k, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
+            break;
+        e = cudaStreamSynchronize(s);
+    } while (0);
+    cudaFreeAsync(dq, s);
+    if (st != GF_OK) return st;
+    if (e != cudaSuccess) return cuda_fail(e, "gf_search_host");
+    return GF_OK;
+}
+
+gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                        uint32_t k, uint32_t* ids_out, float* dist_out, void* stream) {
+    if (!idx) return fail(GF_ERR_ARG, "null index");
+    DeviceGuard2 guard(idx->d.device);
+    return gf::bruteforce(idx, queries, lb, rb, qnum, k, ids_out, dist_out, (cudaStream_t)stream);
+}
+
+}  // extern "C"

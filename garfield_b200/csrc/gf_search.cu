@@ -1,0 +1,631 @@
+// Cell-by-cell filtered beam search: one warp per query, persistent warps pulling
+// queries (most cells first) from a device counter.  Re-design of
+// select_path_contain_attr_filter_V2_without_output_with_post_pre_filter
+// (gpu_graph.cu:3270-4131) and its host driver
+// batch_graph_search_gpu_with_prefilter_and_postfilter (gpu_graph.cu:12464-12616).
+//
+// Per query the warp keeps, in shared memory: the candidate list T (L entries, double
+// buffered for rank merges), the recycle list RL (k entries, double buffered), a batch
+// buffer B, an eviction buffer, the query row (fp32, split in two planes), the box
+// bounds, a row staging area and a visited hash.  A batch of candidate rows is copied
+// into the staging area with cp.async (all rows of an expansion in flight at once,
+// 16-byte coalesced segments; the reference keeps six 8-byte loads in flight per query)
+// and each lane then computes one candidate's canonical distance from shared memory.
+// The range predicate is evaluated alongside and kept as a flag bit, so evictions and
+// the final filter need no further attribute reads.
+#include <algorithm>
+#include <cstdio>
+
+#include "gf_device.cuh"
+#include "gf_internal.h"
+
+namespace gf {
+namespace {
+
+using namespace dev;
+
+constexpr float kInf = __builtin_huge_valf();
+
+struct SArgs {
+    const uint4* __restrict__ vec16;
+    const float* __restrict__ attrs;
+    const uint32_t* __restrict__ graph;
+    const uint32_t* __restrict__ cross;
+    const uint32_t* __restrict__ seg;
+    const uint32_t* __restrict__ i2g;
+    const uint4* __restrict__ q16;
+    const float* __restrict__ lb;
+    const float* __restrict__ rb;
+    const uint32_t* __restrict__ counts;
+    const uint32_t* __restrict__ offsets;
+    const uint32_t* __restrict__ cells;
+    const uint32_t* __restrict__ box;  // box counts (only when prefilter > 0)
+    const uint32_t* __restrict__ task;
+    const uint32_t* __restrict__ entry;
+    uint32_t* queue;
+    uint32_t* out_ids;
+    float* out_d;
+    unsigned long long* stats;
+    uint32_t qnum, nch, nch16, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
+    float prefilter;
+    uint32_t hs, hshift, bcap, stage_rows, warp_words;
+    // word offsets inside a warp's shared-memory slice
+    uint32_t o_qa, o_qb, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
+        o_picks, o_stage, o_hash;
+};
+
+struct Layout {
+    uint32_t o_qa, o_qb, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
+        o_picks, o_stage, o_hash, words;
+};
+
+// Shared-memory layout of one warp, in 32-bit words, every region 16-byte aligned.
+Layout make_layout(uint32_t nch16, uint32_t L, uint32_t K, uint32_t bcap, uint32_t stage_rows, uint32_t hs) {
+    Layout l;
+    uint32_t o = 0;
+    auto take = [&](uint32_t words) {
+        uint32_t r = o;
+        o += (words + 3) & ~3u;
+        return r;
+    };
+    l.o_qa = take(nch16 * 4);
+    l.o_qb = take(nch16 * 4);
+    l.o_lb = take(kMaxAttr);
+    l.o_rb = take(kMaxAttr);
+    l.o_t0d = take(L);
+    l.o_t0w = take(L);
+    l.o_t1d = take(L);
+    l.o_t1w = take(L);
+    l.o_r0d = take(K);
+    l.o_r0w = take(K);
+    l.o_r1d = take(K);
+    l.o_r1w = take(K);
+    l.o_bd = take(bcap);
+    l.o_bw = take(bcap);
+    l.o_ed = take(bcap);
+    l.o_ew = take(bcap);
+    l.o_picks = take(32);
+    l.o_stage = take(stage_rows * nch16 * 4);
+    l.o_hash = take(hs);
+    l.words = o;
+    return l;
+}
+
+// Per-warp view of the shared slice; pointers are recomputed from the base and the
+// offsets (kernel parameters) where used, which keeps few registers live.
+struct W {
+    uint32_t* base;
+    uint32_t tsel, rsel;  // which buffer of T / RL is current
+    __device__ float* td(const SArgs& A) const { return (float*)(base + (tsel ? A.o_t1d : A.o_t0d)); }
+    __device__ uint32_t* tw(const SArgs& A) const { return base + (tsel ? A.o_t1w : A.o_t0w); }
+    __device__ float* nd(const SArgs& A) const { return (float*)(base + (tsel ? A.o_t0d : A.o_t1d)); }
+    __device__ uint32_t* nw(const SArgs& A) const { return base + (tsel ? A.o_t0w : A.o_t1w); }
+    __device__ float* rd(const SArgs& A) const { return (float*)(base + (rsel ? A.o_r1d : A.o_r0d)); }
+    __device__ uint32_t* rw(const SArgs& A) const { return base + (rsel ? A.o_r1w : A.o_r0w); }
+    __device__ float* rnd(const SArgs& A) const { return (float*)(base + (rsel ? A.o_r0d : A.o_r1d)); }
+    __device__ uint32_t* rnw(const SArgs& A) const { return base + (rsel ? A.o_r0w : A.o_r1w); }
+    __device__ float* bd(const SArgs& A) const { return (float*)(base + A.o_bd); }
+    __device__ uint32_t* bw(const SArgs& A) const { return base + A.o_bw; }
+    __device__ float* ed(const SArgs& A) const { return (float*)(base + A.o_ed); }
+    __device__ uint32_t* ew(const SArgs& A) const { return base + A.o_ew; }
+    __device__ uint32_t* picks(const SArgs& A) const { return base + A.o_picks; }
+    __device__ uint32_t* H(const SArgs& A) const { return base + A.o_hash; }
+    __device__ const float* lb(const SArgs& A) const { return (const float*)(base + A.o_lb); }
+    __device__ const float* rb(const SArgs& A) const { return (const float*)(base + A.o_rb); }
+};
+
+__device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 1u << (32 - __clz(x - 1)); }
+
+// Distances + range flags for the positions in B[0..nb): rows are staged through
+// shared memory in rounds of stage_rows.
+__device__ __forceinline__ void eval_batch(const SArgs& A, const W& w, uint32_t nb) {
+    const uint32_t lane = lane_id();
+    uint32_t* bw = w.bw(A);
+    float* bd = w.bd(A);
+    uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
+    const float4* qa = reinterpret_cast<const float4*>(w.base + A.o_qa);
+    const float4* qb = reinterpret_cast<const float4*>(w.base + A.o_qb);
+    for (uint32_t r0 = 0; r0 < nb; r0 += A.stage_rows) {
+        const uint32_t rows = min(A.stage_rows, nb - r0);
+        const uint32_t total = rows * A.nch;
+        for (uint32_t e = lane; e < total; e += 32) {
+            uint32_t r = e / A.nch, c = e - r * A.nch;
+            uint32_t pos = bw[r0 + r];
+            cp_async16(stage + (size_t)r * A.nch16 + c, A.vec16 + (size_t)pos * A.nch + c);
+        }
+        bool inr = false;
+        uint32_t pos = 0;
+        if (lane < rows) {
+            pos = bw[r0 + lane];
+            inr = in_box(A.attrs, pos, A.a, w.lb(A), w.rb(A));
+        }
+        cp_async_wait_all();
+        __syncwarp();
+        if (lane < rows) {
+            float d = dist16_staged(stage + (size_t)lane * A.nch16, qa, qb, A.nch, lane & 15u);
+            bd[r0 + lane] = d;
+            bw[r0 + lane] = pos | (inr ? kInRange : 0u);
+        }
+        __syncwarp();
+    }
+}
+
+// Sort B[0..nb) (pads with empty entries up to the next power of two).
+__device__ __forceinline__ void sort_batch(const SArgs& A, const W& w, uint32_t nb) {
+    uint32_t n = next_pow2(nb < 2 ? 2 : nb);
+    float* bd = w.bd(A);
+    uint32_t* bw = w.bw(A);
+    for (uint32_t j = nb + lane_id(); j < n; j += 32) {
+        bd[j] = kInf;
+        bw[j] = kEmpty;
+    }
+    __syncwarp();
+    warp_sort(bd, bw, n);
+}
+
+// Merge B[b0..b0+nb) into T (length L); with recycling, in-range entries pushed out of
+// T are merged into RL (length k).
+__device__ __forceinline__ void merge_step(const SArgs& A, W& w, uint32_t L, uint32_t b0, uint32_t nb, bool recycle) {
+    if (nb == 0) return;
+    const float* bd = w.bd(A) + b0;
+    const uint32_t* bw = w.bw(A) + b0;
+    {
+        const float* td = w.td(A);
+        const uint32_t* tw = w.tw(A);
+        // nothing can enter a full list whose last entry beats the best candidate
+        if (tw[L - 1] != kEmpty && mkkey(bd[0], bw[0]) > mkkey(td[L - 1], tw[L - 1])) return;
+    }
+    uint32_t nev = merge_list(w.td(A), w.tw(A), w.nd(A), w.nw(A), L, bd, bw, nb, w.ed(A), w.ew(A), recycle);
+    w.tsel ^= 1u;
+    if (nev == 0) return;
+    const uint32_t K = A.K;
+    if (w.rw(A)[K - 1] != kEmpty && mkkey(w.ed(A)[0], w.ew(A)[0]) > mkkey(w.rd(A)[K - 1], w.rw(A)[K - 1])) return;
+    merge_list(w.rd(A), w.rw(A), w.rnd(A), w.rnw(A), K, w.ed(A), w.ew(A), nev, nullptr, nullptr, false);
+    w.rsel ^= 1u;
+}
+
+// Clear the hash and insert the list entries that lie in [lo, hi).
+__device__ __forceinline__ uint32_t hash_rebuild(const SArgs& A, const W& w, uint32_t lo, uint32_t hi) {
+    uint32_t* H = w.H(A);
+    const uint32_t* tw = w.tw(A);
+    hash_clear(H, A.hs);
+    uint32_t cnt = 0;
+    for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
+        uint32_t i = i0 + lane_id();
+        bool ins = false;
+        if (i < A.L) {
+            uint32_t v = tw[i];
+            uint32_t pos = v & kPosMask;
+            if (v != kEmpty && pos >= lo && pos < hi) ins = hash_insert(H, A.hs, A.hshift, pos);
+        }
+        cnt += __popc(__ballot_sync(kFull, ins));
+    }
+    __syncwarp();
+    return cnt;
+}
+
+__device__ __forceinline__ void write_result(const SArgs& A, uint32_t q, const float* d, const uint32_t* wv,
+                                             uint32_t n) {
+    for (uint32_t k = lane_id(); k < A.K; k += 32) {
+        uint32_t wk = k < n ? wv[k] : kEmpty;
+        A.out_ids[(size_t)q * A.K + k] = wk == kEmpty ? kEmpty : A.i2g[wk & kPosMask];
+        if (A.out_d) A.out_d[(size_t)q * A.K + k] = wk == kEmpty ? kInf : d[k];
+    }
+}
+
+// Append the positions held by lanes with ok=true to B at *nb (warp-uniform counter).
+__device__ __forceinline__ void append(uint32_t* bw, uint32_t& nb, bool ok, uint32_t pos) {
+    uint32_t msk = __ballot_sync(kFull, ok);
+    if (ok) bw[nb + __popc(msk & lanemask_lt())] = pos;
+    nb += __popc(msk);
+}
+
+// Exact route (gpu_graph.cu:3788-4022): every in-range point of the query's cells.
+__device__ __forceinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uint32_t q, const uint32_t* cl,
+                                             uint32_t nc) {
+    const uint32_t lane = lane_id();
+    W w{base, 0u, 0u};
+    float* td = w.td(A);
+    uint32_t* tw = w.tw(A);
+    for (uint32_t i = lane; i < A.K; i += 32) {
+        td[i] = kInf;
+        tw[i] = kEmpty;
+    }
+    __syncwarp();
+    uint32_t nb = 0, ndist = 0;
+    const uint32_t flush_at = A.bcap - 32;
+    uint32_t* bw = w.bw(A);
+    for (uint32_t ci = 0; ci < nc; ++ci) {
+        const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
+        for (uint32_t x0 = lo; x0 < hi; x0 += 32) {
+            const uint32_t x = x0 + lane;
+            append(bw, nb, x < hi && in_box(A.attrs, x, A.a, w.lb(A), w.rb(A)), x);
+            const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
+            if (nb > flush_at || (last && nb)) {
+                __syncwarp();
+                eval_batch(A, w, nb);
+                ndist += nb;
+                sort_batch(A, w, nb);
+                merge_step(A, w, A.K, 0, nb, false);
+                nb = 0;
+            }
+        }
+    }
+    __syncwarp();
+    write_result(A, q, w.td(A), w.tw(A), A.K);
+    return ndist;
+}
+
+__global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
+    extern __shared__ __align__(16) uint32_t smem[];
+    const uint32_t lane = lane_id();
+    uint32_t* const base = smem + (threadIdx.x >> 5) * A.warp_words;
+
+    for (;;) {
+        uint32_t slot = 0;
+        if (lane == 0) slot = atomicAdd(A.queue, 1u);
+        slot = __shfl_sync(kFull, slot, 0);
+        if (slot >= A.qnum) break;
+        const uint32_t q = A.task[slot];
+        const uint32_t nc = A.counts[q];
+        const uint32_t* cl = A.cells + A.offsets[q];
+        // query row (fp16 -> fp32, two planes) and box
+        {
+            float4* qa = reinterpret_cast<float4*>(base + A.o_qa);
+            float4* qb = reinterpret_cast<float4*>(base + A.o_qb);
+            for (uint32_t c = lane; c < A.nch; c += 32) {
+                uint4 v = A.q16[(size_t)q * A.nch + c];
+                float2 f0 = __half22float2(*reinterpret_cast<__half2*>(&v.x));
+                float2 f1 = __half22float2(*reinterpret_cast<__half2*>(&v.y));
+                float2 f2 = __half22float2(*reinterpret_cast<__half2*>(&v.z));
+                float2 f3 = __half22float2(*reinterpret_cast<__half2*>(&v.w));
+                qa[c] = make_float4(f0.x, f0.y, f1.x, f1.y);
+                qb[c] = make_float4(f2.x, f2.y, f3.x, f3.y);
+            }
+            if (lane < A.a) {
+                base[A.o_lb + lane] = __float_as_uint(A.lb[(size_t)q * A.a + lane]);
+                base[A.o_rb + lane] = __float_as_uint(A.rb[(size_t)q * A.a + lane]);
+            }
+            __syncwarp();
+        }
+        uint32_t st_dist = 0, st_exp = 0, st_cross = 0, st_hops = 0, st_exact = 0;
+        if (nc == 0) {
+            write_result(A, q, nullptr, nullptr, 0);
+        } else {
+            bool exact = nc >= A.postfilter;
+            if (!exact && A.box) {
+                float prop = (float)((double)A.box[q] / (double)A.n);  // real_dataset_adapter.cuh:380
+                exact = prop <= A.prefilter;
+            }
+            if (exact) {
+                st_exact = 1;
+                st_dist = exact_route(A, base, q, cl, nc);
+            } else {
+                W w{base, 0u, 0u};
+                {
+                    float* td = w.td(A);
+                    uint32_t* tw = w.tw(A);
+                    for (uint32_t i = lane; i < A.L; i += 32) {
+                        td[i] = kInf;
+                        tw[i] = kEmpty;
+                    }
+                    float* rd = w.rd(A);
+                    uint32_t* rw = w.rw(A);
+                    for (uint32_t i = lane; i < A.K; i += 32) {
+                        rd[i] = kInf;
+                        rw[i] = kEmpty;
+                    }
+                }
+                hash_clear(w.H(A), A.hs);
+                uint32_t hcount = 0;
+                // entry set of the first cell (gpu_graph.cu:3347-3351)
+                uint32_t nb = 0;
+                {
+                    const uint32_t cell = cl[0], lo = A.seg[cell], sz = A.seg[cell + 1] - lo;
+                    for (uint32_t i0 = 0; i0 < A.n_entry; i0 += 32) {
+                        uint32_t i = i0 + lane;
+                        bool ok = false;
+                        uint32_t pos = 0;
+                        if (i < A.n_entry) {
+                            uint32_t e = A.entry[i];
+                            if (e < sz) {
+                                pos = lo + e;
+                                ok = hash_insert(w.H(A), A.hs, A.hshift, pos);
+                            }
+                        }
+                        append(w.bw(A), nb, ok, pos);
+                    }
+                    __syncwarp();
+                    hcount = nb;
+                    eval_batch(A, w, nb);
+                    st_dist += nb;
+                    sort_batch(A, w, nb);
+                }
+                for (uint32_t ci = 0; ci < nc; ++ci) {
+                    const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
+                    // (a) entry set -> T, with recycling
+                    merge_step(A, w, A.L, 0, nb, true);
+                    // (b) beam rounds: expand the first W unexplored entries of T
+                    for (uint32_t it = 0; it < A.max_iter; ++it) {
+                        uint32_t np = 0;
+                        {
+                            uint32_t* tw = w.tw(A);
+                            uint32_t* picks = w.picks(A);
+                            for (uint32_t i0 = 0; i0 < A.L && np < A.W; i0 += 32) {
+                                uint32_t i = i0 + lane;
+                                uint32_t v = i < A.L ? tw[i] : kEmpty;
+                                uint32_t msk = __ballot_sync(kFull, v != kEmpty && !(v & kExplored));
+                                while (msk && np < A.W) {
+                                    uint32_t b = __ffs(msk) - 1;
+                                    msk &= msk - 1;
+                                    if (lane == b) {
+                                        tw[i] = v | kExplored;
+                                        picks[np] = v & kPosMask;
+                                    }
+                                    ++np;
+                                }
+                            }
+                            __syncwarp();
+                        }
+                        if (np == 0) break;
+                        st_exp += np;
+                        const uint32_t total = np * A.R;
+                        if (hcount + total > (A.hs >> 1)) hcount = hash_rebuild(A, w, lo, hi);
+                        nb = 0;
+                        {
+                            const uint32_t* picks = w.picks(A);
+                            uint32_t* H = w.H(A);
+                            for (uint32_t j0 = 0; j0 < total; j0 += 32) {
+                                uint32_t j = j0 + lane;
+                                bool ok = false;
+                                uint32_t pos = kEmpty;
+                                if (j < total) {
+                                    uint32_t node = picks[j / A.R];
+                                    pos = __ldg(A.graph + (size_t)node * A.R + (j % A.R));
+                                    if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+                                }
+                                append(w.bw(A), nb, ok, pos);
+                            }
+                            __syncwarp();
+                        }
+                        hcount += nb;
+                        if (nb == 0) continue;
+                        eval_batch(A, w, nb);
+                        st_dist += nb;
+                        sort_batch(A, w, nb);
+                        merge_step(A, w, A.L, 0, nb, true);
+                    }
+                    // (c) everything in T counts as explored from here on
+                    {
+                        uint32_t* tw = w.tw(A);
+                        for (uint32_t i = lane; i < A.L; i += 32)
+                            if (tw[i] != kEmpty) tw[i] |= kExplored;
+                        __syncwarp();
+                    }
+                    // (d) cross-cell hop (gpu_graph.cu:3564-3643)
+                    if (ci + 1 < nc) {
+                        const uint32_t next = cl[ci + 1], nlo = A.seg[next], nsz = A.seg[next + 1] - nlo;
+                        const uint32_t hop_n = A.L < kHopSlots ? A.L : kHopSlots;
+                        const uint32_t* tw = w.tw(A);
+                        uint32_t V = 0;
+                        for (uint32_t i0 = 0; i0 < hop_n; i0 += 32) {
+                            uint32_t i = i0 + lane;
+                            V += __popc(__ballot_sync(kFull, i < hop_n && tw[i] != kEmpty));
+                        }
+                        uint32_t* H = w.H(A);
+                        hash_clear(H, A.hs);
+                        const uint32_t pairs = V * A.E;
+                        const size_t rowlen = (size_t)A.P * A.E;
+                        nb = 0;
+                        for (uint32_t j0 = 0; j0 < pairs; j0 += 32) {
+                            uint32_t j = j0 + lane;
+                            bool ok = false;
+                            uint32_t pos = kEmpty;
+                            if (j < pairs) {
+                                uint32_t src = tw[j / A.E] & kPosMask;
+                                pos = __ldg(A.cross + (size_t)src * rowlen + (size_t)next * A.E + (j % A.E));
+                                if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+                            }
+                            append(w.bw(A), nb, ok, pos);
+                        }
+                        __syncwarp();
+                        st_cross += V;
+                        // filler: smallest local ids of the next cell not among the targets
+                        uint32_t nf = pairs - nb;
+                        uint32_t* bw = w.bw(A);
+                        for (uint32_t x0 = 0; nf > 0 && x0 < nsz; x0 += 32) {
+                            uint32_t x = x0 + lane;
+                            bool ok = x < nsz && !hash_contains(H, A.hs, A.hshift, nlo + x);
+                            uint32_t msk = __ballot_sync(kFull, ok);
+                            uint32_t idx = __popc(msk & lanemask_lt());
+                            if (ok && idx < nf) bw[nb + idx] = nlo + x;
+                            uint32_t take = min((uint32_t)__popc(msk), nf);
+                            nb += take;
+                            nf -= take;
+                        }
+                        __syncwarp();
+                        eval_batch(A, w, nb);
+                        st_dist += nb;
+                        sort_batch(A, w, nb);
+                        const uint32_t ne = min(nb, A.n_entry);
+                        const uint32_t nm = min(nb - ne, kHopSlots);
+                        merge_step(A, w, A.L, ne, nm, false);
+                        // visited set of the next cell: its entry set + its points now in T
+                        hash_clear(H, A.hs);
+                        uint32_t cnt = 0;
+                        for (uint32_t i0 = 0; i0 < ne; i0 += 32) {
+                            uint32_t i = i0 + lane;
+                            bool ins = i < ne && hash_insert(H, A.hs, A.hshift, bw[i] & kPosMask);
+                            cnt += __popc(__ballot_sync(kFull, ins));
+                        }
+                        const uint32_t* tw2 = w.tw(A);
+                        for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
+                            uint32_t i = i0 + lane;
+                            bool ins = false;
+                            if (i < A.L) {
+                                uint32_t v = tw2[i], pos = v & kPosMask;
+                                if (v != kEmpty && pos >= nlo && pos < nlo + nsz)
+                                    ins = hash_insert(H, A.hs, A.hshift, pos);
+                            }
+                            cnt += __popc(__ballot_sync(kFull, ins));
+                        }
+                        __syncwarp();
+                        hcount = cnt;
+                        nb = ne;
+                        ++st_hops;
+                    }
+                }
+                // final post-filter of T and recycle merge (gpu_graph.cu:4025-4048)
+                uint32_t nin = 0;
+                {
+                    const float* td = w.td(A);
+                    const uint32_t* tw = w.tw(A);
+                    float* nd = w.nd(A);
+                    uint32_t* nw = w.nw(A);
+                    for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
+                        uint32_t i = i0 + lane;
+                        uint32_t v = i < A.L ? tw[i] : kEmpty;
+                        bool ok = v != kEmpty && (v & kInRange);
+                        uint32_t msk = __ballot_sync(kFull, ok);
+                        if (ok) {
+                            uint32_t k = nin + __popc(msk & lanemask_lt());
+                            nd[k] = td[i];
+                            nw[k] = v;
+                        }
+                        nin += __popc(msk);
+                    }
+                    __syncwarp();
+                }
+                merge_list(w.rd(A), w.rw(A), w.rnd(A), w.rnw(A), A.K, w.nd(A), w.nw(A), nin, nullptr, nullptr, false);
+                write_result(A, q, w.rnd(A), w.rnw(A), A.K);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            atomicAdd(A.stats + 0, (unsigned long long)st_dist);
+            atomicAdd(A.stats + 1, (unsigned long long)st_exp);
+            atomicAdd(A.stats + 2, (unsigned long long)st_cross);
+            atomicAdd(A.stats + 3, (unsigned long long)st_hops);
+            atomicAdd(A.stats + 4, (unsigned long long)st_exact);
+            atomicAdd(A.stats + 5, 1ull);
+        }
+    }
+}
+
+}  // namespace
+
+gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
+                 cudaStream_t s) {
+    DeviceIndex& d = idx->d;
+    Plan& p = plan->p;
+    if (!p.planned) return fail(GF_ERR_STATE, "gf_search before gf_plan_queries");
+    gf_search_params P;
+    gf_search_defaults(&P);
+    if (prm) P = *prm;
+    if (P.k == 0 || P.k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");
+    if (P.L < P.k || P.L > 4096) return fail(GF_ERR_ARG, "L must be k..4096");
+    if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
+    uint32_t n_entry = P.n_entry ? P.n_entry : d.degree;
+    n_entry = std::min<uint32_t>(n_entry, (uint32_t)d.entry_h.size());
+    if (!ids) return fail(GF_ERR_ARG, "null ids_out");
+    if (p.qnum == 0) return GF_OK;
+
+    SArgs A;
+    A.vec16 = d.vec16;
+    A.attrs = d.attrs;
+    A.graph = d.graph;
+    A.cross = d.cross;
+    A.seg = d.seg;
+    A.i2g = d.i2g;
+    A.q16 = p.q16;
+    A.lb = p.lb;
+    A.rb = p.rb;
+    A.counts = p.counts;
+    A.offsets = p.offsets;
+    A.cells = p.cells;
+    A.box = p.prefilter > 0.0f ? p.box : nullptr;
+    A.task = p.task;
+    A.entry = d.entry;
+    A.queue = p.scratch;
+    A.out_ids = ids;
+    A.out_d = dist;
+    A.stats = p.stats;
+    A.qnum = p.qnum;
+    A.nch = d.d8 / 8;
+    A.nch16 = (A.nch + 15) / 16 * 16;
+    A.a = d.a;
+    A.P = d.ncells;
+    A.R = d.degree;
+    A.E = d.cross ? d.E : 0;
+    A.L = P.L;
+    A.K = P.k;
+    A.W = P.width;
+    A.max_iter = P.max_iter;
+    A.n_entry = n_entry;
+    A.postfilter = P.postfilter;
+    A.n = d.n;
+    A.prefilter = p.prefilter;
+    uint32_t need = std::max<uint32_t>({P.width * d.degree, n_entry, kHopSlots * A.E, 64u});
+    uint32_t bcap = 1;
+    while (bcap < need) bcap <<= 1;
+    A.bcap = bcap;
+    uint32_t hs = P.hash_slots;
+    if (hs == 0) {
+        hs = 256;
+        while (hs < 2 * (P.L + bcap)) hs <<= 1;
+    }
+    if (hs & (hs - 1)) return fail(GF_ERR_ARG, "hash_slots must be a power of two");
+    if (hs < 2 * (P.L + bcap)) return fail(GF_ERR_ARG, "hash_slots below 2*(L + batch)");
+    A.hs = hs;
+    uint32_t lg = 0;
+    while ((1u << lg) < hs) ++lg;
+    A.hshift = 32 - lg;
+    // staging: up to 32 rows, at most 8 KB per warp
+    uint32_t row_bytes = A.nch16 * 16;
+    uint32_t sr = 32;
+    while (sr > 1 && sr * row_bytes > 8192) sr >>= 1;
+    A.stage_rows = sr;
+    Layout lay = make_layout(A.nch16, A.L, A.K, A.bcap, A.stage_rows, A.hs);
+    A.o_qa = lay.o_qa;
+    A.o_qb = lay.o_qb;
+    A.o_lb = lay.o_lb;
+    A.o_rb = lay.o_rb;
+    A.o_t0d = lay.o_t0d;
+    A.o_t0w = lay.o_t0w;
+    A.o_t1d = lay.o_t1d;
+    A.o_t1w = lay.o_t1w;
+    A.o_r0d = lay.o_r0d;
+    A.o_r0w = lay.o_r0w;
+    A.o_r1d = lay.o_r1d;
+    A.o_r1w = lay.o_r1w;
+    A.o_bd = lay.o_bd;
+    A.o_bw = lay.o_bw;
+    A.o_ed = lay.o_ed;
+    A.o_ew = lay.o_ew;
+    A.o_picks = lay.o_picks;
+    A.o_stage = lay.o_stage;
+    A.o_hash = lay.o_hash;
+    A.warp_words = lay.words;
+
+    const int warps_per_block = 4;
+    size_t smem = (size_t)warps_per_block * A.warp_words * 4;
+    int dev = d.device;
+    int max_optin = 0, nsm = 0;
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (smem > (size_t)max_optin) return fail(GF_ERR_ARG, "L/k/hash too large for shared memory");
+    GF_CUDA(cudaFuncSetAttribute(gmg_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    GF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gmg_search_kernel, 128, smem));
+    if (per_sm < 1) return fail(GF_ERR_ARG, "search kernel does not fit on an SM");
+    uint32_t blocks = (uint32_t)(nsm * per_sm);
+    uint32_t need_blocks = (p.qnum + warps_per_block - 1) / warps_per_block;
+    blocks = std::min(blocks, need_blocks);
+    GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
+    GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
+    gmg_search_kernel<<<blocks, 128, smem, s>>>(A);
+    GF_CUDA(cudaGetLastError());
+    return GF_OK;
+}
+
+}  // namespace gf

@@ -1,0 +1,300 @@
+"""GMG index construction for synthetic datasets (test and benchmark inputs).
+
+The reference builds its index offline with cuVS (indexbuild/*.py: CAGRA per-cell
+graphs, CAGRA searches for cross-cell edges, k-means); cuVS is not available here, so
+this module builds the same files with torch (GPU when present, else CPU):
+
+  quantile_grid   indexbuild/tools.py:88-125 grid_scatter_V2 (per-dimension quantile slices)
+  cell_graphs     per-cell navigable graph of degree R (indexbuild/uniform_partition.py:516-563
+                  uses CAGRA); here: exact 2R-NN + R random cell members as candidates,
+                  robust pruning with alpha = 1.2 (the DiskANN/Vamana rule), one reverse-edge
+                  pass, rows padded to R from the nearest neighbours
+  cross_edges     indexbuild/global_graph_build.py:116-157: for every point and every cell, the
+                  E nearest points of that cell (local ids), here exact
+  kmeans          indexbuild/clustering.py:68-88 (cuVS k-means); here Lloyd iterations
+
+Outputs use the reference's on-disk layout (global point order): graphs of all cells
+concatenated in cell order with local ids, cross edges n x (cells * E) local ids.
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+try:
+    import torch
+except ImportError:  # pragma: no cover
+    torch = None
+
+
+def _device(dev=None):
+    if dev is not None:
+        return torch.device(dev)
+    return torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+
+
+def quantile_grid(attrs: np.ndarray, grid):
+    """Restates grid_scatter_V2 (indexbuild/tools.py:88-125): per dimension, a stable
+    argsort cut into grid[j] runs of ceil(n / grid[j]) points (the last run takes the rest);
+    l_quant / r_quant are the first / last sorted value of each run; cell id is the
+    row-major mixed radix of the per-dimension slice ids (last dimension fastest)."""
+    n, a = attrs.shape
+    grid = np.asarray(grid, dtype=np.int64)
+    lq, rq, slices = [], [], np.zeros((n, a), np.int32)
+    for j in range(a):
+        col = attrs[:, j]
+        order = np.argsort(col, kind="stable")
+        srt = col[order]
+        g = int(grid[j])
+        avg = (n + g - 1) // g
+        starts = [s * avg for s in range(g)]
+        ends = [min((s + 1) * avg, n) if s < g - 1 else n for s in range(g)]
+        lq.append(np.array([srt[s] for s in starts], np.int32))
+        rq.append(np.array([srt[e - 1] for e in ends], np.int32))
+        for s in range(g):
+            slices[order[starts[s]:ends[s]], j] = s
+    factors = np.concatenate([np.cumprod(grid[::-1])[::-1][1:], [1]])
+    cell_of = (slices.astype(np.int64) * factors[None, :]).sum(1).astype(np.uint32)
+    return np.concatenate(lq), np.concatenate(rq), slices, cell_of
+
+
+def _sqdist(x, y):
+    """Squared L2 between row sets (torch, fp32)."""
+    xx = (x * x).sum(1, keepdim=True)
+    yy = (y * y).sum(1)[None, :]
+    d = torch.addmm(xx + yy, x, y.t(), beta=1.0, alpha=-2.0)
+    return d.clamp_min_(0.0)
+
+
+def knn(x, k: int, chunk: int = 4096):
+    """Exact k nearest neighbours of every row of x among the other rows of x."""
+    n = x.shape[0]
+    k = min(k, n - 1)
+    idx = torch.empty((n, k), dtype=torch.int64, device=x.device)
+    dst = torch.empty((n, k), dtype=torch.float32, device=x.device)
+    ar = torch.arange(n, device=x.device)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        d = _sqdist(x[s:e], x)
+        d[torch.arange(e - s, device=x.device), ar[s:e]] = float("inf")
+        v, i = torch.topk(d, k, dim=1, largest=False, sorted=True)
+        idx[s:e], dst[s:e] = i, v
+    return idx, dst
+
+
+def _robust_prune(x, node_ids, cand, R: int, alpha: float, batch: int = 2048):
+    """Robust pruning (Vamana RobustPrune) of candidate lists: walk the candidates of each
+    node by increasing distance, keep c unless a kept p* has alpha * d(p*, c) <= d(node, c).
+    cand: (m, M) int64 row ids (may contain -1 / duplicates).  Returns (m, R) ids, -1 padded."""
+    m, M = cand.shape
+    out = torch.full((m, R), -1, dtype=torch.int64, device=x.device)
+    for s in range(0, m, batch):
+        e = min(m, s + batch)
+        c = cand[s:e]
+        valid = c >= 0
+        cs = torch.where(valid, c, torch.zeros_like(c))
+        xv = x[cs]                                      # b x M x d
+        xn = x[node_ids[s:e]]                           # b x d
+        dnc = ((xv - xn[:, None, :]) ** 2).sum(-1)     # b x M
+        dnc = torch.where(valid & (cs != node_ids[s:e, None]), dnc, torch.full_like(dnc, float("inf")))
+        order = torch.argsort(dnc, dim=1, stable=True)
+        c = torch.gather(cs, 1, order)
+        dnc = torch.gather(dnc, 1, order)
+        xv = x[c]
+        # duplicates are adjacent after sorting by (distance, stable position)
+        dup = torch.zeros_like(dnc, dtype=torch.bool)
+        dup[:, 1:] = (c[:, 1:] == c[:, :-1])
+        alive = torch.isfinite(dnc) & ~dup
+        g = torch.bmm(xv, xv.transpose(1, 2))
+        nrm = (xv * xv).sum(-1)
+        dcc = (nrm[:, :, None] + nrm[:, None, :] - 2 * g).clamp_min_(0.0)
+        cnt = torch.zeros(e - s, dtype=torch.int64, device=x.device)
+        sel = torch.zeros_like(alive)
+        for j in range(M):
+            take = alive[:, j] & (cnt < R)
+            sel[:, j] = take
+            cnt += take.long()
+            if j + 1 < M:
+                kill = take[:, None] & (alpha * alpha * dcc[:, j, j + 1:] <= dnc[:, j + 1:])
+                alive[:, j + 1:] &= ~kill
+        # compact the selected ids, in distance order
+        key = torch.where(sel, torch.arange(M, device=x.device)[None, :].expand_as(sel), torch.full_like(c, M))
+        ks, ko = torch.sort(key, dim=1)
+        picked = torch.gather(c, 1, ko)[:, :R]
+        picked = torch.where(ks[:, :R] < M, picked, torch.full_like(picked, -1))
+        out[s:e, : picked.shape[1]] = picked
+    return out
+
+
+def cell_graph(x, R: int, alpha: float = 1.2, n_random: int | None = None, seed: int = 0):
+    """Degree-R navigable graph over the rows of x (local ids)."""
+    n = x.shape[0]
+    if n <= 1:
+        return torch.zeros((n, R), dtype=torch.int64, device=x.device)
+    n_random = R if n_random is None else n_random
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    nn_idx, _ = knn(x, 2 * R)
+    rnd = torch.randint(0, n, (n, n_random), generator=g).to(x.device)
+    ids = torch.arange(n, device=x.device)
+    cand = torch.cat([nn_idx, rnd], 1)
+    first = _robust_prune(x, ids, cand, R, alpha)
+    # reverse edges: each kept edge p -> q offers p to q (at most R offers per node)
+    src = ids[:, None].expand_as(first)
+    ok = first >= 0
+    dst_e, src_e = first[ok], src[ok]
+    order = torch.argsort(dst_e, stable=True)
+    dst_e, src_e = dst_e[order], src_e[order]
+    cnt = torch.bincount(dst_e, minlength=n)
+    start = torch.cumsum(cnt, 0) - cnt
+    rank = torch.arange(dst_e.numel(), device=x.device) - start[dst_e]
+    keep = rank < R
+    rev = torch.full((n, R), -1, dtype=torch.int64, device=x.device)
+    rev[dst_e[keep], rank[keep]] = src_e[keep]
+    second = _robust_prune(x, ids, torch.cat([first, rev], 1), R, alpha)
+    # pad rows to exactly R with the nearest neighbours not yet present
+    out = second.clone()
+    filled = (out >= 0).sum(1)
+    if bool((filled < R).any()):
+        rows = torch.nonzero(filled < R).flatten().tolist()
+        o_cpu = out.cpu()
+        nn_cpu = nn_idx.cpu()
+        for r in rows:
+            have = set(int(v) for v in o_cpu[r] if v >= 0)
+            fill = [int(v) for v in nn_cpu[r] if int(v) not in have]
+            k = int(filled[r])
+            for v in fill:
+                if k >= R:
+                    break
+                o_cpu[r, k] = v
+                k += 1
+            while k < R:  # tiny cells: repeat
+                o_cpu[r, k] = o_cpu[r, k % max(1, int(filled[r]))] if filled[r] > 0 else (r + 1) % n
+                k += 1
+        out = o_cpu.to(x.device)
+    return out
+
+
+def cross_edges(x, cell_of_t, seg, E: int = 2, chunk: int = 8192):
+    """For every point and every cell, the E nearest points of that cell (local ids)."""
+    n = x.shape[0]
+    P = len(seg) - 1
+    out = torch.empty((n, P * E), dtype=torch.int64, device=x.device)
+    for c in range(P):
+        lo, hi = int(seg[c]), int(seg[c + 1])
+        y = x[lo:hi]
+        e = min(E, hi - lo)
+        for s in range(0, n, chunk):
+            t = min(n, s + chunk)
+            d = _sqdist(x[s:t], y)
+            _, i = torch.topk(d, e, dim=1, largest=False, sorted=True)
+            if e < E:
+                i = torch.cat([i, i[:, :1].expand(-1, E - e)], 1)
+            out[s:t, c * E:(c + 1) * E] = i
+    return out
+
+
+def kmeans(x, C: int, iters: int = 10, seed: int = 0, chunk: int = 65536):
+    """Lloyd k-means; returns int32 labels."""
+    n = x.shape[0]
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    cent = x[torch.randperm(n, generator=g)[:C].to(x.device)].clone()
+    labels = torch.empty(n, dtype=torch.int64, device=x.device)
+    for _ in range(iters):
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            labels[s:e] = _sqdist(x[s:e], cent).argmin(1)
+        sums = torch.zeros_like(cent).index_add_(0, labels, x)
+        cnt = torch.bincount(labels, minlength=C).float()
+        nz = cnt > 0
+        cent[nz] = sums[nz] / cnt[nz, None]
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        labels[s:e] = _sqdist(x[s:e], cent).argmin(1)
+    return labels.to(torch.int32)
+
+
+@dataclass
+class GmgArrays:
+    """Index arrays in the reference's layout (global point order)."""
+    grid: np.ndarray        # uint32 a
+    l_quant: np.ndarray     # int32 sum(grid)
+    r_quant: np.ndarray
+    slices: np.ndarray      # int32 n x a (per-dimension slice ids)
+    cell_of: np.ndarray     # uint32 n
+    graphs: np.ndarray      # uint32 n x R, per-cell graphs concatenated in cell order, local ids
+    cross: np.ndarray       # uint32 n x (cells*E), local ids
+    labels: np.ndarray      # int32 n
+    degree: int
+    cross_e: int
+
+
+def build(vectors: np.ndarray, attrs: np.ndarray, grid, R: int = 32, E: int = 2, C: int = 1000,
+          kmeans_iters: int = 10, seed: int = 0, device=None) -> GmgArrays:
+    dev = _device(device)
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        lq, rq, slices, cell_of = quantile_grid(attrs, grid)
+        P = int(np.prod(grid))
+        x = torch.from_numpy(np.ascontiguousarray(vectors, np.float32)).to(dev)
+        n = x.shape[0]
+        order = np.argsort(cell_of, kind="stable")          # positions: cell-major, increasing id
+        sizes = np.bincount(cell_of, minlength=P)
+        seg = np.concatenate([[0], np.cumsum(sizes)])
+        xo = x[torch.from_numpy(order).to(dev)]
+        graphs = np.zeros((n, R), np.uint32)
+        for c in range(P):
+            lo, hi = int(seg[c]), int(seg[c + 1])
+            if hi == lo:
+                continue
+            gcell = cell_graph(xo[lo:hi], R, seed=seed + c)
+            graphs[lo:hi] = gcell.cpu().numpy().astype(np.uint32)
+        cr = cross_edges(xo, None, seg, E)
+        cross = np.empty((n, P * E), np.uint32)
+        cross[order] = cr.cpu().numpy().astype(np.uint32)
+        labels = kmeans(x, min(C, n), kmeans_iters, seed).cpu().numpy().astype(np.int32)
+        return GmgArrays(np.asarray(grid, np.uint32), lq, rq, slices, cell_of, graphs, cross, labels, R, E)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old_tf32
+
+
+def write_files(out_dir, name: str, ds, ix: GmgArrays, gt: np.ndarray | None = None) -> dict:
+    """Write the reference's index/query files; returns the realdataset_search flags."""
+    from . import write_attrs, write_fvecs, write_ranges, write_u32mat
+    d = Path(out_dir)
+    d.mkdir(parents=True, exist_ok=True)
+    paths = dict(
+        data_path=d / f"{name}_base.fvecs", query_path=d / f"{name}_query.fvecs", range=d / f"{name}.range",
+        gt=d / f"{name}.gt", cagra_prefix=str(d / f"{name}_cell"), cagra_suffix=f".cagra{ix.degree}",
+        global_graph=d / f"{name}_global.graph", grid=d / f"{name}.grid", attrs=d / f"{name}.attrs",
+        cluster=d / f"{name}_cluster.bin",
+    )
+    write_fvecs(paths["data_path"], ds.vectors)
+    write_fvecs(paths["query_path"], ds.queries)
+    write_ranges(paths["range"], ds.lo, ds.hi)
+    write_attrs(paths["attrs"], ds.attrs)
+    P = int(np.prod(ix.grid))
+    seg = np.concatenate([[0], np.cumsum(np.bincount(ix.cell_of, minlength=P))])
+    for c in range(P):
+        write_u32mat(f"{paths['cagra_prefix']}{c}{paths['cagra_suffix']}", ix.graphs[seg[c]:seg[c + 1]])
+    write_u32mat(paths["global_graph"], ix.cross)
+    # grid_info (indexbuild/tools.py:127-141)
+    n, a = ix.slices.shape
+    blob = [np.array([n, a], np.int32).tobytes(), ix.grid.astype(np.int32).tobytes()]
+    off = 0
+    for j in range(a):
+        g = int(ix.grid[j])
+        blob += [ix.l_quant[off:off + g].astype(np.int32).tobytes(), ix.r_quant[off:off + g].astype(np.int32).tobytes(),
+                 ix.slices[:, j].astype(np.int32).tobytes()]
+        off += g
+    blob.append(ix.cell_of.astype(np.int32).tobytes())
+    with open(paths["grid"], "wb") as f:
+        f.write(b"".join(blob))
+    with open(paths["cluster"], "wb") as f:
+        f.write(np.array([n], np.int32).tobytes() + ix.labels.astype(np.int32).tobytes())
+    if gt is not None:
+        write_u32mat(paths["gt"], gt.astype(np.uint32))
+    return {k: str(v) for k, v in paths.items()}

@@ -1,0 +1,224 @@
+/*
+ * garfield.h -- C ABI of garfield_b200, a B200 (sm_100a) implementation of the
+ * Garfield GMG query path: range-filtered approximate nearest-neighbour search over a
+ * grid of per-cell graphs joined by cross-cell edges.
+ *
+ * The reference (ZJU-DAILY/Garfield) has no library surface; its query path is a set
+ * of templated host functions inside one CUDA translation unit.  Each entry point
+ * below names the reference function it replaces.  Conventions:
+ *   - every call returns gf_status (GF_OK = 0); nothing exits or prints;
+ *     gf_last_error() holds a message for the calling thread;
+ *   - pointers documented "device" are CUDA device pointers on the index's device,
+ *     "host" are ordinary host pointers; sizes are element counts;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     calls only enqueue work unless they return host data;
+ *   - ids returned to callers are the reference's global point ids (row numbers of
+ *     the data file); 0xFFFFFFFF marks "no result".
+ */
+#ifndef GARFIELD_B200_H
+#define GARFIELD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    GF_OK = 0,
+    GF_ERR_ARG = 1,     /* invalid argument or size */
+    GF_ERR_IO = 2,      /* file cannot be opened / read / written */
+    GF_ERR_FORMAT = 3,  /* file or array contents inconsistent */
+    GF_ERR_OOM = 4,     /* device or host allocation failed */
+    GF_ERR_CUDA = 5,    /* CUDA runtime error */
+    GF_ERR_TIMEOUT = 6, /* a bounded wait ran out */
+    GF_ERR_STATE = 7    /* call out of order (e.g. search before plan) */
+} gf_status;
+
+#define GF_NO_ID 0xFFFFFFFFu
+
+typedef struct gf_index gf_index;
+typedef struct gf_plan gf_plan;
+
+/*
+ * Host description of an index in the reference's on-disk layout (global point order).
+ * Replaces the loading block of real_dataset_test_multiD (realdataset_search.cu:2118-2393):
+ * get_graph_info (check.cu:406), load_grid_infos/load2GPU (real_dataset_adapter.cuh:563,589),
+ * get_idx_mapper (tools.cuh:862), load_result for the global graph (tools.cuh:205),
+ * load_attrs (tools.cuh:747), f2h (tools.cuh:308), load_clustering (tools.cuh:569).
+ */
+typedef struct {
+    uint32_t n;            /* points */
+    uint32_t dim;          /* vector dimension */
+    uint32_t n_attr;       /* attributes per point (grid dimensions) */
+    const float* vectors;  /* host, n x dim fp32 */
+    const float* attrs;    /* host, n x n_attr (integer attributes converted to float) */
+    const uint32_t* grid;  /* host, n_attr slice counts */
+    const float* l_quant;  /* host, sum(grid): closed lower bound of each slice, per dim */
+    const float* r_quant;  /* host, sum(grid): closed upper bound of each slice */
+    const uint32_t* cell_of; /* host, n: grid cell of each point (grid_info global_pid) */
+    uint32_t degree;       /* per-cell graph degree R */
+    const uint32_t* graphs; /* host, n x degree: per-cell graphs concatenated in cell order,
+                               rows in local order, entries = local ids in the same cell */
+    uint32_t cross_e;      /* cross-cell edges per (point, cell) E */
+    const uint32_t* cross; /* host, n x (ncells*cross_e), global row order, local ids */
+    uint32_t n_clusters;   /* 0 = no cluster-guided ordering (cells keep id order) */
+    const int32_t* labels; /* host, n cluster labels (cluster.bin), or NULL */
+    float f2h_factor;      /* --f2h_factor: vectors are stored as half(x * f2h_factor) */
+    uint32_t keep_fp32;    /* 1 = also keep fp32 vectors on the device (gf_bruteforce) */
+} gf_index_desc;
+
+/* Paths of the reference's index files (realdataset_search flags, README.md:101-170). */
+typedef struct {
+    const char* data_path;    /* --data_path  .fvecs */
+    const char* cagra_prefix; /* --cagra_prefix  graph of cell c = prefix + c + suffix */
+    const char* cagra_suffix; /* --cagra_suffix */
+    const char* global_graph; /* --global_graph  cross-cell edges */
+    const char* grid;         /* --grid  grid_info */
+    const char* attrs;        /* --attrs  attrs.bin */
+    const char* cluster;      /* --cluster  cluster.bin, or NULL */
+    uint32_t degree;          /* --degree */
+    float f2h_factor;         /* --f2h_factor */
+    uint32_t keep_fp32;
+} gf_index_files;
+
+/* Search knobs.  The defaults (gf_search_defaults) are the reference's values. */
+typedef struct {
+    uint32_t L;          /* candidate list length ("ef", realdataset_search.cu:2757) */
+    uint32_t k;          /* results per query (10 in the reference, :2495) */
+    uint32_t width;      /* list entries expanded per round (1 in the reference) */
+    uint32_t max_iter;   /* rounds per cell (MAX_ITER = 10000, gpu_graph.cu:39) */
+    uint32_t n_entry;    /* entry points of the first cell (= degree in the reference) */
+    uint32_t postfilter; /* --postfilter: queries with >= this many cells scan exactly */
+    uint32_t hash_slots; /* visited-hash slots per query, power of two; 0 = automatic */
+    uint32_t reserved;
+} gf_search_params;
+
+/* Per-search counters (device-side, summed over queries). */
+typedef struct {
+    uint64_t n_dist;    /* distance evaluations */
+    uint64_t n_exp;     /* expanded list entries */
+    uint64_t n_cross;   /* cross-edge rows read */
+    uint64_t n_hops;    /* cell-to-cell hops */
+    uint64_t n_exact;   /* queries answered by the exact route */
+    uint64_t n_queries;
+} gf_search_stats;
+
+typedef struct {
+    uint32_t n, dim, n_attr, n_cells, degree, cross_e, n_clusters;
+    uint32_t d_stored;       /* stored row length (dim rounded up to 8) */
+    uint32_t min_cell_size;  /* entry ids are drawn below this */
+    uint64_t device_bytes;   /* device memory held by the index */
+} gf_index_info;
+
+const char* gf_status_string(gf_status s);
+const char* gf_last_error(void);
+/* Library version string. */
+const char* gf_version(void);
+
+void gf_search_defaults(gf_search_params* p);
+
+/* ---------------------------------------------------------------- index */
+
+/* Build a device index from host arrays.  Replaces the loading block of
+ * real_dataset_test_multiD (realdataset_search.cu:2118-2393). */
+gf_status gf_index_create(const gf_index_desc* desc, int device, gf_index** out);
+/* Load the reference's index files and build a device index (same block, from files). */
+gf_status gf_index_open(const gf_index_files* files, int device, gf_index** out);
+gf_status gf_index_info_get(const gf_index* idx, gf_index_info* out);
+/* Copy the entry local ids (first n of the deterministic entry sequence) to host. */
+gf_status gf_index_entry_points(const gf_index* idx, uint32_t n, uint32_t* out_host);
+gf_status gf_index_destroy(gf_index* idx);
+
+/* ----------------------------------------------------------------- plan */
+
+/* Plan buffers for up to max_queries queries. */
+gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out);
+gf_status gf_plan_destroy(gf_plan* plan);
+
+/*
+ * Cell intersection + cluster-guided ordering for a batch of queries: the reference's
+ * cost1 + cost2.  Replaces intersection_area_mark_little_seg_V2
+ * (real_dataset_adapter.cuh:390-519, incl. prefiltering_tag_elements :347) followed by
+ * get_partitions_access_order_V2 (gpu_graph.cu:11742-11845).
+ *   queries: device, qnum x dim fp32; lb/rb: device, qnum x n_attr closed bounds.
+ *   prefilter: --prefilter (box count / n <= prefilter => exact route); the box count
+ *   pass runs only when prefilter > 0.
+ */
+gf_status gf_plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
+                          uint32_t qnum, float prefilter, void* stream);
+
+/*
+ * Copy the ordered cell lists of the last gf_plan_queries to host (test / inspection).
+ * counts, offsets: qnum entries; cells: cap entries; top4: qnum x 4 (may be NULL);
+ * box_counts: qnum (may be NULL; valid only when prefilter > 0).  Synchronises.
+ */
+gf_status gf_plan_read(gf_plan* plan, uint32_t* counts, uint32_t* offsets, uint32_t* cells, uint64_t cap,
+                       uint32_t* top4, uint32_t* box_counts);
+
+/*
+ * Cell-by-cell filtered beam search of the planned queries.  Replaces
+ * batch_graph_search_gpu_with_prefilter_and_postfilter (gpu_graph.cu:12464-12616) and
+ * its kernel select_path_contain_attr_filter_V2_without_output_with_post_pre_filter
+ * (gpu_graph.cu:3270-4131).  ids_out: device qnum x k global ids; dist_out: device
+ * qnum x k squared distances in the stored (scaled) space, or NULL.
+ */
+gf_status gf_search(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint32_t* ids_out,
+                    float* dist_out, void* stream);
+
+/* Counters of the last gf_search on this plan (synchronises the plan's stream). */
+gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out);
+
+/*
+ * End-to-end call from host memory: copies queries and bounds to the device, plans,
+ * searches and copies ids (and distances, if dist_host != NULL) back.  Synchronises.
+ * The host buffers may be pinned (faster) or pageable.
+ */
+gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* params, const float* queries_host,
+                         const float* lb_host, const float* rb_host, uint32_t qnum, float prefilter,
+                         uint32_t* ids_host, float* dist_host, void* stream);
+
+/*
+ * Exact filtered k-NN: every point whose attributes lie inside the query's box competes;
+ * squared L2 on the fp32 vectors; (distance, global id) order.  Replaces
+ * naive_brute_force_with_filter (gpu_graph.cu:10782) and prefiltering_and_bruteforce
+ * (brute_force.cuh:331).  Needs keep_fp32.  queries: device qnum x dim; lb/rb device.
+ * Missing results are GF_NO_ID / +inf.
+ */
+gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                        uint32_t k, uint32_t* ids_out, float* dist_out, void* stream);
+
+/* ------------------------------------------------------ file formats (host) */
+/* Readers allocate with malloc; release with gf_free. */
+void gf_free(void* p);
+
+/* .fvecs: per row int32 d then d float32 (tools.cuh:85-106). */
+gf_status gf_read_fvecs(const char* path, float** data, uint32_t* n, uint32_t* dim);
+gf_status gf_write_fvecs(const char* path, const float* data, uint32_t n, uint32_t dim);
+/* u8bin: uint32 n, uint32 d, n*d uint8 (tools.cuh:108-150). */
+gf_status gf_read_u8bin(const char* path, uint8_t** data, uint32_t* n, uint32_t* dim);
+/* attrs.bin: uint32 n, uint32 a, n*a int32 (tools.cuh:747-765). */
+gf_status gf_read_attrs(const char* path, int32_t** attrs, uint32_t* n, uint32_t* a);
+gf_status gf_write_attrs(const char* path, const int32_t* attrs, uint32_t n, uint32_t a);
+/* graph / global graph / result blob: uint32 n, uint32 k, n*k uint32 (tools.cuh:205-223;
+ * the per-cell .cagraN files use the same header with int32 fields). */
+gf_status gf_read_u32mat(const char* path, uint32_t** data, uint32_t* n, uint32_t* k);
+gf_status gf_write_u32mat(const char* path, const uint32_t* data, uint32_t n, uint32_t k);
+/* range file: per query per attribute int32 l, int32 r, no header (tools.cuh:275-291). */
+gf_status gf_read_ranges(const char* path, uint32_t qnum, uint32_t a, int32_t* l_out, int32_t* r_out);
+gf_status gf_write_ranges(const char* path, const int32_t* l, const int32_t* r, uint32_t qnum, uint32_t a);
+/* cluster.bin: int32 n, n int32 labels (tools.cuh:547-567). */
+gf_status gf_read_labels(const char* path, int32_t** labels, uint32_t* n);
+/*
+ * grid_info: int32 N, int32 a, int32 grid[a]; per dim int32 l_quant[g], r_quant[g],
+ * pid_list[N]; then int32 global_pid[N] (real_dataset_adapter.cuh:563-586).
+ * quant arrays: sum(grid) entries; cell_of: N.  Outputs are malloc'd.
+ */
+gf_status gf_read_grid(const char* path, uint32_t* n, uint32_t* a, uint32_t** grid, int32_t** l_quant,
+                       int32_t** r_quant, uint32_t** cell_of);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,192 @@
+"""ctypes binding of the CPU oracle (gf_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: used by tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline as the checker.  No product code path imports this module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+EMPTY = 0xFFFFFFFF
+
+
+def build() -> Path:
+    src = HERE / "gf_oracle.c"
+    if not LIB.exists() or LIB.stat().st_mtime < src.stat().st_mtime:
+        env = dict(os.environ)
+        env.pop("CC", None)
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True, env=env)
+    return LIB
+
+
+_L = None
+
+
+class OrcIndex(C.Structure):
+    _fields_ = [("n", C.c_uint32), ("d8", C.c_uint32), ("a", C.c_uint32), ("ncells", C.c_uint32),
+                ("degree", C.c_uint32), ("cross_e", C.c_uint32), ("vec16", C.c_void_p), ("attrs", C.c_void_p),
+                ("cell_of", C.c_void_p), ("graphs", C.c_void_p), ("cross", C.c_void_p)]
+
+
+class OrcParams(C.Structure):
+    _fields_ = [("L", C.c_uint32), ("K", C.c_uint32), ("width", C.c_uint32), ("max_iter", C.c_uint32),
+                ("postfilter", C.c_uint32), ("prefilter", C.c_float), ("n_entry", C.c_uint32)]
+
+
+def lib() -> C.CDLL:
+    global _L
+    if _L is None:
+        build()
+        _L = C.CDLL(str(LIB))
+        P, U = C.c_void_p, C.c_uint32
+        _L.orc_dist16.restype = C.c_float
+        _L.orc_dist16.argtypes = [P, P, U]
+        _L.orc_dist32.restype = C.c_float
+        _L.orc_dist32.argtypes = [P, P, U]
+        _L.orc_dist_seq.restype = C.c_float
+        _L.orc_dist_seq.argtypes = [P, P, U]
+        _L.orc_f2h.argtypes = [P, U, U, U, C.c_float, P]
+        _L.orc_count_in_box.argtypes = [P, U, U, P, P, U, P]
+        _L.orc_bruteforce.argtypes = [P, U, U, P, U, P, P, P, U, U, P, P, C.c_int]
+        _L.orc_plan_cells.restype = C.c_long
+        _L.orc_plan_cells.argtypes = [P, P, U, U, P, P, P, P, P, P, C.c_uint64]
+        _L.orc_cluster_info.argtypes = [P, U, U, P, P, U, U, P, P]
+        _L.orc_order_cells.argtypes = [P, U, U, P, U, P, P, P, P, P]
+        _L.orc_search.argtypes = [C.POINTER(OrcIndex), C.POINTER(OrcParams), P, U, C.c_float, P, P, U, P, P, P, P,
+                                  P, P, P, P, C.c_int]
+        _L.orc_recall.restype = C.c_double
+        _L.orc_recall.argtypes = [P, U, P, U, U]
+    return _L
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+def f2h(x: np.ndarray, d_pad: int, alpha: float = 1.0) -> np.ndarray:
+    x = _c(x, np.float32)
+    n, dim = x.shape
+    out = np.zeros((n, d_pad), np.uint16)
+    lib().orc_f2h(_p(x), n, dim, d_pad, alpha, _p(out))
+    return out
+
+
+def pad(x: np.ndarray, mult: int) -> np.ndarray:
+    n, d = x.shape
+    dp = (d + mult - 1) // mult * mult
+    out = np.zeros((n, dp), np.float32)
+    out[:, :d] = x
+    return out
+
+
+def dist16(q16: np.ndarray, x16: np.ndarray) -> float:
+    q16, x16 = _c(q16, np.uint16), _c(x16, np.uint16)
+    return lib().orc_dist16(_p(q16), _p(x16), q16.shape[-1])
+
+
+def dist32(q: np.ndarray, x: np.ndarray) -> float:
+    q, x = _c(q, np.float32), _c(x, np.float32)
+    return lib().orc_dist32(_p(q), _p(x), q.shape[-1])
+
+
+def bruteforce(data, attrs, queries, lo, hi, k: int, threads: int = 0):
+    """Exact filtered top-k: (ids uint32 q x k, squared dists)."""
+    d4 = pad(data, 4)
+    q4 = pad(queries, 4)
+    attrs = _c(attrs, np.float32)
+    lo, hi = _c(lo, np.float32), _c(hi, np.float32)
+    qn = q4.shape[0]
+    ids = np.zeros((qn, k), np.uint32)
+    dist = np.zeros((qn, k), np.float32)
+    lib().orc_bruteforce(_p(d4), d4.shape[0], d4.shape[1], _p(attrs), attrs.shape[1], _p(q4), _p(lo), _p(hi),
+                         qn, k, _p(ids), _p(dist), threads)
+    return ids, dist
+
+
+def count_in_box(attrs, lo, hi):
+    attrs, lo, hi = _c(attrs, np.float32), _c(lo, np.float32), _c(hi, np.float32)
+    out = np.zeros(lo.shape[0], np.uint32)
+    lib().orc_count_in_box(_p(attrs), attrs.shape[0], attrs.shape[1], _p(lo), _p(hi), lo.shape[0], _p(out))
+    return out
+
+
+def plan_cells(lo, hi, grid, l_quant, r_quant):
+    lo, hi = _c(lo, np.float32), _c(hi, np.float32)
+    grid = _c(grid, np.uint32)
+    lq, rq = _c(l_quant, np.float32), _c(r_quant, np.float32)
+    qn, a = lo.shape
+    counts = np.zeros(qn, np.uint32)
+    offsets = np.zeros(qn, np.uint32)
+    cap = qn * int(np.prod(grid)) + 1
+    cells = np.zeros(cap, np.uint32)
+    tot = lib().orc_plan_cells(_p(lo), _p(hi), qn, a, _p(grid), _p(lq), _p(rq), _p(counts), _p(offsets), _p(cells),
+                               cap)
+    assert tot >= 0
+    return counts, offsets, cells[:tot].copy()
+
+
+def cluster_info(data, labels, cell_of, ncells: int):
+    data = _c(data, np.float32)
+    labels = _c(labels, np.int32)
+    cell_of = _c(cell_of, np.uint32)
+    C_ = int(labels.max()) + 1
+    cent = np.zeros((C_, data.shape[1]), np.float32)
+    hist = np.zeros((ncells, C_), np.uint32)
+    lib().orc_cluster_info(_p(data), data.shape[0], data.shape[1], _p(labels), _p(cell_of), ncells, C_, _p(cent),
+                           _p(hist))
+    return cent, hist
+
+
+def order_cells(queries, centroids, hist, counts, offsets, cells):
+    queries, centroids = _c(queries, np.float32), _c(centroids, np.float32)
+    hist = _c(hist, np.uint32)
+    counts, offsets = _c(counts, np.uint32), _c(offsets, np.uint32)
+    cells = _c(cells, np.uint32).copy()
+    top4 = np.zeros((queries.shape[0], 4), np.uint32)
+    lib().orc_order_cells(_p(queries), queries.shape[0], queries.shape[1], _p(centroids), centroids.shape[0],
+                          _p(hist), _p(counts), _p(offsets), _p(cells), _p(top4))
+    return cells, top4
+
+
+def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells, entry, *, L, K, width=1,
+           max_iter=10000, postfilter=0xFFFFFFFF, prefilter=0.0, box_counts=None, alpha=1.0, threads=0):
+    """Beam search restatement; index_arrays: an indexbuild.GmgArrays (reference layout)."""
+    vectors = _c(vectors, np.float32)
+    n, dim = vectors.shape
+    d8 = (dim + 7) // 8 * 8
+    vec16 = f2h(vectors, d8, alpha)
+    attrs = _c(attrs, np.float32)
+    cell_of = _c(index_arrays.cell_of, np.uint32)
+    graphs = _c(index_arrays.graphs, np.uint32)
+    cross = _c(index_arrays.cross, np.uint32)
+    ix = OrcIndex(n, d8, attrs.shape[1], int(np.prod(index_arrays.grid)), index_arrays.degree, index_arrays.cross_e,
+                  _p(vec16), _p(attrs), _p(cell_of), _p(graphs), _p(cross))
+    entry = _c(entry, np.uint32)
+    prm = OrcParams(L, K, width, max_iter, postfilter, prefilter, len(entry))
+    queries = _c(queries, np.float32)
+    lo, hi = _c(lo, np.float32), _c(hi, np.float32)
+    counts, offsets, cells = _c(counts, np.uint32), _c(offsets, np.uint32), _c(cells, np.uint32)
+    box = None if box_counts is None else _c(box_counts, np.uint32)
+    qn = queries.shape[0]
+    ids = np.zeros((qn, K), np.uint32)
+    dist = np.zeros((qn, K), np.float32)
+    stats = np.zeros(4, np.uint64)
+    lib().orc_search(C.byref(ix), C.byref(prm), _p(queries), dim, alpha, _p(lo), _p(hi), qn, _p(counts), _p(offsets),
+                     _p(cells), _p(box), _p(entry), _p(ids), _p(dist), _p(stats), threads)
+    return ids, dist, stats
+
+
+def recall(res, gt) -> float:
+    res, gt = _c(res, np.uint32), _c(gt, np.uint32)
+    return lib().orc_recall(_p(res), res.shape[1], _p(gt), gt.shape[1], res.shape[0])
