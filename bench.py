@@ -1,0 +1,416 @@
+#!/usr/bin/env python
+"""Benchmark of the GMG query path: QPS at recall@10 >= 0.95 on BASELINE config 2
+(1M x 128 fp32, 1000-center Gaussian mixture, 2 attributes on a 4x4 quantile grid,
+R = 32 per-cell graphs + 2 cross-cell edges, 1000 k-means clusters, 10k queries with
+10%-selectivity boxes, k = 10).
+
+A step = planning (cell intersection + cluster-guided ordering) + the cell-by-cell search
+of all 10k queries, with the index resident in HBM: the reference's QPS definition
+qnum / (cost1 + cost2 + cost3) (realdataset_search.cu:2506-2508).  L is the smallest list
+length in a fixed sweep whose recall on the ground-truth sample reaches the target.
+
+  python bench.py [--gpus N --steps K --warmup W]           this implementation
+  python bench.py --impl reference                          CPU exact filtered scan (the
+                                                            oracle's restatement of the
+                                                            reference's CPU path) on host cores
+  python bench.py --impl reference-cuda                     the reference's own CUDA binary
+                                                            (oracle/_ref) on the same index files
+Multi-GPU (torchrun): every rank holds a replica of the index and runs the full query
+batch (weak scaling); the only collective is the max-over-ranks of the timings.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+L_SWEEP = [16, 24, 32, 40, 48, 64, 80, 96, 128, 160, 192, 256, 320, 384, 512]
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        def run():
+            q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.samples.append([s.strip() for s in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=6)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if "Active" in s[3 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def peak_hbm() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- data
+
+def dataset_and_index(args, device):
+    """Config-2 synthetic dataset and its index (cached per process tree under --cache)."""
+    import torch
+    from garfield_b200 import indexbuild, synth
+    t0 = time.time()
+    ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    log(f"dataset {ds.vectors.shape} in {time.time() - t0:.1f}s")
+    key = f"cfg2_n{args.n}_s{args.seed}_R{args.R}_E{args.E}_C{args.C}.npz"
+    cache = Path(args.cache) / key if args.cache else None
+    if cache is not None and cache.exists():
+        z = np.load(cache)
+        ix = indexbuild.GmgArrays(z["grid"], z["l_quant"], z["r_quant"], z["slices"], z["cell_of"], z["graphs"],
+                                  z["cross"], z["labels"], int(z["degree"]), int(z["cross_e"]))
+        log(f"index loaded from {cache}")
+    else:
+        t0 = time.time()
+        ix = indexbuild.build(ds.vectors, ds.attrs, ds.grid, R=args.R, E=args.E, C=args.C, seed=args.seed,
+                              device=device)
+        torch.cuda.synchronize()
+        log(f"index built in {time.time() - t0:.1f}s")
+        if cache is not None:
+            try:
+                cache.parent.mkdir(parents=True, exist_ok=True)
+                tmp = cache.with_suffix(f".{os.getpid()}.tmp.npz")
+                np.savez(tmp, grid=ix.grid, l_quant=ix.l_quant, r_quant=ix.r_quant, slices=ix.slices,
+                         cell_of=ix.cell_of, graphs=ix.graphs, cross=ix.cross, labels=ix.labels,
+                         degree=ix.degree, cross_e=ix.cross_e)
+                os.replace(tmp, cache)
+            except OSError:
+                pass
+    return ds, ix
+
+
+def cpu_baseline(ds, sample: int, threads: int) -> dict:
+    """The oracle's exact filtered scan (naive_brute_force_with_filter restated) on host cores."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    q = ds.queries[:sample]
+    oracle.bruteforce(ds.vectors, ds.attrs, q[:4], ds.lo[:4], ds.hi[:4], 10, threads)  # warm
+    t0 = time.perf_counter()
+    oracle.bruteforce(ds.vectors, ds.attrs, q, ds.lo[:sample], ds.hi[:sample], 10, threads)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} config-2 queries, exact filtered scan over all {ds.vectors.shape[0]} points "
+                      f"({dt:.1f}s)"}
+
+
+# --------------------------------------------------------------------------- arms
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import garfield_b200 as gf
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    ds, ix = dataset_and_index(args, device)
+    t0 = time.time()
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, keep_fp32=True,
+                            device=local)
+    log(f"device index {index.device_bytes / 2**30:.2f} GiB in {time.time() - t0:.1f}s")
+    qnum = ds.queries.shape[0]
+    qd = torch.from_numpy(ds.queries).to(device)
+    lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
+    hid = torch.from_numpy(ds.hi.astype(np.float32)).to(device)
+    # ground truth on a sample (exact, GPU brute force)
+    S = min(args.gt_sample, qnum)
+    t0 = time.time()
+    gt_ids, _ = index.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), 10)
+    gt = gt_ids.cpu().numpy().view(np.uint32)
+    log(f"ground truth for {S} queries in {time.time() - t0:.1f}s")
+    stream = torch.cuda.Stream(device)
+    plan = index.plan(qnum)
+    ids = torch.empty((qnum, 10), dtype=torch.int32, device=device)
+    dist_t = torch.empty((qnum, 10), dtype=torch.float32, device=device)
+
+    def step(L, width):
+        plan.build(qd, lod, hid, 0.0, stream)
+        plan.search(gf.SearchParams(L=L, k=10, width=width), stream, ids=ids, dist=dist_t)
+
+    chosen, sweep = None, []
+    Ls = [args.L] if args.L else L_SWEEP
+    for L in Ls:
+        with torch.cuda.stream(stream):
+            step(L, args.width)
+        stream.synchronize()
+        r = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)
+        sweep.append((L, round(r, 4)))
+        log(f"L={L} recall@10={r:.4f}")
+        if r >= args.target and chosen is None:
+            chosen = (L, r)
+            break
+    if chosen is None:
+        chosen = (Ls[-1], sweep[-1][1])
+    L, recall = chosen
+    # L2 flush buffer (> 126 MB L2)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            step(L, args.width)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(float(i))
+                ev[i][0].record(stream)
+                plan.build(qd, lod, hid, 0.0, stream)
+                ev[i][1].record(stream)
+                plan.search(gf.SearchParams(L=L, k=10, width=args.width), stream, ids=ids, dist=dist_t)
+                ev[i][2].record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(c) for a, b, c in ev]
+    plan_ms = [a.elapsed_time(b) for a, b, c in ev]
+    search_ms = [b.elapsed_time(c) for a, b, c in ev]
+    st = plan.stats()
+    total_ms = float(sum(step_ms))
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * qnum / (ms_per_step / 1e3)
+    # end to end through the C ABI from pinned host buffers
+    qh = torch.from_numpy(ds.queries).pin_memory().numpy()
+    lh = torch.from_numpy(ds.lo.astype(np.float32)).pin_memory().numpy()
+    hh = torch.from_numpy(ds.hi.astype(np.float32)).pin_memory().numpy()
+    e2e_plan = index.plan(qnum)
+    params = gf.SearchParams(L=L, k=10, width=args.width)
+    for _ in range(args.warmup):
+        index.search_host(qh, lh, hh, e2e_plan, params, stream=stream)
+    e_ms = []
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(float(i))
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        res_ids, _ = index.search_host(qh, lh, hh, e2e_plan, params, stream=stream)
+        b.record(stream)
+        b.synchronize()
+        e_ms.append(a.elapsed_time(b))
+    e2e_total = float(sum(e_ms))
+    if world > 1:
+        t = torch.tensor([e2e_total], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_total = float(t.item())
+    e2e_value = world * qnum / (e2e_total / args.steps / 1e3)
+    assert np.array_equal(res_ids, ids.cpu().numpy().view(np.uint32))
+    # roofline of the search kernel: algorithmic bytes from the device counters
+    D, a_attr = ds.vectors.shape[1], ds.attrs.shape[1]
+    bytes_step = (st["n_dist"] * (((D + 7) // 8 * 8) * 2 + a_attr * 4) + st["n_exp"] * ix.degree * 4 +
+                  st["n_cross"] * ix.cross_e * 4)
+    kern_s = float(np.mean(search_ms)) / 1e3
+    achieved = bytes_step / kern_s / 1e9
+    peak, peak_kind = peak_hbm()
+    out = {
+        "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
+        "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
+        "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
+        "config": {"workload": "config2: 1M x 128 fp32, 4x4 grid, R=32, E=2, C=1000, 10k queries, sel 10%, k=10",
+                   "L": L, "width": args.width, "recall_at_10": round(recall, 4), "recall_sample": S,
+                   "l2": "flushed (256 MiB write) between timed steps", "parallelism": f"replicas x{world}",
+                   "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
+                   "sweep": sweep},
+        "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * 10 * 4)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "gmg_search_kernel", "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": int(bytes_step),
+                     "counters": {k: int(v) for k, v in st.items()}},
+        "clocks": clocks.summary(),
+        "gpu_launches": 7 * args.steps,  # per step: f2h, cell count, cell fill, centroid top-4, order, iota, search
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def run_reference_cpu(args):
+    """Reference arm: the CPU exact filtered scan on the host cores, same metric/config."""
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    from garfield_b200 import synth
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    threads = os.cpu_count() or 1
+    S = args.cpu_sample
+    oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[:2], ds.lo[:2], ds.hi[:2], 10, threads)
+    times = []
+    for i in range(args.warmup + args.steps):
+        s0 = (i * S) % max(1, ds.queries.shape[0] - S)
+        t0 = time.perf_counter()
+        oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[s0:s0 + S], ds.lo[s0:s0 + S], ds.hi[s0:s0 + S], 10,
+                          threads)
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    value = S / float(np.mean(times))
+    out = {
+        "impl": "reference", "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
+        "value": round(value, 2), "unit": "queries/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(float(np.mean(times)) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
+        "config": {"workload": "config2: 1M x 128 fp32, 2 attrs, 10k queries, sel 10%, k=10",
+                   "step": f"{S} queries (bounded sample), exact scan (recall 1.0)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"{S} queries per step, exact filtered scan over {ds.vectors.shape[0]} points"},
+        "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def run_reference_cuda(args):
+    """The reference's own CUDA search (oracle/_ref/realdataset_search) on this index."""
+    import torch
+    import garfield_b200 as gf
+    from garfield_b200 import indexbuild
+    binary = ROOT / "oracle" / "_ref" / "realdataset_search"
+    if not binary.exists():
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/realdataset_search not built"}))
+        return
+    device = torch.device("cuda", 0)
+    ds, ix = dataset_and_index(args, device)
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=True)
+    q = ds.queries.shape[0]
+    gt, _ = index.bruteforce(torch.from_numpy(ds.queries).cuda(), torch.from_numpy(ds.lo.astype(np.float32)).cuda(),
+                             torch.from_numpy(ds.hi.astype(np.float32)).cuda(), 10)
+    gt = gt.cpu().numpy().view(np.uint32)
+    index.close()
+    d = Path(args.cache or "/tmp/gf_cache") / "ref_files"
+    paths = indexbuild.write_files(d, "cfg2", ds, ix, gt=gt)
+    res = []
+    for alpha in args.alphas:
+        out_csv = d / f"result_{alpha}.csv"
+        cmd = [str(binary), "--data_path", paths["data_path"], "--query_path", paths["query_path"], "--range",
+               paths["range"], "--gt", paths["gt"], "--cagra_prefix", paths["cagra_prefix"], "--cagra_suffix",
+               paths["cagra_suffix"], "--global_graph", paths["global_graph"], "--grid", paths["grid"], "--attrs",
+               paths["attrs"], "--cluster", paths["cluster"], "--result", str(out_csv), "--prefilter", "0.0",
+               "--postfilter", "17", "--f2h_factor", str(alpha), "--degree", str(ix.degree)]
+        t0 = time.time()
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=args.ref_timeout)
+        log(f"reference alpha={alpha} rc={r.returncode} in {time.time() - t0:.0f}s")
+        (d / f"stdout_{alpha}.log").write_text(r.stdout[-200000:] + "\n---stderr---\n" + r.stderr[-20000:])
+        if r.returncode != 0 or not out_csv.exists():
+            continue
+        rows = [l.split(",") for l in out_csv.read_text().strip().splitlines()[1:]]
+        rows = [(int(a), float(b), float(c)) for a, b, c, *_ in rows]
+        res.append({"alpha": alpha, "rows": rows})
+    best = None
+    for r in res:
+        for ef, rec, qps in r["rows"]:
+            if rec >= args.target and (best is None or qps > best[2]):
+                best = (ef, rec, qps, r["alpha"])
+    print(json.dumps({"impl": "reference-cuda", "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
+                      "value": None if best is None else round(best[2], 1), "unit": "queries/s",
+                      "best": best, "sweeps": res, "qnum": q}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
+    ap.add_argument("--sel", type=float, default=0.10)
+    ap.add_argument("--target", type=float, default=0.95)
+    ap.add_argument("--L", type=int, default=0)
+    ap.add_argument("--width", type=int, default=1)
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--qnum", type=int, default=10_000)
+    ap.add_argument("--R", type=int, default=32)
+    ap.add_argument("--E", type=int, default=2)
+    ap.add_argument("--C", type=int, default=1000)
+    ap.add_argument("--seed", type=int, default=20261201)
+    ap.add_argument("--gt-sample", dest="gt_sample", type=int, default=1000)
+    ap.add_argument("--cpu-sample", dest="cpu_sample", type=int, default=200)
+    ap.add_argument("--no-cpu-baseline", dest="no_cpu_baseline", action="store_true")
+    ap.add_argument("--cache", default="/tmp/gf_cache")
+    ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
+    ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_cpu(args)
+    elif args.impl == "reference-cuda":
+        run_reference_cuda(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -419,6 +419,18 @@ def read_grid(path):
     return grid, _take(lq, tot, np.int32), _take(rq, tot, np.int32), _take(co, n.value, np.uint32)
 
 
+def recall(res: np.ndarray, gt: np.ndarray) -> float:
+    """Mean over queries of |res ∩ gt| / |gt| (cal_recall_show_partition_multi_attrs,
+    tools.cuh:456-544); an empty ground-truth row counts as 1; NO_ID entries are ignored."""
+    res = np.asarray(res, np.uint32)
+    gt = np.asarray(gt, np.uint32)
+    total = 0.0
+    for r, g in zip(res, gt):
+        g = g[g != NO_ID]
+        total += 1.0 if g.size == 0 else np.isin(g, r[r != NO_ID]).sum() / g.size
+    return total / max(1, res.shape[0])
+
+
 def version() -> str:
     return lib().gf_version().decode()
 

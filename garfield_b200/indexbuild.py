@@ -5,10 +5,10 @@ graphs, CAGRA searches for cross-cell edges, k-means); cuVS is not available her
 this module builds the same files with torch (GPU when present, else CPU):
 
   quantile_grid   indexbuild/tools.py:88-125 grid_scatter_V2 (per-dimension quantile slices)
-  cell_graphs     per-cell navigable graph of degree R (indexbuild/uniform_partition.py:516-563
-                  uses CAGRA); here: exact 2R-NN + R random cell members as candidates,
-                  robust pruning with alpha = 1.2 (the DiskANN/Vamana rule), one reverse-edge
-                  pass, rows padded to R from the nearest neighbours
+  cell_graph      per-cell navigable graph of degree R (indexbuild/uniform_partition.py:516-563
+                  uses CAGRA); here: half of each row from the exact 2R-NN, half from the 4R
+                  nearest points of other k-means clusters (links to neighbouring clusters),
+                  each robust-pruned with alpha = 1.2 (the DiskANN/Vamana rule)
   cross_edges     indexbuild/global_graph_build.py:116-157: for every point and every cell, the
                   E nearest points of that cell (local ids), here exact
   kmeans          indexbuild/clustering.py:68-88 (cuVS k-means); here Lloyd iterations
@@ -129,51 +129,64 @@ def _robust_prune(x, node_ids, cand, R: int, alpha: float, batch: int = 2048):
     return out
 
 
-def cell_graph(x, R: int, alpha: float = 1.2, n_random: int | None = None, seed: int = 0):
-    """Degree-R navigable graph over the rows of x (local ids)."""
+def _first_distinct(cand, R: int):
+    """Per row, the first R distinct non-negative ids of cand (in column order), -1 padded."""
+    n, M = cand.shape
+    big = torch.iinfo(torch.int64).max
+    key = torch.where(cand >= 0, cand, torch.full_like(cand, big))
+    srt, order = torch.sort(key, dim=1, stable=True)
+    dup_s = torch.zeros_like(srt, dtype=torch.bool)
+    dup_s[:, 1:] = srt[:, 1:] == srt[:, :-1]
+    dup = torch.zeros_like(dup_s).scatter_(1, order, dup_s)
+    keep = (cand >= 0) & ~dup
+    rank = torch.cumsum(keep.long(), 1) - 1
+    keep &= rank < R
+    out = torch.full((n, R), -1, dtype=torch.int64, device=cand.device)
+    rows = torch.arange(n, device=cand.device)[:, None].expand_as(cand)
+    out[rows[keep], rank[keep]] = cand[keep]
+    return out
+
+
+def knn_other_label(x, labels, k: int, chunk: int = 4096):
+    """k nearest neighbours of every row among the rows with a different label."""
+    n = x.shape[0]
+    idx = torch.full((n, k), -1, dtype=torch.int64, device=x.device)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        d = _sqdist(x[s:e], x)
+        d[labels[s:e, None] == labels[None, :]] = float("inf")
+        kk = min(k, n)
+        v, i = torch.topk(d, kk, dim=1, largest=False, sorted=True)
+        idx[s:e, :kk] = torch.where(torch.isfinite(v), i, torch.full_like(i, -1))
+    return idx
+
+
+def cell_graph(x, R: int, labels=None, alpha: float = 1.2):
+    """Degree-R navigable graph over the rows of x (local ids).
+
+    Half of each row comes from the 2R nearest neighbours, robust-pruned.  The other half
+    comes from the 4R nearest points whose cluster label differs from the node's, robust-
+    pruned: links into the neighbouring clusters, so that greedy search can route between
+    clusters instead of staying in the cluster of its entry point (with well separated
+    clusters, nearest-neighbour edges never leave the cluster).  Rows are completed to R
+    from the nearest-neighbour order.  Without labels the whole row is pruned 2R-NN."""
     n = x.shape[0]
     if n <= 1:
         return torch.zeros((n, R), dtype=torch.int64, device=x.device)
-    n_random = R if n_random is None else n_random
-    g = torch.Generator(device="cpu").manual_seed(seed)
     nn_idx, _ = knn(x, 2 * R)
-    rnd = torch.randint(0, n, (n, n_random), generator=g).to(x.device)
     ids = torch.arange(n, device=x.device)
-    cand = torch.cat([nn_idx, rnd], 1)
-    first = _robust_prune(x, ids, cand, R, alpha)
-    # reverse edges: each kept edge p -> q offers p to q (at most R offers per node)
-    src = ids[:, None].expand_as(first)
-    ok = first >= 0
-    dst_e, src_e = first[ok], src[ok]
-    order = torch.argsort(dst_e, stable=True)
-    dst_e, src_e = dst_e[order], src_e[order]
-    cnt = torch.bincount(dst_e, minlength=n)
-    start = torch.cumsum(cnt, 0) - cnt
-    rank = torch.arange(dst_e.numel(), device=x.device) - start[dst_e]
-    keep = rank < R
-    rev = torch.full((n, R), -1, dtype=torch.int64, device=x.device)
-    rev[dst_e[keep], rank[keep]] = src_e[keep]
-    second = _robust_prune(x, ids, torch.cat([first, rev], 1), R, alpha)
-    # pad rows to exactly R with the nearest neighbours not yet present
-    out = second.clone()
-    filled = (out >= 0).sum(1)
-    if bool((filled < R).any()):
-        rows = torch.nonzero(filled < R).flatten().tolist()
-        o_cpu = out.cpu()
-        nn_cpu = nn_idx.cpu()
-        for r in rows:
-            have = set(int(v) for v in o_cpu[r] if v >= 0)
-            fill = [int(v) for v in nn_cpu[r] if int(v) not in have]
-            k = int(filled[r])
-            for v in fill:
-                if k >= R:
-                    break
-                o_cpu[r, k] = v
-                k += 1
-            while k < R:  # tiny cells: repeat
-                o_cpu[r, k] = o_cpu[r, k % max(1, int(filled[r]))] if filled[r] > 0 else (r + 1) % n
-                k += 1
-        out = o_cpu.to(x.device)
+    r_far = R // 2 if labels is not None else 0
+    near = _robust_prune(x, ids, nn_idx, R - r_far, alpha)
+    parts = [near]
+    if r_far:
+        far = _robust_prune(x, ids, knn_other_label(x, labels, 4 * R), r_far, alpha)
+        parts.append(far)
+    out = _first_distinct(torch.cat(parts + [nn_idx], 1), R)
+    if bool((out < 0).any()):  # cells smaller than R + 1 points: repeat entries
+        cnt = (out >= 0).sum(1, keepdim=True).clamp_min(1)
+        col = torch.arange(R, device=x.device)[None, :] % cnt
+        rep = torch.gather(torch.where(out >= 0, out, torch.zeros_like(out)), 1, col)
+        out = torch.where(out >= 0, out, rep)
     return out
 
 
@@ -232,7 +245,7 @@ class GmgArrays:
 
 
 def build(vectors: np.ndarray, attrs: np.ndarray, grid, R: int = 32, E: int = 2, C: int = 1000,
-          kmeans_iters: int = 10, seed: int = 0, device=None) -> GmgArrays:
+          kmeans_iters: int = 10, seed: int = 0, device=None, cluster_links: bool = True) -> GmgArrays:
     dev = _device(device)
     old_tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -241,21 +254,24 @@ def build(vectors: np.ndarray, attrs: np.ndarray, grid, R: int = 32, E: int = 2,
         P = int(np.prod(grid))
         x = torch.from_numpy(np.ascontiguousarray(vectors, np.float32)).to(dev)
         n = x.shape[0]
+        labels = kmeans(x, min(C, n), kmeans_iters, seed)
         order = np.argsort(cell_of, kind="stable")          # positions: cell-major, increasing id
         sizes = np.bincount(cell_of, minlength=P)
         seg = np.concatenate([[0], np.cumsum(sizes)])
-        xo = x[torch.from_numpy(order).to(dev)]
+        order_t = torch.from_numpy(order).to(dev)
+        xo = x[order_t]
+        lo_lab = labels[order_t]
         graphs = np.zeros((n, R), np.uint32)
         for c in range(P):
             lo, hi = int(seg[c]), int(seg[c + 1])
             if hi == lo:
                 continue
-            gcell = cell_graph(xo[lo:hi], R, seed=seed + c)
+            gcell = cell_graph(xo[lo:hi], R, labels=lo_lab[lo:hi] if cluster_links else None)
             graphs[lo:hi] = gcell.cpu().numpy().astype(np.uint32)
         cr = cross_edges(xo, None, seg, E)
         cross = np.empty((n, P * E), np.uint32)
         cross[order] = cr.cpu().numpy().astype(np.uint32)
-        labels = kmeans(x, min(C, n), kmeans_iters, seed).cpu().numpy().astype(np.int32)
+        labels = labels.cpu().numpy().astype(np.int32)
         return GmgArrays(np.asarray(grid, np.uint32), lq, rq, slices, cell_of, graphs, cross, labels, R, E)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32

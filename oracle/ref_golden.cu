@@ -1,0 +1,68 @@
+// Test infrastructure: a driver that runs two host-side (CPU) functions of the
+// reference's query path, compiled from the reference's own sources, to produce golden
+// vectors for the oracle:
+//   bf       naive_brute_force_with_filter (gpu_graph.cu:10782-10812), one call per query
+//   cluster  load_clustering (tools.cuh:569-602): centroids and the cell x cluster histogram
+// Built by oracle/Makefile (target ref_golden) into oracle/_ref/; never linked into the
+// product.  Input/output files are plain little-endian arrays described below.
+#include <unordered_map>
+#include <unordered_set>
+
+#include "gpu_graph.cu"
+
+#include <cstdio>
+#include <cstdlib>
+
+static void write_u32(const char* path, const std::vector<unsigned>& v) {
+    FILE* f = fopen(path, "wb");
+    fwrite(v.data(), 4, v.size(), f);
+    fclose(f);
+}
+
+int main(int argc, char** argv) {
+    if (argc < 2) return 2;
+    std::string mode = argv[1];
+    if (mode == "bf" && argc == 8) {
+        // bf data.fvecs attrs.bin queries.fvecs ranges.bin k out.u32
+        unsigned num, dim, qnum, qdim, an, ad;
+        float *data, *queries;
+        int* attrs_i;
+        load_data(std::string(argv[2]), data, num, dim);
+        load_attrs<int>(std::string(argv[3]), attrs_i, ad, an);
+        load_data(std::string(argv[4]), queries, qnum, qdim);
+        std::vector<int> li(qnum * ad), ri(qnum * ad);
+        load_range<int>(std::string(argv[5]), li.data(), ri.data(), ad, qnum);
+        unsigned k = (unsigned)atoi(argv[6]);
+        std::vector<float> attrs((size_t)an * ad), lf(li.begin(), li.end()), rf(ri.begin(), ri.end());
+        for (size_t i = 0; i < attrs.size(); ++i) attrs[i] = (float)attrs_i[i];
+        std::vector<unsigned> out((size_t)qnum * k, 0xFFFFFFFFu);
+        for (unsigned q = 0; q < qnum; ++q) {
+            std::vector<unsigned> r = naive_brute_force_with_filter(queries + (size_t)q * dim, data, dim, num, k,
+                                                                    lf.data() + q * ad, rf.data() + q * ad,
+                                                                    attrs.data(), ad);
+            for (size_t j = 0; j < r.size() && j < k; ++j) out[(size_t)q * k + j] = r[j];
+        }
+        write_u32(argv[7], out);
+        return 0;
+    }
+    if (mode == "cluster" && argc == 6) {
+        // cluster data.fvecs cluster.bin centroids.f32 hist.u32
+        unsigned num, dim;
+        float* data;
+        load_data(std::string(argv[2]), data, num, dim);
+        std::vector<unsigned> cid;
+        float* centers = nullptr;
+        std::vector<std::vector<unsigned>> ncp;
+        load_clustering(cid, std::string(argv[3]), centers, dim, ncp, data);
+        unsigned C = ncp[0].size();
+        FILE* f = fopen(argv[4], "wb");
+        fwrite(centers, 4, (size_t)C * dim, f);
+        fclose(f);
+        std::vector<unsigned> h;
+        for (auto& row : ncp) h.insert(h.end(), row.begin(), row.end());
+        write_u32(argv[5], h);
+        return 0;
+    }
+    fprintf(stderr, "usage: bf data attrs queries ranges k out | cluster data labels centroids hist\n");
+    return 2;
+}

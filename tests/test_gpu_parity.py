@@ -1,0 +1,168 @@
+"""GPU parity: every CUDA stage through the C ABI against the CPU oracle on the same
+inputs.  Integer outputs (ids, cell lists, counters) must match exactly; distances are
+computed in the same fixed fp32 order on both sides and must match bit for bit."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import garfield_b200 as gf
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def make_index(c, alpha=1.0):
+    return gf.Index.create(vectors=c.ds.vectors, attrs=c.ds.attrs.astype(np.float32), grid=c.ix.grid,
+                           l_quant=c.ix.l_quant, r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs,
+                           degree=c.ix.degree, cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels,
+                           f2h_factor=alpha, keep_fp32=True)
+
+
+def dev(a, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to("cuda", dtype)
+
+
+@pytest.fixture(scope="module")
+def g_small(small):
+    return make_index(small)
+
+
+@pytest.fixture(scope="module")
+def g_odd(odd):
+    return make_index(odd)
+
+
+def as_u32(t):
+    return t.cpu().numpy().view(np.uint32) if t.dtype == torch.int32 else t.cpu().numpy().astype(np.uint32)
+
+
+def test_index_info_and_entry_points(small, g_small):
+    from conftest import mt_entry
+    assert g_small.n == small.ds.vectors.shape[0] and g_small.n_cells == small.ncells
+    minc = int(np.bincount(small.ix.cell_of).min())
+    assert g_small.min_cell_size == minc
+    assert np.array_equal(g_small.entry_points(32), mt_entry(32, minc))
+
+
+@pytest.mark.parametrize("which", ["small", "odd"])
+def test_bruteforce_bit_exact(which, request):
+    c = request.getfixturevalue(which)
+    g = request.getfixturevalue("g_" + which)
+    for k in (10, 37):
+        ids, dist = g.bruteforce(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi), k)
+        ref_ids, ref_d = oracle.bruteforce(c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, k)
+        assert np.array_equal(as_u32(ids), ref_ids)
+        assert np.array_equal(dist.cpu().numpy(), ref_d)
+
+
+@pytest.mark.parametrize("which", ["small", "odd"])
+def test_plan_matches_oracle(which, request):
+    c = request.getfixturevalue(which)
+    g = request.getfixturevalue("g_" + which)
+    plan = g.plan(c.ds.queries.shape[0])
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi), prefilter=0.5)
+    counts, offsets, cells, top4, box = plan.read()
+    assert np.array_equal(counts, c.counts) and np.array_equal(offsets, c.offsets)
+    assert np.array_equal(top4, c.top4)
+    assert np.array_equal(cells, c.cells)
+    assert np.array_equal(box, oracle.count_in_box(c.ds.attrs, c.ds.lo, c.ds.hi))
+
+
+def _oracle_search(c, **kw):
+    ent = c.entry(kw.pop("n_entry", c.ix.degree))
+    return oracle.search(c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts, c.offsets,
+                         c.cells, ent, **kw)
+
+
+@pytest.mark.parametrize("which", ["small", "odd"])
+@pytest.mark.parametrize("L,width", [(16, 1), (64, 1), (160, 1), (64, 2), (96, 4)])
+def test_search_matches_oracle(which, L, width, request):
+    c = request.getfixturevalue(which)
+    g = request.getfixturevalue("g_" + which)
+    params = gf.SearchParams(L=L, k=10, width=width)
+    plan = g.plan(c.ds.queries.shape[0])
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+    ids, dist = plan.search(params)
+    st = plan.stats()
+    ref_ids, ref_d, ref_st = _oracle_search(c, L=L, K=10, width=width)
+    got = as_u32(ids)
+    assert np.array_equal(got, ref_ids), np.argwhere(got != ref_ids)[:5]
+    assert np.array_equal(dist.cpu().numpy(), ref_d)
+    assert st["n_exp"] == ref_st[1] and st["n_cross"] == ref_st[2] and st["n_hops"] == ref_st[3]
+    assert st["n_queries"] == c.ds.queries.shape[0]
+
+
+def test_exact_and_prefilter_routes(small, g_small):
+    c = small
+    q = c.ds.queries.shape[0]
+    plan = g_small.plan(q)
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+    ids, dist = plan.search(gf.SearchParams(L=16, k=10, postfilter=1))
+    ref_ids, ref_d, _ = _oracle_search(c, L=16, K=10, postfilter=1)
+    assert np.array_equal(as_u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+    assert plan.stats()["n_exact"] == int((c.counts >= 1).sum())
+    box = oracle.count_in_box(c.ds.attrs, c.ds.lo, c.ds.hi)
+    thr = float(np.median(box) / c.ds.vectors.shape[0])
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi), prefilter=thr)
+    ids, dist = plan.search(gf.SearchParams(L=32, k=10))
+    ref_ids, ref_d, _ = _oracle_search(c, L=32, K=10, prefilter=thr, box_counts=box)
+    assert np.array_equal(as_u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+
+
+def test_search_host_matches_device(small, g_small):
+    c = small
+    q = c.ds.queries.shape[0]
+    plan = g_small.plan(q)
+    params = gf.SearchParams(L=48, k=10)
+    ids_h, d_h = g_small.search_host(c.ds.queries.astype(np.float32), c.ds.lo.astype(np.float32),
+                                     c.ds.hi.astype(np.float32), plan, params, with_dist=True)
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+    ids, dist = plan.search(params)
+    assert np.array_equal(ids_h, as_u32(ids)) and np.array_equal(d_h, dist.cpu().numpy())
+
+
+def test_filter_validity_and_recall(small, g_small):
+    c = small
+    ids, _ = g_small.search(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi), gf.SearchParams(L=160, k=10))
+    ids = as_u32(ids)
+    for q in range(ids.shape[0]):
+        for i in ids[q]:
+            if i != gf.NO_ID:
+                assert ((c.ds.attrs[i] >= c.ds.lo[q]) & (c.ds.attrs[i] <= c.ds.hi[q])).all()
+    assert oracle.recall(ids, c.gt) >= 0.97
+
+
+def test_edge_cases(small, g_small):
+    c = small
+    q = np.ascontiguousarray(c.ds.queries[:6])
+    lo = np.array([[-9, -9], [20000, 0], [0, 0], [c.ds.attrs[7, 0], c.ds.attrs[7, 1]], [5, 3], [0, 0]], np.int32)
+    hi = np.array([[-5, 99], [30000, 99], [9999, 9999], [c.ds.attrs[7, 0], c.ds.attrs[7, 1]], [4, 9999],
+                   [9999, 9999]], np.int32)
+    params = gf.SearchParams(L=20, k=20)
+    ids, dist = g_small.search(dev(q), dev(lo), dev(hi), params)
+    ids = as_u32(ids)
+    assert (ids[0] == gf.NO_ID).all() and (ids[1] == gf.NO_ID).all() and (ids[4] == gf.NO_ID).all()
+    assert np.isinf(dist.cpu().numpy()[0]).all()
+    # a box around one point's attributes: only points with exactly those attributes qualify
+    same = np.where((c.ds.attrs == c.ds.attrs[7]).all(1))[0]
+    got = [int(v) for v in ids[3] if v != gf.NO_ID]
+    assert set(got) <= set(same.tolist())
+    # L == k and a single query
+    ids1, _ = g_small.search(dev(q[:1]), dev(lo[2:3]), dev(hi[2:3]), gf.SearchParams(L=10, k=10))
+    assert ids1.shape == (1, 10)
+    with pytest.raises(gf.GarfieldError):
+        g_small.search(dev(q[:1]), dev(lo[2:3]), dev(hi[2:3]), gf.SearchParams(L=5, k=10))
+
+
+def test_f2h_factor(small):
+    c = small
+    g = make_index(c, alpha=0.01)
+    params = gf.SearchParams(L=64, k=10)
+    ids, dist = g.search(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi), params)
+    ref_ids, ref_d, _ = oracle.search(c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts,
+                                      c.offsets, c.cells, c.entry(c.ix.degree), L=64, K=10, alpha=0.01)
+    assert np.array_equal(as_u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+    g.close()
