@@ -82,7 +82,8 @@ class ClockSampler:
         sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
         mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if "Active" in s[3 + i]})
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 3 + i and s[3 + i].strip() == "Active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(self.samples)}
 
@@ -307,7 +308,7 @@ def run_reference_cpu(args):
     import oracle
     ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
     threads = os.cpu_count() or 1
-    S = args.cpu_sample
+    S = args.ref_sample
     oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[:2], ds.lo[:2], ds.hi[:2], 10, threads)
     times = []
     for i in range(args.warmup + args.steps):
@@ -384,7 +385,7 @@ def run_reference_cuda(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--sel", type=float, default=0.10)
@@ -397,8 +398,9 @@ def main():
     ap.add_argument("--E", type=int, default=2)
     ap.add_argument("--C", type=int, default=1000)
     ap.add_argument("--seed", type=int, default=20261201)
-    ap.add_argument("--gt-sample", dest="gt_sample", type=int, default=1000)
+    ap.add_argument("--gt-sample", dest="gt_sample", type=int, default=10_000)
     ap.add_argument("--cpu-sample", dest="cpu_sample", type=int, default=200)
+    ap.add_argument("--ref-sample", dest="ref_sample", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", dest="no_cpu_baseline", action="store_true")
     ap.add_argument("--cache", default="/tmp/gf_cache")
     ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
