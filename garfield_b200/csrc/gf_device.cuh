@@ -26,119 +26,86 @@ __device__ __forceinline__ uint64_t mkkey(float d, uint32_t w) {
     return ((uint64_t)__float_as_uint(d) << 32) | (w == kEmpty ? kEmpty : (w & kPosMask));
 }
 
-// Row chunks loaded per batch in dist16 (loads in flight per lane).
-#ifndef GF_DIST_GROUP
-#define GF_DIST_GROUP 8
-#endif
-constexpr int kDistGroup = GF_DIST_GROUP;
-
 // 16-byte read-only load of a stored row chunk.
 __device__ __forceinline__ uint4 ldg16(const uint4* p) { return __ldg(p); }
 
-// Canonical fp16 squared distance (same order as the oracle's orc_dist16): sixteen
-// partials, partial u takes chunks u, u+16, ... (8 halves each) with one fused
-// multiply-add per element on fp32 differences, then the pairwise tree 8/4/2/1.
-// qs: the query as fp32 (converted from its fp16 row), nch = row chunks.
-__device__ __forceinline__ float dist16(const uint4* __restrict__ row, const float* __restrict__ qs, uint32_t nch) {
-    float p[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) p[u] = 0.0f;
-    for (uint32_t c0 = 0; c0 < nch; c0 += 16) {
-#pragma unroll
-        for (int h = 0; h < 16; h += kDistGroup) {
-        uint4 x[kDistGroup];
-#pragma unroll
-        for (int v = 0; v < kDistGroup; ++v)
-            if (c0 + h + v < nch) x[v] = ldg16(row + c0 + h + v);
-#pragma unroll
-        for (int v = 0; v < kDistGroup; ++v) {
-            const int u = h + v;
-            if (c0 + u < nch) {
-                const float4 qa = *reinterpret_cast<const float4*>(qs + (c0 + u) * 8);
-                const float4 qb = *reinterpret_cast<const float4*>(qs + (c0 + u) * 8 + 4);
-                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x[v].x));
-                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x[v].y));
-                const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&x[v].z));
-                const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&x[v].w));
-                float acc = p[u], t;
-                t = __fsub_rn(qa.x, f0.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qa.y, f0.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qa.z, f1.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qa.w, f1.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qb.x, f2.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qb.y, f2.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qb.z, f3.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qb.w, f3.y); acc = __fmaf_rn(t, t, acc);
-                p[u] = acc;
-            }
-        }
-        }
-    }
-#pragma unroll
-    for (int s = 8; s >= 1; s >>= 1)
-#pragma unroll
-        for (int i = 0; i < s; ++i) p[i] = __fadd_rn(p[i], p[i + s]);
-    return p[0];
+// Packed two-wide fp32 arithmetic (sm_100a): each half is an independent IEEE
+// round-to-nearest operation, so the results equal the scalar ones bit for bit.
+typedef unsigned long long f2x;  // (first, second) float in (low, high) 32 bits
+__device__ __forceinline__ f2x pack2(float a, float b) {
+    return ((f2x)__float_as_uint(b) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ float lo2(f2x v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi2(f2x v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ f2x sub2(f2x a, f2x b) {
+    f2x d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f2x sqacc2(f2x d, f2x acc) {  // d*d + acc, fused, per half
+    f2x r;
+    asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(r) : "l"(d), "l"(acc));
+    return r;
+}
+__device__ __forceinline__ f2x h2_to_f2x(uint32_t h) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    return pack2(f.x, f.y);
 }
 
-// Canonical fp16 distance of a row staged in shared memory (nch chunks of 8 halves,
-// row stride a multiple of 16 chunks).  Lane r reads chunk c0 + ((c + r) & 15) at step c,
-// so the 8 lanes of a shared-memory phase touch 8 different 16-byte bank groups.
-// Partial c of this lane then holds canonical partial (c + r) & 15; the pairwise tree
-// pairs indices that differ in one bit (i, i ^ s), a pairing that rotation by r maps
-// onto itself, and fp32 addition is commutative, so the result equals dist16 / the
-// oracle's orc_dist16 bit for bit.  qa/qb: the query's first/second 4 floats of each chunk.
-__device__ __forceinline__ float dist16_staged(const uint4* srow, const float4* qa, const float4* qb, uint32_t nch,
-                                               uint32_t rot) {
-    float p[16];
+// End of the canonical sum: s[u] = even + odd partial, then the pairwise tree 8/4/2/1.
+__device__ __forceinline__ float finish32(const f2x* p) {
+    float s[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) p[u] = 0.0f;
+    for (int u = 0; u < 16; ++u) s[u] = __fadd_rn(lo2(p[u]), hi2(p[u]));
+#pragma unroll
+    for (int st = 8; st >= 1; st >>= 1)
+#pragma unroll
+        for (int i = 0; i < st; ++i) s[i] = __fadd_rn(s[i], s[i + st]);
+    return s[0];
+}
+
+// Slot of chunk c of staged row r: chunks are XOR-swizzled within groups of 16 so that
+// lanes reading chunk c of consecutive rows hit different shared-memory bank groups.
+__device__ __forceinline__ uint32_t stage_slot(uint32_t c, uint32_t r) { return (c & ~15u) | ((c ^ r) & 15u); }
+
+// Canonical fp16 squared distance (oracle orc_dist16) of a row staged in shared memory
+// (nch chunks of 8 halves, swizzled by stage_slot with key r) against the query held as
+// fp32 pairs q2[c*4 .. c*4+3] = (q0,q1),(q2,q3),(q4,q5),(q6,q7) of chunk c.  Thirty-two
+// partials: packed register p[u] holds the even/odd-element partials of chunk lane u.
+template <int NCH>
+__device__ __forceinline__ float dist16_staged(const uint4* srow, const f2x* q2, uint32_t nch_rt, uint32_t r) {
+    const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
+    f2x p[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) p[u] = 0ull;
     for (uint32_t c0 = 0; c0 < nch; c0 += 16) {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const uint32_t u = c0 + ((c + rot) & 15u);
-            if (u < nch) {
-                const uint4 x = srow[u];
-                const float4 a = qa[u];
-                const float4 b = qb[u];
-                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&x.x));
-                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&x.y));
-                const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&x.z));
-                const float2 f3 = __half22float2(*reinterpret_cast<const __half2*>(&x.w));
-                float acc = p[c], t;
-                t = __fsub_rn(a.x, f0.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(a.y, f0.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(a.z, f1.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(a.w, f1.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(b.x, f2.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(b.y, f2.y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(b.z, f3.x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(b.w, f3.y); acc = __fmaf_rn(t, t, acc);
-                p[c] = acc;
+        for (int u = 0; u < 16; ++u) {
+            const uint32_t c = c0 + u;
+            if (NCH == 0 || (NCH % 16) == 0 || c < nch) {
+                if (c < nch) {
+                    const uint4 x = srow[stage_slot(c, r)];
+                    const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q2 + c * 4);
+                    const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q2 + c * 4 + 2);
+                    f2x acc = p[u];
+                    acc = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), acc);
+                    acc = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), acc);
+                    acc = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), acc);
+                    acc = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), acc);
+                    p[u] = acc;
+                }
             }
         }
     }
-#pragma unroll
-    for (int s = 8; s >= 1; s >>= 1)
-#pragma unroll
-        for (int i = 0; i < s; ++i) p[i] = __fadd_rn(p[i], p[i + s]);
-    return p[0];
+    return finish32(p);
 }
 
-// 16-byte asynchronous global -> shared copy (cp.async, L2 only) and its fences.
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-    uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-}
-
-// Canonical fp32 squared distance (oracle orc_dist32): chunks of 4 floats.
+// Canonical fp32 squared distance (oracle orc_dist32) of a global row of nch float4
+// chunks against a query row in shared memory.
 __device__ __forceinline__ float dist32(const float4* __restrict__ row, const float4* __restrict__ q, uint32_t nch) {
-    float p[16];
+    f2x p[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) p[u] = 0.0f;
+    for (int u = 0; u < 16; ++u) p[u] = 0ull;
     for (uint32_t c0 = 0; c0 < nch; c0 += 16) {
         float4 x[16];
 #pragma unroll
@@ -148,20 +115,23 @@ __device__ __forceinline__ float dist32(const float4* __restrict__ row, const fl
         for (int u = 0; u < 16; ++u) {
             if (c0 + u < nch) {
                 const float4 qv = q[c0 + u];
-                float acc = p[u], t;
-                t = __fsub_rn(qv.x, x[u].x); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qv.y, x[u].y); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qv.z, x[u].z); acc = __fmaf_rn(t, t, acc);
-                t = __fsub_rn(qv.w, x[u].w); acc = __fmaf_rn(t, t, acc);
+                f2x acc = p[u];
+                acc = sqacc2(sub2(pack2(qv.x, qv.y), pack2(x[u].x, x[u].y)), acc);
+                acc = sqacc2(sub2(pack2(qv.z, qv.w), pack2(x[u].z, x[u].w)), acc);
                 p[u] = acc;
             }
         }
     }
-#pragma unroll
-    for (int s = 8; s >= 1; s >>= 1)
-#pragma unroll
-        for (int i = 0; i < s; ++i) p[i] = __fadd_rn(p[i], p[i + s]);
-    return p[0];
+    return finish32(p);
+}
+
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only) and its fences.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
 // Closed-box test of one point (merge_top_with_recycle_list's filter, gpu_graph.cu:514-520).
@@ -178,14 +148,16 @@ __device__ __forceinline__ bool in_box(const float* __restrict__ attrs, uint32_t
 // Warp bitonic sort of (d, w) pairs in shared memory by mkkey; n is a power of two.
 __device__ __forceinline__ void warp_sort(float* d, uint32_t* w, uint32_t n) {
     const uint32_t lane = lane_id();
-    for (uint32_t k = 2; k <= n; k <<= 1) {
-        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+    for (uint32_t lk = 1; (1u << lk) <= n; ++lk) {
+        const uint32_t k = 1u << lk;
+        for (int lj = (int)lk - 1; lj >= 0; --lj) {
+            const uint32_t j = 1u << lj;
             for (uint32_t i = lane; i < (n >> 1); i += 32) {
-                uint32_t lo = 2 * j * (i / j) + (i % j);
-                uint32_t hi = lo + j;
-                bool asc = (lo & k) == 0;
-                float dl = d[lo], dh = d[hi];
-                uint32_t wl = w[lo], wh = w[hi];
+                const uint32_t lo = ((i >> lj) << (lj + 1)) | (i & (j - 1));
+                const uint32_t hi = lo + j;
+                const bool asc = (lo & k) == 0;
+                const float dl = d[lo], dh = d[hi];
+                const uint32_t wl = w[lo], wh = w[hi];
                 if ((mkkey(dl, wl) > mkkey(dh, wh)) == asc) {
                     d[lo] = dh;
                     d[hi] = dl;
@@ -194,6 +166,25 @@ __device__ __forceinline__ void warp_sort(float* d, uint32_t* w, uint32_t n) {
                 }
             }
             __syncwarp();
+        }
+    }
+}
+
+// Bitonic sort of 32 (d, w) pairs held one per lane, ascending by mkkey, in registers.
+__device__ __forceinline__ void warp_sort32(float& d, uint32_t& w) {
+    const uint32_t lane = lane_id();
+#pragma unroll
+    for (uint32_t k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            const float od = __shfl_xor_sync(kFull, d, j);
+            const uint32_t ow = __shfl_xor_sync(kFull, w, j);
+            const uint64_t mk = mkkey(d, w), ok = mkkey(od, ow);
+            const bool keep_min = ((lane & j) == 0) == ((lane & k) == 0);
+            if (keep_min ? (ok < mk) : (ok > mk)) {
+                d = od;
+                w = ow;
+            }
         }
     }
 }

@@ -6,13 +6,13 @@
 //
 // Per query the warp keeps, in shared memory: the candidate list T (L entries, double
 // buffered for rank merges), the recycle list RL (k entries, double buffered), a batch
-// buffer B, an eviction buffer, the query row (fp32, split in two planes), the box
-// bounds, a row staging area and a visited hash.  A batch of candidate rows is copied
-// into the staging area with cp.async (all rows of an expansion in flight at once,
-// 16-byte coalesced segments; the reference keeps six 8-byte loads in flight per query)
-// and each lane then computes one candidate's canonical distance from shared memory.
-// The range predicate is evaluated alongside and kept as a flag bit, so evictions and
-// the final filter need no further attribute reads.
+// buffer B, an eviction buffer, the query row (fp32 pairs), the box bounds, a row
+// staging area and a visited hash.  A batch of candidate rows is copied into the staging
+// area with cp.async (all rows of an expansion in flight at once, 16-byte coalesced
+// segments; the reference keeps six 8-byte loads in flight per query) and each lane then
+// computes one candidate's canonical distance from shared memory with packed fp32x2
+// arithmetic.  The range predicate is evaluated alongside and kept as a flag bit, so
+// evictions and the final filter need no further attribute reads.
 #include <algorithm>
 #include <cstdio>
 
@@ -46,49 +46,41 @@ struct SArgs {
     uint32_t* out_ids;
     float* out_d;
     unsigned long long* stats;
-    uint32_t qnum, nch, nch16, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
+    uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, warp_words;
     // word offsets inside a warp's shared-memory slice
-    uint32_t o_qa, o_qb, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
+    uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
         o_picks, o_stage, o_hash;
 };
 
-struct Layout {
-    uint32_t o_qa, o_qb, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
-        o_picks, o_stage, o_hash, words;
-};
-
 // Shared-memory layout of one warp, in 32-bit words, every region 16-byte aligned.
-Layout make_layout(uint32_t nch16, uint32_t L, uint32_t K, uint32_t bcap, uint32_t stage_rows, uint32_t hs) {
-    Layout l;
+void make_layout(SArgs& A, uint32_t nch16) {
     uint32_t o = 0;
     auto take = [&](uint32_t words) {
         uint32_t r = o;
         o += (words + 3) & ~3u;
         return r;
     };
-    l.o_qa = take(nch16 * 4);
-    l.o_qb = take(nch16 * 4);
-    l.o_lb = take(kMaxAttr);
-    l.o_rb = take(kMaxAttr);
-    l.o_t0d = take(L);
-    l.o_t0w = take(L);
-    l.o_t1d = take(L);
-    l.o_t1w = take(L);
-    l.o_r0d = take(K);
-    l.o_r0w = take(K);
-    l.o_r1d = take(K);
-    l.o_r1w = take(K);
-    l.o_bd = take(bcap);
-    l.o_bw = take(bcap);
-    l.o_ed = take(bcap);
-    l.o_ew = take(bcap);
-    l.o_picks = take(32);
-    l.o_stage = take(stage_rows * nch16 * 4);
-    l.o_hash = take(hs);
-    l.words = o;
-    return l;
+    A.o_q = take(nch16 * 8);  // fp32 query as (even, odd) element pairs, 4 pairs per chunk
+    A.o_lb = take(kMaxAttr);
+    A.o_rb = take(kMaxAttr);
+    A.o_t0d = take(A.L);
+    A.o_t0w = take(A.L);
+    A.o_t1d = take(A.L);
+    A.o_t1w = take(A.L);
+    A.o_r0d = take(A.K);
+    A.o_r0w = take(A.K);
+    A.o_r1d = take(A.K);
+    A.o_r1w = take(A.K);
+    A.o_bd = take(A.bcap);
+    A.o_bw = take(A.bcap);
+    A.o_ed = take(A.bcap);
+    A.o_ew = take(A.bcap);
+    A.o_picks = take(32);
+    A.o_stage = take(A.stage_rows * nch16 * 4);
+    A.o_hash = take(A.hs);
+    A.warp_words = o;
 }
 
 // Per-warp view of the shared slice; pointers are recomputed from the base and the
@@ -116,22 +108,30 @@ struct W {
 
 __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 1u << (32 - __clz(x - 1)); }
 
-// Distances + range flags for the positions in B[0..nb): rows are staged through
-// shared memory in rounds of stage_rows.
-__device__ __forceinline__ void eval_batch(const SArgs& A, const W& w, uint32_t nb) {
+// Distances + range flags for the positions in B[0..nb), sorted ascending into B (padded
+// with empty entries to a power of two >= 32).  Rows are staged through shared memory
+// with cp.async, stage_rows at a time, chunk c of staged row r at stage_slot(c, r); each
+// lane computes the distance of one staged row.  Batches of at most 32 are sorted in
+// registers, larger ones in shared memory.
+template <int NCH>
+__device__ __forceinline__ void eval_sort(const SArgs& A, const W& w, uint32_t nb) {
     const uint32_t lane = lane_id();
+    const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
+    const uint32_t nch16 = (nch + 15u) & ~15u;
     uint32_t* bw = w.bw(A);
     float* bd = w.bd(A);
     uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
-    const float4* qa = reinterpret_cast<const float4*>(w.base + A.o_qa);
-    const float4* qb = reinterpret_cast<const float4*>(w.base + A.o_qb);
-    for (uint32_t r0 = 0; r0 < nb; r0 += A.stage_rows) {
-        const uint32_t rows = min(A.stage_rows, nb - r0);
-        const uint32_t total = rows * A.nch;
+    const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
+    const uint32_t SR = A.stage_rows;
+    float dreg = kInf;
+    uint32_t wreg = kEmpty;
+    for (uint32_t r0 = 0; r0 < nb; r0 += SR) {
+        const uint32_t rows = min(SR, nb - r0);
+        const uint32_t total = rows * nch;
         for (uint32_t e = lane; e < total; e += 32) {
-            uint32_t r = e / A.nch, c = e - r * A.nch;
-            uint32_t pos = bw[r0 + r];
-            cp_async16(stage + (size_t)r * A.nch16 + c, A.vec16 + (size_t)pos * A.nch + c);
+            const uint32_t r = e / nch, c = e - r * nch;
+            const uint32_t pos = bw[r0 + r];
+            cp_async16(stage + (size_t)r * nch16 + stage_slot(c, r), A.vec16 + (size_t)pos * nch + c);
         }
         bool inr = false;
         uint32_t pos = 0;
@@ -142,20 +142,27 @@ __device__ __forceinline__ void eval_batch(const SArgs& A, const W& w, uint32_t 
         cp_async_wait_all();
         __syncwarp();
         if (lane < rows) {
-            float d = dist16_staged(stage + (size_t)lane * A.nch16, qa, qb, A.nch, lane & 15u);
-            bd[r0 + lane] = d;
-            bw[r0 + lane] = pos | (inr ? kInRange : 0u);
+            const float d = dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
+            const uint32_t wv = pos | (inr ? kInRange : 0u);
+            if (nb <= 32) {
+                dreg = d;
+                wreg = wv;
+            } else {
+                bd[r0 + lane] = d;
+                bw[r0 + lane] = wv;
+            }
         }
         __syncwarp();
     }
-}
-
-// Sort B[0..nb) (pads with empty entries up to the next power of two).
-__device__ __forceinline__ void sort_batch(const SArgs& A, const W& w, uint32_t nb) {
-    uint32_t n = next_pow2(nb < 2 ? 2 : nb);
-    float* bd = w.bd(A);
-    uint32_t* bw = w.bw(A);
-    for (uint32_t j = nb + lane_id(); j < n; j += 32) {
+    if (nb <= 32) {
+        warp_sort32(dreg, wreg);
+        bd[lane] = dreg;
+        bw[lane] = wreg;
+        __syncwarp();
+        return;
+    }
+    const uint32_t n = next_pow2(nb);
+    for (uint32_t j = nb + lane; j < n; j += 32) {
         bd[j] = kInf;
         bw[j] = kEmpty;
     }
@@ -184,7 +191,7 @@ __device__ __forceinline__ void merge_step(const SArgs& A, W& w, uint32_t L, uin
     w.rsel ^= 1u;
 }
 
-// Clear the hash and insert the list entries that lie in [lo, hi).
+// Clear the hash and insert the list entries that lie in [lo, hi); returns how many.
 __device__ __forceinline__ uint32_t hash_rebuild(const SArgs& A, const W& w, uint32_t lo, uint32_t hi) {
     uint32_t* H = w.H(A);
     const uint32_t* tw = w.tw(A);
@@ -213,7 +220,7 @@ __device__ __forceinline__ void write_result(const SArgs& A, uint32_t q, const f
     }
 }
 
-// Append the positions held by lanes with ok=true to B at *nb (warp-uniform counter).
+// Append the positions held by lanes with ok=true to B at nb (warp-uniform counter).
 __device__ __forceinline__ void append(uint32_t* bw, uint32_t& nb, bool ok, uint32_t pos) {
     uint32_t msk = __ballot_sync(kFull, ok);
     if (ok) bw[nb + __popc(msk & lanemask_lt())] = pos;
@@ -221,7 +228,8 @@ __device__ __forceinline__ void append(uint32_t* bw, uint32_t& nb, bool ok, uint
 }
 
 // Exact route (gpu_graph.cu:3788-4022): every in-range point of the query's cells.
-__device__ __forceinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uint32_t q, const uint32_t* cl,
+template <int NCH>
+__device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uint32_t q, const uint32_t* cl,
                                              uint32_t nc) {
     const uint32_t lane = lane_id();
     W w{base, 0u, 0u};
@@ -243,9 +251,8 @@ __device__ __forceinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, 
             const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
-                eval_batch(A, w, nb);
+                eval_sort<NCH>(A, w, nb);
                 ndist += nb;
-                sort_batch(A, w, nb);
                 merge_step(A, w, A.K, 0, nb, false);
                 nb = 0;
             }
@@ -256,10 +263,89 @@ __device__ __forceinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, 
     return ndist;
 }
 
-__global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
+// Cross-cell hop into cell `next` (gpu_graph.cu:3564-3643): the distinct cross-edge
+// targets of the first min(L, 64) list entries plus the smallest unused local ids of
+// the next cell as filler are evaluated and sorted; the first n_entry become the next
+// entry set (left sorted in B[0..ne)), the following 64 are merged into T without
+// recycling.  Rebuilds the visited hash for the next cell.  Returns ne; adds to stats.
+template <int NCH>
+__device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, uint32_t& hcount, uint32_t& st_dist,
+                                           uint32_t& st_cross) {
+    const uint32_t lane = lane_id();
+    const uint32_t nlo = A.seg[next], nsz = A.seg[next + 1] - nlo;
+    const uint32_t hop_n = A.L < kHopSlots ? A.L : kHopSlots;
+    const uint32_t* tw = w.tw(A);
+    uint32_t V = 0;
+    for (uint32_t i0 = 0; i0 < hop_n; i0 += 32) {
+        uint32_t i = i0 + lane;
+        V += __popc(__ballot_sync(kFull, i < hop_n && tw[i] != kEmpty));
+    }
+    uint32_t* H = w.H(A);
+    hash_clear(H, A.hs);
+    const uint32_t pairs = V * A.E;
+    const size_t rowlen = (size_t)A.P * A.E;
+    uint32_t nb = 0;
+    uint32_t* bw = w.bw(A);
+    for (uint32_t j0 = 0; j0 < pairs; j0 += 32) {
+        uint32_t j = j0 + lane;
+        bool ok = false;
+        uint32_t pos = kEmpty;
+        if (j < pairs) {
+            uint32_t src = tw[j / A.E] & kPosMask;
+            pos = __ldg(A.cross + (size_t)src * rowlen + (size_t)next * A.E + (j % A.E));
+            if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+        }
+        append(bw, nb, ok, pos);
+    }
+    __syncwarp();
+    st_cross += V;
+    // filler: smallest local ids of the next cell not among the targets
+    uint32_t nf = pairs - nb;
+    for (uint32_t x0 = 0; nf > 0 && x0 < nsz; x0 += 32) {
+        uint32_t x = x0 + lane;
+        bool ok = x < nsz && !hash_contains(H, A.hs, A.hshift, nlo + x);
+        uint32_t msk = __ballot_sync(kFull, ok);
+        uint32_t idx = __popc(msk & lanemask_lt());
+        if (ok && idx < nf) bw[nb + idx] = nlo + x;
+        uint32_t take = min((uint32_t)__popc(msk), nf);
+        nb += take;
+        nf -= take;
+    }
+    __syncwarp();
+    eval_sort<NCH>(A, w, nb);
+    st_dist += nb;
+    const uint32_t ne = min(nb, A.n_entry);
+    const uint32_t nm = min(nb - ne, kHopSlots);
+    merge_step(A, w, A.L, ne, nm, false);
+    // visited set of the next cell: its entry set + its points now in T
+    hash_clear(H, A.hs);
+    uint32_t cnt = 0;
+    for (uint32_t i0 = 0; i0 < ne; i0 += 32) {
+        uint32_t i = i0 + lane;
+        bool ins = i < ne && hash_insert(H, A.hs, A.hshift, bw[i] & kPosMask);
+        cnt += __popc(__ballot_sync(kFull, ins));
+    }
+    const uint32_t* tw2 = w.tw(A);
+    for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
+        uint32_t i = i0 + lane;
+        bool ins = false;
+        if (i < A.L) {
+            uint32_t v = tw2[i], pos = v & kPosMask;
+            if (v != kEmpty && pos >= nlo && pos < nlo + nsz) ins = hash_insert(H, A.hs, A.hshift, pos);
+        }
+        cnt += __popc(__ballot_sync(kFull, ins));
+    }
+    __syncwarp();
+    hcount = cnt;
+    return ne;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constant__ SArgs A) {
     extern __shared__ __align__(16) uint32_t smem[];
     const uint32_t lane = lane_id();
     uint32_t* const base = smem + (threadIdx.x >> 5) * A.warp_words;
+    const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
 
     for (;;) {
         uint32_t slot = 0;
@@ -269,18 +355,15 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
         const uint32_t q = A.task[slot];
         const uint32_t nc = A.counts[q];
         const uint32_t* cl = A.cells + A.offsets[q];
-        // query row (fp16 -> fp32, two planes) and box
+        // query row (fp16 -> fp32 element pairs) and box
         {
-            float4* qa = reinterpret_cast<float4*>(base + A.o_qa);
-            float4* qb = reinterpret_cast<float4*>(base + A.o_qb);
-            for (uint32_t c = lane; c < A.nch; c += 32) {
-                uint4 v = A.q16[(size_t)q * A.nch + c];
-                float2 f0 = __half22float2(*reinterpret_cast<__half2*>(&v.x));
-                float2 f1 = __half22float2(*reinterpret_cast<__half2*>(&v.y));
-                float2 f2 = __half22float2(*reinterpret_cast<__half2*>(&v.z));
-                float2 f3 = __half22float2(*reinterpret_cast<__half2*>(&v.w));
-                qa[c] = make_float4(f0.x, f0.y, f1.x, f1.y);
-                qb[c] = make_float4(f2.x, f2.y, f3.x, f3.y);
+            f2x* q2 = reinterpret_cast<f2x*>(base + A.o_q);
+            for (uint32_t c = lane; c < nch; c += 32) {
+                const uint4 v = A.q16[(size_t)q * nch + c];
+                q2[c * 4 + 0] = h2_to_f2x(v.x);
+                q2[c * 4 + 1] = h2_to_f2x(v.y);
+                q2[c * 4 + 2] = h2_to_f2x(v.z);
+                q2[c * 4 + 3] = h2_to_f2x(v.w);
             }
             if (lane < A.a) {
                 base[A.o_lb + lane] = __float_as_uint(A.lb[(size_t)q * A.a + lane]);
@@ -299,7 +382,7 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
             }
             if (exact) {
                 st_exact = 1;
-                st_dist = exact_route(A, base, q, cl, nc);
+                st_dist = exact_route<NCH>(A, base, q, cl, nc);
             } else {
                 W w{base, 0u, 0u};
                 {
@@ -337,9 +420,8 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_batch(A, w, nb);
+                    eval_sort<NCH>(A, w, nb);
                     st_dist += nb;
-                    sort_batch(A, w, nb);
                 }
                 for (uint32_t ci = 0; ci < nc; ++ci) {
                     const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
@@ -390,9 +472,8 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
                         }
                         hcount += nb;
                         if (nb == 0) continue;
-                        eval_batch(A, w, nb);
+                        eval_sort<NCH>(A, w, nb);
                         st_dist += nb;
-                        sort_batch(A, w, nb);
                         merge_step(A, w, A.L, 0, nb, true);
                     }
                     // (c) everything in T counts as explored from here on
@@ -402,76 +483,9 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
                             if (tw[i] != kEmpty) tw[i] |= kExplored;
                         __syncwarp();
                     }
-                    // (d) cross-cell hop (gpu_graph.cu:3564-3643)
+                    // (d) cross-cell hop
                     if (ci + 1 < nc) {
-                        const uint32_t next = cl[ci + 1], nlo = A.seg[next], nsz = A.seg[next + 1] - nlo;
-                        const uint32_t hop_n = A.L < kHopSlots ? A.L : kHopSlots;
-                        const uint32_t* tw = w.tw(A);
-                        uint32_t V = 0;
-                        for (uint32_t i0 = 0; i0 < hop_n; i0 += 32) {
-                            uint32_t i = i0 + lane;
-                            V += __popc(__ballot_sync(kFull, i < hop_n && tw[i] != kEmpty));
-                        }
-                        uint32_t* H = w.H(A);
-                        hash_clear(H, A.hs);
-                        const uint32_t pairs = V * A.E;
-                        const size_t rowlen = (size_t)A.P * A.E;
-                        nb = 0;
-                        for (uint32_t j0 = 0; j0 < pairs; j0 += 32) {
-                            uint32_t j = j0 + lane;
-                            bool ok = false;
-                            uint32_t pos = kEmpty;
-                            if (j < pairs) {
-                                uint32_t src = tw[j / A.E] & kPosMask;
-                                pos = __ldg(A.cross + (size_t)src * rowlen + (size_t)next * A.E + (j % A.E));
-                                if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
-                            }
-                            append(w.bw(A), nb, ok, pos);
-                        }
-                        __syncwarp();
-                        st_cross += V;
-                        // filler: smallest local ids of the next cell not among the targets
-                        uint32_t nf = pairs - nb;
-                        uint32_t* bw = w.bw(A);
-                        for (uint32_t x0 = 0; nf > 0 && x0 < nsz; x0 += 32) {
-                            uint32_t x = x0 + lane;
-                            bool ok = x < nsz && !hash_contains(H, A.hs, A.hshift, nlo + x);
-                            uint32_t msk = __ballot_sync(kFull, ok);
-                            uint32_t idx = __popc(msk & lanemask_lt());
-                            if (ok && idx < nf) bw[nb + idx] = nlo + x;
-                            uint32_t take = min((uint32_t)__popc(msk), nf);
-                            nb += take;
-                            nf -= take;
-                        }
-                        __syncwarp();
-                        eval_batch(A, w, nb);
-                        st_dist += nb;
-                        sort_batch(A, w, nb);
-                        const uint32_t ne = min(nb, A.n_entry);
-                        const uint32_t nm = min(nb - ne, kHopSlots);
-                        merge_step(A, w, A.L, ne, nm, false);
-                        // visited set of the next cell: its entry set + its points now in T
-                        hash_clear(H, A.hs);
-                        uint32_t cnt = 0;
-                        for (uint32_t i0 = 0; i0 < ne; i0 += 32) {
-                            uint32_t i = i0 + lane;
-                            bool ins = i < ne && hash_insert(H, A.hs, A.hshift, bw[i] & kPosMask);
-                            cnt += __popc(__ballot_sync(kFull, ins));
-                        }
-                        const uint32_t* tw2 = w.tw(A);
-                        for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
-                            uint32_t i = i0 + lane;
-                            bool ins = false;
-                            if (i < A.L) {
-                                uint32_t v = tw2[i], pos = v & kPosMask;
-                                if (v != kEmpty && pos >= nlo && pos < nlo + nsz)
-                                    ins = hash_insert(H, A.hs, A.hshift, pos);
-                            }
-                            cnt += __popc(__ballot_sync(kFull, ins));
-                        }
-                        __syncwarp();
-                        hcount = cnt;
-                        nb = ne;
+                        nb = cross_hop<NCH>(A, w, cl[ci + 1], hcount, st_dist, st_cross);
                         ++st_hops;
                     }
                 }
@@ -509,6 +523,21 @@ __global__ void __launch_bounds__(128, 6) gmg_search_kernel(SArgs A) {
             atomicAdd(A.stats + 4, (unsigned long long)st_exact);
             atomicAdd(A.stats + 5, 1ull);
         }
+    }
+}
+
+typedef void (*KernelFn)(const SArgs);
+
+// Row lengths compiled with a fixed chunk count (d8 / 8); others use the generic kernel.
+KernelFn pick_kernel(uint32_t nch) {
+    switch (nch) {
+        case 4: return gmg_search_kernel<4>;
+        case 8: return gmg_search_kernel<8>;
+        case 12: return gmg_search_kernel<12>;
+        case 16: return gmg_search_kernel<16>;
+        case 32: return gmg_search_kernel<32>;
+        case 96: return gmg_search_kernel<96>;
+        default: return gmg_search_kernel<0>;
     }
 }
 
@@ -552,7 +581,6 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.stats = p.stats;
     A.qnum = p.qnum;
     A.nch = d.d8 / 8;
-    A.nch16 = (A.nch + 15) / 16 * 16;
     A.a = d.a;
     A.P = d.ncells;
     A.R = d.degree;
@@ -581,32 +609,14 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     while ((1u << lg) < hs) ++lg;
     A.hshift = 32 - lg;
     // staging: up to 32 rows, at most 8 KB per warp
-    uint32_t row_bytes = A.nch16 * 16;
+    const uint32_t nch16 = (A.nch + 15) / 16 * 16;
+    uint32_t row_bytes = nch16 * 16;
     uint32_t sr = 32;
     while (sr > 1 && sr * row_bytes > 8192) sr >>= 1;
     A.stage_rows = sr;
-    Layout lay = make_layout(A.nch16, A.L, A.K, A.bcap, A.stage_rows, A.hs);
-    A.o_qa = lay.o_qa;
-    A.o_qb = lay.o_qb;
-    A.o_lb = lay.o_lb;
-    A.o_rb = lay.o_rb;
-    A.o_t0d = lay.o_t0d;
-    A.o_t0w = lay.o_t0w;
-    A.o_t1d = lay.o_t1d;
-    A.o_t1w = lay.o_t1w;
-    A.o_r0d = lay.o_r0d;
-    A.o_r0w = lay.o_r0w;
-    A.o_r1d = lay.o_r1d;
-    A.o_r1w = lay.o_r1w;
-    A.o_bd = lay.o_bd;
-    A.o_bw = lay.o_bw;
-    A.o_ed = lay.o_ed;
-    A.o_ew = lay.o_ew;
-    A.o_picks = lay.o_picks;
-    A.o_stage = lay.o_stage;
-    A.o_hash = lay.o_hash;
-    A.warp_words = lay.words;
+    make_layout(A, nch16);
 
+    KernelFn kern = pick_kernel(A.nch);
     const int warps_per_block = 4;
     size_t smem = (size_t)warps_per_block * A.warp_words * 4;
     int dev = d.device;
@@ -614,16 +624,16 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     if (smem > (size_t)max_optin) return fail(GF_ERR_ARG, "L/k/hash too large for shared memory");
-    GF_CUDA(cudaFuncSetAttribute(gmg_search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GF_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
-    GF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gmg_search_kernel, 128, smem));
+    GF_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem));
     if (per_sm < 1) return fail(GF_ERR_ARG, "search kernel does not fit on an SM");
     uint32_t blocks = (uint32_t)(nsm * per_sm);
     uint32_t need_blocks = (p.qnum + warps_per_block - 1) / warps_per_block;
     blocks = std::min(blocks, need_blocks);
     GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
     GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
-    gmg_search_kernel<<<blocks, 128, smem, s>>>(A);
+    kern<<<blocks, 128, smem, s>>>(A);
     GF_CUDA(cudaGetLastError());
     return GF_OK;
 }

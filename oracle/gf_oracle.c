@@ -26,11 +26,13 @@
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
  *   - orc_dist16 / orc_dist32: squared L2 of two rows split into 16-byte chunks
- *     (8 fp16 or 4 fp32 elements).  Sixteen partial sums; partial l accumulates the
- *     chunks c = l, l+16, l+32, ... in increasing order, each element with one fused
- *     multiply-add acc = fma(q-x, q-x, acc) (q-x rounded to fp32 first).  The sixteen
- *     partials are then added pairwise: p[i] += p[i+8] (i<8), p[i] += p[i+4] (i<4),
- *     p[i] += p[i+2] (i<2), p[0] += p[1].
+ *     (8 fp16 or 4 fp32 elements).  Thirty-two partial sums p[u][h]: chunk c feeds
+ *     u = c mod 16, its even-indexed elements feed h = 0 and its odd-indexed elements
+ *     h = 1, in increasing order of chunk and element, each with one fused multiply-add
+ *     acc = fma(q-x, q-x, acc) (q-x rounded to fp32 first).  Then s[u] = p[u][0] + p[u][1]
+ *     and the sixteen s[u] are added pairwise: s[i] += s[i+8] (i<8), s[i] += s[i+4]
+ *     (i<4), s[i] += s[i+2] (i<2), s[0] += s[1].  (The element-parity split is what
+ *     packed two-wide fp32 instructions compute.)
  *   - orc_dist_seq: squared L2 with one fma chain over d = 0..D-1 (used for the
  *     query-centroid distances of the cell ordering).
  * The reference accumulates candidate distances in fp16 (gpu_graph.cu:3394-3403) and
@@ -97,34 +99,34 @@ static inline float tree16(float* p) {
     return p[0];
 }
 
+static inline float finish32(float p[16][2]) {
+    float s[16];
+    for (int u = 0; u < 16; ++u) s[u] = p[u][0] + p[u][1];
+    return tree16(s);
+}
+
 /* fp16 rows of d8 elements (d8 % 8 == 0). */
 float orc_dist16(const uint16_t* q, const uint16_t* x, uint32_t d8) {
-    float p[16] = {0};
+    float p[16][2] = {{0}};
     uint32_t nch = d8 / 8;
-    for (uint32_t c = 0; c < nch; ++c) {
-        float acc = p[c & 15];
+    for (uint32_t c = 0; c < nch; ++c)
         for (uint32_t e = 0; e < 8; ++e) {
             float diff = f16_bits_to_f32(q[c * 8 + e]) - f16_bits_to_f32(x[c * 8 + e]);
-            acc = fmaf(diff, diff, acc);
+            p[c & 15][e & 1] = fmaf(diff, diff, p[c & 15][e & 1]);
         }
-        p[c & 15] = acc;
-    }
-    return tree16(p);
+    return finish32(p);
 }
 
 /* fp32 rows of d4 elements (d4 % 4 == 0). */
 float orc_dist32(const float* q, const float* x, uint32_t d4) {
-    float p[16] = {0};
+    float p[16][2] = {{0}};
     uint32_t nch = d4 / 4;
-    for (uint32_t c = 0; c < nch; ++c) {
-        float acc = p[c & 15];
+    for (uint32_t c = 0; c < nch; ++c)
         for (uint32_t e = 0; e < 4; ++e) {
             float diff = q[c * 4 + e] - x[c * 4 + e];
-            acc = fmaf(diff, diff, acc);
+            p[c & 15][e & 1] = fmaf(diff, diff, p[c & 15][e & 1]);
         }
-        p[c & 15] = acc;
-    }
-    return tree16(p);
+    return finish32(p);
 }
 
 float orc_dist_seq(const float* q, const float* x, uint32_t dim) {
