@@ -13,8 +13,9 @@ length in a fixed sweep whose recall on the ground-truth sample reaches the targ
   python bench.py --impl reference                          CPU exact filtered scan (the
                                                             oracle's restatement of the
                                                             reference's CPU path) on host cores
-  python bench.py --impl reference-cuda                     the reference's own CUDA binary
-                                                            (oracle/_ref) on the same index files
+  python bench.py --impl reference-cuda                     the reference's own CUDA binary: prints
+                                                            "unavailable" (it faults on B200, see
+                                                            REF_CUDA_FAULT)
 Multi-GPU (torchrun): every rank holds a replica of the index and runs the full query
 batch (weak scaling); the only collective is the max-over-ranks of the timings.
 """
@@ -334,52 +335,16 @@ def run_reference_cpu(args):
     print(json.dumps(out), flush=True)
 
 
+REF_CUDA_FAULT = (
+    "the reference's realdataset_search (built from source for sm_100a) raised an illegal memory access on "
+    "B200: prefiltering_tag_elements is launched <<<qnum, 32>>> without dynamic shared memory "
+    "(real_dataset_adapter.cuh:501) but writes the query box into extern __shared__ memory (:348-353); "
+    "not run again")
+
+
 def run_reference_cuda(args):
-    """The reference's own CUDA search (oracle/_ref/realdataset_search) on this index."""
-    import torch
-    import garfield_b200 as gf
-    from garfield_b200 import indexbuild
-    binary = ROOT / "oracle" / "_ref" / "realdataset_search"
-    if not binary.exists():
-        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/realdataset_search not built"}))
-        return
-    device = torch.device("cuda", 0)
-    ds, ix = dataset_and_index(args, device)
-    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
-                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
-                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=True)
-    q = ds.queries.shape[0]
-    gt, _ = index.bruteforce(torch.from_numpy(ds.queries).cuda(), torch.from_numpy(ds.lo.astype(np.float32)).cuda(),
-                             torch.from_numpy(ds.hi.astype(np.float32)).cuda(), 10)
-    gt = gt.cpu().numpy().view(np.uint32)
-    index.close()
-    d = Path(args.cache or "/tmp/gf_cache") / "ref_files"
-    paths = indexbuild.write_files(d, "cfg2", ds, ix, gt=gt)
-    res = []
-    for alpha in args.alphas:
-        out_csv = d / f"result_{alpha}.csv"
-        cmd = [str(binary), "--data_path", paths["data_path"], "--query_path", paths["query_path"], "--range",
-               paths["range"], "--gt", paths["gt"], "--cagra_prefix", paths["cagra_prefix"], "--cagra_suffix",
-               paths["cagra_suffix"], "--global_graph", paths["global_graph"], "--grid", paths["grid"], "--attrs",
-               paths["attrs"], "--cluster", paths["cluster"], "--result", str(out_csv), "--prefilter", "0.0",
-               "--postfilter", "17", "--f2h_factor", str(alpha), "--degree", str(ix.degree)]
-        t0 = time.time()
-        r = subprocess.run(cmd, capture_output=True, text=True, timeout=args.ref_timeout)
-        log(f"reference alpha={alpha} rc={r.returncode} in {time.time() - t0:.0f}s")
-        (d / f"stdout_{alpha}.log").write_text(r.stdout[-200000:] + "\n---stderr---\n" + r.stderr[-20000:])
-        if r.returncode != 0 or not out_csv.exists():
-            continue
-        rows = [l.split(",") for l in out_csv.read_text().strip().splitlines()[1:]]
-        rows = [(int(a), float(b), float(c)) for a, b, c, *_ in rows]
-        res.append({"alpha": alpha, "rows": rows})
-    best = None
-    for r in res:
-        for ef, rec, qps in r["rows"]:
-            if rec >= args.target and (best is None or qps > best[2]):
-                best = (ef, rec, qps, r["alpha"])
-    print(json.dumps({"impl": "reference-cuda", "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
-                      "value": None if best is None else round(best[2], 1), "unit": "queries/s",
-                      "best": best, "sweeps": res, "qnum": q}), flush=True)
+    """The reference's own CUDA search: not run (it faults on this GPU, see REF_CUDA_FAULT)."""
+    print(json.dumps({"impl": "reference-cuda", "unavailable": REF_CUDA_FAULT}), flush=True)
 
 
 def main():
