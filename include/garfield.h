@@ -189,6 +189,24 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
 gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
                         uint32_t k, uint32_t* ids_out, float* dist_out, void* stream);
 
+/*
+ * Plan + search of one batch without allocating memory.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory at query time
+ * (a latency-bound serving thread cannot absorb a cudaMalloc, which may synchronise the
+ * device; a process whose device memory another allocator has already claimed has none
+ * to give; an embedded caller may forbid allocation after start-up).  Same arguments and
+ * results as gf_plan_queries followed by gf_search (queries, lb, rb, ids_out, dist_out
+ * are device arrays the caller owns).  All working memory lives in one 4 MiB array of
+ * device memory per GPU, reserved when the library is loaded and held until exit; a
+ * batch that needs more (about 890 bytes per query at 128 dimensions and 16 cells)
+ * returns GF_ERR_ARG.  The first call on a device looks up that array's device address
+ * and should come before any stream capture.  Calls share the array: calls that overlap
+ * on the GPU (different streams or threads) race and must be serialised by the caller.
+ */
+gf_status gf_search_noalloc(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                            float prefilter, const gf_search_params* params, uint32_t* ids_out, float* dist_out,
+                            void* stream);
+
 /* ------------------------------------------------------ file formats (host) */
 /* Readers allocate with malloc; release with gf_free. */
 void gf_free(void* p);
