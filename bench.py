@@ -89,6 +89,17 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+def ncu_traffic() -> float | None:
+    """DRAM bytes of one search launch from the committed ncu summary (None if absent)."""
+    import re
+    p = ROOT / "profiles" / "gmg_search_kernel_config2.md"
+    if p.exists():
+        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
 def peak_hbm() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -283,7 +294,7 @@ def run_ours(args):
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                 "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * 10 * 4)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
                      "kernel": "gmg_search_kernel", "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": int(bytes_step),
                      "counters": {k: int(v) for k, v in st.items()}},
