@@ -200,21 +200,41 @@ def run_ours(args):
         plan.build(qd, lod, hid, 0.0, stream)
         plan.search(gf.SearchParams(L=L, k=10, width=width), stream, ids=ids, dist=dist_t)
 
-    chosen, sweep = None, []
-    Ls = [args.L] if args.L else L_SWEEP
-    for L in Ls:
+    def find_L(width):
+        """Smallest L of the sweep whose recall reaches the target at this width."""
+        sweep = []
+        for L in ([args.L] if args.L else L_SWEEP):
+            with torch.cuda.stream(stream):
+                step(L, width)
+            stream.synchronize()
+            r = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)
+            sweep.append((L, round(r, 4)))
+            log(f"width={width} L={L} recall@10={r:.4f}")
+            if r >= args.target:
+                return L, r, sweep
+        return sweep[-1][0], sweep[-1][1], sweep
+
+    def quick_ms(L, width, n=20):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
-            step(L, args.width)
-        stream.synchronize()
-        r = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)
-        sweep.append((L, round(r, 4)))
-        log(f"L={L} recall@10={r:.4f}")
-        if r >= args.target and chosen is None:
-            chosen = (L, r)
-            break
-    if chosen is None:
-        chosen = (Ls[-1], sweep[-1][1])
-    L, recall = chosen
+            for _ in range(3):
+                step(L, width)
+            a.record(stream)
+            for _ in range(n):
+                step(L, width)
+            b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) / n
+
+    widths = [args.width] if args.width else [1, 2, 4]
+    best = None
+    for wd in widths:
+        L_w, r_w, sw = find_L(wd)
+        ms = quick_ms(L_w, wd) if r_w >= args.target or len(widths) == 1 else float("inf")
+        log(f"width={wd}: L={L_w} recall={r_w:.4f} {ms:.3f} ms/step")
+        if best is None or ms < best[3]:
+            best = (wd, L_w, r_w, ms, sw)
+    args.width, L, recall, _, sweep = best
     # L2 flush buffer (> 126 MB L2)
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
@@ -367,7 +387,7 @@ def main():
     ap.add_argument("--sel", type=float, default=0.10)
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
-    ap.add_argument("--width", type=int, default=1)
+    ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--qnum", type=int, default=10_000)
     ap.add_argument("--R", type=int, default=32)

@@ -282,3 +282,128 @@ __device__ __forceinline__ void hash_clear(uint32_t* H, uint32_t hs) {
 
 }  // namespace dev
 }  // namespace gf
+
+namespace gf {
+namespace dev {
+
+// ------------------------------------------------------------------ 64-bit list keys
+// A list entry is one 64-bit word that is also its sort key:
+//   bits 63..32  distance (fp32 bits; distances are >= +0 so the bits order like values)
+//   bits 31..2   cell-major position
+//   bit 1        explored,  bit 0  in range
+// Ordering by the word orders by (distance, position); the flag bits never decide an
+// order because two entries never share a position.  kEmptyKey (all ones) sorts last.
+typedef unsigned long long key_t;
+constexpr key_t kEmptyKey = ~0ull;
+constexpr uint32_t kKeyExplored = 2u, kKeyInRange = 1u;
+
+__device__ __forceinline__ key_t make_key(float d, uint32_t pos, uint32_t flags) {
+    return ((key_t)__float_as_uint(d) << 32) | ((key_t)pos << 2) | flags;
+}
+__device__ __forceinline__ uint32_t key_pos(key_t k) { return ((uint32_t)k) >> 2; }
+__device__ __forceinline__ float key_dist(key_t k) { return __uint_as_float((uint32_t)(k >> 32)); }
+
+__device__ __forceinline__ key_t shfl_xor_key(key_t k, uint32_t m) {
+    uint32_t lo = __shfl_xor_sync(kFull, (uint32_t)k, m);
+    uint32_t hi = __shfl_xor_sync(kFull, (uint32_t)(k >> 32), m);
+    return ((key_t)hi << 32) | lo;
+}
+
+// Bitonic sort of 32 keys held one per lane, ascending.
+__device__ __forceinline__ key_t warp_sort32_key(key_t k) {
+    const uint32_t lane = lane_id();
+#pragma unroll
+    for (uint32_t s = 2; s <= 32; s <<= 1) {
+#pragma unroll
+        for (uint32_t j = s >> 1; j > 0; j >>= 1) {
+            const key_t o = shfl_xor_key(k, j);
+            const bool keep_min = ((lane & j) == 0) == ((lane & s) == 0);
+            k = keep_min ? (o < k ? o : k) : (o > k ? o : k);
+        }
+    }
+    return k;
+}
+
+// Bitonic sort of n (power of two) keys in shared memory, ascending.
+__device__ __forceinline__ void warp_sort_keys(key_t* a, uint32_t n) {
+    const uint32_t lane = lane_id();
+    for (uint32_t ls = 1; (1u << ls) <= n; ++ls) {
+        const uint32_t s = 1u << ls;
+        for (int lj = (int)ls - 1; lj >= 0; --lj) {
+            const uint32_t j = 1u << lj;
+            for (uint32_t i = lane; i < (n >> 1); i += 32) {
+                const uint32_t lo = ((i >> lj) << (lj + 1)) | (i & (j - 1));
+                const uint32_t hi = lo + j;
+                const key_t x = a[lo], y = a[hi];
+                if ((x > y) == ((lo & s) == 0)) {
+                    a[lo] = y;
+                    a[hi] = x;
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// Number of keys of the sorted array a[0..n) below `key`.
+__device__ __forceinline__ uint32_t keys_below(const key_t* a, uint32_t n, key_t key) {
+    uint32_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (a[mid] < key)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+// Merge the sorted batch b[0..nb) (no empty keys) into the sorted list t[0..L), writing
+// the first L keys of the union to o (t and o distinct).  Only the batch prefix that
+// enters is processed, and list entries before the first insertion point are copied.
+// With `recycle`, list entries pushed out that are in range are appended in order to ev
+// (merge_top_with_recycle_list, gpu_graph.cu:482-581).  Returns (entered << 16) | evicted;
+// entered == 0 means o was not written.
+static __device__ __noinline__ uint32_t merge_keys(const key_t* t, key_t* o, uint32_t L, const key_t* b, uint32_t nb,
+                                            key_t* ev, bool recycle) {
+    const uint32_t lane = lane_id();
+    // entering batch prefix: b[j] enters iff j + #(t < b[j]) < L (increasing in j)
+    uint32_t m = 0;
+    for (uint32_t j0 = 0; j0 < nb; j0 += 32) {
+        const uint32_t j = j0 + lane;
+        uint32_t pos = 0xFFFFFFFFu;
+        key_t kj = kEmptyKey;
+        if (j < nb) {
+            kj = b[j];
+            pos = j + keys_below(t, L, kj);
+        }
+        const uint32_t msk = __ballot_sync(kFull, pos < L);
+        if (pos < L) o[pos] = kj;
+        m += __popc(msk);
+        if (__popc(msk) < 32) break;
+    }
+    if (m == 0) return 0;
+    const uint32_t first = __shfl_sync(kFull, keys_below(t, L, b[0]), 0);
+    uint32_t nev = 0;
+    for (uint32_t i0 = 0; i0 < L; i0 += 32) {
+        const uint32_t i = i0 + lane;
+        bool out = false;
+        key_t ki = kEmptyKey;
+        if (i < L) {
+            ki = t[i];
+            const uint32_t pos = i < first ? i : i + keys_below(b, m, ki);
+            if (pos < L)
+                o[pos] = ki;
+            else
+                out = recycle && ki != kEmptyKey && (ki & kKeyInRange);
+        }
+        const uint32_t msk = __ballot_sync(kFull, out);
+        if (out) ev[nev + __popc(msk & lanemask_lt())] = ki;
+        nev += __popc(msk);
+    }
+    __syncwarp();
+    return (m << 16) | nev;
+}
+
+}  // namespace dev
+}  // namespace gf

@@ -73,6 +73,8 @@ struct Plan {
     uint32_t* offsets = nullptr; // max_q
     uint32_t* cells = nullptr;   // max_q x ncells
     uint32_t* top4 = nullptr;    // max_q x 4
+    float* part_d = nullptr;     // max_q x splits x 4 per-range centroid candidates
+    uint32_t* part_i = nullptr;
     uint32_t* box = nullptr;     // max_q (box counts)
     uint32_t* task = nullptr;    // max_q processing order
     uint32_t* scratch = nullptr; // small counters: [0] queue head, [1..] histogram
@@ -95,6 +97,8 @@ struct gf_plan {
 
 namespace gf {
 // gf_plan.cu
+uint32_t centroid_splits(uint32_t C);  // centroid ranges of the top-4 kernel
+uint32_t centroid_chunk(uint32_t C);   // centroids per range (multiple of 64)
 gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
                        uint32_t qnum, float prefilter, cudaStream_t s);
 // gf_search.cu

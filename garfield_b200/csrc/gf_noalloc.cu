@@ -100,6 +100,8 @@ extern "C" gf_status gf_search_noalloc(gf_index* idx, const float* queries, cons
     p.offsets = cv.take<uint32_t>(Q);
     p.cells = cv.take<uint32_t>(Q * d.ncells);
     p.top4 = cv.take<uint32_t>(Q * 4);
+    p.part_d = cv.take<float>(Q * centroid_splits(d.C) * 4);
+    p.part_i = cv.take<uint32_t>(Q * centroid_splits(d.C) * 4);
     p.box = cv.take<uint32_t>(Q);
     p.task = cv.take<uint32_t>(Q * 3);
     p.scratch = cv.take<uint32_t>(16);

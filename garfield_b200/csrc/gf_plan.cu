@@ -133,19 +133,23 @@ __global__ void box_count_kernel(const float* __restrict__ attrs, uint32_t n, ui
 
 // Four nearest centroids per query (dis_cal_tensor_core + select_topk_by_reduce_min,
 // tools.cuh:1399-1537), distances by one fma chain over d (oracle orc_dist_seq), ties
-// by centroid id.  Block: 32 queries x 64-centroid tiles; thread t owns queries
-// 4*(t%8)..+3 and centroids 4*(t/8)..+3 of the tile; both tiles are stored
-// dimension-major in shared memory so each step reads two float4.
+// by centroid id.  Block (x, y): 32 queries x the y-th range of c_chunk centroids, in
+// 64-centroid tiles; thread t owns queries 4*(t%8)..+3 and centroids 4*(t/8)..+3 of the
+// tile; both tiles are stored dimension-major in shared memory so each step reads two
+// float4.  Each block writes the 4 best of its range per query to part (q, y); a second
+// kernel merges the ranges.
 constexpr uint32_t kTQ = 32, kTC = 64, kTD = 32;
 __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restrict__ queries, uint32_t qnum,
                                                             uint32_t dim, const float* __restrict__ cent,
-                                                            uint32_t C, uint32_t* __restrict__ top4) {
+                                                            uint32_t C, uint32_t c_chunk, float* __restrict__ part_d,
+                                                            uint32_t* __restrict__ part_i) {
     __shared__ __align__(16) float qt[kTD][kTQ];
     __shared__ __align__(16) float ct[kTD][kTC];
     __shared__ float md[kTQ][16][4];
     __shared__ uint32_t mi[kTQ][16][4];
     const uint32_t t = threadIdx.x, qg = t & 7, cg = t >> 3;
     const uint32_t q0 = blockIdx.x * kTQ;
+    const uint32_t cbeg = blockIdx.y * c_chunk, cend = min(C, cbeg + c_chunk);
     float bd[4][4];
     uint32_t bi[4][4];
 #pragma unroll
@@ -155,7 +159,7 @@ __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restr
             bd[i][r] = __int_as_float(0x7f800000);
             bi[i][r] = kEmpty;
         }
-    for (uint32_t c0 = 0; c0 < C; c0 += kTC) {
+    for (uint32_t c0 = cbeg; c0 < cend; c0 += kTC) {
         float acc[4][4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -171,7 +175,7 @@ __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restr
             for (uint32_t e = t; e < kTC * kTD; e += blockDim.x) {
                 uint32_t r = e / kTD, dd = e % kTD;
                 uint32_t c = c0 + r, d = d0 + dd;
-                ct[dd][r] = (c < C && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
+                ct[dd][r] = (c < cend && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
             }
             __syncthreads();
             const uint32_t dn = min(kTD, dim - d0);
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restr
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             uint32_t c = c0 + cg * 4 + j;
-            if (c >= C) continue;
+            if (c >= cend) continue;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float dv = acc[i][j];
@@ -247,8 +251,41 @@ __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restr
                     }
                 }
             }
-        for (int r = 0; r < 4; ++r) top4[(size_t)(q0 + t) * 4 + r] = fi[r];
+        const size_t o = ((size_t)(q0 + t) * gridDim.y + blockIdx.y) * 4;
+        for (int r = 0; r < 4; ++r) {
+            part_d[o + r] = fd[r];
+            part_i[o + r] = fi[r];
+        }
     }
+}
+
+// Merge the per-range candidates of each query into its 4 nearest centroids.
+__global__ void centroid_merge_kernel(uint32_t qnum, uint32_t splits, const float* __restrict__ part_d,
+                                      const uint32_t* __restrict__ part_i, uint32_t* __restrict__ top4) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= qnum) return;
+    float fd[4];
+    uint32_t fi[4];
+    for (int r = 0; r < 4; ++r) {
+        fd[r] = __int_as_float(0x7f800000);
+        fi[r] = kEmpty;
+    }
+    for (uint32_t e = 0; e < splits * 4; ++e) {
+        const float dv = part_d[(size_t)q * splits * 4 + e];
+        const uint32_t c = part_i[(size_t)q * splits * 4 + e];
+        if (c == kEmpty || !(mkkey(dv, c) < mkkey(fd[3], fi[3]))) continue;
+        fd[3] = dv;
+        fi[3] = c;
+        for (int k = 3; k > 0 && mkkey(fd[k], fi[k]) < mkkey(fd[k - 1], fi[k - 1]); --k) {
+            float td = fd[k];
+            fd[k] = fd[k - 1];
+            fd[k - 1] = td;
+            uint32_t ti = fi[k];
+            fi[k] = fi[k - 1];
+            fi[k - 1] = ti;
+        }
+    }
+    for (int r = 0; r < 4; ++r) top4[(size_t)q * 4 + r] = fi[r];
 }
 
 // Score = sum over the 4 nearest centroids of hist[cell][centroid]; cells ordered by
@@ -291,6 +328,21 @@ __global__ void iota_kernel(uint32_t* v, uint32_t n) {
 
 }  // namespace
 
+uint32_t centroid_chunk(uint32_t C) {
+    uint32_t S = centroid_splits(C);
+    uint32_t chunk = (C + S - 1) / std::max(S, 1u);
+    return (chunk + kTC - 1) / kTC * kTC;
+}
+
+uint32_t centroid_splits(uint32_t C) {
+    uint32_t S = (C + 127) / 128;
+    S = std::min(S, 32u);
+    S = std::max(S, 1u);
+    // all ranges non-empty
+    uint32_t chunk = ((C + S - 1) / S + kTC - 1) / kTC * kTC;
+    return std::max(1u, (C + chunk - 1) / chunk);
+}
+
 gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
                        uint32_t qnum, float prefilter, cudaStream_t s) {
     DeviceIndex& d = idx->d;
@@ -317,7 +369,10 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     plan_fill_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts, p.offsets,
                                        p.cells);
     if (d.C) {
-        centroid_top4_kernel<<<(qnum + kTQ - 1) / kTQ, 128, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, p.top4);
+        const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
+        dim3 grid((qnum + kTQ - 1) / kTQ, S);
+        centroid_top4_kernel<<<grid, 128, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i);
+        centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, s>>>(qnum, S, p.part_d, p.part_i, p.top4);
         order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
     } else {
         GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
@@ -355,7 +410,7 @@ struct DeviceGuard2 {
 
 void free_plan(Plan& p) {
     void* ptrs[] = {p.q16, p.q32, p.lb, p.rb, p.counts, p.offsets, p.cells, p.top4, p.box, p.task, p.scratch,
-                    p.stats, p.scan_tmp};
+                    p.stats, p.scan_tmp, p.part_d, p.part_i};
     for (void* x : ptrs)
         if (x) cudaFree(x);
     if (p.h_stage) cudaFreeHost(p.h_stage);
@@ -387,6 +442,8 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
     A((void**)&p.offsets, Q * 4);
     A((void**)&p.cells, Q * d.ncells * 4);
     A((void**)&p.top4, Q * 16);
+    A((void**)&p.part_d, Q * centroid_splits(d.C) * 16);
+    A((void**)&p.part_i, Q * centroid_splits(d.C) * 16);
     A((void**)&p.box, Q * 4);
     A((void**)&p.task, Q * 3 * 4);
     A((void**)&p.scratch, 64);

@@ -55,6 +55,9 @@ struct SArgs {
 };
 
 // Shared-memory layout of one warp, in 32-bit words, every region 16-byte aligned.
+// Lists hold 64-bit keys (see key_t): T and T' (L each), RL and RL' (k each), the batch B
+// and the eviction buffer E (bcap each).  Candidate positions of a batch are gathered
+// into E (as 32-bit words) before evaluation, while E is otherwise unused.
 void make_layout(SArgs& A, uint32_t nch16) {
     uint32_t o = 0;
     auto take = [&](uint32_t words) {
@@ -65,18 +68,13 @@ void make_layout(SArgs& A, uint32_t nch16) {
     A.o_q = take(nch16 * 8);  // fp32 query as (even, odd) element pairs, 4 pairs per chunk
     A.o_lb = take(kMaxAttr);
     A.o_rb = take(kMaxAttr);
-    A.o_t0d = take(A.L);
-    A.o_t0w = take(A.L);
-    A.o_t1d = take(A.L);
-    A.o_t1w = take(A.L);
-    A.o_r0d = take(A.K);
-    A.o_r0w = take(A.K);
-    A.o_r1d = take(A.K);
-    A.o_r1w = take(A.K);
-    A.o_bd = take(A.bcap);
-    A.o_bw = take(A.bcap);
-    A.o_ed = take(A.bcap);
-    A.o_ew = take(A.bcap);
+    A.o_t0d = take(2 * A.L);
+    A.o_t1d = take(2 * A.L);
+    A.o_r0d = take(2 * A.K);
+    A.o_r1d = take(2 * A.K);
+    A.o_bd = take(2 * A.bcap);
+    A.o_ed = take(2 * A.bcap);
+    A.o_t0w = A.o_t1w = A.o_r0w = A.o_r1w = A.o_bw = A.o_ew = 0;
     A.o_picks = take(32);
     A.o_stage = take(A.stage_rows * nch16 * 4);
     A.o_hash = take(A.hs);
@@ -88,18 +86,13 @@ void make_layout(SArgs& A, uint32_t nch16) {
 struct W {
     uint32_t* base;
     uint32_t tsel, rsel;  // which buffer of T / RL is current
-    __device__ float* td(const SArgs& A) const { return (float*)(base + (tsel ? A.o_t1d : A.o_t0d)); }
-    __device__ uint32_t* tw(const SArgs& A) const { return base + (tsel ? A.o_t1w : A.o_t0w); }
-    __device__ float* nd(const SArgs& A) const { return (float*)(base + (tsel ? A.o_t0d : A.o_t1d)); }
-    __device__ uint32_t* nw(const SArgs& A) const { return base + (tsel ? A.o_t0w : A.o_t1w); }
-    __device__ float* rd(const SArgs& A) const { return (float*)(base + (rsel ? A.o_r1d : A.o_r0d)); }
-    __device__ uint32_t* rw(const SArgs& A) const { return base + (rsel ? A.o_r1w : A.o_r0w); }
-    __device__ float* rnd(const SArgs& A) const { return (float*)(base + (rsel ? A.o_r0d : A.o_r1d)); }
-    __device__ uint32_t* rnw(const SArgs& A) const { return base + (rsel ? A.o_r0w : A.o_r1w); }
-    __device__ float* bd(const SArgs& A) const { return (float*)(base + A.o_bd); }
-    __device__ uint32_t* bw(const SArgs& A) const { return base + A.o_bw; }
-    __device__ float* ed(const SArgs& A) const { return (float*)(base + A.o_ed); }
-    __device__ uint32_t* ew(const SArgs& A) const { return base + A.o_ew; }
+    __device__ key_t* T(const SArgs& A) const { return (key_t*)(base + (tsel ? A.o_t1d : A.o_t0d)); }
+    __device__ key_t* Tn(const SArgs& A) const { return (key_t*)(base + (tsel ? A.o_t0d : A.o_t1d)); }
+    __device__ key_t* RL(const SArgs& A) const { return (key_t*)(base + (rsel ? A.o_r1d : A.o_r0d)); }
+    __device__ key_t* RLn(const SArgs& A) const { return (key_t*)(base + (rsel ? A.o_r0d : A.o_r1d)); }
+    __device__ key_t* B(const SArgs& A) const { return (key_t*)(base + A.o_bd); }
+    __device__ key_t* E(const SArgs& A) const { return (key_t*)(base + A.o_ed); }
+    __device__ uint32_t* P(const SArgs& A) const { return base + A.o_ed; }  // batch positions (aliases E)
     __device__ uint32_t* picks(const SArgs& A) const { return base + A.o_picks; }
     __device__ uint32_t* H(const SArgs& A) const { return base + A.o_hash; }
     __device__ const float* lb(const SArgs& A) const { return (const float*)(base + A.o_lb); }
@@ -108,102 +101,93 @@ struct W {
 
 __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 1u << (32 - __clz(x - 1)); }
 
-// Distances + range flags for the positions in B[0..nb), sorted ascending into B (padded
-// with empty entries to a power of two >= 32).  Rows are staged through shared memory
-// with cp.async, stage_rows at a time, chunk c of staged row r at stage_slot(c, r); each
-// lane computes the distance of one staged row.  Batches of at most 32 are sorted in
-// registers, larger ones in shared memory.
+// Distances + range flags of the positions P[0..nb), written as sorted keys to B[0..)
+// (padded with empty keys to a power of two >= 32).  Rows are staged through shared
+// memory with cp.async, stage_rows at a time, chunk c of staged row r at stage_slot(c, r);
+// each lane computes the distance of one staged row.  Batches of at most 32 are sorted
+// in registers, larger ones in shared memory.
 template <int NCH>
 __device__ __forceinline__ void eval_sort(const SArgs& A, const W& w, uint32_t nb) {
     const uint32_t lane = lane_id();
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
     const uint32_t nch16 = (nch + 15u) & ~15u;
-    uint32_t* bw = w.bw(A);
-    float* bd = w.bd(A);
+    const uint32_t* P = w.P(A);
+    key_t* B = w.B(A);
     uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
     const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
     const uint32_t SR = A.stage_rows;
-    float dreg = kInf;
-    uint32_t wreg = kEmpty;
+    key_t kreg = kEmptyKey;
     for (uint32_t r0 = 0; r0 < nb; r0 += SR) {
         const uint32_t rows = min(SR, nb - r0);
         const uint32_t total = rows * nch;
         for (uint32_t e = lane; e < total; e += 32) {
             const uint32_t r = e / nch, c = e - r * nch;
-            const uint32_t pos = bw[r0 + r];
+            const uint32_t pos = P[r0 + r];
             cp_async16(stage + (size_t)r * nch16 + stage_slot(c, r), A.vec16 + (size_t)pos * nch + c);
         }
         bool inr = false;
         uint32_t pos = 0;
         if (lane < rows) {
-            pos = bw[r0 + lane];
+            pos = P[r0 + lane];
             inr = in_box(A.attrs, pos, A.a, w.lb(A), w.rb(A));
         }
         cp_async_wait_all();
         __syncwarp();
         if (lane < rows) {
             const float d = dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
-            const uint32_t wv = pos | (inr ? kInRange : 0u);
-            if (nb <= 32) {
-                dreg = d;
-                wreg = wv;
-            } else {
-                bd[r0 + lane] = d;
-                bw[r0 + lane] = wv;
-            }
+            const key_t k = make_key(d, pos, inr ? kKeyInRange : 0u);
+            if (nb <= 32)
+                kreg = k;
+            else
+                B[r0 + lane] = k;
         }
         __syncwarp();
     }
     if (nb <= 32) {
-        warp_sort32(dreg, wreg);
-        bd[lane] = dreg;
-        bw[lane] = wreg;
+        B[lane] = warp_sort32_key(kreg);
         __syncwarp();
         return;
     }
     const uint32_t n = next_pow2(nb);
-    for (uint32_t j = nb + lane; j < n; j += 32) {
-        bd[j] = kInf;
-        bw[j] = kEmpty;
-    }
+    for (uint32_t j = nb + lane; j < n; j += 32) B[j] = kEmptyKey;
     __syncwarp();
-    warp_sort(bd, bw, n);
+    warp_sort_keys(B, n);
 }
 
 // Merge B[b0..b0+nb) into T (length L); with recycling, in-range entries pushed out of
 // T are merged into RL (length k).
 __device__ __forceinline__ void merge_step(const SArgs& A, W& w, uint32_t L, uint32_t b0, uint32_t nb, bool recycle) {
     if (nb == 0) return;
-    const float* bd = w.bd(A) + b0;
-    const uint32_t* bw = w.bw(A) + b0;
+    const key_t* B = w.B(A) + b0;
     {
-        const float* td = w.td(A);
-        const uint32_t* tw = w.tw(A);
+        const key_t last = w.T(A)[L - 1];
         // nothing can enter a full list whose last entry beats the best candidate
-        if (tw[L - 1] != kEmpty && mkkey(bd[0], bw[0]) > mkkey(td[L - 1], tw[L - 1])) return;
+        if (last != kEmptyKey && B[0] > last) return;
     }
-    uint32_t nev = merge_list(w.td(A), w.tw(A), w.nd(A), w.nw(A), L, bd, bw, nb, w.ed(A), w.ew(A), recycle);
+    const uint32_t r = merge_keys(w.T(A), w.Tn(A), L, B, nb, w.E(A), recycle);
+    if ((r >> 16) == 0) return;
     w.tsel ^= 1u;
+    const uint32_t nev = r & 0xFFFFu;
     if (nev == 0) return;
-    const uint32_t K = A.K;
-    if (w.rw(A)[K - 1] != kEmpty && mkkey(w.ed(A)[0], w.ew(A)[0]) > mkkey(w.rd(A)[K - 1], w.rw(A)[K - 1])) return;
-    merge_list(w.rd(A), w.rw(A), w.rnd(A), w.rnw(A), K, w.ed(A), w.ew(A), nev, nullptr, nullptr, false);
-    w.rsel ^= 1u;
+    const key_t rlast = w.RL(A)[A.K - 1];
+    if (rlast != kEmptyKey && w.E(A)[0] > rlast) return;
+    const uint32_t r2 = merge_keys(w.RL(A), w.RLn(A), A.K, w.E(A), nev, nullptr, false);
+    if ((r2 >> 16) != 0) w.rsel ^= 1u;
 }
 
 // Clear the hash and insert the list entries that lie in [lo, hi); returns how many.
 __device__ __forceinline__ uint32_t hash_rebuild(const SArgs& A, const W& w, uint32_t lo, uint32_t hi) {
     uint32_t* H = w.H(A);
-    const uint32_t* tw = w.tw(A);
+    const key_t* T = w.T(A);
     hash_clear(H, A.hs);
     uint32_t cnt = 0;
     for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
         uint32_t i = i0 + lane_id();
         bool ins = false;
         if (i < A.L) {
-            uint32_t v = tw[i];
-            uint32_t pos = v & kPosMask;
-            if (v != kEmpty && pos >= lo && pos < hi) ins = hash_insert(H, A.hs, A.hshift, pos);
+            const key_t k = T[i];
+            const uint32_t pos = key_pos(k);
+            if (k != kEmptyKey && pos >= lo && pos < hi) ins = hash_insert(H, A.hs, A.hshift, pos);
         }
         cnt += __popc(__ballot_sync(kFull, ins));
     }
@@ -211,19 +195,18 @@ __device__ __forceinline__ uint32_t hash_rebuild(const SArgs& A, const W& w, uin
     return cnt;
 }
 
-__device__ __forceinline__ void write_result(const SArgs& A, uint32_t q, const float* d, const uint32_t* wv,
-                                             uint32_t n) {
+__device__ __forceinline__ void write_result(const SArgs& A, uint32_t q, const key_t* list, uint32_t n) {
     for (uint32_t k = lane_id(); k < A.K; k += 32) {
-        uint32_t wk = k < n ? wv[k] : kEmpty;
-        A.out_ids[(size_t)q * A.K + k] = wk == kEmpty ? kEmpty : A.i2g[wk & kPosMask];
-        if (A.out_d) A.out_d[(size_t)q * A.K + k] = wk == kEmpty ? kInf : d[k];
+        const key_t v = k < n ? list[k] : kEmptyKey;
+        A.out_ids[(size_t)q * A.K + k] = v == kEmptyKey ? kEmpty : A.i2g[key_pos(v)];
+        if (A.out_d) A.out_d[(size_t)q * A.K + k] = v == kEmptyKey ? kInf : key_dist(v);
     }
 }
 
-// Append the positions held by lanes with ok=true to B at nb (warp-uniform counter).
-__device__ __forceinline__ void append(uint32_t* bw, uint32_t& nb, bool ok, uint32_t pos) {
+// Append the positions held by lanes with ok=true to P at nb (warp-uniform counter).
+__device__ __forceinline__ void append(uint32_t* P, uint32_t& nb, bool ok, uint32_t pos) {
     uint32_t msk = __ballot_sync(kFull, ok);
-    if (ok) bw[nb + __popc(msk & lanemask_lt())] = pos;
+    if (ok) P[nb + __popc(msk & lanemask_lt())] = pos;
     nb += __popc(msk);
 }
 
@@ -233,21 +216,15 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
                                              uint32_t nc) {
     const uint32_t lane = lane_id();
     W w{base, 0u, 0u};
-    float* td = w.td(A);
-    uint32_t* tw = w.tw(A);
-    for (uint32_t i = lane; i < A.K; i += 32) {
-        td[i] = kInf;
-        tw[i] = kEmpty;
-    }
+    for (uint32_t i = lane; i < A.K; i += 32) w.T(A)[i] = kEmptyKey;
     __syncwarp();
     uint32_t nb = 0, ndist = 0;
     const uint32_t flush_at = A.bcap - 32;
-    uint32_t* bw = w.bw(A);
     for (uint32_t ci = 0; ci < nc; ++ci) {
         const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
         for (uint32_t x0 = lo; x0 < hi; x0 += 32) {
             const uint32_t x = x0 + lane;
-            append(bw, nb, x < hi && in_box(A.attrs, x, A.a, w.lb(A), w.rb(A)), x);
+            append(w.P(A), nb, x < hi && in_box(A.attrs, x, A.a, w.lb(A), w.rb(A)), x);
             const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
@@ -259,7 +236,7 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
         }
     }
     __syncwarp();
-    write_result(A, q, w.td(A), w.tw(A), A.K);
+    write_result(A, q, w.T(A), A.K);
     return ndist;
 }
 
@@ -274,28 +251,28 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
     const uint32_t lane = lane_id();
     const uint32_t nlo = A.seg[next], nsz = A.seg[next + 1] - nlo;
     const uint32_t hop_n = A.L < kHopSlots ? A.L : kHopSlots;
-    const uint32_t* tw = w.tw(A);
+    const key_t* T = w.T(A);
     uint32_t V = 0;
     for (uint32_t i0 = 0; i0 < hop_n; i0 += 32) {
         uint32_t i = i0 + lane;
-        V += __popc(__ballot_sync(kFull, i < hop_n && tw[i] != kEmpty));
+        V += __popc(__ballot_sync(kFull, i < hop_n && T[i] != kEmptyKey));
     }
     uint32_t* H = w.H(A);
     hash_clear(H, A.hs);
     const uint32_t pairs = V * A.E;
     const size_t rowlen = (size_t)A.P * A.E;
     uint32_t nb = 0;
-    uint32_t* bw = w.bw(A);
+    uint32_t* P = w.P(A);
     for (uint32_t j0 = 0; j0 < pairs; j0 += 32) {
         uint32_t j = j0 + lane;
         bool ok = false;
         uint32_t pos = kEmpty;
         if (j < pairs) {
-            uint32_t src = tw[j / A.E] & kPosMask;
+            uint32_t src = key_pos(T[j / A.E]);
             pos = __ldg(A.cross + (size_t)src * rowlen + (size_t)next * A.E + (j % A.E));
             if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
         }
-        append(bw, nb, ok, pos);
+        append(P, nb, ok, pos);
     }
     __syncwarp();
     st_cross += V;
@@ -306,7 +283,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         bool ok = x < nsz && !hash_contains(H, A.hs, A.hshift, nlo + x);
         uint32_t msk = __ballot_sync(kFull, ok);
         uint32_t idx = __popc(msk & lanemask_lt());
-        if (ok && idx < nf) bw[nb + idx] = nlo + x;
+        if (ok && idx < nf) P[nb + idx] = nlo + x;
         uint32_t take = min((uint32_t)__popc(msk), nf);
         nb += take;
         nf -= take;
@@ -319,19 +296,21 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
     merge_step(A, w, A.L, ne, nm, false);
     // visited set of the next cell: its entry set + its points now in T
     hash_clear(H, A.hs);
+    const key_t* B = w.B(A);
     uint32_t cnt = 0;
     for (uint32_t i0 = 0; i0 < ne; i0 += 32) {
         uint32_t i = i0 + lane;
-        bool ins = i < ne && hash_insert(H, A.hs, A.hshift, bw[i] & kPosMask);
+        bool ins = i < ne && hash_insert(H, A.hs, A.hshift, key_pos(B[i]));
         cnt += __popc(__ballot_sync(kFull, ins));
     }
-    const uint32_t* tw2 = w.tw(A);
+    const key_t* T2 = w.T(A);
     for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
         uint32_t i = i0 + lane;
         bool ins = false;
         if (i < A.L) {
-            uint32_t v = tw2[i], pos = v & kPosMask;
-            if (v != kEmpty && pos >= nlo && pos < nlo + nsz) ins = hash_insert(H, A.hs, A.hshift, pos);
+            const key_t k = T2[i];
+            const uint32_t pos = key_pos(k);
+            if (k != kEmptyKey && pos >= nlo && pos < nlo + nsz) ins = hash_insert(H, A.hs, A.hshift, pos);
         }
         cnt += __popc(__ballot_sync(kFull, ins));
     }
@@ -373,7 +352,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
         }
         uint32_t st_dist = 0, st_exp = 0, st_cross = 0, st_hops = 0, st_exact = 0;
         if (nc == 0) {
-            write_result(A, q, nullptr, nullptr, 0);
+            write_result(A, q, nullptr, 0);
         } else {
             bool exact = nc >= A.postfilter;
             if (!exact && A.box) {
@@ -385,20 +364,8 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                 st_dist = exact_route<NCH>(A, base, q, cl, nc);
             } else {
                 W w{base, 0u, 0u};
-                {
-                    float* td = w.td(A);
-                    uint32_t* tw = w.tw(A);
-                    for (uint32_t i = lane; i < A.L; i += 32) {
-                        td[i] = kInf;
-                        tw[i] = kEmpty;
-                    }
-                    float* rd = w.rd(A);
-                    uint32_t* rw = w.rw(A);
-                    for (uint32_t i = lane; i < A.K; i += 32) {
-                        rd[i] = kInf;
-                        rw[i] = kEmpty;
-                    }
-                }
+                for (uint32_t i = lane; i < A.L; i += 32) w.T(A)[i] = kEmptyKey;
+                for (uint32_t i = lane; i < A.K; i += 32) w.RL(A)[i] = kEmptyKey;
                 hash_clear(w.H(A), A.hs);
                 uint32_t hcount = 0;
                 // entry set of the first cell (gpu_graph.cu:3347-3351)
@@ -416,7 +383,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                                 ok = hash_insert(w.H(A), A.hs, A.hshift, pos);
                             }
                         }
-                        append(w.bw(A), nb, ok, pos);
+                        append(w.P(A), nb, ok, pos);
                     }
                     __syncwarp();
                     hcount = nb;
@@ -431,18 +398,18 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     for (uint32_t it = 0; it < A.max_iter; ++it) {
                         uint32_t np = 0;
                         {
-                            uint32_t* tw = w.tw(A);
+                            key_t* T = w.T(A);
                             uint32_t* picks = w.picks(A);
                             for (uint32_t i0 = 0; i0 < A.L && np < A.W; i0 += 32) {
                                 uint32_t i = i0 + lane;
-                                uint32_t v = i < A.L ? tw[i] : kEmpty;
-                                uint32_t msk = __ballot_sync(kFull, v != kEmpty && !(v & kExplored));
+                                key_t k = i < A.L ? T[i] : kEmptyKey;
+                                uint32_t msk = __ballot_sync(kFull, (k & kKeyExplored) == 0);
                                 while (msk && np < A.W) {
                                     uint32_t b = __ffs(msk) - 1;
                                     msk &= msk - 1;
                                     if (lane == b) {
-                                        tw[i] = v | kExplored;
-                                        picks[np] = v & kPosMask;
+                                        T[i] = k | kKeyExplored;
+                                        picks[np] = key_pos(k);
                                     }
                                     ++np;
                                 }
@@ -466,7 +433,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                                     pos = __ldg(A.graph + (size_t)node * A.R + (j % A.R));
                                     if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
                                 }
-                                append(w.bw(A), nb, ok, pos);
+                                append(w.P(A), nb, ok, pos);
                             }
                             __syncwarp();
                         }
@@ -478,9 +445,8 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     }
                     // (c) everything in T counts as explored from here on
                     {
-                        uint32_t* tw = w.tw(A);
-                        for (uint32_t i = lane; i < A.L; i += 32)
-                            if (tw[i] != kEmpty) tw[i] |= kExplored;
+                        key_t* T = w.T(A);
+                        for (uint32_t i = lane; i < A.L; i += 32) T[i] |= kKeyExplored;
                         __syncwarp();
                     }
                     // (d) cross-cell hop
@@ -492,26 +458,24 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                 // final post-filter of T and recycle merge (gpu_graph.cu:4025-4048)
                 uint32_t nin = 0;
                 {
-                    const float* td = w.td(A);
-                    const uint32_t* tw = w.tw(A);
-                    float* nd = w.nd(A);
-                    uint32_t* nw = w.nw(A);
+                    const key_t* T = w.T(A);
+                    key_t* Tn = w.Tn(A);
                     for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
                         uint32_t i = i0 + lane;
-                        uint32_t v = i < A.L ? tw[i] : kEmpty;
-                        bool ok = v != kEmpty && (v & kInRange);
+                        key_t k = i < A.L ? T[i] : kEmptyKey;
+                        bool ok = k != kEmptyKey && (k & kKeyInRange);
                         uint32_t msk = __ballot_sync(kFull, ok);
-                        if (ok) {
-                            uint32_t k = nin + __popc(msk & lanemask_lt());
-                            nd[k] = td[i];
-                            nw[k] = v;
-                        }
+                        if (ok) Tn[nin + __popc(msk & lanemask_lt())] = k;
                         nin += __popc(msk);
                     }
                     __syncwarp();
                 }
-                merge_list(w.rd(A), w.rw(A), w.rnd(A), w.rnw(A), A.K, w.nd(A), w.nw(A), nin, nullptr, nullptr, false);
-                write_result(A, q, w.rnd(A), w.rnw(A), A.K);
+                const key_t* res = w.RL(A);
+                if (nin) {
+                    const uint32_t r = merge_keys(w.RL(A), w.RLn(A), A.K, w.Tn(A), nin, nullptr, false);
+                    if ((r >> 16) != 0) res = w.RLn(A);
+                }
+                write_result(A, q, res, A.K);
             }
         }
         __syncwarp();
