@@ -226,7 +226,7 @@ def run_ours(args):
         b.synchronize()
         return a.elapsed_time(b) / n
 
-    widths = [args.width] if args.width else [1, 2, 4]
+    widths = [args.width] if args.width else [1, 2, 4, 8]
     best = None
     for wd in widths:
         L_w, r_w, sw = find_L(wd)
@@ -387,7 +387,7 @@ def main():
     ap.add_argument("--sel", type=float, default=0.10)
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
-    ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4
+    ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4, 8
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--qnum", type=int, default=10_000)
     ap.add_argument("--R", type=int, default=32)

@@ -57,7 +57,8 @@ class _IndexFiles(C.Structure):
         ("data_path", C.c_char_p), ("cagra_prefix", C.c_char_p), ("cagra_suffix", C.c_char_p),
         ("global_graph", C.c_char_p), ("grid", C.c_char_p), ("attrs", C.c_char_p),
         ("cluster", C.c_char_p), ("degree", C.c_uint32), ("f2h_factor", C.c_float),
-        ("keep_fp32", C.c_uint32),
+        ("keep_fp32", C.c_uint32), ("uniform_dims", C.c_uint32), ("uniform_shape", C.c_void_p),
+        ("uniform_lo", C.c_float), ("uniform_hi", C.c_float),
     ]
 
 
@@ -217,15 +218,23 @@ class Index:
         return cls(h)
 
     @classmethod
-    def open(cls, *, data_path, cagra_prefix, cagra_suffix, global_graph, grid, attrs, cluster=None,
-             degree=32, f2h_factor=1.0, keep_fp32=False, device=0) -> "Index":
-        """Load the reference's index files (realdataset_search flags)."""
+    def open(cls, *, data_path, cagra_prefix, cagra_suffix, global_graph, grid=None, attrs, cluster=None,
+             degree=32, f2h_factor=1.0, keep_fp32=False, device=0, uniform_shape=None, uniform_lo=0.0,
+             uniform_hi=1e6) -> "Index":
+        """Load the reference's index files (realdataset_search flags).  Without a grid file,
+        `uniform_shape` gives the uniform grid of normaldataset_search."""
         f = _IndexFiles()
         f.data_path, f.cagra_prefix, f.cagra_suffix = (str(data_path).encode(), str(cagra_prefix).encode(),
                                                        str(cagra_suffix).encode())
-        f.global_graph, f.grid, f.attrs = str(global_graph).encode(), str(grid).encode(), str(attrs).encode()
+        f.global_graph, f.attrs = str(global_graph).encode(), str(attrs).encode()
+        f.grid = None if grid is None else str(grid).encode()
         f.cluster = None if cluster is None else str(cluster).encode()
         f.degree, f.f2h_factor, f.keep_fp32 = degree, f2h_factor, 1 if keep_fp32 else 0
+        shape = None
+        if uniform_shape is not None:
+            shape = np.ascontiguousarray(uniform_shape, dtype=np.uint32)
+            f.uniform_dims, f.uniform_shape = len(shape), _np_ptr(shape)
+            f.uniform_lo, f.uniform_hi = uniform_lo, uniform_hi
         h = C.c_void_p()
         _check(lib().gf_index_open(C.byref(f), device, C.byref(h)), "gf_index_open")
         return cls(h)

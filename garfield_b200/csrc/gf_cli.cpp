@@ -7,6 +7,10 @@
 // qps = qnum / (cost1 + cost2 + cost3) as in realdataset_search.cu:2506-2508.
 // Extra flags: --ef "10,20,..." (default: the reference's 33-value sweep), --k,
 // --width, --device, --max_iter.
+// Invoked as normaldataset_search (normaldataset_search.cu:1748-2104) the grid is
+// uniform instead of read from --grid: --shape "16" (slices per attribute, the
+// reference's compiled-in default) over [--domain_lo, --domain_hi) = [0, 1e6), and the
+// graph degree defaults to 16 (the reference fixes it there).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -14,6 +18,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <strings.h>
 #include <vector>
 
 #include "garfield.h"
@@ -44,6 +49,11 @@ int main(int argc, char** argv) {
     float prefilter = 0.0f, f2h = 1.0f;
     uint32_t postfilter = 0xFFFFFFFFu, degree = 32, k = 10, width = 1, max_iter = 10000;
     int device = 0;
+    std::string prog = argv[0];
+    const bool normal = prog.size() >= 20 && prog.compare(prog.size() - 20, 20, "normaldataset_search") == 0;
+    std::vector<uint32_t> shape = {16};
+    float domain_lo = 0.0f, domain_hi = 1000000.0f;
+    if (normal) degree = 16;
     // realdataset_search.cu:2757-2760, ascending
     std::vector<uint32_t> ef = {10,  10,  15,  20,  25,  30,  35,  40,  45,  50,   55,   60,   70,   80,   90,   100, 120,
                                 140, 160, 180, 200, 250, 300, 400, 500, 600, 700, 800, 900, 1000, 1100, 1400, 1700};
@@ -69,11 +79,14 @@ int main(int argc, char** argv) {
         else if (a == "--width") width = (uint32_t)std::stoul(v);
         else if (a == "--max_iter") max_iter = (uint32_t)std::stoul(v);
         else if (a == "--device") device = std::stoi(v);
+        else if (a == "--shape") shape = parse_list(v);
+        else if (a == "--domain_lo") domain_lo = std::stof(v);
+        else if (a == "--domain_hi") domain_hi = std::stof(v);
         else continue;
         ++i;
     }
     if (data.empty() || query.empty() || range.empty() || gt.empty() || cprefix.empty() || global.empty() ||
-        grid.empty() || attrs.empty()) {
+        (grid.empty() && !normal) || attrs.empty()) {
         fprintf(stderr,
                 "usage: %s --data_path F --query_path F --range F --gt F --cagra_prefix P --cagra_suffix S "
                 "--global_graph F --grid F --attrs F [--cluster F] [--result F] [--prefilter x] [--postfilter n] "
@@ -87,7 +100,11 @@ int main(int argc, char** argv) {
     fs.cagra_prefix = cprefix.c_str();
     fs.cagra_suffix = csuffix.c_str();
     fs.global_graph = global.c_str();
-    fs.grid = grid.c_str();
+    fs.grid = (normal && grid.empty()) ? nullptr : grid.c_str();
+    fs.uniform_dims = (uint32_t)shape.size();
+    fs.uniform_shape = shape.data();
+    fs.uniform_lo = domain_lo;
+    fs.uniform_hi = domain_hi;
     fs.attrs = attrs.c_str();
     fs.cluster = cluster.empty() ? nullptr : cluster.c_str();
     fs.degree = degree;

@@ -2,6 +2,8 @@
 // Every reader checks the file size against its header and returns GF_ERR_IO /
 // GF_ERR_FORMAT instead of exiting (the reference prints and calls exit(-1),
 // tools.cuh:66,207).
+#include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -292,18 +294,52 @@ gf_status gf_index_open(const gf_index_files* fs, int device, gf_index** out) {
     uint32_t n = 0, dim = 0;
     TRY(gf_read_fvecs(fs->data_path, &vec, &n, &dim));
     hold.keep(vec);
-    uint32_t gn, ga, *grid, *cell_of;
-    int32_t *lq, *rq;
-    TRY(gf_read_grid(fs->grid, &gn, &ga, &grid, &lq, &rq, &cell_of));
-    hold.keep(grid);
-    hold.keep(lq);
-    hold.keep(rq);
-    hold.keep(cell_of);
-    if (gn != n) return fail(GF_ERR_FORMAT, "grid point count differs from the data file");
     int32_t* attrs_i;
     uint32_t an, aa;
     TRY(gf_read_attrs(fs->attrs, &attrs_i, &an, &aa));
     hold.keep(attrs_i);
+    uint32_t gn, ga, *grid, *cell_of;
+    int32_t *lq, *rq;
+    std::vector<uint32_t> ugrid, ucell;
+    std::vector<int32_t> ulq, urq;
+    if (fs->grid && fs->grid[0]) {
+        TRY(gf_read_grid(fs->grid, &gn, &ga, &grid, &lq, &rq, &cell_of));
+        hold.keep(grid);
+        hold.keep(lq);
+        hold.keep(rq);
+        hold.keep(cell_of);
+    } else {
+        // uniform grid: slices of equal width over [lo, hi), cells by attribute value
+        if (!fs->uniform_shape || fs->uniform_dims != aa || !(fs->uniform_hi > fs->uniform_lo))
+            return fail(GF_ERR_ARG, "no grid file and no uniform grid matching the attribute count");
+        gn = an;
+        ga = aa;
+        ugrid.assign(fs->uniform_shape, fs->uniform_shape + ga);
+        for (uint32_t j = 0; j < ga; ++j) {
+            if (ugrid[j] == 0) return fail(GF_ERR_ARG, "zero uniform grid size");
+            const double w = ((double)fs->uniform_hi - fs->uniform_lo) / ugrid[j];
+            for (uint32_t sl = 0; sl < ugrid[j]; ++sl) {
+                ulq.push_back((int32_t)std::ceil(fs->uniform_lo + sl * w));
+                urq.push_back((int32_t)std::ceil(fs->uniform_lo + (sl + 1) * w) - 1);
+            }
+        }
+        ucell.resize(an);
+        for (uint32_t i = 0; i < an; ++i) {
+            uint32_t cell = 0;
+            for (uint32_t j = 0; j < ga; ++j) {
+                const double w = ((double)fs->uniform_hi - fs->uniform_lo) / ugrid[j];
+                double sl = std::floor((attrs_i[(size_t)i * aa + j] - (double)fs->uniform_lo) / w);
+                sl = std::min(std::max(sl, 0.0), (double)(ugrid[j] - 1));
+                cell = cell * ugrid[j] + (uint32_t)sl;
+            }
+            ucell[i] = cell;
+        }
+        grid = ugrid.data();
+        lq = ulq.data();
+        rq = urq.data();
+        cell_of = ucell.data();
+    }
+    if (gn != n) return fail(GF_ERR_FORMAT, "grid point count differs from the data file");
     if (an != n || aa != ga) return fail(GF_ERR_FORMAT, "attrs shape differs from data/grid");
     uint32_t ncells = 1, nq = 0;
     for (uint32_t j = 0; j < ga; ++j) {

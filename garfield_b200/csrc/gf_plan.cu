@@ -167,15 +167,25 @@ __global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restr
             for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
         for (uint32_t d0 = 0; d0 < dim; d0 += kTD) {
             __syncthreads();
-            for (uint32_t e = t; e < kTQ * kTD; e += blockDim.x) {
-                uint32_t r = e / kTD, dd = e % kTD;
-                uint32_t q = q0 + r, d = d0 + dd;
-                qt[dd][r] = (q < qnum && d < dim) ? queries[(size_t)q * dim + d] : 0.0f;
+            // lanes of a warp take consecutive rows at the same 4 dimensions, so the
+            // transposed shared-memory stores hit 32 different banks
+            for (uint32_t e = t; e < kTQ * (kTD / 4); e += blockDim.x) {
+                const uint32_t r = e % kTQ, dd = (e / kTQ) * 4;
+                const uint32_t q = q0 + r;
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i) {
+                    const uint32_t d = d0 + dd + i;
+                    qt[dd + i][r] = (q < qnum && d < dim) ? queries[(size_t)q * dim + d] : 0.0f;
+                }
             }
-            for (uint32_t e = t; e < kTC * kTD; e += blockDim.x) {
-                uint32_t r = e / kTD, dd = e % kTD;
-                uint32_t c = c0 + r, d = d0 + dd;
-                ct[dd][r] = (c < cend && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
+            for (uint32_t e = t; e < kTC * (kTD / 4); e += blockDim.x) {
+                const uint32_t r = e % kTC, dd = (e / kTC) * 4;
+                const uint32_t c = c0 + r;
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i) {
+                    const uint32_t d = d0 + dd + i;
+                    ct[dd + i][r] = (c < cend && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
+                }
             }
             __syncthreads();
             const uint32_t dn = min(kTD, dim - d0);

@@ -101,13 +101,15 @@ struct W {
 
 __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 1u << (32 - __clz(x - 1)); }
 
-// Distances + range flags of the positions P[0..nb), written as sorted keys to B[0..)
-// (padded with empty keys to a power of two >= 32).  Rows are staged through shared
-// memory with cp.async, stage_rows at a time, chunk c of staged row r at stage_slot(c, r);
-// each lane computes the distance of one staged row.  Batches of at most 32 are sorted
-// in registers, larger ones in shared memory.
+// Distances + range flags of the positions P[0..nb); the keys below `thr` (the list's
+// worst entry, or kEmptyKey for no bound) are written sorted to B[0..ns), padded with
+// empty keys to a power of two >= 32; returns ns.  A key at or above the list's worst
+// entry cannot enter the list, so dropping it before the sort leaves every merge result
+// unchanged.  Rows are staged through shared memory with cp.async, stage_rows at a time,
+// chunk c of staged row r at stage_slot(c, r); each lane computes the distance of one
+// staged row.  At most 32 survivors are sorted in registers, more in shared memory.
 template <int NCH>
-__device__ __forceinline__ void eval_sort(const SArgs& A, const W& w, uint32_t nb) {
+__device__ __forceinline__ uint32_t eval_sort(const SArgs& A, const W& w, uint32_t nb, key_t thr) {
     const uint32_t lane = lane_id();
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
     const uint32_t nch16 = (nch + 15u) & ~15u;
@@ -116,7 +118,7 @@ __device__ __forceinline__ void eval_sort(const SArgs& A, const W& w, uint32_t n
     uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
     const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
     const uint32_t SR = A.stage_rows;
-    key_t kreg = kEmptyKey;
+    uint32_t ns = 0;
     for (uint32_t r0 = 0; r0 < nb; r0 += SR) {
         const uint32_t rows = min(SR, nb - r0);
         const uint32_t total = rows * nch;
@@ -133,25 +135,31 @@ __device__ __forceinline__ void eval_sort(const SArgs& A, const W& w, uint32_t n
         }
         cp_async_wait_all();
         __syncwarp();
+        key_t k = kEmptyKey;
         if (lane < rows) {
             const float d = dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
-            const key_t k = make_key(d, pos, inr ? kKeyInRange : 0u);
-            if (nb <= 32)
-                kreg = k;
-            else
-                B[r0 + lane] = k;
+            k = make_key(d, pos, inr ? kKeyInRange : 0u);
         }
+        const bool keep = k < thr;
+        const uint32_t msk = __ballot_sync(kFull, keep);
+        if (keep) B[ns + __popc(msk & lanemask_lt())] = k;
+        ns += __popc(msk);
         __syncwarp();
     }
-    if (nb <= 32) {
-        B[lane] = warp_sort32_key(kreg);
-        __syncwarp();
-        return;
+    if (ns <= 32) {
+        if (ns) {
+            const key_t k = lane < ns ? B[lane] : kEmptyKey;
+            __syncwarp();
+            B[lane] = warp_sort32_key(k);
+            __syncwarp();
+        }
+        return ns;
     }
-    const uint32_t n = next_pow2(nb);
-    for (uint32_t j = nb + lane; j < n; j += 32) B[j] = kEmptyKey;
+    const uint32_t n = next_pow2(ns);
+    for (uint32_t j = ns + lane; j < n; j += 32) B[j] = kEmptyKey;
     __syncwarp();
     warp_sort_keys(B, n);
+    return ns;
 }
 
 // Merge B[b0..b0+nb) into T (length L); with recycling, in-range entries pushed out of
@@ -228,9 +236,9 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
             const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
-                eval_sort<NCH>(A, w, nb);
+                const uint32_t ns = eval_sort<NCH>(A, w, nb, w.T(A)[A.K - 1]);
                 ndist += nb;
-                merge_step(A, w, A.K, 0, nb, false);
+                merge_step(A, w, A.K, 0, ns, false);
                 nb = 0;
             }
         }
@@ -289,7 +297,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         nf -= take;
     }
     __syncwarp();
-    eval_sort<NCH>(A, w, nb);
+    eval_sort<NCH>(A, w, nb, kEmptyKey);
     st_dist += nb;
     const uint32_t ne = min(nb, A.n_entry);
     const uint32_t nm = min(nb - ne, kHopSlots);
@@ -387,7 +395,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_sort<NCH>(A, w, nb);
+                    eval_sort<NCH>(A, w, nb, kEmptyKey);
                     st_dist += nb;
                 }
                 for (uint32_t ci = 0; ci < nc; ++ci) {
@@ -439,9 +447,9 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                         }
                         hcount += nb;
                         if (nb == 0) continue;
-                        eval_sort<NCH>(A, w, nb);
+                        const uint32_t ns = eval_sort<NCH>(A, w, nb, w.T(A)[A.L - 1]);
                         st_dist += nb;
-                        merge_step(A, w, A.L, 0, nb, true);
+                        merge_step(A, w, A.L, 0, ns, true);
                     }
                     // (c) everything in T counts as explored from here on
                     {

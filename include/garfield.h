@@ -81,6 +81,13 @@ typedef struct {
     uint32_t degree;          /* --degree */
     float f2h_factor;         /* --f2h_factor */
     uint32_t keep_fp32;
+    /* Uniform grid (normaldataset_search, normaldataset_search.cu:1748-2104), used when
+     * grid is NULL: attribute j is cut into uniform_shape[j] equal slices of
+     * [uniform_lo, uniform_hi) (the reference compiles shape {16} and [0, 1e6) in);
+     * slice s holds integer values lo + s*w .. lo + (s+1)*w - 1, w = (hi - lo) / shape. */
+    uint32_t uniform_dims;
+    const uint32_t* uniform_shape;
+    float uniform_lo, uniform_hi;
 } gf_index_files;
 
 /* Search knobs.  The defaults (gf_search_defaults) are the reference's values. */
