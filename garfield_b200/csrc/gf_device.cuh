@@ -52,16 +52,17 @@ __device__ __forceinline__ f2x h2_to_f2x(uint32_t h) {
     return pack2(f.x, f.y);
 }
 
-// End of the canonical sum: s[u] = even + odd partial, then the pairwise tree 8/4/2/1.
-__device__ __forceinline__ float finish32(const f2x* p) {
-    float s[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) s[u] = __fadd_rn(lo2(p[u]), hi2(p[u]));
-#pragma unroll
-    for (int st = 8; st >= 1; st >>= 1)
-#pragma unroll
-        for (int i = 0; i < st; ++i) s[i] = __fadd_rn(s[i], s[i + st]);
-    return s[0];
+__device__ __forceinline__ f2x add2(f2x a, f2x b) {
+    f2x r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// End of the canonical sum over the eight partials p[0..7], held as the packed pairs
+// acc[j] = (p[2j], p[2j+1]): s[j] = p[j] + p[j+4], t[j] = s[j] + s[j+2], t[0] + t[1].
+__device__ __forceinline__ float finish8(f2x a0, f2x a1, f2x a2, f2x a3) {
+    const f2x t = add2(add2(a0, a2), add2(a1, a3));
+    return __fadd_rn(lo2(t), hi2(t));
 }
 
 // Slot of chunk c of staged row r: chunks are XOR-swizzled within groups of 16 so that
@@ -70,59 +71,50 @@ __device__ __forceinline__ uint32_t stage_slot(uint32_t c, uint32_t r) { return 
 
 // Canonical fp16 squared distance (oracle orc_dist16) of a row staged in shared memory
 // (nch chunks of 8 halves, swizzled by stage_slot with key r) against the query held as
-// fp32 pairs q2[c*4 .. c*4+3] = (q0,q1),(q2,q3),(q4,q5),(q6,q7) of chunk c.  Thirty-two
-// partials: packed register p[u] holds the even/odd-element partials of chunk lane u.
+// fp32 pairs q2[c*4 .. c*4+3] = (q0,q1),(q2,q3),(q4,q5),(q6,q7) of chunk c.  Element i
+// of the row feeds partial i mod 8, so packed accumulator j takes pair j of every chunk
+// and the chunk loop stays rolled (four chunks per trip): a small loop body keeps the
+// search kernel's instruction footprint inside the instruction cache.
 template <int NCH>
 __device__ __forceinline__ float dist16_staged(const uint4* srow, const f2x* q2, uint32_t nch_rt, uint32_t r) {
     const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
-    f2x p[16];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) p[u] = 0ull;
-    for (uint32_t c0 = 0; c0 < nch; c0 += 16) {
-#pragma unroll
-        for (int u = 0; u < 16; ++u) {
-            const uint32_t c = c0 + u;
-            if (NCH == 0 || (NCH % 16) == 0 || c < nch) {
-                if (c < nch) {
-                    const uint4 x = srow[stage_slot(c, r)];
-                    const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q2 + c * 4);
-                    const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q2 + c * 4 + 2);
-                    f2x acc = p[u];
-                    acc = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), acc);
-                    acc = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), acc);
-                    acc = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), acc);
-                    acc = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), acc);
-                    p[u] = acc;
-                }
-            }
-        }
+    const uint32_t key = r & 15u;
+    f2x p0 = 0ull, p1 = 0ull, p2 = 0ull, p3 = 0ull;
+#pragma unroll 4
+    for (uint32_t c = 0; c < nch; ++c) {
+        const uint4 x = srow[c ^ key];  // == stage_slot(c, r)
+        const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q2 + c * 4);
+        const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q2 + c * 4 + 2);
+        p0 = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), p0);
+        p1 = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), p1);
+        p2 = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), p2);
+        p3 = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), p3);
     }
-    return finish32(p);
+    return finish8(p0, p1, p2, p3);
 }
 
 // Canonical fp32 squared distance (oracle orc_dist32) of a global row of nch float4
-// chunks against a query row in shared memory.
+// chunks against a query row in shared memory: chunk c covers elements 4c..4c+3, which
+// feed the partial pairs 2(c mod 2) and 2(c mod 2)+1.  Eight chunks are loaded before
+// they are accumulated, to keep several loads in flight.
 __device__ __forceinline__ float dist32(const float4* __restrict__ row, const float4* __restrict__ q, uint32_t nch) {
-    f2x p[16];
+    f2x p[4] = {0ull, 0ull, 0ull, 0ull};
+    for (uint32_t c0 = 0; c0 < nch; c0 += 8) {
+        float4 x[8];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) p[u] = 0ull;
-    for (uint32_t c0 = 0; c0 < nch; c0 += 16) {
-        float4 x[16];
-#pragma unroll
-        for (int u = 0; u < 16; ++u)
+        for (int u = 0; u < 8; ++u)
             if (c0 + u < nch) x[u] = __ldg(row + c0 + u);
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < 8; ++u) {
             if (c0 + u < nch) {
                 const float4 qv = q[c0 + u];
-                f2x acc = p[u];
-                acc = sqacc2(sub2(pack2(qv.x, qv.y), pack2(x[u].x, x[u].y)), acc);
-                acc = sqacc2(sub2(pack2(qv.z, qv.w), pack2(x[u].z, x[u].w)), acc);
-                p[u] = acc;
+                const int j = (u & 1) * 2;
+                p[j] = sqacc2(sub2(pack2(qv.x, qv.y), pack2(x[u].x, x[u].y)), p[j]);
+                p[j + 1] = sqacc2(sub2(pack2(qv.z, qv.w), pack2(x[u].z, x[u].w)), p[j + 1]);
             }
         }
     }
-    return finish32(p);
+    return finish8(p[0], p[1], p[2], p[3]);
 }
 
 // 16-byte asynchronous global -> shared copy (cp.async, L2 only) and its fences.

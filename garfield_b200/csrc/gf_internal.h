@@ -81,8 +81,10 @@ struct Plan {
     unsigned long long* stats = nullptr;  // 8 counters
     void* scan_tmp = nullptr;
     size_t scan_tmp_bytes = 0;
-    // host staging for gf_search_host
-    float* h_stage = nullptr;
+    // device copies of gf_search_host's inputs and outputs; grown on demand, kept
+    // between calls so that steady-state calls allocate nothing
+    void* io = nullptr;
+    size_t io_bytes = 0;
 };
 
 }  // namespace gf

@@ -423,7 +423,7 @@ void free_plan(Plan& p) {
                     p.stats, p.scan_tmp, p.part_d, p.part_i};
     for (void* x : ptrs)
         if (x) cudaFree(x);
-    if (p.h_stage) cudaFreeHost(p.h_stage);
+    if (p.io) cudaFree(p.io);
 }
 }  // namespace
 
@@ -555,20 +555,24 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
     gf_search_params P;
     gf_search_defaults(&P);
     if (params) P = *params;
-    // device staging: the plan's own buffers are the copy targets; outputs go to the
-    // tail of the cells buffer is not safe, so use dedicated scratch carved from q32 of
-    // the next queries is not possible either: allocate once, lazily.
-    static_assert(sizeof(float) == 4, "");
-    float *dq = nullptr, *dl = nullptr, *dr = nullptr;
-    uint32_t* dids = nullptr;
-    float* ddist = nullptr;
-    size_t need = (size_t)qnum * (d.dim + 2 * d.a + 2 * P.k);
-    cudaError_t e = cudaMallocAsync((void**)&dq, std::max<size_t>(need, 1) * 4, s);
-    if (e != cudaSuccess) return cuda_fail(e, "staging buffer");
-    dl = dq + (size_t)qnum * d.dim;
-    dr = dl + (size_t)qnum * d.a;
-    dids = reinterpret_cast<uint32_t*>(dr + (size_t)qnum * d.a);
-    ddist = reinterpret_cast<float*>(dids + (size_t)qnum * P.k);
+    // device copies of the host arrays, in one buffer owned by the plan
+    const size_t need = std::max<size_t>((size_t)qnum * (d.dim + 2 * d.a + 2 * P.k), 1) * 4;
+    cudaError_t e = cudaSuccess;
+    if (need > p.io_bytes) {
+        if (p.io) {
+            if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "gf_search_host");
+            cudaFree(p.io);
+            p.io = nullptr;
+            p.io_bytes = 0;
+        }
+        if ((e = cudaMalloc(&p.io, need)) != cudaSuccess) return cuda_fail(e, "gf_search_host staging buffer");
+        p.io_bytes = need;
+    }
+    float* dq = static_cast<float*>(p.io);
+    float* dl = dq + (size_t)qnum * d.dim;
+    float* dr = dl + (size_t)qnum * d.a;
+    uint32_t* dids = reinterpret_cast<uint32_t*>(dr + (size_t)qnum * d.a);
+    float* ddist = reinterpret_cast<float*>(dids + (size_t)qnum * P.k);
     gf_status st = GF_OK;
     do {
         if ((e = cudaMemcpyAsync(dq, queries_host, 4ull * qnum * d.dim, cudaMemcpyHostToDevice, s)) != cudaSuccess) break;
@@ -584,7 +588,6 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
             break;
         e = cudaStreamSynchronize(s);
     } while (0);
-    cudaFreeAsync(dq, s);
     if (st != GF_OK) return st;
     if (e != cudaSuccess) return cuda_fail(e, "gf_search_host");
     return GF_OK;

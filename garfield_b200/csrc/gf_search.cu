@@ -108,8 +108,11 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 // unchanged.  Rows are staged through shared memory with cp.async, stage_rows at a time,
 // chunk c of staged row r at stage_slot(c, r); each lane computes the distance of one
 // staged row.  At most 32 survivors are sorted in registers, more in shared memory.
+// Kept out of line: one copy of the distance loop and sort network serves the entry
+// set, the beam rounds, the hop and the exact route.
 template <int NCH>
-__device__ __forceinline__ uint32_t eval_sort(const SArgs& A, const W& w, uint32_t nb, key_t thr) {
+__device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr) {
+    const W w{base, 0u, 0u};
     const uint32_t lane = lane_id();
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
     const uint32_t nch16 = (nch + 15u) & ~15u;
@@ -236,7 +239,7 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
             const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
-                const uint32_t ns = eval_sort<NCH>(A, w, nb, w.T(A)[A.K - 1]);
+                const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.K - 1]);
                 ndist += nb;
                 merge_step(A, w, A.K, 0, ns, false);
                 nb = 0;
@@ -297,7 +300,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         nf -= take;
     }
     __syncwarp();
-    eval_sort<NCH>(A, w, nb, kEmptyKey);
+    eval_sort<NCH>(A, w.base, nb, kEmptyKey);
     st_dist += nb;
     const uint32_t ne = min(nb, A.n_entry);
     const uint32_t nm = min(nb - ne, kHopSlots);
@@ -395,7 +398,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_sort<NCH>(A, w, nb, kEmptyKey);
+                    eval_sort<NCH>(A, w.base, nb, kEmptyKey);
                     st_dist += nb;
                 }
                 for (uint32_t ci = 0; ci < nc; ++ci) {
@@ -447,7 +450,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                         }
                         hcount += nb;
                         if (nb == 0) continue;
-                        const uint32_t ns = eval_sort<NCH>(A, w, nb, w.T(A)[A.L - 1]);
+                        const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.L - 1]);
                         st_dist += nb;
                         merge_step(A, w, A.L, 0, ns, true);
                     }

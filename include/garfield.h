@@ -180,7 +180,9 @@ gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out);
 /*
  * End-to-end call from host memory: copies queries and bounds to the device, plans,
  * searches and copies ids (and distances, if dist_host != NULL) back.  Synchronises.
- * The host buffers may be pinned (faster) or pageable.
+ * The host buffers may be pinned (faster) or pageable.  The device copies live in a
+ * buffer owned by the plan, allocated by the first call and grown when a call needs more
+ * (qnum x (dim + 2a + 2k) floats); later calls of that size or smaller allocate nothing.
  */
 gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* params, const float* queries_host,
                          const float* lb_host, const float* rb_host, uint32_t qnum, float prefilter,

@@ -25,14 +25,12 @@
  *   orc_recall         tools.cuh:456-544               cal_recall_show_partition_multi_attrs
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
- *   - orc_dist16 / orc_dist32: squared L2 of two rows split into 16-byte chunks
- *     (8 fp16 or 4 fp32 elements).  Thirty-two partial sums p[u][h]: chunk c feeds
- *     u = c mod 16, its even-indexed elements feed h = 0 and its odd-indexed elements
- *     h = 1, in increasing order of chunk and element, each with one fused multiply-add
- *     acc = fma(q-x, q-x, acc) (q-x rounded to fp32 first).  Then s[u] = p[u][0] + p[u][1]
- *     and the sixteen s[u] are added pairwise: s[i] += s[i+8] (i<8), s[i] += s[i+4]
- *     (i<4), s[i] += s[i+2] (i<2), s[0] += s[1].  (The element-parity split is what
- *     packed two-wide fp32 instructions compute.)
+ *   - orc_dist16 / orc_dist32: squared L2 of two rows of padded length (a multiple of 8).
+ *     Eight partial sums: element i feeds p[i mod 8], in increasing order of i, with one
+ *     fused multiply-add p = fma(q-x, q-x, p) (q-x rounded to fp32 first).  Then
+ *     s[j] = p[j] + p[j+4] (j<4), t[j] = s[j] + s[j+2] (j<2), result = t[0] + t[1].
+ *     (Adjacent partials are the two halves of one packed two-wide fp32 register on the
+ *     GPU, so every step is one packed instruction and the chunk loop needs no unrolling.)
  *   - orc_dist_seq: squared L2 with one fma chain over d = 0..D-1 (used for the
  *     query-centroid distances of the cell ordering).
  * The reference accumulates candidate distances in fp16 (gpu_graph.cu:3394-3403) and
@@ -93,40 +91,31 @@ void orc_f2h(const float* in, uint32_t n, uint32_t dim, uint32_t d_pad, float al
 
 /* ----------------------------------------------------- canonical distances */
 
-static inline float tree16(float* p) {
-    for (int s = 8; s >= 1; s >>= 1)
-        for (int i = 0; i < s; ++i) p[i] = p[i] + p[i + s];
-    return p[0];
-}
-
-static inline float finish32(float p[16][2]) {
-    float s[16];
-    for (int u = 0; u < 16; ++u) s[u] = p[u][0] + p[u][1];
-    return tree16(s);
+static inline float finish8(const float p[8]) {
+    float s[4], t[2];
+    for (int j = 0; j < 4; ++j) s[j] = p[j] + p[j + 4];
+    for (int j = 0; j < 2; ++j) t[j] = s[j] + s[j + 2];
+    return t[0] + t[1];
 }
 
 /* fp16 rows of d8 elements (d8 % 8 == 0). */
 float orc_dist16(const uint16_t* q, const uint16_t* x, uint32_t d8) {
-    float p[16][2] = {{0}};
-    uint32_t nch = d8 / 8;
-    for (uint32_t c = 0; c < nch; ++c)
-        for (uint32_t e = 0; e < 8; ++e) {
-            float diff = f16_bits_to_f32(q[c * 8 + e]) - f16_bits_to_f32(x[c * 8 + e]);
-            p[c & 15][e & 1] = fmaf(diff, diff, p[c & 15][e & 1]);
-        }
-    return finish32(p);
+    float p[8] = {0};
+    for (uint32_t i = 0; i < d8; ++i) {
+        float diff = f16_bits_to_f32(q[i]) - f16_bits_to_f32(x[i]);
+        p[i & 7] = fmaf(diff, diff, p[i & 7]);
+    }
+    return finish8(p);
 }
 
 /* fp32 rows of d4 elements (d4 % 4 == 0). */
 float orc_dist32(const float* q, const float* x, uint32_t d4) {
-    float p[16][2] = {{0}};
-    uint32_t nch = d4 / 4;
-    for (uint32_t c = 0; c < nch; ++c)
-        for (uint32_t e = 0; e < 4; ++e) {
-            float diff = q[c * 4 + e] - x[c * 4 + e];
-            p[c & 15][e & 1] = fmaf(diff, diff, p[c & 15][e & 1]);
-        }
-    return finish32(p);
+    float p[8] = {0};
+    for (uint32_t i = 0; i < d4; ++i) {
+        float diff = q[i] - x[i];
+        p[i & 7] = fmaf(diff, diff, p[i & 7]);
+    }
+    return finish8(p);
 }
 
 float orc_dist_seq(const float* q, const float* x, uint32_t dim) {
