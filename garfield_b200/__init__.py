@@ -48,7 +48,7 @@ class _IndexDesc(C.Structure):
         ("l_quant", C.c_void_p), ("r_quant", C.c_void_p), ("cell_of", C.c_void_p),
         ("degree", C.c_uint32), ("graphs", C.c_void_p), ("cross_e", C.c_uint32),
         ("cross", C.c_void_p), ("n_clusters", C.c_uint32), ("labels", C.c_void_p),
-        ("f2h_factor", C.c_float), ("keep_fp32", C.c_uint32),
+        ("f2h_factor", C.c_float), ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32),
     ]
 
 
@@ -57,7 +57,8 @@ class _IndexFiles(C.Structure):
         ("data_path", C.c_char_p), ("cagra_prefix", C.c_char_p), ("cagra_suffix", C.c_char_p),
         ("global_graph", C.c_char_p), ("grid", C.c_char_p), ("attrs", C.c_char_p),
         ("cluster", C.c_char_p), ("degree", C.c_uint32), ("f2h_factor", C.c_float),
-        ("keep_fp32", C.c_uint32), ("uniform_dims", C.c_uint32), ("uniform_shape", C.c_void_p),
+        ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32), ("uniform_dims", C.c_uint32),
+        ("uniform_shape", C.c_void_p),
         ("uniform_lo", C.c_float), ("uniform_hi", C.c_float),
     ]
 
@@ -108,6 +109,7 @@ def lib() -> C.CDLL:
         "gf_search": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _P]),
         "gf_search_stats_read": (C.c_int, [_P, _PTR(_SearchStats)]),
         "gf_search_host": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _P, _U32, C.c_float, _P, _P, _P]),
+        "gf_search_batched": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _U32, _P, _P, _P]),
         "gf_bruteforce": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _P]),
         "gf_free": (None, [_P]),
         "gf_read_fvecs": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
@@ -193,8 +195,10 @@ class Index:
 
     @classmethod
     def create(cls, *, vectors, attrs, grid, l_quant, r_quant, cell_of, graphs, degree, cross=None,
-               cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, device=0) -> "Index":
-        """Build from host arrays in the reference's layout (see gf_index_desc)."""
+               cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, host_graph=False, device=0) -> "Index":
+        """Build from host arrays in the reference's layout (see gf_index_desc).  With
+        host_graph the graphs and cross edges stay in pinned host memory (search with
+        Plan.search_batched)."""
         vectors = np.ascontiguousarray(vectors, dtype=np.float32)
         attrs = np.ascontiguousarray(attrs, dtype=np.float32)
         grid = np.ascontiguousarray(grid, dtype=np.uint32)
@@ -213,6 +217,7 @@ class Index:
         d.cross_e, d.cross = (cross_e if cross is not None else 0), _np_ptr(cross)
         d.n_clusters, d.labels = (1 if labels is not None else 0), _np_ptr(labels)
         d.f2h_factor, d.keep_fp32 = f2h_factor, 1 if keep_fp32 else 0
+        d.host_graph = 1 if host_graph else 0
         h = C.c_void_p()
         _check(lib().gf_index_create(C.byref(d), device, C.byref(h)), "gf_index_create")
         return cls(h)
@@ -220,7 +225,7 @@ class Index:
     @classmethod
     def open(cls, *, data_path, cagra_prefix, cagra_suffix, global_graph, grid=None, attrs, cluster=None,
              degree=32, f2h_factor=1.0, keep_fp32=False, device=0, uniform_shape=None, uniform_lo=0.0,
-             uniform_hi=1e6) -> "Index":
+             uniform_hi=1e6, host_graph=False) -> "Index":
         """Load the reference's index files (realdataset_search flags).  Without a grid file,
         `uniform_shape` gives the uniform grid of normaldataset_search."""
         f = _IndexFiles()
@@ -230,6 +235,7 @@ class Index:
         f.grid = None if grid is None else str(grid).encode()
         f.cluster = None if cluster is None else str(cluster).encode()
         f.degree, f.f2h_factor, f.keep_fp32 = degree, f2h_factor, 1 if keep_fp32 else 0
+        f.host_graph = 1 if host_graph else 0
         shape = None
         if uniform_shape is not None:
             shape = np.ascontiguousarray(uniform_shape, dtype=np.uint32)
@@ -348,6 +354,24 @@ class Plan:
         cp = params._c()
         _check(lib().gf_search(self.index._h, self._h, C.byref(cp), _dev_ptr(ids), _dev_ptr(dist),
                                _stream_ptr(stream)), "gf_search")
+        return ids, dist
+
+    def search_batched(self, batches, params: SearchParams | None = None, stream=None, ids=None, dist=None):
+        """gf_search_batched: `batches` is a list of cell-id lists (each cell in at most one)."""
+        import torch
+        params = params or SearchParams()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if ids is None:
+            ids = torch.empty((self.qnum, params.k), dtype=torch.int32, device=dev)
+        if dist is None:
+            dist = torch.empty((self.qnum, params.k), dtype=torch.float32, device=dev)
+        sizes = np.array([len(b) for b in batches], np.uint32)
+        cells = np.ascontiguousarray(np.concatenate([np.asarray(b, np.uint32) for b in batches])
+                                     if len(batches) else np.zeros(0, np.uint32), dtype=np.uint32)
+        cp = params._c()
+        _check(lib().gf_search_batched(self.index._h, self._h, C.byref(cp), _np_ptr(cells), _np_ptr(sizes),
+                                       len(batches), _dev_ptr(ids), _dev_ptr(dist), _stream_ptr(stream)),
+               "gf_search_batched")
         return ids, dist
 
     def stats(self) -> dict:

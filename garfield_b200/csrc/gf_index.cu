@@ -77,6 +77,8 @@ static void free_index(DeviceIndex& d) {
                     d.lq_d,  d.rq_d,  d.centroids, d.hist, d.entry};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    if (d.graph_h) cudaFreeHost(d.graph_h);
+    if (d.cross_h) cudaFreeHost(d.cross_h);
 }
 
 // Deterministic entry local ids: std::mt19937 with its default seed (as the reference,
@@ -163,29 +165,54 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         }
     }
     d.entry_h = make_entry(std::max<uint32_t>(R, 64), d.min_cell);
+    d.host_graph = ds->host_graph != 0;
 
-    // graph rows are already in position order; local ids -> positions
-    std::vector<uint32_t> graph((size_t)n * R);
+    // Graph rows are already in position order; local ids -> positions.  Cross edges:
+    // source-major (position, target cell, edge) on the device; with host_graph,
+    // target-major (target cell, position, edge) in pinned host memory, so that the block
+    // of one (target, source cell) pair is contiguous for the per-batch copies
+    // (the transposed layout of big_dataset_adapterV3.cuh:3539-3542).
+    std::vector<uint32_t> graph, cross;
+    uint32_t* gdst = nullptr;
+    uint32_t* xdst = nullptr;
+    if (d.host_graph) {
+        DeviceGuard g0(device);
+        cudaError_t e = cudaMallocHost((void**)&d.graph_h, std::max<size_t>((size_t)n * R, 1) * 4);
+        if (e == cudaSuccess && E) e = cudaMallocHost((void**)&d.cross_h, std::max<size_t>((size_t)n * P * E, 1) * 4);
+        if (e != cudaSuccess) {
+            free_index(d);
+            delete ix;
+            return cuda_fail(e, "pinned host graph");
+        }
+        gdst = d.graph_h;
+        xdst = d.cross_h;
+    } else {
+        graph.resize((size_t)n * R);
+        gdst = graph.data();
+        if (E) {
+            cross.resize((size_t)n * P * E);
+            xdst = cross.data();
+        }
+    }
     for (uint32_t c = 0; c < P; ++c) {
         uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
         for (size_t r = base; r < (size_t)base + sz; ++r)
             for (uint32_t j = 0; j < R; ++j) {
                 uint32_t loc = ds->graphs[r * R + j];
-                graph[r * R + j] = loc < sz ? base + loc : kEmpty;
+                gdst[r * R + j] = loc < sz ? base + loc : kEmpty;
             }
     }
-    std::vector<uint32_t> cross;
     if (E) {
-        cross.resize((size_t)n * P * E);
         const size_t rowlen = (size_t)P * E;
         for (uint32_t g = 0; g < n; ++g) {
             const uint32_t* src = ds->cross + (size_t)g * rowlen;
-            uint32_t* dst = cross.data() + (size_t)pos_of[g] * rowlen;
+            const size_t pos = pos_of[g];
             for (uint32_t c = 0; c < P; ++c) {
                 uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
+                uint32_t* dst = d.host_graph ? xdst + ((size_t)c * n + pos) * E : xdst + pos * rowlen + (size_t)c * E;
                 for (uint32_t j = 0; j < E; ++j) {
                     uint32_t loc = src[c * E + j];
-                    dst[c * E + j] = loc < sz ? base + loc : kEmpty;
+                    dst[j] = loc < sz ? base + loc : kEmpty;
                 }
             }
         }
@@ -202,6 +229,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         int32_t mx = -1;
         for (uint32_t i = 0; i < n; ++i) {
             if (ds->labels[i] < 0) {
+                free_index(d);
                 delete ix;
                 return fail(GF_ERR_FORMAT, "negative cluster label");
             }
@@ -233,8 +261,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     do {
         if (!chk(dalloc(&d.vec16, (size_t)n * d.d8 / 8, &d.bytes))) break;
         if (!chk(dalloc(&d.attrs, (size_t)n * d.a, &d.bytes))) break;
-        if (!chk(dalloc(&d.graph, (size_t)n * R, &d.bytes))) break;
-        if (E && !chk(dalloc(&d.cross, (size_t)n * P * E, &d.bytes))) break;
+        if (!d.host_graph && !chk(dalloc(&d.graph, (size_t)n * R, &d.bytes))) break;
+        if (!d.host_graph && E && !chk(dalloc(&d.cross, (size_t)n * P * E, &d.bytes))) break;
         if (!chk(dalloc(&d.i2g, n, &d.bytes))) break;
         if (!chk(dalloc(&d.seg, P + 1, &d.bytes))) break;
         if (!chk(dalloc(&d.grid_d, d.a, &d.bytes))) break;

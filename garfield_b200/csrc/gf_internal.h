@@ -46,8 +46,13 @@ struct DeviceIndex {
     uint4* vec16 = nullptr;      // n x d8 halves (alpha-scaled), as 16-byte chunks
     float4* vec32 = nullptr;     // n x d4 fp32 (optional)
     float* attrs = nullptr;      // n x a
-    uint32_t* graph = nullptr;   // n x degree positions
-    uint32_t* cross = nullptr;   // n x (ncells*E) positions
+    uint32_t* graph = nullptr;   // n x degree positions (NULL when host_graph)
+    uint32_t* cross = nullptr;   // n x (ncells*E) positions (NULL when host_graph)
+    // host_graph: graphs and cross edges stay in pinned host memory and are copied to the
+    // device per batch of cells (gf_search_batched)
+    bool host_graph = false;
+    uint32_t* graph_h = nullptr; // pinned, n x degree positions (position order)
+    uint32_t* cross_h = nullptr; // pinned, ncells x n x E: [target cell][source position][edge]
     uint32_t* i2g = nullptr;     // position -> global id
     uint32_t* seg = nullptr;     // ncells + 1
     uint32_t* grid_d = nullptr;  // a
@@ -57,6 +62,9 @@ struct DeviceIndex {
     uint32_t* hist = nullptr;    // ncells x C
     uint32_t* entry = nullptr;   // entry_h on device
 };
+
+struct BatchState;  // gf_batch.cu: buffers, streams and events of gf_search_batched
+void free_batch_state(BatchState* b);
 
 struct Plan {
     gf_index* idx = nullptr;
@@ -85,6 +93,7 @@ struct Plan {
     // between calls so that steady-state calls allocate nothing
     void* io = nullptr;
     size_t io_bytes = 0;
+    BatchState* batch = nullptr;  // created by the first gf_search_batched
 };
 
 }  // namespace gf
@@ -104,8 +113,27 @@ uint32_t centroid_chunk(uint32_t C);   // centroids per range (multiple of 64)
 gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
                        uint32_t qnum, float prefilter, cudaStream_t s);
 // gf_search.cu
+// Restriction of one search launch to a set of cells ("slots"), whose graph rows and
+// cross-edge rows may lie anywhere in device memory (batched and out-of-core search).
+// Row of position pos (cell c, slot b = slot[c]): graph + gofs[b] + (pos - seg[c]) * R.
+// Cross edges of source pos (cell s) toward cell t: cross + xofs[slot[t] * nslots +
+// slot[s]] + (pos - seg[s]) * xstride.  Each query's results are merged into run[q]
+// (k keys, sorted) instead of being written as ids.
+struct CellView {
+    const int32_t* slot = nullptr;    // device, ncells; -1 = cell not searched
+    const long long* gofs = nullptr;  // device, nslots
+    const long long* xofs = nullptr;  // device, nslots x nslots
+    const uint32_t* graph = nullptr;
+    const uint32_t* cross = nullptr;
+    uint32_t nslots = 0, xstride = 0;
+    unsigned long long* run = nullptr;  // device, qnum x k
+    bool accumulate_stats = false;      // add to the plan's counters instead of resetting them
+};
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
-                 cudaStream_t s);
+                 cudaStream_t s, const CellView* view = nullptr);
+// run keys -> ids (via position -> global id) and distances
+gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t total, uint32_t* ids, float* dist,
+                     cudaStream_t s);
 // gf_bruteforce.cu
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
                      uint32_t k, uint32_t* ids, float* dist, cudaStream_t s);

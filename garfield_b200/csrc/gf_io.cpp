@@ -401,6 +401,7 @@ gf_status gf_index_open(const gf_index_files* fs, int device, gf_index** out) {
     d.labels = labels;
     d.f2h_factor = fs->f2h_factor;
     d.keep_fp32 = fs->keep_fp32;
+    d.host_graph = fs->host_graph;
     return gf_index_create(&d, device, out);
 }
 

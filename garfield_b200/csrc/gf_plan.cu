@@ -424,6 +424,8 @@ void free_plan(Plan& p) {
     for (void* x : ptrs)
         if (x) cudaFree(x);
     if (p.io) cudaFree(p.io);
+    free_batch_state(p.batch);
+    p.batch = nullptr;
 }
 }  // namespace
 

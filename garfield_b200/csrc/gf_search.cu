@@ -46,6 +46,12 @@ struct SArgs {
     uint32_t* out_ids;
     float* out_d;
     unsigned long long* stats;
+    // cell view (NULL slot: every cell, rows at graph + pos*R and cross + pos*P*E + t*E)
+    const int32_t* __restrict__ slot;
+    const long long* __restrict__ gofs;
+    const long long* __restrict__ xofs;
+    unsigned long long* run;
+    uint32_t nslots, xstride;
     uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, warp_words;
@@ -214,6 +220,55 @@ __device__ __forceinline__ void write_result(const SArgs& A, uint32_t q, const k
     }
 }
 
+// Result of query q: the sorted k-list `res` is written as ids, or, under a cell view,
+// merged into the query's running keys run[q] (ta, tb: k-key scratch lists).
+__device__ __noinline__ void emit(const SArgs& A, uint32_t q, const key_t* res, key_t* ta, key_t* tb) {
+    if (!A.run) {
+        write_result(A, q, res, A.K);
+        return;
+    }
+    const uint32_t lane = lane_id();
+    unsigned long long* rq = A.run + (size_t)q * A.K;
+    uint32_t nres = 0;
+    for (uint32_t i0 = 0; i0 < A.K; i0 += 32) {
+        const uint32_t i = i0 + lane;
+        nres += __popc(__ballot_sync(kFull, i < A.K && res[i] != kEmptyKey));
+    }
+    if (nres == 0) return;
+    for (uint32_t i = lane; i < A.K; i += 32) ta[i] = rq[i];
+    __syncwarp();
+    const uint32_t r = merge_keys(ta, tb, A.K, res, nres, nullptr, false);
+    if ((r >> 16) == 0) return;
+    for (uint32_t i = lane; i < A.K; i += 32) rq[i] = tb[i];
+}
+
+// Index in cl[0..nc) of the first cell at or after ci that this launch searches.
+__device__ __forceinline__ uint32_t next_cell(const SArgs& A, const uint32_t* cl, uint32_t nc, uint32_t ci) {
+    if (A.slot)
+        while (ci < nc && A.slot[cl[ci]] < 0) ++ci;
+    return ci;
+}
+
+// Element offset from A.graph of the row of position p in `cell` (seg start lo) is
+// gbase + p * R.
+__device__ __forceinline__ long long graph_base(const SArgs& A, uint32_t cell, uint32_t lo) {
+    return A.slot ? A.gofs[A.slot[cell]] - (long long)lo * A.R : 0ll;
+}
+
+// Element offset from A.cross of the cross edges of position src toward cell `next`.
+__device__ __forceinline__ long long cross_row(const SArgs& A, uint32_t src, uint32_t next) {
+    if (!A.slot) return (long long)src * A.P * A.E + (long long)next * A.E;
+    uint32_t lo = 0, hi = A.P;  // A.seg[lo] <= src < A.seg[hi]
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (A.seg[mid] <= src)
+            lo = mid;
+        else
+            hi = mid;
+    }
+    return A.xofs[(long long)A.slot[next] * A.nslots + A.slot[lo]] + (long long)(src - A.seg[lo]) * A.xstride;
+}
+
 // Append the positions held by lanes with ok=true to P at nb (warp-uniform counter).
 __device__ __forceinline__ void append(uint32_t* P, uint32_t& nb, bool ok, uint32_t pos) {
     uint32_t msk = __ballot_sync(kFull, ok);
@@ -231,12 +286,13 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
     __syncwarp();
     uint32_t nb = 0, ndist = 0;
     const uint32_t flush_at = A.bcap - 32;
-    for (uint32_t ci = 0; ci < nc; ++ci) {
+    for (uint32_t ci = next_cell(A, cl, nc, 0); ci < nc;) {
         const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
+        const uint32_t cn = next_cell(A, cl, nc, ci + 1);
         for (uint32_t x0 = lo; x0 < hi; x0 += 32) {
             const uint32_t x = x0 + lane;
             append(w.P(A), nb, x < hi && in_box(A.attrs, x, A.a, w.lb(A), w.rb(A)), x);
-            const bool last = (ci + 1 == nc) && (x0 + 32 >= hi);
+            const bool last = (cn == nc) && (x0 + 32 >= hi);
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
                 const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.K - 1]);
@@ -245,9 +301,10 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
                 nb = 0;
             }
         }
+        ci = cn;
     }
     __syncwarp();
-    write_result(A, q, w.T(A), A.K);
+    emit(A, q, w.T(A), w.RL(A), w.RLn(A));
     return ndist;
 }
 
@@ -271,7 +328,6 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
     uint32_t* H = w.H(A);
     hash_clear(H, A.hs);
     const uint32_t pairs = V * A.E;
-    const size_t rowlen = (size_t)A.P * A.E;
     uint32_t nb = 0;
     uint32_t* P = w.P(A);
     for (uint32_t j0 = 0; j0 < pairs; j0 += 32) {
@@ -279,8 +335,8 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         bool ok = false;
         uint32_t pos = kEmpty;
         if (j < pairs) {
-            uint32_t src = key_pos(T[j / A.E]);
-            pos = __ldg(A.cross + (size_t)src * rowlen + (size_t)next * A.E + (j % A.E));
+            const uint32_t src = key_pos(T[j / A.E]);
+            pos = __ldg(A.cross + cross_row(A, src, next) + (j % A.E));
             if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
         }
         append(P, nb, ok, pos);
@@ -362,8 +418,9 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
             __syncwarp();
         }
         uint32_t st_dist = 0, st_exp = 0, st_cross = 0, st_hops = 0, st_exact = 0;
-        if (nc == 0) {
-            write_result(A, q, nullptr, 0);
+        const uint32_t c0 = next_cell(A, cl, nc, 0);
+        if (c0 == nc) {
+            if (!A.run) write_result(A, q, nullptr, 0);
         } else {
             bool exact = nc >= A.postfilter;
             if (!exact && A.box) {
@@ -382,7 +439,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                 // entry set of the first cell (gpu_graph.cu:3347-3351)
                 uint32_t nb = 0;
                 {
-                    const uint32_t cell = cl[0], lo = A.seg[cell], sz = A.seg[cell + 1] - lo;
+                    const uint32_t cell = cl[c0], lo = A.seg[cell], sz = A.seg[cell + 1] - lo;
                     for (uint32_t i0 = 0; i0 < A.n_entry; i0 += 32) {
                         uint32_t i = i0 + lane;
                         bool ok = false;
@@ -401,8 +458,9 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     eval_sort<NCH>(A, w.base, nb, kEmptyKey);
                     st_dist += nb;
                 }
-                for (uint32_t ci = 0; ci < nc; ++ci) {
+                for (uint32_t ci = c0; ci < nc;) {
                     const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
+                    const long long gbase = graph_base(A, cell, lo);
                     // (a) entry set -> T, with recycling
                     merge_step(A, w, A.L, 0, nb, true);
                     // (b) beam rounds: expand the first W unexplored entries of T
@@ -441,7 +499,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                                 uint32_t pos = kEmpty;
                                 if (j < total) {
                                     uint32_t node = picks[j / A.R];
-                                    pos = __ldg(A.graph + (size_t)node * A.R + (j % A.R));
+                                    pos = __ldg(A.graph + (gbase + (long long)node * A.R + (j % A.R)));
                                     if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
                                 }
                                 append(w.P(A), nb, ok, pos);
@@ -461,10 +519,12 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                         __syncwarp();
                     }
                     // (d) cross-cell hop
-                    if (ci + 1 < nc) {
-                        nb = cross_hop<NCH>(A, w, cl[ci + 1], hcount, st_dist, st_cross);
+                    const uint32_t cn = next_cell(A, cl, nc, ci + 1);
+                    if (cn < nc) {
+                        nb = cross_hop<NCH>(A, w, cl[cn], hcount, st_dist, st_cross);
                         ++st_hops;
                     }
+                    ci = cn;
                 }
                 // final post-filter of T and recycle merge (gpu_graph.cu:4025-4048)
                 uint32_t nin = 0;
@@ -486,7 +546,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     const uint32_t r = merge_keys(w.RL(A), w.RLn(A), A.K, w.Tn(A), nin, nullptr, false);
                     if ((r >> 16) != 0) res = w.RLn(A);
                 }
-                write_result(A, q, res, A.K);
+                emit(A, q, res, w.T(A), w.Tn(A));
             }
         }
         __syncwarp();
@@ -499,6 +559,15 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
             atomicAdd(A.stats + 5, 1ull);
         }
     }
+}
+
+__global__ void run_to_ids_kernel(const unsigned long long* __restrict__ run, uint32_t total,
+                                  const uint32_t* __restrict__ i2g, uint32_t* ids, float* dist) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const key_t k = run[i];
+    if (ids) ids[i] = k == kEmptyKey ? kEmpty : i2g[key_pos(k)];
+    if (dist) dist[i] = k == kEmptyKey ? kInf : key_dist(k);
 }
 
 typedef void (*KernelFn)(const SArgs);
@@ -519,7 +588,7 @@ KernelFn pick_kernel(uint32_t nch) {
 }  // namespace
 
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
-                 cudaStream_t s) {
+                 cudaStream_t s, const CellView* view) {
     DeviceIndex& d = idx->d;
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "gf_search before gf_plan_queries");
@@ -531,14 +600,22 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
     uint32_t n_entry = P.n_entry ? P.n_entry : d.degree;
     n_entry = std::min<uint32_t>(n_entry, (uint32_t)d.entry_h.size());
-    if (!ids) return fail(GF_ERR_ARG, "null ids_out");
+    if (!ids && !(view && view->run)) return fail(GF_ERR_ARG, "null ids_out");
+    if (!view && d.host_graph)
+        return fail(GF_ERR_STATE, "the index keeps its graphs in host memory: search it with gf_search_batched");
     if (p.qnum == 0) return GF_OK;
 
     SArgs A;
     A.vec16 = d.vec16;
     A.attrs = d.attrs;
-    A.graph = d.graph;
-    A.cross = d.cross;
+    A.graph = view ? view->graph : d.graph;
+    A.cross = view ? view->cross : d.cross;
+    A.slot = view ? view->slot : nullptr;
+    A.gofs = view ? view->gofs : nullptr;
+    A.xofs = view ? view->xofs : nullptr;
+    A.run = view ? view->run : nullptr;
+    A.nslots = view ? view->nslots : 0;
+    A.xstride = view ? view->xstride : 0;
     A.seg = d.seg;
     A.i2g = d.i2g;
     A.q16 = p.q16;
@@ -559,7 +636,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.a = d.a;
     A.P = d.ncells;
     A.R = d.degree;
-    A.E = d.cross ? d.E : 0;
+    A.E = (d.cross || d.cross_h) ? d.E : 0;
     A.L = P.L;
     A.K = P.k;
     A.W = P.width;
@@ -607,8 +684,16 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t need_blocks = (p.qnum + warps_per_block - 1) / warps_per_block;
     blocks = std::min(blocks, need_blocks);
     GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
-    GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
+    if (!(view && view->accumulate_stats)) GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
     kern<<<blocks, 128, smem, s>>>(A);
+    GF_CUDA(cudaGetLastError());
+    return GF_OK;
+}
+
+gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t total, uint32_t* ids, float* dist,
+                     cudaStream_t s) {
+    if (total == 0) return GF_OK;
+    run_to_ids_kernel<<<(total + 255) / 256, 256, 0, s>>>(run, total, idx->d.i2g, ids, dist);
     GF_CUDA(cudaGetLastError());
     return GF_OK;
 }

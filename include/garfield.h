@@ -67,6 +67,10 @@ typedef struct {
     const int32_t* labels; /* host, n cluster labels (cluster.bin), or NULL */
     float f2h_factor;      /* --f2h_factor: vectors are stored as half(x * f2h_factor) */
     uint32_t keep_fp32;    /* 1 = also keep fp32 vectors on the device (gf_bruteforce) */
+    uint32_t host_graph;   /* 1 = keep the graphs and cross edges in pinned host memory and
+                              copy them to the device per batch of cells (gf_search_batched;
+                              the dataset-resident out-of-core mode of
+                              big_dataset_adapterV3.cuh:3321) */
 } gf_index_desc;
 
 /* Paths of the reference's index files (realdataset_search flags, README.md:101-170). */
@@ -81,6 +85,7 @@ typedef struct {
     uint32_t degree;          /* --degree */
     float f2h_factor;         /* --f2h_factor */
     uint32_t keep_fp32;
+    uint32_t host_graph;      /* as gf_index_desc.host_graph */
     /* Uniform grid (normaldataset_search, normaldataset_search.cu:1748-2104), used when
      * grid is NULL: attribute j is cut into uniform_shape[j] equal slices of
      * [uniform_lo, uniform_hi) (the reference compiles shape {16} and [0, 1e6) in);
@@ -187,6 +192,27 @@ gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out);
 gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* params, const float* queries_host,
                          const float* lb_host, const float* rb_host, uint32_t qnum, float prefilter,
                          uint32_t* ids_host, float* dist_host, void* stream);
+
+/*
+ * Search restricted to batches of cells, results merged over the batches.  Replaces the
+ * out-of-core driver batch_graph_search_gpu_with_prefilter_batch_process_compressed_graph_
+ * T_dataset_resident (big_dataset_adapterV3.cuh:3321-3715) with its per-batch cell lists
+ * (fill_partition_info03, tools.cuh:1646) and host-side merge (:3343-3395).
+ * batch_cells (host) holds the cells of every batch back to back, batch_sizes[b] (host) how
+ * many belong to batch b; a cell may appear in at most one batch, and cells in no batch are
+ * not searched.  In batch b every query visits the planned cells that b holds, in planned
+ * order, starting from the entry set in the first of them (the route, graph or exact, is
+ * decided from the query's full cell list); the batch's k best in-range results are merged
+ * into the query's running k best by (distance, position).  One batch holding every cell
+ * gives exactly gf_search's results.  For an index with host_graph the graph rows of a
+ * batch's cells and the cross-edge blocks between them are copied from pinned host memory
+ * on a copy stream, double-buffered, so that the copies of batch b+1 overlap the search of
+ * batch b (ordered by stream events).  Needs gf_plan_queries first; ids_out / dist_out
+ * (dist may be NULL) device, qnum x k.  Counters (gf_search_stats_read) sum over batches.
+ */
+gf_status gf_search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* params,
+                            const uint32_t* batch_cells, const uint32_t* batch_sizes, uint32_t n_batches,
+                            uint32_t* ids_out, float* dist_out, void* stream);
 
 /*
  * Exact filtered k-NN: every point whose attributes lie inside the query's box competes;

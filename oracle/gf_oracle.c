@@ -477,7 +477,14 @@ static inline ent evaluate(const qctx* c, uint32_t pos) {
  * query has >= postfilter cells (the reference then returns an empty list, :3377 +
  * :4025; the scan is what the route is for).
  */
-static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, uint32_t nc, uint32_t box_count,
+static int route_exact(const orc_index* ix, const orc_params* p, uint32_t nc, uint32_t box_count) {
+    float prop = (float)((double)box_count / (double)ix->n); /* real_dataset_adapter.cuh:380 */
+    return (nc >= p->postfilter) || (prop <= p->prefilter);
+}
+
+/* cl[0..nc) are the cells to visit; `exact` the route (route_exact of the query's full
+ * cell list).  Results: K (global id, distance) pairs, ORC_EMPTY / +inf padded. */
+static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, uint32_t nc, int exact,
                        const uint32_t* entry, uint32_t* out_ids, float* out_d) {
     const orc_index* ix = c->ix;
     const uint32_t K = p->K, L = p->L, R = ix->degree;
@@ -486,8 +493,6 @@ static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, u
         out_d[k] = INFINITY;
     }
     if (nc == 0) return;
-    float prop = (float)((double)box_count / (double)ix->n); /* real_dataset_adapter.cuh:380 */
-    int exact = (nc >= p->postfilter) || (prop <= p->prefilter);
     if (exact) {
         orc_pair* best = (orc_pair*)malloc(sizeof(orc_pair) * K);
         uint32_t nb = 0;
@@ -639,6 +644,27 @@ static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, u
     free(touched);
 }
 
+/* Cell-major positions (tools.cuh:862-889 get_idx_mapper): seg[c] .. seg[c+1]-1 are the
+ * points of cell c in increasing global id; g_of maps position -> id, p_of id -> position. */
+static void make_positions(const orc_index* ix, uint32_t** seg_out, uint32_t** g_out, uint32_t** p_out) {
+    uint32_t* seg = (uint32_t*)calloc(ix->ncells + 1, sizeof(uint32_t));
+    uint32_t* g_of = (uint32_t*)malloc(sizeof(uint32_t) * (ix->n ? ix->n : 1));
+    uint32_t* p_of = (uint32_t*)malloc(sizeof(uint32_t) * (ix->n ? ix->n : 1));
+    for (uint32_t i = 0; i < ix->n; ++i) seg[ix->cell_of[i] + 1]++;
+    for (uint32_t c = 0; c < ix->ncells; ++c) seg[c + 1] += seg[c];
+    uint32_t* fill = (uint32_t*)calloc(ix->ncells ? ix->ncells : 1, sizeof(uint32_t));
+    for (uint32_t i = 0; i < ix->n; ++i) {
+        uint32_t c = ix->cell_of[i];
+        uint32_t pos = seg[c] + fill[c]++;
+        g_of[pos] = i;
+        p_of[i] = pos;
+    }
+    free(fill);
+    *seg_out = seg;
+    *g_out = g_of;
+    *p_out = p_of;
+}
+
 /*
  * Batch driver (gpu_graph.cu:12464-12616 minus the launch): cells/counts/offsets are the
  * ordered CSR from orc_plan_cells + orc_order_cells; box_counts from orc_count_in_box
@@ -650,21 +676,8 @@ void orc_search(const orc_index* ix, const orc_params* p, const float* queries, 
                 const float* lb, const float* rb, uint32_t qnum, const uint32_t* counts, const uint32_t* offsets,
                 const uint32_t* cells, const uint32_t* box_counts, const uint32_t* entry, uint32_t* ids_out,
                 float* dist_out, uint64_t* stats, int threads) {
-    uint32_t* seg = (uint32_t*)calloc(ix->ncells + 1, sizeof(uint32_t));
-    uint32_t* g_of = (uint32_t*)malloc(sizeof(uint32_t) * ix->n);
-    uint32_t* p_of = (uint32_t*)malloc(sizeof(uint32_t) * ix->n);
-    for (uint32_t i = 0; i < ix->n; ++i) seg[ix->cell_of[i] + 1]++;
-    for (uint32_t c = 0; c < ix->ncells; ++c) seg[c + 1] += seg[c];
-    {
-        uint32_t* fill = (uint32_t*)calloc(ix->ncells, sizeof(uint32_t));
-        for (uint32_t i = 0; i < ix->n; ++i) { /* tools.cuh:862-889 get_idx_mapper */
-            uint32_t c = ix->cell_of[i];
-            uint32_t pos = seg[c] + fill[c]++;
-            g_of[pos] = i;
-            p_of[i] = pos;
-        }
-        free(fill);
-    }
+    uint32_t *seg, *g_of, *p_of;
+    make_positions(ix, &seg, &g_of, &p_of);
     uint64_t tot[4] = {0, 0, 0, 0};
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
@@ -677,12 +690,86 @@ void orc_search(const orc_index* ix, const orc_params* p, const float* queries, 
         for (long q = 0; q < (long)qnum; ++q) {
             orc_f2h(queries + (size_t)q * dim, 1, dim, ix->d8, alpha, q16);
             qctx c = {ix, seg, g_of, p_of, q16, lb + q * ix->a, rb + q * ix->a, st};
-            search_one(&c, p, cells + offsets[q], counts[q], box_counts ? box_counts[q] : ix->n, entry,
-                       ids_out + (size_t)q * p->K, dist_out + (size_t)q * p->K);
+            int exact = route_exact(ix, p, counts[q], box_counts ? box_counts[q] : ix->n);
+            search_one(&c, p, cells + offsets[q], counts[q], exact, entry, ids_out + (size_t)q * p->K,
+                       dist_out + (size_t)q * p->K);
         }
 #pragma omp critical
         for (int i = 0; i < 4; ++i) tot[i] += st[i];
         free(q16);
+    }
+    if (stats)
+        for (int i = 0; i < 4; ++i) stats[i] += tot[i];
+    free(seg);
+    free(g_of);
+    free(p_of);
+}
+
+/*
+ * Search over batches of cells (the out-of-core driver,
+ * big_dataset_adapterV3.cuh:3321-3715, with its per-batch kernel :754-1390 and the
+ * per-batch cell lists of fill_partition_info03, tools.cuh:1646-1670).
+ * batch_of[c] is the batch holding cell c, or ORC_EMPTY when c is searched in no batch.
+ * For batch b = 0 .. n_batches-1 each query visits the cells of its planned list that
+ * batch b holds, in planned order, with search_one (entry set in the first of them; the
+ * route is decided once from the query's full list); the K results of the batch are
+ * merged into the query's running K best by (distance, position), which replaces the
+ * reference's host-side merge of each batch's list (:3347-3395).
+ */
+void orc_search_batched(const orc_index* ix, const orc_params* p, const float* queries, uint32_t dim, float alpha,
+                        const float* lb, const float* rb, uint32_t qnum, const uint32_t* counts,
+                        const uint32_t* offsets, const uint32_t* cells, const uint32_t* box_counts,
+                        const uint32_t* entry, const uint32_t* batch_of, uint32_t n_batches, uint32_t* ids_out,
+                        float* dist_out, uint64_t* stats, int threads) {
+    uint32_t *seg, *g_of, *p_of;
+    make_positions(ix, &seg, &g_of, &p_of);
+    const uint32_t K = p->K;
+    uint64_t tot[4] = {0, 0, 0, 0};
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#endif
+#pragma omp parallel
+    {
+        uint64_t st[4] = {0, 0, 0, 0};
+        uint16_t* q16 = (uint16_t*)malloc(sizeof(uint16_t) * ix->d8);
+        uint32_t* sub = (uint32_t*)malloc(sizeof(uint32_t) * (ix->ncells ? ix->ncells : 1));
+        uint32_t* bid = (uint32_t*)malloc(sizeof(uint32_t) * K);
+        float* bd = (float*)malloc(sizeof(float) * K);
+        ent* run = (ent*)malloc(sizeof(ent) * K);
+        ent* got = (ent*)malloc(sizeof(ent) * K);
+        ent* tmp = (ent*)malloc(sizeof(ent) * 2 * K);
+#pragma omp for schedule(dynamic, 1)
+        for (long q = 0; q < (long)qnum; ++q) {
+            orc_f2h(queries + (size_t)q * dim, 1, dim, ix->d8, alpha, q16);
+            qctx c = {ix, seg, g_of, p_of, q16, lb + q * ix->a, rb + q * ix->a, st};
+            const uint32_t* cl = cells + offsets[q];
+            int exact = route_exact(ix, p, counts[q], box_counts ? box_counts[q] : ix->n);
+            for (uint32_t k = 0; k < K; ++k) run[k] = (ent){INFINITY, ORC_EMPTY};
+            for (uint32_t b = 0; b < n_batches; ++b) {
+                uint32_t ns = 0;
+                for (uint32_t i = 0; i < counts[q]; ++i)
+                    if (batch_of[cl[i]] == b) sub[ns++] = cl[i];
+                if (ns == 0) continue;
+                search_one(&c, p, sub, ns, exact, entry, bid, bd);
+                uint32_t ng = 0;
+                for (uint32_t k = 0; k < K; ++k)
+                    if (bid[k] != ORC_EMPTY) got[ng++] = (ent){bd[k], p_of[bid[k]]};
+                merge_into(run, K, got, ng, NULL, 0, tmp);
+            }
+            for (uint32_t k = 0; k < K; ++k) {
+                ids_out[(size_t)q * K + k] = run[k].w == ORC_EMPTY ? ORC_EMPTY : g_of[run[k].w & ORC_POSMASK];
+                dist_out[(size_t)q * K + k] = run[k].w == ORC_EMPTY ? INFINITY : run[k].d;
+            }
+        }
+#pragma omp critical
+        for (int i = 0; i < 4; ++i) tot[i] += st[i];
+        free(q16);
+        free(sub);
+        free(bid);
+        free(bd);
+        free(run);
+        free(got);
+        free(tmp);
     }
     if (stats)
         for (int i = 0; i < 4; ++i) stats[i] += tot[i];

@@ -61,6 +61,8 @@ def lib() -> C.CDLL:
         _L.orc_order_cells.argtypes = [P, U, U, P, U, P, P, P, P, P]
         _L.orc_search.argtypes = [C.POINTER(OrcIndex), C.POINTER(OrcParams), P, U, C.c_float, P, P, U, P, P, P, P,
                                   P, P, P, P, C.c_int]
+        _L.orc_search_batched.argtypes = [C.POINTER(OrcIndex), C.POINTER(OrcParams), P, U, C.c_float, P, P, U, P,
+                                          P, P, P, P, P, U, P, P, P, C.c_int]
         _L.orc_recall.restype = C.c_double
         _L.orc_recall.argtypes = [P, U, P, U, U]
     return _L
@@ -160,8 +162,12 @@ def order_cells(queries, centroids, hist, counts, offsets, cells):
 
 
 def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells, entry, *, L, K, width=1,
-           max_iter=10000, postfilter=0xFFFFFFFF, prefilter=0.0, box_counts=None, alpha=1.0, threads=0):
-    """Beam search restatement; index_arrays: an indexbuild.GmgArrays (reference layout)."""
+           max_iter=10000, postfilter=0xFFFFFFFF, prefilter=0.0, box_counts=None, alpha=1.0, threads=0,
+           batches=None):
+    """Beam search restatement; index_arrays: an indexbuild.GmgArrays (reference layout).
+
+    With `batches` (a list of cell lists), the batched driver orc_search_batched runs
+    instead: each batch is searched on its own and the results merged."""
     vectors = _c(vectors, np.float32)
     n, dim = vectors.shape
     d8 = (dim + 7) // 8 * 8
@@ -170,7 +176,8 @@ def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells
     cell_of = _c(index_arrays.cell_of, np.uint32)
     graphs = _c(index_arrays.graphs, np.uint32)
     cross = _c(index_arrays.cross, np.uint32)
-    ix = OrcIndex(n, d8, attrs.shape[1], int(np.prod(index_arrays.grid)), index_arrays.degree, index_arrays.cross_e,
+    ncells = int(np.prod(index_arrays.grid))
+    ix = OrcIndex(n, d8, attrs.shape[1], ncells, index_arrays.degree, index_arrays.cross_e,
                   _p(vec16), _p(attrs), _p(cell_of), _p(graphs), _p(cross))
     entry = _c(entry, np.uint32)
     prm = OrcParams(L, K, width, max_iter, postfilter, prefilter, len(entry))
@@ -182,8 +189,17 @@ def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells
     ids = np.zeros((qn, K), np.uint32)
     dist = np.zeros((qn, K), np.float32)
     stats = np.zeros(4, np.uint64)
-    lib().orc_search(C.byref(ix), C.byref(prm), _p(queries), dim, alpha, _p(lo), _p(hi), qn, _p(counts), _p(offsets),
-                     _p(cells), _p(box), _p(entry), _p(ids), _p(dist), _p(stats), threads)
+    if batches is None:
+        lib().orc_search(C.byref(ix), C.byref(prm), _p(queries), dim, alpha, _p(lo), _p(hi), qn, _p(counts),
+                         _p(offsets), _p(cells), _p(box), _p(entry), _p(ids), _p(dist), _p(stats), threads)
+    else:
+        batch_of = np.full(ncells, 0xFFFFFFFF, np.uint32)
+        for b, cl in enumerate(batches):
+            for c in cl:
+                batch_of[int(c)] = b
+        lib().orc_search_batched(C.byref(ix), C.byref(prm), _p(queries), dim, alpha, _p(lo), _p(hi), qn,
+                                 _p(counts), _p(offsets), _p(cells), _p(box), _p(entry), _p(batch_of), len(batches),
+                                 _p(ids), _p(dist), _p(stats), threads)
     return ids, dist, stats
 
 

@@ -149,3 +149,29 @@ def test_recall_semantics():
     gt = np.array([[1, 2, 3, oracle.EMPTY], [oracle.EMPTY] * 4], np.uint32)
     res = np.array([[3, 9, 1, 7], [5, 6, 7, 8]], np.uint32)
     assert abs(oracle.recall(res, gt) - (2 / 3 + 1.0) / 2) < 1e-12
+
+
+def test_batched_search_properties(small, odd):
+    """orc_search_batched: one batch of every cell is the plain search; any split keeps
+    results valid and sorted; the exact route stays exact under any split."""
+    for c in (small, odd):
+        ent = c.entry(c.ix.degree)
+        args = (c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts, c.offsets, c.cells, ent)
+        ids0, d0, st0 = oracle.search(*args, L=48, K=10)
+        ids1, d1, st1 = oracle.search(*args, L=48, K=10, batches=[list(range(c.ncells))])
+        assert (ids0 == ids1).all() and (d0 == d1).all() and (st0 == st1).all()
+        rng = np.random.default_rng(7)
+        perm = rng.permutation(c.ncells)
+        split = [sorted(perm[: c.ncells // 2].tolist()), sorted(perm[c.ncells // 2:].tolist())]
+        ids2, d2, _ = oracle.search(*args, L=48, K=10, batches=split)
+        assert _valid(ids2, c.ds.attrs, c.ds.lo, c.ds.hi)
+        assert (np.diff(d2, axis=1)[np.isfinite(d2[:, 1:])] >= 0).all()
+        assert oracle.recall(ids2, c.gt) >= 0.85  # splits lose cross-cell reuse
+        # exact route: the merge of per-batch exact lists is the exact list
+        ids3, _, _ = oracle.search(*args, L=16, K=10, postfilter=1, batches=[[x] for x in perm.tolist()])
+        ids4, _, _ = oracle.search(*args, L=16, K=10, postfilter=1)
+        assert (ids3 == ids4).all()
+        # a cell searched in no batch contributes nothing
+        ids5, _, _ = oracle.search(*args, L=16, K=10, postfilter=1, batches=[[0]])
+        in0 = np.isin(ids5, np.flatnonzero(c.ix.cell_of == 0)) | (ids5 == oracle.EMPTY)
+        assert in0.all()
