@@ -25,7 +25,7 @@ from pathlib import Path
 import numpy as np
 
 __all__ = [
-    "GarfieldError", "lib", "lib_path", "SearchParams", "Index", "Plan", "NO_ID",
+    "GarfieldError", "lib", "lib_path", "SearchParams", "Index", "Plan", "NO_ID", "schedule_batches",
     "read_fvecs", "write_fvecs", "read_attrs", "write_attrs", "read_u32mat", "write_u32mat",
     "read_ranges", "write_ranges", "read_labels", "read_grid",
 ]
@@ -110,6 +110,9 @@ def lib() -> C.CDLL:
         "gf_search_stats_read": (C.c_int, [_P, _PTR(_SearchStats)]),
         "gf_search_host": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _P, _U32, C.c_float, _P, _P, _P]),
         "gf_search_batched": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _U32, _P, _P, _P]),
+        "gf_schedule_batches": (C.c_int, [_P, _U32, _P, _P, _PTR(_U32), _PTR(C.c_uint64)]),
+        "gf_schedule_batches_host": (C.c_int, [_U32, _U32, _P, _P, _P, _U32, _P, _P, _PTR(_U32),
+                                               _PTR(C.c_uint64)]),
         "gf_bruteforce": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _P]),
         "gf_free": (None, [_P]),
         "gf_read_fvecs": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
@@ -374,6 +377,15 @@ class Plan:
                "gf_search_batched")
         return ids, dist
 
+    def schedule(self, max_cells: int):
+        """gf_schedule_batches: (list of cell lists, splits) for search_batched."""
+        n = self.index.n_cells
+        cells, sizes = np.zeros(n, np.uint32), np.zeros(n, np.uint32)
+        nb, splits = _U32(), C.c_uint64()
+        _check(lib().gf_schedule_batches(self._h, max_cells, _np_ptr(cells), _np_ptr(sizes), C.byref(nb),
+                                         C.byref(splits)), "gf_schedule_batches")
+        return _unpack_batches(cells, sizes, nb.value), int(splits.value)
+
     def stats(self) -> dict:
         s = _SearchStats()
         _check(lib().gf_search_stats_read(self._h, C.byref(s)), "gf_search_stats_read")
@@ -381,6 +393,27 @@ class Plan:
 
 
 # ------------------------------------------------------------------ file formats
+
+def _unpack_batches(cells, sizes, nb):
+    out, o = [], 0
+    for b in range(nb):
+        out.append(cells[o:o + int(sizes[b])].tolist())
+        o += int(sizes[b])
+    return out
+
+
+def schedule_batches(ncells: int, counts, offsets, cells, max_cells: int):
+    """gf_schedule_batches_host on host plan arrays: (list of cell lists, splits)."""
+    counts = np.ascontiguousarray(counts, np.uint32)
+    offsets = np.ascontiguousarray(offsets, np.uint32)
+    cells = np.ascontiguousarray(cells, np.uint32)
+    bc, bs = np.zeros(max(ncells, 1), np.uint32), np.zeros(max(ncells, 1), np.uint32)
+    nb, splits = _U32(), C.c_uint64()
+    _check(lib().gf_schedule_batches_host(ncells, len(counts), _np_ptr(counts), _np_ptr(offsets), _np_ptr(cells),
+                                          max_cells, _np_ptr(bc), _np_ptr(bs), C.byref(nb), C.byref(splits)),
+           "gf_schedule_batches_host")
+    return _unpack_batches(bc, bs, nb.value), int(splits.value)
+
 
 def _take(ptr: C.c_void_p, count: int, dtype) -> np.ndarray:
     arr = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(np.ctypeslib.as_ctypes_type(dtype))), shape=(count,)).copy()

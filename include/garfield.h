@@ -215,6 +215,25 @@ gf_status gf_search_batched(gf_index* idx, gf_plan* plan, const gf_search_params
                             uint32_t* ids_out, float* dist_out, void* stream);
 
 /*
+ * Batches of at most max_cells cells for gf_search_batched, grouped so that few queries
+ * are split across batches.  The reference uses a fixed random partition of the cells
+ * (bigdataset_experiment.cu:271-277); its README (README.md:5) describes minimising the
+ * queries active in several batches, which is the objective here: the number of
+ * (query, batch) pairs ("splits").  Greedy: a batch starts from the unscheduled cell that
+ * most queries visit and adds the cell sharing the most queries with the batch so far.
+ * Only cells that some query visits are scheduled.  Outputs (host): batch_cells_out
+ * (capacity ncells) and batch_sizes_out (capacity ncells) back to back as
+ * gf_search_batched takes them, *n_batches_out, and *splits_out (may be NULL).
+ * gf_schedule_batches reads the plan (synchronises its stream); _host takes the plan's
+ * cell lists in gf_plan_read's form.
+ */
+gf_status gf_schedule_batches(gf_plan* plan, uint32_t max_cells, uint32_t* batch_cells_out,
+                              uint32_t* batch_sizes_out, uint32_t* n_batches_out, uint64_t* splits_out);
+gf_status gf_schedule_batches_host(uint32_t ncells, uint32_t qnum, const uint32_t* counts, const uint32_t* offsets,
+                                   const uint32_t* cells, uint32_t max_cells, uint32_t* batch_cells_out,
+                                   uint32_t* batch_sizes_out, uint32_t* n_batches_out, uint64_t* splits_out);
+
+/*
  * Exact filtered k-NN: every point whose attributes lie inside the query's box competes;
  * squared L2 on the fp32 vectors; (distance, global id) order.  Replaces
  * naive_brute_force_with_filter (gpu_graph.cu:10782) and prefiltering_and_bruteforce
