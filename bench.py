@@ -15,6 +15,8 @@ length in a fixed sweep whose recall on the ground-truth sample reaches the targ
                                                             reference's CPU path) on host cores
   python bench.py --mode out-of-core [--batch-cells B]     graphs in pinned host memory, streamed
                                                             per scheduled batch of B cells (row a17)
+  torchrun ... bench.py --mode sharded                     cell-sharded index over the ranks, keys
+                                                            all-gathered over NCCL and merged (row e)
   python bench.py --impl reference-cuda                     the reference's own CUDA binary: prints
                                                             "unavailable" (it faults on B200, see
                                                             REF_CUDA_FAULT)
@@ -415,6 +417,110 @@ def run_out_of_core(args):
     print(json.dumps(out), flush=True)
 
 
+def run_sharded(args):
+    """Cell-sharded mode (row e, strong scaling): rank r of N holds the cells
+    dist.shard_cells(grid, N)[r] only; a step plans all queries on every rank, searches them
+    among the local cells (gf_search_keys), all-gathers the (qnum, k) merge keys over NCCL
+    and merges them (gf_merge_keys) on every rank."""
+    import torch
+    import torch.distributed as dist
+    import garfield_b200 as gf
+    from garfield_b200.dist import exchange_keys, shard_cells
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+    ds, ix = dataset_and_index(args, device)
+    mine = shard_cells(ix.grid, world)[rank]
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, keep_fp32=False,
+                            shard_cells=mine if world > 1 else None, device=local)
+    qnum = ds.queries.shape[0]
+    qd = torch.from_numpy(ds.queries).to(device)
+    lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
+    hid = torch.from_numpy(ds.hi.astype(np.float32)).to(device)
+    S = min(args.gt_sample, qnum)
+    stream = torch.cuda.Stream(device)
+    plan = index.plan(qnum)
+    width = args.width or 4
+    keys = torch.empty((qnum, 10), dtype=torch.int64, device=device)
+
+    def step(L):
+        plan.build(qd, lod, hid, 0.0, stream)
+        plan.search_keys(gf.SearchParams(L=L, k=10, width=width), stream, keys=keys)
+        with torch.cuda.stream(stream):
+            allk = exchange_keys(keys) if world > 1 else keys[None]
+        return index.merge_keys(allk, 10, stream)
+
+    # ground truth: exact scan on a whole index on rank 0, broadcast
+    gt = torch.zeros((S, 10), dtype=torch.int32, device=device)
+    if rank == 0:
+        whole = gf.Index.create(vectors=ds.vectors,
+                                attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                                r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                                cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=True, device=local)
+        gt.copy_(whole.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), 10)[0])
+        whole.close()
+        del whole
+    if world > 1:
+        dist.broadcast(gt, 0)
+    gt_np = gt.cpu().numpy().view(np.uint32)
+    L, recall, sweep = None, 0.0, []
+    for Lc in ([args.L] if args.L else L_SWEEP):
+        ids, _ = step(Lc)
+        stream.synchronize()
+        recall = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt_np)
+        sweep.append((Lc, round(recall, 4)))
+        L = Lc
+        if recall >= args.target:
+            break
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
+    for _ in range(args.warmup):
+        step(L)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(float(i))
+                ev[i][0].record(stream)
+            step(L)
+            with torch.cuda.stream(stream):
+                ev[i][1].record(stream)
+        stream.synchronize()
+    total_ms = float(sum(a.elapsed_time(b) for a, b in ev))
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms = total_ms / args.steps
+    out = {"metric": "QPS at recall@10>=0.95, cell-sharded index (1M x 128, 2 attrs, 10% sel.)",
+           "value": round(qnum / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
+           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
+           "config": {"workload": "config2, cell-sharded", "parallelism": f"cell shards x{world}", "L": L,
+                      "width": width, "recall_at_10": round(recall, 4), "recall_sample": S, "sweep": sweep,
+                      "shard_cells": mine, "device_bytes_rank0": index.device_bytes,
+                      "exchange_bytes_per_rank": qnum * 10 * 8,
+                      "l2": "flushed (256 MiB write) between timed steps"},
+           "clocks": clocks.summary()}
+    plan.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def run_reference_cpu(args):
     """Reference arm: the CPU exact filtered scan on the host cores, same metric/config."""
     rank = int(os.environ.get("RANK", 0))
@@ -486,11 +592,13 @@ def main():
     ap.add_argument("--cache", default="/tmp/gf_cache")
     ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
-    ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core"])
+    ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core", "sharded"])
     ap.add_argument("--batch-cells", dest="batch_cells", type=int, default=4)
     args = ap.parse_args()
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
+    elif args.impl == "ours" and args.mode == "sharded":
+        run_sharded(args)
     elif args.impl == "reference":
         run_reference_cpu(args)
     elif args.impl == "reference-cuda":

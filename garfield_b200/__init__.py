@@ -49,6 +49,7 @@ class _IndexDesc(C.Structure):
         ("degree", C.c_uint32), ("graphs", C.c_void_p), ("cross_e", C.c_uint32),
         ("cross", C.c_void_p), ("n_clusters", C.c_uint32), ("labels", C.c_void_p),
         ("f2h_factor", C.c_float), ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32),
+        ("shard_cells", C.c_void_p), ("n_shard_cells", C.c_uint32),
     ]
 
 
@@ -110,6 +111,8 @@ def lib() -> C.CDLL:
         "gf_search_stats_read": (C.c_int, [_P, _PTR(_SearchStats)]),
         "gf_search_host": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _P, _U32, C.c_float, _P, _P, _P]),
         "gf_search_batched": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _U32, _P, _P, _P]),
+        "gf_search_keys": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P]),
+        "gf_merge_keys": (C.c_int, [_P, _P, _U32, _U32, _U32, _P, _P, _P]),
         "gf_schedule_batches": (C.c_int, [_P, _U32, _P, _P, _PTR(_U32), _PTR(C.c_uint64)]),
         "gf_schedule_batches_host": (C.c_int, [_U32, _U32, _P, _P, _P, _U32, _P, _P, _PTR(_U32),
                                                _PTR(C.c_uint64)]),
@@ -198,10 +201,12 @@ class Index:
 
     @classmethod
     def create(cls, *, vectors, attrs, grid, l_quant, r_quant, cell_of, graphs, degree, cross=None,
-               cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, host_graph=False, device=0) -> "Index":
+               cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, host_graph=False, shard_cells=None,
+               device=0) -> "Index":
         """Build from host arrays in the reference's layout (see gf_index_desc).  With
         host_graph the graphs and cross edges stay in pinned host memory (search with
-        Plan.search_batched)."""
+        Plan.search_batched); with shard_cells the device holds only those cells (a shard
+        of a cell-sharded index: Plan.search_keys + Index.merge_keys)."""
         vectors = np.ascontiguousarray(vectors, dtype=np.float32)
         attrs = np.ascontiguousarray(attrs, dtype=np.float32)
         grid = np.ascontiguousarray(grid, dtype=np.uint32)
@@ -221,6 +226,11 @@ class Index:
         d.n_clusters, d.labels = (1 if labels is not None else 0), _np_ptr(labels)
         d.f2h_factor, d.keep_fp32 = f2h_factor, 1 if keep_fp32 else 0
         d.host_graph = 1 if host_graph else 0
+        shard = None
+        if shard_cells is not None:
+            shard = np.ascontiguousarray(shard_cells, dtype=np.uint32)
+            d.shard_cells, d.n_shard_cells = _np_ptr(shard), len(shard)
+            d.keep_fp32 = 0
         h = C.c_void_p()
         _check(lib().gf_index_create(C.byref(d), device, C.byref(h)), "gf_index_create")
         return cls(h)
@@ -266,6 +276,16 @@ class Index:
 
     def plan(self, max_queries: int) -> "Plan":
         return Plan(self, max_queries)
+
+    def merge_keys(self, keys, k: int, stream=None):
+        """gf_merge_keys: keys (lists, qnum, k) int64 CUDA tensor -> (ids int32, dists)."""
+        import torch
+        lists, q = keys.shape[0], keys.shape[1]
+        ids = torch.empty((q, k), dtype=torch.int32, device=keys.device)
+        dist = torch.empty((q, k), dtype=torch.float32, device=keys.device)
+        _check(lib().gf_merge_keys(self._h, _dev_ptr(keys), lists, q, k, _dev_ptr(ids), _dev_ptr(dist),
+                                   _stream_ptr(stream)), "gf_merge_keys")
+        return ids, dist
 
     def bruteforce(self, queries, lb, rb, k: int, stream=None):
         """Exact filtered k-NN on the device; returns (ids, dists) CUDA tensors."""
@@ -376,6 +396,18 @@ class Plan:
                                        len(batches), _dev_ptr(ids), _dev_ptr(dist), _stream_ptr(stream)),
                "gf_search_batched")
         return ids, dist
+
+    def search_keys(self, params: SearchParams | None = None, stream=None, keys=None):
+        """gf_search_keys: (qnum, k) int64 CUDA tensor of merge keys."""
+        import torch
+        params = params or SearchParams()
+        if keys is None:
+            keys = torch.empty((self.qnum, params.k), dtype=torch.int64,
+                               device=torch.device("cuda", torch.cuda.current_device()))
+        cp = params._c()
+        _check(lib().gf_search_keys(self.index._h, self._h, C.byref(cp), _dev_ptr(keys), _stream_ptr(stream)),
+               "gf_search_keys")
+        return keys
 
     def schedule(self, max_cells: int):
         """gf_schedule_batches: (list of cell lists, splits) for search_batched."""

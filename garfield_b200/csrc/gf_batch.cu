@@ -85,6 +85,7 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
     DeviceIndex& d = idx->d;
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "gf_search_batched before gf_plan_queries");
+    if (d.sharded) return fail(GF_ERR_STATE, "gf_search_batched on a shard: search it with gf_search_keys");
     gf_search_params P;
     gf_search_defaults(&P);
     if (prm) P = *prm;

@@ -127,11 +127,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // Closed-box test of one point (merge_top_with_recycle_list's filter, gpu_graph.cu:514-520).
-__device__ __forceinline__ bool in_box(const float* __restrict__ attrs, uint32_t pos, uint32_t a,
+__device__ __forceinline__ bool in_box(const float* __restrict__ attrs, long long row, uint32_t a,
                                        const float* __restrict__ lb, const float* __restrict__ rb) {
     bool ok = true;
     for (uint32_t j = 0; j < a; ++j) {
-        float v = __ldg(attrs + (size_t)pos * a + j);
+        float v = __ldg(attrs + row * a + j);
         ok = ok && (v >= lb[j]) && (v <= rb[j]);
     }
     return ok;

@@ -73,8 +73,9 @@ static gf_status dalloc(T** p, size_t count, uint64_t* bytes) {
     } while (0)
 
 static void free_index(DeviceIndex& d) {
-    void* ptrs[] = {d.vec16, d.vec32, d.attrs, d.graph, d.cross, d.i2g, d.seg, d.grid_d,
-                    d.lq_d,  d.rq_d,  d.centroids, d.hist, d.entry};
+    void* ptrs[] = {d.vec16,   d.vec32,   d.attrs,     d.graph,   d.cross,   d.i2g,     d.seg,
+                    d.grid_d,  d.lq_d,    d.rq_d,      d.centroids, d.hist,  d.entry,   d.sh_slot,
+                    d.sh_gofs, d.sh_xofs, d.sh_vsh};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);
@@ -112,6 +113,9 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     if (ds->degree == 0 || ds->degree > 256) return fail(GF_ERR_ARG, "degree must be 1..256");
     if (ds->cross_e > 4) return fail(GF_ERR_ARG, "cross_e must be 0..4");
     if (ds->cross_e && !ds->cross) return fail(GF_ERR_ARG, "missing cross edges");
+    const bool sharded = ds->shard_cells && ds->n_shard_cells;
+    if (sharded && (ds->host_graph || ds->keep_fp32))
+        return fail(GF_ERR_ARG, "a shard cannot keep host graphs or fp32 vectors");
     uint64_t ncells = 1, nq = 0;
     for (uint32_t j = 0; j < ds->n_attr; ++j) {
         if (ds->grid[j] == 0) return fail(GF_ERR_ARG, "zero grid size");
@@ -166,6 +170,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     }
     d.entry_h = make_entry(std::max<uint32_t>(R, 64), d.min_cell);
     d.host_graph = ds->host_graph != 0;
+    d.n_stored = n;
 
     // Graph rows are already in position order; local ids -> positions.  Cross edges:
     // source-major (position, target cell, edge) on the device; with host_graph,
@@ -175,7 +180,61 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     std::vector<uint32_t> graph, cross;
     uint32_t* gdst = nullptr;
     uint32_t* xdst = nullptr;
-    if (d.host_graph) {
+    // stored rows: every position, or the shard's cells back to back in shard order
+    std::vector<uint32_t> row_pos;  // stored row -> position (shard only)
+    std::vector<int32_t> sh_slot;
+    std::vector<long long> sh_gofs, sh_xofs, sh_vsh;
+    if (sharded) {
+        const uint32_t S = ds->n_shard_cells;
+        d.sharded = true;
+        d.shard_cells.assign(ds->shard_cells, ds->shard_cells + S);
+        sh_slot.assign(P, -1);
+        for (uint32_t b = 0; b < S; ++b) {
+            const uint32_t c = d.shard_cells[b];
+            if (c >= P || sh_slot[c] >= 0) {
+                delete ix;
+                return fail(GF_ERR_ARG, "shard cell out of range or repeated");
+            }
+            sh_slot[c] = (int32_t)b;
+        }
+        for (uint32_t b = 0; b < S; ++b) {
+            const uint32_t c = d.shard_cells[b];
+            sh_vsh.push_back((long long)row_pos.size() - d.seg_h[c]);
+            sh_gofs.push_back((long long)row_pos.size() * R);
+            for (uint32_t p = d.seg_h[c]; p < d.seg_h[c + 1]; ++p) row_pos.push_back(p);
+        }
+        d.n_stored = (uint32_t)row_pos.size();
+        graph.assign((size_t)d.n_stored * R, kEmpty);
+        for (size_t r = 0; r < row_pos.size(); ++r) {
+            const uint32_t pos = row_pos[r], c = ds->cell_of[i2g[pos]];
+            const uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
+            for (uint32_t j = 0; j < R; ++j) {
+                const uint32_t loc = ds->graphs[(size_t)pos * R + j];
+                graph[r * R + j] = loc < sz ? base + loc : kEmpty;
+            }
+        }
+        // cross blocks [target slot][source slot]: source rows of the source cell, E each
+        sh_xofs.assign((size_t)S * S, 0);
+        long long x = 0;
+        for (uint32_t bt = 0; bt < S; ++bt)
+            for (uint32_t bs = 0; bs < S; ++bs) {
+                sh_xofs[(size_t)bt * S + bs] = x;
+                x += (long long)(d.seg_h[d.shard_cells[bs] + 1] - d.seg_h[d.shard_cells[bs]]) * E;
+            }
+        cross.assign(std::max<long long>(x, 1), kEmpty);
+        for (uint32_t bt = 0; bt < S && E; ++bt) {
+            const uint32_t ct = d.shard_cells[bt], tbase = d.seg_h[ct], tsz = d.seg_h[ct + 1] - tbase;
+            for (uint32_t bs = 0; bs < S; ++bs) {
+                const uint32_t cs = d.shard_cells[bs];
+                uint32_t* dst = cross.data() + sh_xofs[(size_t)bt * S + bs];
+                for (uint32_t p = d.seg_h[cs]; p < d.seg_h[cs + 1]; ++p)
+                    for (uint32_t j = 0; j < E; ++j) {
+                        const uint32_t loc = ds->cross[(size_t)i2g[p] * P * E + (size_t)ct * E + j];
+                        dst[(size_t)(p - d.seg_h[cs]) * E + j] = loc < tsz ? tbase + loc : kEmpty;
+                    }
+            }
+        }
+    } else if (d.host_graph) {
         DeviceGuard g0(device);
         cudaError_t e = cudaMallocHost((void**)&d.graph_h, std::max<size_t>((size_t)n * R, 1) * 4);
         if (e == cudaSuccess && E) e = cudaMallocHost((void**)&d.cross_h, std::max<size_t>((size_t)n * P * E, 1) * 4);
@@ -194,7 +253,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             xdst = cross.data();
         }
     }
-    for (uint32_t c = 0; c < P; ++c) {
+    for (uint32_t c = 0; c < P && !sharded; ++c) {
         uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
         for (size_t r = base; r < (size_t)base + sz; ++r)
             for (uint32_t j = 0; j < R; ++j) {
@@ -202,7 +261,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
                 gdst[r * R + j] = loc < sz ? base + loc : kEmpty;
             }
     }
-    if (E) {
+    if (E && !sharded) {
         const size_t rowlen = (size_t)P * E;
         for (uint32_t g = 0; g < n; ++g) {
             const uint32_t* src = ds->cross + (size_t)g * rowlen;
@@ -259,10 +318,17 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     };
     float* vtmp = nullptr;
     do {
-        if (!chk(dalloc(&d.vec16, (size_t)n * d.d8 / 8, &d.bytes))) break;
+        const uint32_t nrows = sharded ? d.n_stored : n;
+        if (!chk(dalloc(&d.vec16, (size_t)nrows * d.d8 / 8, &d.bytes))) break;
         if (!chk(dalloc(&d.attrs, (size_t)n * d.a, &d.bytes))) break;
-        if (!d.host_graph && !chk(dalloc(&d.graph, (size_t)n * R, &d.bytes))) break;
-        if (!d.host_graph && E && !chk(dalloc(&d.cross, (size_t)n * P * E, &d.bytes))) break;
+        if (!d.host_graph && !chk(dalloc(&d.graph, graph.size(), &d.bytes))) break;
+        if (!d.host_graph && E && !chk(dalloc(&d.cross, cross.size(), &d.bytes))) break;
+        if (sharded) {
+            if (!chk(dalloc(&d.sh_slot, sh_slot.size(), &d.bytes))) break;
+            if (!chk(dalloc(&d.sh_gofs, sh_gofs.size(), &d.bytes))) break;
+            if (!chk(dalloc(&d.sh_xofs, sh_xofs.size(), &d.bytes))) break;
+            if (!chk(dalloc(&d.sh_vsh, sh_vsh.size(), &d.bytes))) break;
+        }
         if (!chk(dalloc(&d.i2g, n, &d.bytes))) break;
         if (!chk(dalloc(&d.seg, P + 1, &d.bytes))) break;
         if (!chk(dalloc(&d.grid_d, d.a, &d.bytes))) break;
@@ -278,20 +344,21 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         if (ds->keep_fp32) {
             if (!chk(dalloc(&d.vec32, (size_t)n * d.d4 / 4, &d.bytes))) break;
         }
-        if (!chk(dalloc(&vtmp, (size_t)n * d.dim, &dummy))) break;
-        std::vector<float> rows((size_t)std::min<uint32_t>(n, 65536) * d.dim);
-        const uint32_t chunk = std::min<uint32_t>(n, 65536);
-        for (uint32_t p0 = 0; p0 < n && st == GF_OK; p0 += chunk) {
-            uint32_t cnt = std::min(chunk, n - p0);
-            for (uint32_t r = 0; r < cnt; ++r)
-                std::memcpy(&rows[(size_t)r * d.dim], ds->vectors + (size_t)i2g[p0 + r] * d.dim,
-                            sizeof(float) * d.dim);
+        if (!chk(dalloc(&vtmp, (size_t)nrows * d.dim, &dummy))) break;
+        std::vector<float> rows((size_t)std::min<uint32_t>(std::max<uint32_t>(nrows, 1), 65536) * d.dim);
+        const uint32_t chunk = std::min<uint32_t>(std::max<uint32_t>(nrows, 1), 65536);
+        for (uint32_t p0 = 0; p0 < nrows && st == GF_OK; p0 += chunk) {
+            uint32_t cnt = std::min(chunk, nrows - p0);
+            for (uint32_t r = 0; r < cnt; ++r) {
+                const uint32_t pos = sharded ? row_pos[p0 + r] : p0 + r;
+                std::memcpy(&rows[(size_t)r * d.dim], ds->vectors + (size_t)i2g[pos] * d.dim, sizeof(float) * d.dim);
+            }
             cudaError_t e = cudaMemcpy(vtmp + (size_t)p0 * d.dim, rows.data(), sizeof(float) * cnt * d.dim,
                                        cudaMemcpyHostToDevice);
             if (e != cudaSuccess) st = cuda_fail(e, "upload vectors");
         }
         if (st != GF_OK) break;
-        launch_f2h(vtmp, n, d.dim, d.d8, d.alpha, d.vec16, 0);
+        if (nrows) launch_f2h(vtmp, nrows, d.dim, d.d8, d.alpha, d.vec16, 0);
         if (d.vec32) {
             cudaError_t e = cudaMemset2D(d.vec32, sizeof(float) * d.d4, 0, sizeof(float) * d.d4, n);
             if (e == cudaSuccess)
@@ -318,6 +385,10 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             {d.entry, d.entry_h.data(), d.entry_h.size() * 4},
             {d.centroids, centroids.data(), centroids.size() * 4},
             {d.hist, hist.data(), hist.size() * 4},
+            {d.sh_slot, sh_slot.data(), sh_slot.size() * 4},
+            {d.sh_gofs, sh_gofs.data(), sh_gofs.size() * 8},
+            {d.sh_xofs, sh_xofs.data(), sh_xofs.size() * 8},
+            {d.sh_vsh, sh_vsh.data(), sh_vsh.size() * 8},
         };
         for (auto& u : ups) {
             if (!u.dst || u.bytes == 0) continue;

@@ -53,6 +53,15 @@ struct DeviceIndex {
     bool host_graph = false;
     uint32_t* graph_h = nullptr; // pinned, n x degree positions (position order)
     uint32_t* cross_h = nullptr; // pinned, ncells x n x E: [target cell][source position][edge]
+    // shard: the device holds the vectors, graph rows and cross blocks of shard_cells only
+    // (compact, in shard order); positions, attributes and ids stay global
+    bool sharded = false;
+    std::vector<uint32_t> shard_cells;
+    uint32_t n_stored = 0;         // vector / graph rows held
+    int32_t* sh_slot = nullptr;    // ncells: shard slot of each cell, -1 = not held
+    long long* sh_gofs = nullptr;  // per slot: graph element offset of the cell's first row
+    long long* sh_xofs = nullptr;  // slot x slot: cross block offset [target][source]
+    long long* sh_vsh = nullptr;   // per slot: vector row - position
     uint32_t* i2g = nullptr;     // position -> global id
     uint32_t* seg = nullptr;     // ncells + 1
     uint32_t* grid_d = nullptr;  // a
@@ -94,6 +103,8 @@ struct Plan {
     void* io = nullptr;
     size_t io_bytes = 0;
     BatchState* batch = nullptr;  // created by the first gf_search_batched
+    unsigned long long* run = nullptr;  // running keys of searches on a shard index
+    size_t run_cap = 0;
 };
 
 }  // namespace gf
@@ -117,12 +128,14 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
 // cross-edge rows may lie anywhere in device memory (batched and out-of-core search).
 // Row of position pos (cell c, slot b = slot[c]): graph + gofs[b] + (pos - seg[c]) * R.
 // Cross edges of source pos (cell s) toward cell t: cross + xofs[slot[t] * nslots +
-// slot[s]] + (pos - seg[s]) * xstride.  Each query's results are merged into run[q]
+// slot[s]] + (pos - seg[s]) * xstride.  Vector rows: pos + vsh[slot[c]].
+// Each query's results are merged into run[q]
 // (k keys, sorted) instead of being written as ids.
 struct CellView {
     const int32_t* slot = nullptr;    // device, ncells; -1 = cell not searched
     const long long* gofs = nullptr;  // device, nslots
     const long long* xofs = nullptr;  // device, nslots x nslots
+    const long long* vsh = nullptr;   // device, nslots: vector row = pos + vsh[slot] (NULL: pos)
     const uint32_t* graph = nullptr;
     const uint32_t* cross = nullptr;
     uint32_t nslots = 0, xstride = 0;
@@ -131,6 +144,7 @@ struct CellView {
 };
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
                  cudaStream_t s, const CellView* view = nullptr);
+CellView shard_view(const DeviceIndex& d);
 // run keys -> ids (via position -> global id) and distances
 gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t total, uint32_t* ids, float* dist,
                      cudaStream_t s);

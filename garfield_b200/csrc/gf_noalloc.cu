@@ -80,6 +80,7 @@ extern "C" gf_status gf_search_noalloc(gf_index* idx, const float* queries, cons
     if (qnum == 0) return GF_OK;
     if (!queries || !lb || !rb || !ids_out) return fail(GF_ERR_ARG, "null argument");
     DeviceIndex& d = idx->d;
+    if (d.sharded || d.host_graph) return fail(GF_ERR_STATE, "gf_search_noalloc needs a whole device-resident index");
     DeviceGuard3 guard(d.device);
     unsigned char* scratch = nullptr;
     gf_status st = scratch_address(d.device, &scratch);

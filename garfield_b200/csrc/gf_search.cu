@@ -50,6 +50,7 @@ struct SArgs {
     const int32_t* __restrict__ slot;
     const long long* __restrict__ gofs;
     const long long* __restrict__ xofs;
+    const long long* __restrict__ vsh;  // per slot: vector row = position + vsh (NULL: 0)
     unsigned long long* run;
     uint32_t nslots, xstride;
     uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
@@ -117,7 +118,7 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 // Kept out of line: one copy of the distance loop and sort network serves the entry
 // set, the beam rounds, the hop and the exact route.
 template <int NCH>
-__device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr) {
+__device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr, long long vsh) {
     const W w{base, 0u, 0u};
     const uint32_t lane = lane_id();
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
@@ -134,7 +135,7 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         for (uint32_t e = lane; e < total; e += 32) {
             const uint32_t r = e / nch, c = e - r * nch;
             const uint32_t pos = P[r0 + r];
-            cp_async16(stage + (size_t)r * nch16 + stage_slot(c, r), A.vec16 + (size_t)pos * nch + c);
+            cp_async16(stage + (size_t)r * nch16 + stage_slot(c, r), A.vec16 + (pos + vsh) * nch + c);
         }
         bool inr = false;
         uint32_t pos = 0;
@@ -242,6 +243,11 @@ __device__ __noinline__ void emit(const SArgs& A, uint32_t q, const key_t* res, 
     for (uint32_t i = lane; i < A.K; i += 32) rq[i] = tb[i];
 }
 
+// Row offset of a cell's stored vectors: row = position + cell_vsh.
+__device__ __forceinline__ long long cell_vsh(const SArgs& A, uint32_t cell) {
+    return A.vsh ? A.vsh[A.slot[cell]] : 0ll;
+}
+
 // Index in cl[0..nc) of the first cell at or after ci that this launch searches.
 __device__ __forceinline__ uint32_t next_cell(const SArgs& A, const uint32_t* cl, uint32_t nc, uint32_t ci) {
     if (A.slot)
@@ -289,13 +295,14 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
     for (uint32_t ci = next_cell(A, cl, nc, 0); ci < nc;) {
         const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
         const uint32_t cn = next_cell(A, cl, nc, ci + 1);
+        const long long vsh = cell_vsh(A, cell);
         for (uint32_t x0 = lo; x0 < hi; x0 += 32) {
             const uint32_t x = x0 + lane;
             append(w.P(A), nb, x < hi && in_box(A.attrs, x, A.a, w.lb(A), w.rb(A)), x);
-            const bool last = (cn == nc) && (x0 + 32 >= hi);
+            const bool last = x0 + 32 >= hi;  // batches never span cells (rows are per cell)
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
-                const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.K - 1]);
+                const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.K - 1], vsh);
                 ndist += nb;
                 merge_step(A, w, A.K, 0, ns, false);
                 nb = 0;
@@ -356,7 +363,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         nf -= take;
     }
     __syncwarp();
-    eval_sort<NCH>(A, w.base, nb, kEmptyKey);
+    eval_sort<NCH>(A, w.base, nb, kEmptyKey, cell_vsh(A, next));
     st_dist += nb;
     const uint32_t ne = min(nb, A.n_entry);
     const uint32_t nm = min(nb - ne, kHopSlots);
@@ -455,12 +462,13 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_sort<NCH>(A, w.base, nb, kEmptyKey);
+                    eval_sort<NCH>(A, w.base, nb, kEmptyKey, cell_vsh(A, cell));
                     st_dist += nb;
                 }
                 for (uint32_t ci = c0; ci < nc;) {
                     const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
                     const long long gbase = graph_base(A, cell, lo);
+                    const long long vsh = cell_vsh(A, cell);
                     // (a) entry set -> T, with recycling
                     merge_step(A, w, A.L, 0, nb, true);
                     // (b) beam rounds: expand the first W unexplored entries of T
@@ -508,7 +516,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                         }
                         hcount += nb;
                         if (nb == 0) continue;
-                        const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.L - 1]);
+                        const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.L - 1], vsh);
                         st_dist += nb;
                         merge_step(A, w, A.L, 0, ns, true);
                     }
@@ -570,6 +578,32 @@ __global__ void run_to_ids_kernel(const unsigned long long* __restrict__ run, ui
     if (dist) dist[i] = k == kEmptyKey ? kInf : key_dist(k);
 }
 
+// k-way merge of per-shard result keys: keys[(g * qnum + q) * k + i], each list sorted and
+// the lists disjoint; one warp per query ranks every key against all lists.
+__global__ void merge_lists_kernel(const unsigned long long* __restrict__ keys, uint32_t lists, uint32_t qnum,
+                                   uint32_t k, const uint32_t* __restrict__ i2g, uint32_t* ids, float* dist) {
+    const uint32_t q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (q >= qnum) return;
+    const uint32_t lane = lane_id();
+    for (uint32_t i = lane; i < k; i += 32) {
+        ids[(size_t)q * k + i] = kEmpty;
+        if (dist) dist[(size_t)q * k + i] = kInf;
+    }
+    __syncwarp();
+    for (uint32_t j = lane; j < lists * k; j += 32) {
+        const uint32_t g = j / k, i = j - g * k;
+        const key_t x = keys[((size_t)g * qnum + q) * k + i];
+        if (x == kEmptyKey) continue;
+        uint32_t rank = i;
+        for (uint32_t h = 0; h < lists && rank < k; ++h)
+            if (h != g) rank += keys_below(keys + ((size_t)h * qnum + q) * k, k, x);
+        if (rank < k) {
+            ids[(size_t)q * k + rank] = i2g[key_pos(x)];
+            if (dist) dist[(size_t)q * k + rank] = key_dist(x);
+        }
+    }
+}
+
 typedef void (*KernelFn)(const SArgs);
 
 // Row lengths compiled with a fixed chunk count (d8 / 8); others use the generic kernel.
@@ -587,6 +621,19 @@ KernelFn pick_kernel(uint32_t nch) {
 
 }  // namespace
 
+CellView shard_view(const DeviceIndex& d) {
+    CellView v;
+    v.slot = d.sh_slot;
+    v.gofs = d.sh_gofs;
+    v.xofs = d.sh_xofs;
+    v.vsh = d.sh_vsh;
+    v.graph = d.graph;
+    v.cross = d.cross;
+    v.nslots = (uint32_t)d.shard_cells.size();
+    v.xstride = d.E;
+    return v;
+}
+
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
                  cudaStream_t s, const CellView* view) {
     DeviceIndex& d = idx->d;
@@ -601,6 +648,24 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t n_entry = P.n_entry ? P.n_entry : d.degree;
     n_entry = std::min<uint32_t>(n_entry, (uint32_t)d.entry_h.size());
     if (!ids && !(view && view->run)) return fail(GF_ERR_ARG, "null ids_out");
+    if (!view && d.sharded) {
+        // a shard: search its cells through its view, merge into the plan's running keys
+        const size_t need = (size_t)p.qnum * P.k;
+        if (need > p.run_cap) {
+            GF_CUDA(cudaStreamSynchronize(s));
+            if (p.run) cudaFree(p.run);
+            p.run = nullptr;
+            p.run_cap = 0;
+            GF_CUDA(cudaMalloc((void**)&p.run, std::max<size_t>(need, 1) * 8));
+            p.run_cap = need;
+        }
+        CellView v = shard_view(d);
+        v.run = p.run;
+        GF_CUDA(cudaMemsetAsync(p.run, 0xFF, need * 8, s));
+        gf_status st = search(idx, plan, &P, nullptr, nullptr, s, &v);
+        if (st != GF_OK) return st;
+        return finish_run(idx, p.run, (uint32_t)need, ids, dist, s);
+    }
     if (!view && d.host_graph)
         return fail(GF_ERR_STATE, "the index keeps its graphs in host memory: search it with gf_search_batched");
     if (p.qnum == 0) return GF_OK;
@@ -613,6 +678,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.slot = view ? view->slot : nullptr;
     A.gofs = view ? view->gofs : nullptr;
     A.xofs = view ? view->xofs : nullptr;
+    A.vsh = view ? view->vsh : nullptr;
     A.run = view ? view->run : nullptr;
     A.nslots = view ? view->nslots : 0;
     A.xstride = view ? view->xstride : 0;
@@ -699,3 +765,54 @@ gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t tota
 }
 
 }  // namespace gf
+
+using namespace gf;
+
+extern "C" gf_status gf_search_keys(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint64_t* keys_out,
+                                    void* stream) {
+    if (!idx || !plan || plan->p.idx != idx) return fail(GF_ERR_ARG, "plan does not belong to this index");
+    if (!keys_out) return fail(GF_ERR_ARG, "null keys_out");
+    DeviceIndex& d = idx->d;
+    if (d.host_graph) return fail(GF_ERR_STATE, "the index keeps its graphs in host memory");
+    if (!plan->p.planned) return fail(GF_ERR_STATE, "gf_search_keys before gf_plan_queries");
+    gf_search_params P;
+    gf_search_defaults(&P);
+    if (params) P = *params;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d.device);
+    CellView v;
+    if (d.sharded) {
+        v = shard_view(d);
+    } else {
+        v.graph = d.graph;
+        v.cross = d.cross;
+    }
+    v.run = reinterpret_cast<unsigned long long*>(keys_out);
+    const cudaStream_t s = (cudaStream_t)stream;
+    gf_status st = GF_OK;
+    cudaError_t e = cudaMemsetAsync(keys_out, 0xFF, (size_t)plan->p.qnum * P.k * 8, s);
+    if (e != cudaSuccess)
+        st = cuda_fail(e, "gf_search_keys");
+    else
+        st = gf::search(idx, plan, &P, nullptr, nullptr, s, &v);
+    if (prev >= 0) cudaSetDevice(prev);
+    return st;
+}
+
+extern "C" gf_status gf_merge_keys(gf_index* idx, const uint64_t* keys, uint32_t n_lists, uint32_t qnum, uint32_t k,
+                                   uint32_t* ids_out, float* dist_out, void* stream) {
+    if (!idx) return fail(GF_ERR_ARG, "null index");
+    if (qnum == 0) return GF_OK;
+    if (!keys || !ids_out || n_lists == 0 || k == 0) return fail(GF_ERR_ARG, "null argument or zero size");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(idx->d.device);
+    const uint32_t warps = 4;
+    merge_lists_kernel<<<(qnum + warps - 1) / warps, 32 * warps, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const unsigned long long*>(keys), n_lists, qnum, k, idx->d.i2g, ids_out, dist_out);
+    cudaError_t e = cudaGetLastError();
+    if (prev >= 0) cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "gf_merge_keys");
+    return GF_OK;
+}

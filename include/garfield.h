@@ -71,6 +71,13 @@ typedef struct {
                               copy them to the device per batch of cells (gf_search_batched;
                               the dataset-resident out-of-core mode of
                               big_dataset_adapterV3.cuh:3321) */
+    const uint32_t* shard_cells; /* host, or NULL: build a shard holding only these cells'
+                              vectors, graph rows and the cross edges among them (cell
+                              sharding over GPUs).  Positions, attributes, ids, the planner
+                              data and the entry sequence stay those of the whole index, so
+                              shard results merge by (distance, position) (gf_search_keys,
+                              gf_merge_keys).  Not with host_graph or keep_fp32. */
+    uint32_t n_shard_cells;
 } gf_index_desc;
 
 /* Paths of the reference's index files (realdataset_search flags, README.md:101-170). */
@@ -213,6 +220,26 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
 gf_status gf_search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* params,
                             const uint32_t* batch_cells, const uint32_t* batch_sizes, uint32_t n_batches,
                             uint32_t* ids_out, float* dist_out, void* stream);
+
+/*
+ * Search whose results are merge keys instead of ids: keys_out (device, qnum x k) gets each
+ * query's k best as (float bits of the distance << 32) | (position << 2) | flags, sorted
+ * ascending, 0xFFFFFFFFFFFFFFFF for "none"; positions are cell-major over the whole index.
+ * For a shard index (gf_index_desc.shard_cells) these are the results among the shard's
+ * cells; the shards' lists are then exchanged (an all-gather) and merged by gf_merge_keys,
+ * the merge step of cell-sharded search over GPUs.  The reference has no multi-GPU path.
+ */
+gf_status gf_search_keys(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint64_t* keys_out,
+                         void* stream);
+
+/*
+ * k-way merge of n_lists disjoint sorted key lists per query (device keys laid out
+ * [list][query][k], as gathered from gf_search_keys) into the k best ids and distances
+ * (device, qnum x k; dist_out may be NULL).  One warp per query ranks every key against
+ * the other lists by binary search.
+ */
+gf_status gf_merge_keys(gf_index* idx, const uint64_t* keys, uint32_t n_lists, uint32_t qnum, uint32_t k,
+                        uint32_t* ids_out, float* dist_out, void* stream);
 
 /*
  * Batches of at most max_cells cells for gf_search_batched, grouped so that few queries

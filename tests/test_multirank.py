@@ -58,3 +58,73 @@ def test_two_gloo_ranks_match_single_process(tmp_path):
     port = 29500 + (os.getpid() % 1000)
     mp.spawn(_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     assert bool(np.load(tmp_path / "ok.npy")[0])
+
+
+def test_shard_cells_tile_grid():
+    from garfield_b200.dist import shard_cells
+    for grid in ((4, 4), (2, 2, 2), (16,), (3, 5)):
+        n = int(np.prod(grid))
+        for w in (1, 2, 3, 4, 8):
+            if w > n:
+                continue
+            sh = shard_cells(grid, w)
+            assert len(sh) == w and sorted(x for s in sh for x in s) == list(range(n))
+            sizes = [len(s) for s in sh]
+            if n % w == 0 and (n & (n - 1)) == 0:
+                assert len(set(sizes)) == 1  # power-of-two grids split evenly
+    # 4x4 over 4 ranks: the four 2x2 blocks
+    assert shard_cells((4, 4), 4) == [[0, 1, 4, 5], [2, 3, 6, 7], [8, 9, 12, 13], [10, 11, 14, 15]]
+    with pytest.raises(ValueError):
+        shard_cells((2, 2), 5)
+
+
+def _positions(cell_of):
+    order = np.lexsort((np.arange(len(cell_of)), cell_of))
+    pos = np.empty(len(cell_of), np.uint64)
+    pos[order] = np.arange(len(cell_of), dtype=np.uint64)
+    return pos
+
+
+def _keys(ids, dist, pos_of):
+    keys = np.full(ids.shape, np.uint64(0xFFFFFFFFFFFFFFFF), np.uint64)
+    ok = ids != 0xFFFFFFFF
+    bits = dist.astype(np.float32).view(np.uint32).astype(np.uint64)
+    keys[ok] = (bits[ok] << np.uint64(32)) | (pos_of[ids[ok]] << np.uint64(2))
+    return keys
+
+
+def _shard_worker(rank, world, port, out_dir):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    sys.path.insert(0, str(ROOT / "tests"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import oracle
+    from conftest import Case
+    from garfield_b200.dist import exchange_keys, merge_keys_host, shard_cells
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    c = Case(6000, 32, 20, 101, (2, 2), 0.2, R=16, E=2, C=20, seed=9)
+    ent = c.entry(16)
+    shards = shard_cells(c.ix.grid, world)
+    args = (c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts, c.offsets, c.cells, ent)
+    ids, d, _ = oracle.search(*args, L=32, K=10, threads=1, batches=[shards[rank]])
+    pos_of = _positions(c.ix.cell_of)
+    mine = torch.from_numpy(_keys(ids, d, pos_of).view(np.int64))
+    allk = exchange_keys(mine).numpy().view(np.uint64)
+    merged = merge_keys_host(allk, 10)
+    if rank == 0:
+        # the merge of the shards' results is the batched search with the shards as batches
+        ref_ids, ref_d, _ = oracle.search(*args, L=32, K=10, threads=1, batches=shards)
+        ok = np.array_equal(merged, _keys(ref_ids, ref_d, pos_of))
+        np.save(os.path.join(out_dir, "ok.npy"), np.array([ok]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_cell_sharded(tmp_path):
+    import torch.multiprocessing as mp
+    port = 30500 + (os.getpid() % 1000)
+    mp.spawn(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    assert bool(np.load(tmp_path / "ok.npy")[0])
