@@ -50,6 +50,8 @@ class _IndexDesc(C.Structure):
         ("cross", C.c_void_p), ("n_clusters", C.c_uint32), ("labels", C.c_void_p),
         ("f2h_factor", C.c_float), ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32),
         ("shard_cells", C.c_void_p), ("n_shard_cells", C.c_uint32),
+        ("codec", C.c_uint32), ("codes", C.c_void_p), ("code_scales", C.c_void_p),
+        ("code_zero_points", C.c_void_p),
     ]
 
 
@@ -58,7 +60,8 @@ class _IndexFiles(C.Structure):
         ("data_path", C.c_char_p), ("cagra_prefix", C.c_char_p), ("cagra_suffix", C.c_char_p),
         ("global_graph", C.c_char_p), ("grid", C.c_char_p), ("attrs", C.c_char_p),
         ("cluster", C.c_char_p), ("degree", C.c_uint32), ("f2h_factor", C.c_float),
-        ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32), ("uniform_dims", C.c_uint32),
+        ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32), ("codec", C.c_uint32),
+        ("quantized", C.c_char_p), ("uniform_dims", C.c_uint32),
         ("uniform_shape", C.c_void_p),
         ("uniform_lo", C.c_float), ("uniform_hi", C.c_float),
     ]
@@ -122,6 +125,10 @@ def lib() -> C.CDLL:
         "gf_write_fvecs": (C.c_int, [C.c_char_p, _P, _U32, _U32]),
         "gf_read_u8bin": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
         "gf_read_attrs": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
+        "gf_read_q": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_P), _PTR(_P), _PTR(_U32), _PTR(_U32)]),
+        "gf_write_q": (C.c_int, [C.c_char_p, _P, _P, _P, _U32, _U32]),
+        "gf_quantize_i8": (C.c_int, [_P, _U32, _U32, C.c_float, _P, _P, _P, _P]),
+        "gf_quantize_i8_host": (C.c_int, [_P, _U32, _U32, C.c_float, _P, _P, _P]),
         "gf_write_attrs": (C.c_int, [C.c_char_p, _P, _U32, _U32]),
         "gf_read_u32mat": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
         "gf_write_u32mat": (C.c_int, [C.c_char_p, _P, _U32, _U32]),
@@ -202,7 +209,7 @@ class Index:
     @classmethod
     def create(cls, *, vectors, attrs, grid, l_quant, r_quant, cell_of, graphs, degree, cross=None,
                cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, host_graph=False, shard_cells=None,
-               device=0) -> "Index":
+               codec=0, codes=None, code_scales=None, code_zero_points=None, device=0) -> "Index":
         """Build from host arrays in the reference's layout (see gf_index_desc).  With
         host_graph the graphs and cross edges stay in pinned host memory (search with
         Plan.search_batched); with shard_cells the device holds only those cells (a shard
@@ -231,6 +238,20 @@ class Index:
             shard = np.ascontiguousarray(shard_cells, dtype=np.uint32)
             d.shard_cells, d.n_shard_cells = _np_ptr(shard), len(shard)
             d.keep_fp32 = 0
+        d.codec = codec
+        keep = []
+        if codes is not None:
+            codes = np.ascontiguousarray(codes).view(np.uint8)
+            keep.append(codes)
+            d.codes = _np_ptr(codes)
+        if code_scales is not None:
+            code_scales = np.ascontiguousarray(code_scales, dtype=np.float32)
+            keep.append(code_scales)
+            d.code_scales = _np_ptr(code_scales)
+        if code_zero_points is not None:
+            code_zero_points = np.ascontiguousarray(code_zero_points, dtype=np.int32)
+            keep.append(code_zero_points)
+            d.code_zero_points = _np_ptr(code_zero_points)
         h = C.c_void_p()
         _check(lib().gf_index_create(C.byref(d), device, C.byref(h)), "gf_index_create")
         return cls(h)
@@ -238,7 +259,7 @@ class Index:
     @classmethod
     def open(cls, *, data_path, cagra_prefix, cagra_suffix, global_graph, grid=None, attrs, cluster=None,
              degree=32, f2h_factor=1.0, keep_fp32=False, device=0, uniform_shape=None, uniform_lo=0.0,
-             uniform_hi=1e6, host_graph=False) -> "Index":
+             uniform_hi=1e6, host_graph=False, codec=0, quantized=None) -> "Index":
         """Load the reference's index files (realdataset_search flags).  Without a grid file,
         `uniform_shape` gives the uniform grid of normaldataset_search."""
         f = _IndexFiles()
@@ -249,6 +270,8 @@ class Index:
         f.cluster = None if cluster is None else str(cluster).encode()
         f.degree, f.f2h_factor, f.keep_fp32 = degree, f2h_factor, 1 if keep_fp32 else 0
         f.host_graph = 1 if host_graph else 0
+        f.codec = codec
+        f.quantized = None if quantized is None else str(quantized).encode()
         shape = None
         if uniform_shape is not None:
             shape = np.ascontiguousarray(uniform_shape, dtype=np.uint32)
@@ -445,6 +468,47 @@ def schedule_batches(ncells: int, counts, offsets, cells, max_cells: int):
                                           max_cells, _np_ptr(bc), _np_ptr(bs), C.byref(nb), C.byref(splits)),
            "gf_schedule_batches_host")
     return _unpack_batches(bc, bs, nb.value), int(splits.value)
+
+
+def quantize_i8_host(data: np.ndarray, alpha: float = 1.0):
+    """gf_quantize_i8_host: (codes int8 n x dim, scales, zero points)."""
+    data = np.ascontiguousarray(data, dtype=np.float32)
+    n, dim = data.shape
+    q = np.zeros((n, dim), np.int8)
+    sc, zp = np.zeros(dim, np.float32), np.zeros(dim, np.int32)
+    _check(lib().gf_quantize_i8_host(_np_ptr(data), n, dim, alpha, _np_ptr(q), _np_ptr(sc), _np_ptr(zp)),
+           "gf_quantize_i8_host")
+    return q, sc, zp
+
+
+def quantize_i8(data, alpha: float = 1.0, stream=None):
+    """gf_quantize_i8 on a CUDA tensor: (codes int8, scales, zero points) CUDA tensors."""
+    import torch
+    n, dim = data.shape
+    q = torch.empty((n, dim), dtype=torch.int8, device=data.device)
+    sc = torch.empty(dim, dtype=torch.float32, device=data.device)
+    zp = torch.empty(dim, dtype=torch.int32, device=data.device)
+    _check(lib().gf_quantize_i8(_dev_ptr(data), n, dim, alpha, _dev_ptr(q), _dev_ptr(sc), _dev_ptr(zp),
+                                _stream_ptr(stream)), "gf_quantize_i8")
+    return q, sc, zp
+
+
+def read_q(path):
+    """.q file -> (codes int8 n x dim, scales, zero points)."""
+    q, sc, zp = _P(), _P(), _P()
+    n, d = _U32(), _U32()
+    _check(lib().gf_read_q(str(path).encode(), C.byref(q), C.byref(sc), C.byref(zp), C.byref(n), C.byref(d)),
+           "gf_read_q")
+    codes = _take(q, n.value * d.value, np.int8).reshape(n.value, d.value)
+    return codes, _take(sc, d.value, np.float32), _take(zp, d.value, np.int32)
+
+
+def write_q(path, codes, scales, zero_points) -> None:
+    codes = np.ascontiguousarray(codes, dtype=np.int8)
+    sc = np.ascontiguousarray(scales, dtype=np.float32)
+    zp = np.ascontiguousarray(zero_points, dtype=np.int32)
+    _check(lib().gf_write_q(str(path).encode(), _np_ptr(codes), _np_ptr(sc), _np_ptr(zp), codes.shape[0],
+                            codes.shape[1]), "gf_write_q")
 
 
 def _take(ptr: C.c_void_p, count: int, dtype) -> np.ndarray:

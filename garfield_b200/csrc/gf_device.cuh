@@ -52,6 +52,11 @@ __device__ __forceinline__ f2x h2_to_f2x(uint32_t h) {
     return pack2(f.x, f.y);
 }
 
+__device__ __forceinline__ f2x mul2(f2x a, f2x b) {
+    f2x r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
 __device__ __forceinline__ f2x add2(f2x a, f2x b) {
     f2x r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -91,6 +96,39 @@ __device__ __forceinline__ float dist16_staged(const uint4* srow, const f2x* q2,
         p3 = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), p3);
     }
     return finish8(p0, p1, p2, p3);
+}
+
+// Byte element e (0..3) of w as the float 2^23 + byte (exact): the byte is placed under
+// the exponent bits of 2^23 with one byte permute.
+__device__ __forceinline__ float byte_f23(uint32_t w, uint32_t e) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | e));
+}
+
+// Canonical squared distance (oracle orc_dist8) of a byte row staged in shared memory
+// (nch chunks of 16 bytes, swizzled by stage_slot with key r): element i decodes to
+// x^ = scale[i] * (byte ^ xmask - bias[i]), computed as ((2^23 + byte) - (2^23 + bias))
+// * scale with the exact integer difference; diff = q[i] - x^; partial i mod 8.  q2, s2,
+// b2: the query, scales and 2^23 + bias as fp32 pairs.
+template <int NCH>
+__device__ __forceinline__ float dist8_staged(const uint4* srow, const f2x* q2, const f2x* s2, const f2x* b2,
+                                              uint32_t xmask, uint32_t nch_rt, uint32_t r) {
+    const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
+    const uint32_t key = r & 15u;
+    f2x p[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll 2
+    for (uint32_t c = 0; c < nch; ++c) {
+        const uint4 x = srow[c ^ key];
+        const uint32_t w[4] = {x.x ^ xmask, x.y ^ xmask, x.z ^ xmask, x.w ^ xmask};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // element pairs 2j, 2j+1 of the chunk -> partial pair j % 4
+            const uint32_t word = w[j >> 1], e = (j & 1) * 2;
+            const f2x u = pack2(byte_f23(word, e), byte_f23(word, e + 1));
+            const uint32_t k = c * 8 + j;  // pair index in the row
+            const f2x xh = mul2(sub2(u, b2[k]), s2[k]);
+            p[j & 3] = sqacc2(sub2(q2[k], xh), p[j & 3]);
+        }
+    }
+    return finish8(p[0], p[1], p[2], p[3]);
 }
 
 // Canonical fp32 squared distance (oracle orc_dist32) of a global row of nch float4

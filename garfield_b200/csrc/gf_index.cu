@@ -75,7 +75,7 @@ static gf_status dalloc(T** p, size_t count, uint64_t* bytes) {
 static void free_index(DeviceIndex& d) {
     void* ptrs[] = {d.vec16,   d.vec32,   d.attrs,     d.graph,   d.cross,   d.i2g,     d.seg,
                     d.grid_d,  d.lq_d,    d.rq_d,      d.centroids, d.hist,  d.entry,   d.sh_slot,
-                    d.sh_gofs, d.sh_xofs, d.sh_vsh};
+                    d.sh_gofs, d.sh_xofs, d.sh_vsh,    d.vec8,      d.csc,   d.cbi};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);
@@ -114,6 +114,10 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     if (ds->cross_e > 4) return fail(GF_ERR_ARG, "cross_e must be 0..4");
     if (ds->cross_e && !ds->cross) return fail(GF_ERR_ARG, "missing cross edges");
     const bool sharded = ds->shard_cells && ds->n_shard_cells;
+    if (ds->codec > 2) return fail(GF_ERR_ARG, "codec must be 0 (fp16), 1 (int8) or 2 (uint8)");
+    if (ds->codec == 2 && !ds->codes) return fail(GF_ERR_ARG, "uint8 codec needs codes");
+    if (ds->codec == 1 && ds->codes && (!ds->code_scales || !ds->code_zero_points))
+        return fail(GF_ERR_ARG, "int8 codes need their scales and zero points");
     if (sharded && (ds->host_graph || ds->keep_fp32))
         return fail(GF_ERR_ARG, "a shard cannot keep host graphs or fp32 vectors");
     uint64_t ncells = 1, nq = 0;
@@ -171,6 +175,20 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     d.entry_h = make_entry(std::max<uint32_t>(R, 64), d.min_cell);
     d.host_graph = ds->host_graph != 0;
     d.n_stored = n;
+    d.codec = ds->codec;
+    d.d16 = (d.dim + 15) / 16 * 16;
+    std::vector<int8_t> qcodes;  // int8 codes quantised here (global order)
+    if (d.codec) {
+        d.scales_h.assign(d.dim, 0.01f);
+        d.zps_h.assign(d.dim, 0);
+        if (d.codec == 1 && !ds->codes) {
+            qcodes.resize((size_t)n * d.dim);
+            quantize_i8_host(ds->vectors, n, d.dim, d.alpha, qcodes.data(), d.scales_h.data(), d.zps_h.data());
+        } else {
+            if (ds->code_scales) d.scales_h.assign(ds->code_scales, ds->code_scales + d.dim);
+            if (ds->code_zero_points) d.zps_h.assign(ds->code_zero_points, ds->code_zero_points + d.dim);
+        }
+    }
 
     // Graph rows are already in position order; local ids -> positions.  Cross edges:
     // source-major (position, target cell, edge) on the device; with host_graph,
@@ -319,7 +337,31 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     float* vtmp = nullptr;
     do {
         const uint32_t nrows = sharded ? d.n_stored : n;
-        if (!chk(dalloc(&d.vec16, (size_t)nrows * d.d8 / 8, &d.bytes))) break;
+        if (!d.codec && !chk(dalloc(&d.vec16, (size_t)nrows * d.d8 / 8, &d.bytes))) break;
+        if (d.codec) {
+            if (!chk(dalloc(&d.vec8, (size_t)nrows * d.d16 / 16, &d.bytes))) break;
+            if (!chk(dalloc(&d.csc, d.d16, &d.bytes))) break;
+            if (!chk(dalloc(&d.cbi, d.d16, &d.bytes))) break;
+            // byte rows in stored order, zero padded; scale 0 past dim decodes padding to 0
+            const uint8_t* codes = ds->codes ? ds->codes : reinterpret_cast<const uint8_t*>(qcodes.data());
+            std::vector<uint8_t> rows8((size_t)nrows * d.d16, 0);
+            for (size_t r = 0; r < nrows; ++r) {
+                const uint32_t pos = sharded ? row_pos[r] : (uint32_t)r;
+                std::memcpy(&rows8[r * d.d16], codes + (size_t)i2g[pos] * d.dim, d.dim);
+            }
+            std::vector<float> sc(d.d16, 0.0f), bi(d.d16, 8388608.0f);
+            for (uint32_t j = 0; j < d.dim; ++j) {
+                sc[j] = d.scales_h[j];
+                bi[j] = 8388608.0f + (float)(d.zps_h[j] + (d.codec == 1 ? 128 : 0));
+            }
+            cudaError_t e = cudaMemcpy(d.vec8, rows8.data(), rows8.size(), cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) e = cudaMemcpy(d.csc, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) e = cudaMemcpy(d.cbi, bi.data(), bi.size() * 4, cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                st = cuda_fail(e, "upload byte rows");
+                break;
+            }
+        }
         if (!chk(dalloc(&d.attrs, (size_t)n * d.a, &d.bytes))) break;
         if (!d.host_graph && !chk(dalloc(&d.graph, graph.size(), &d.bytes))) break;
         if (!d.host_graph && E && !chk(dalloc(&d.cross, cross.size(), &d.bytes))) break;
@@ -344,10 +386,11 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         if (ds->keep_fp32) {
             if (!chk(dalloc(&d.vec32, (size_t)n * d.d4 / 4, &d.bytes))) break;
         }
-        if (!chk(dalloc(&vtmp, (size_t)nrows * d.dim, &dummy))) break;
+        const bool need_f32 = !d.codec || d.vec32;  // fp16 conversion or kept fp32 rows
+        if (need_f32 && !chk(dalloc(&vtmp, (size_t)nrows * d.dim, &dummy))) break;
         std::vector<float> rows((size_t)std::min<uint32_t>(std::max<uint32_t>(nrows, 1), 65536) * d.dim);
         const uint32_t chunk = std::min<uint32_t>(std::max<uint32_t>(nrows, 1), 65536);
-        for (uint32_t p0 = 0; p0 < nrows && st == GF_OK; p0 += chunk) {
+        for (uint32_t p0 = 0; need_f32 && p0 < nrows && st == GF_OK; p0 += chunk) {
             uint32_t cnt = std::min(chunk, nrows - p0);
             for (uint32_t r = 0; r < cnt; ++r) {
                 const uint32_t pos = sharded ? row_pos[p0 + r] : p0 + r;
@@ -358,7 +401,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             if (e != cudaSuccess) st = cuda_fail(e, "upload vectors");
         }
         if (st != GF_OK) break;
-        if (nrows) launch_f2h(vtmp, nrows, d.dim, d.d8, d.alpha, d.vec16, 0);
+        if (nrows && !d.codec) launch_f2h(vtmp, nrows, d.dim, d.d8, d.alpha, d.vec16, 0);
         if (d.vec32) {
             cudaError_t e = cudaMemset2D(d.vec32, sizeof(float) * d.d4, 0, sizeof(float) * d.d4, n);
             if (e == cudaSuccess)

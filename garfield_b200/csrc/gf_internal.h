@@ -43,7 +43,14 @@ struct DeviceIndex {
     std::vector<uint32_t> entry_h;    // deterministic entry local ids
     uint64_t bytes = 0;
     // device arrays
-    uint4* vec16 = nullptr;      // n x d8 halves (alpha-scaled), as 16-byte chunks
+    uint4* vec16 = nullptr;      // n x d8 halves (alpha-scaled), as 16-byte chunks (codec 0)
+    // byte codecs (codec 1 = int8, 2 = uint8): rows of d16 bytes, decoded scale * (q - zp)
+    uint32_t codec = 0, d16 = 0;
+    uint4* vec8 = nullptr;       // rows x d16 bytes
+    float* csc = nullptr;        // d16 per-element scale (0 past dim)
+    float* cbi = nullptr;        // d16 per-element 2^23 + bias (bias = zp + 128 for int8, zp for uint8)
+    std::vector<float> scales_h; // dim
+    std::vector<int32_t> zps_h;  // dim
     float4* vec32 = nullptr;     // n x d4 fp32 (optional)
     float* attrs = nullptr;      // n x a
     uint32_t* graph = nullptr;   // n x degree positions (NULL when host_graph)
@@ -151,6 +158,9 @@ gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t tota
 // gf_bruteforce.cu
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
                      uint32_t k, uint32_t* ids, float* dist, cudaStream_t s);
+// gf_codec.cu
+void quantize_i8_host(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q, float* scales,
+                      int32_t* zps);
 // gf_index.cu
 void launch_f2h(const float* in, uint32_t n, uint32_t dim, uint32_t d8, float alpha, uint4* out, cudaStream_t s);
 }  // namespace gf

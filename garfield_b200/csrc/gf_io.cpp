@@ -137,6 +137,52 @@ gf_status gf_read_u8bin(const char* path, uint8_t** data, uint32_t* n, uint32_t*
     return GF_OK;
 }
 
+// .q file (save_dataset_quantified / load_dataset_quantified, production_adapter.cuh:240-285):
+// uint32 n, uint32 d, d x float32 scales, d x int32 zero points, n*d int8 codes.
+gf_status gf_read_q(const char* path, int8_t** codes, float** scales, int32_t** zero_points, uint32_t* n,
+                    uint32_t* dim) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    uint32_t h[2];
+    TRY(rd(fl, h, 8, path));
+    if (h[1] == 0 || 8 + 8ll * h[1] + (long long)h[0] * h[1] != size) return fail(GF_ERR_FORMAT, ".q size mismatch");
+    float* sc = xmalloc<float>(h[1]);
+    int32_t* zp = xmalloc<int32_t>(h[1]);
+    int8_t* q = xmalloc<int8_t>(std::max<size_t>((size_t)h[0] * h[1], 1));
+    if (!sc || !zp || !q) {
+        free(sc);
+        free(zp);
+        free(q);
+        return fail(GF_ERR_OOM, "host allocation");
+    }
+    if (rd(fl, sc, 4ull * h[1], path) != GF_OK || rd(fl, zp, 4ull * h[1], path) != GF_OK ||
+        rd(fl, q, (size_t)h[0] * h[1], path) != GF_OK) {
+        free(sc);
+        free(zp);
+        free(q);
+        return GF_ERR_FORMAT;
+    }
+    *codes = q;
+    *scales = sc;
+    *zero_points = zp;
+    *n = h[0];
+    *dim = h[1];
+    return GF_OK;
+}
+
+gf_status gf_write_q(const char* path, const int8_t* codes, const float* scales, const int32_t* zero_points,
+                     uint32_t n, uint32_t dim) {
+    File fl;
+    TRY(open_write(fl, path));
+    uint32_t h[2] = {n, dim};
+    TRY(wr(fl, h, 8, path));
+    TRY(wr(fl, scales, 4ull * dim, path));
+    TRY(wr(fl, zero_points, 4ull * dim, path));
+    TRY(wr(fl, codes, (size_t)n * dim, path));
+    return GF_OK;
+}
+
 gf_status gf_read_attrs(const char* path, int32_t** attrs, uint32_t* n, uint32_t* a) {
     File fl;
     long long size;
@@ -292,8 +338,28 @@ gf_status gf_index_open(const gf_index_files* fs, int device, gf_index** out) {
     Holder hold;
     float* vec = nullptr;
     uint32_t n = 0, dim = 0;
-    TRY(gf_read_fvecs(fs->data_path, &vec, &n, &dim));
+    uint8_t* u8 = nullptr;
+    if (fs->codec == 2) {  // u8bin data (load_data_u8, tools.cuh:108-150); fp32 copy for the planner
+        TRY(gf_read_u8bin(fs->data_path, &u8, &n, &dim));
+        hold.keep(u8);
+        vec = xmalloc<float>(std::max<size_t>((size_t)n * dim, 1));
+        if (!vec) return fail(GF_ERR_OOM, "host allocation");
+        for (size_t i = 0; i < (size_t)n * dim; ++i) vec[i] = (float)u8[i];
+    } else {
+        TRY(gf_read_fvecs(fs->data_path, &vec, &n, &dim));
+    }
     hold.keep(vec);
+    int8_t* qcodes = nullptr;
+    float* qscales = nullptr;
+    int32_t* qzps = nullptr;
+    if (fs->codec == 1 && fs->quantized) {
+        uint32_t qn = 0, qd = 0;
+        TRY(gf_read_q(fs->quantized, &qcodes, &qscales, &qzps, &qn, &qd));
+        hold.keep(qcodes);
+        hold.keep(qscales);
+        hold.keep(qzps);
+        if (qn != n || qd != dim) return fail(GF_ERR_FORMAT, ".q file does not match the data file");
+    }
     int32_t* attrs_i;
     uint32_t an, aa;
     TRY(gf_read_attrs(fs->attrs, &attrs_i, &an, &aa));
@@ -402,6 +468,14 @@ gf_status gf_index_open(const gf_index_files* fs, int device, gf_index** out) {
     d.f2h_factor = fs->f2h_factor;
     d.keep_fp32 = fs->keep_fp32;
     d.host_graph = fs->host_graph;
+    d.codec = fs->codec;
+    if (fs->codec == 1 && qcodes) {
+        d.codes = reinterpret_cast<const uint8_t*>(qcodes);
+        d.code_scales = qscales;
+        d.code_zero_points = qzps;
+    } else if (fs->codec == 2) {
+        d.codes = u8;
+    }
     return gf_index_create(&d, device, out);
 }
 

@@ -27,13 +27,18 @@ using namespace dev;
 constexpr float kInf = __builtin_huge_valf();
 
 struct SArgs {
-    const uint4* __restrict__ vec16;
+    const uint4* __restrict__ vec16;  // stored rows (fp16, or bytes for the byte codecs), 16-byte chunks
     const float* __restrict__ attrs;
     const uint32_t* __restrict__ graph;
     const uint32_t* __restrict__ cross;
     const uint32_t* __restrict__ seg;
     const uint32_t* __restrict__ i2g;
     const uint4* __restrict__ q16;
+    const float* __restrict__ q32;    // fp32 queries (byte codecs: times alpha, fp32)
+    const float* __restrict__ csc;    // byte codecs: per-element scale (d16)
+    const float* __restrict__ cbi;    // byte codecs: per-element 2^23 + bias (d16)
+    float alpha;
+    uint32_t xmask, dim;
     const float* __restrict__ lb;
     const float* __restrict__ rb;
     const uint32_t* __restrict__ counts;
@@ -57,6 +62,7 @@ struct SArgs {
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, warp_words;
     // word offsets inside a warp's shared-memory slice
+    uint32_t o_sc, o_bi;  // byte codecs: scale and 2^23 + bias pairs
     uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
         o_picks, o_stage, o_hash;
 };
@@ -65,14 +71,17 @@ struct SArgs {
 // Lists hold 64-bit keys (see key_t): T and T' (L each), RL and RL' (k each), the batch B
 // and the eviction buffer E (bcap each).  Candidate positions of a batch are gathered
 // into E (as 32-bit words) before evaluation, while E is otherwise unused.
-void make_layout(SArgs& A, uint32_t nch16) {
+void make_layout(SArgs& A, uint32_t nch16, bool bytes) {
     uint32_t o = 0;
     auto take = [&](uint32_t words) {
         uint32_t r = o;
         o += (words + 3) & ~3u;
         return r;
     };
-    A.o_q = take(nch16 * 8);  // fp32 query as (even, odd) element pairs, 4 pairs per chunk
+    // fp32 query as (even, odd) element pairs: 4 pairs per fp16 chunk, 8 per byte chunk
+    A.o_q = take(nch16 * (bytes ? 16 : 8));
+    A.o_sc = bytes ? take(nch16 * 16) : 0;
+    A.o_bi = bytes ? take(nch16 * 16) : 0;
     A.o_lb = take(kMaxAttr);
     A.o_rb = take(kMaxAttr);
     A.o_t0d = take(2 * A.L);
@@ -117,7 +126,7 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 // staged row.  At most 32 survivors are sorted in registers, more in shared memory.
 // Kept out of line: one copy of the distance loop and sort network serves the entry
 // set, the beam rounds, the hop and the exact route.
-template <int NCH>
+template <int NCH, bool BYTES>
 __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr, long long vsh) {
     const W w{base, 0u, 0u};
     const uint32_t lane = lane_id();
@@ -147,7 +156,11 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         __syncwarp();
         key_t k = kEmptyKey;
         if (lane < rows) {
-            const float d = dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
+            const float d = BYTES ? dist8_staged<NCH>(stage + (size_t)lane * nch16, q2,
+                                                      reinterpret_cast<const f2x*>(w.base + A.o_sc),
+                                                      reinterpret_cast<const f2x*>(w.base + A.o_bi), A.xmask, nch,
+                                                      lane)
+                                  : dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
             k = make_key(d, pos, inr ? kKeyInRange : 0u);
         }
         const bool keep = k < thr;
@@ -283,7 +296,7 @@ __device__ __forceinline__ void append(uint32_t* P, uint32_t& nb, bool ok, uint3
 }
 
 // Exact route (gpu_graph.cu:3788-4022): every in-range point of the query's cells.
-template <int NCH>
+template <int NCH, bool BYTES>
 __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uint32_t q, const uint32_t* cl,
                                              uint32_t nc) {
     const uint32_t lane = lane_id();
@@ -302,7 +315,7 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
             const bool last = x0 + 32 >= hi;  // batches never span cells (rows are per cell)
             if (nb > flush_at || (last && nb)) {
                 __syncwarp();
-                const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.K - 1], vsh);
+                const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, w.T(A)[A.K - 1], vsh);
                 ndist += nb;
                 merge_step(A, w, A.K, 0, ns, false);
                 nb = 0;
@@ -320,7 +333,7 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
 // the next cell as filler are evaluated and sorted; the first n_entry become the next
 // entry set (left sorted in B[0..ne)), the following 64 are merged into T without
 // recycling.  Rebuilds the visited hash for the next cell.  Returns ne; adds to stats.
-template <int NCH>
+template <int NCH, bool BYTES>
 __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, uint32_t& hcount, uint32_t& st_dist,
                                            uint32_t& st_cross) {
     const uint32_t lane = lane_id();
@@ -363,7 +376,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         nf -= take;
     }
     __syncwarp();
-    eval_sort<NCH>(A, w.base, nb, kEmptyKey, cell_vsh(A, next));
+    eval_sort<NCH, BYTES>(A, w.base, nb, kEmptyKey, cell_vsh(A, next));
     st_dist += nb;
     const uint32_t ne = min(nb, A.n_entry);
     const uint32_t nm = min(nb - ne, kHopSlots);
@@ -393,7 +406,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
     return ne;
 }
 
-template <int NCH>
+template <int NCH, bool BYTES>
 __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constant__ SArgs A) {
     extern __shared__ __align__(16) uint32_t smem[];
     const uint32_t lane = lane_id();
@@ -410,13 +423,24 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
         const uint32_t* cl = A.cells + A.offsets[q];
         // query row (fp16 -> fp32 element pairs) and box
         {
-            f2x* q2 = reinterpret_cast<f2x*>(base + A.o_q);
-            for (uint32_t c = lane; c < nch; c += 32) {
-                const uint4 v = A.q16[(size_t)q * nch + c];
-                q2[c * 4 + 0] = h2_to_f2x(v.x);
-                q2[c * 4 + 1] = h2_to_f2x(v.y);
-                q2[c * 4 + 2] = h2_to_f2x(v.z);
-                q2[c * 4 + 3] = h2_to_f2x(v.w);
+            if (BYTES) {
+                float* qf = reinterpret_cast<float*>(base + A.o_q);
+                float* sc = reinterpret_cast<float*>(base + A.o_sc);
+                float* bi = reinterpret_cast<float*>(base + A.o_bi);
+                for (uint32_t i = lane; i < nch * 16; i += 32) {
+                    qf[i] = i < A.dim ? __fmul_rn(A.q32[(size_t)q * A.dim + i], A.alpha) : 0.0f;
+                    sc[i] = A.csc[i];
+                    bi[i] = A.cbi[i];
+                }
+            } else {
+                f2x* q2 = reinterpret_cast<f2x*>(base + A.o_q);
+                for (uint32_t c = lane; c < nch; c += 32) {
+                    const uint4 v = A.q16[(size_t)q * nch + c];
+                    q2[c * 4 + 0] = h2_to_f2x(v.x);
+                    q2[c * 4 + 1] = h2_to_f2x(v.y);
+                    q2[c * 4 + 2] = h2_to_f2x(v.z);
+                    q2[c * 4 + 3] = h2_to_f2x(v.w);
+                }
             }
             if (lane < A.a) {
                 base[A.o_lb + lane] = __float_as_uint(A.lb[(size_t)q * A.a + lane]);
@@ -436,7 +460,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
             }
             if (exact) {
                 st_exact = 1;
-                st_dist = exact_route<NCH>(A, base, q, cl, nc);
+                st_dist = exact_route<NCH, BYTES>(A, base, q, cl, nc);
             } else {
                 W w{base, 0u, 0u};
                 for (uint32_t i = lane; i < A.L; i += 32) w.T(A)[i] = kEmptyKey;
@@ -462,7 +486,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_sort<NCH>(A, w.base, nb, kEmptyKey, cell_vsh(A, cell));
+                    eval_sort<NCH, BYTES>(A, w.base, nb, kEmptyKey, cell_vsh(A, cell));
                     st_dist += nb;
                 }
                 for (uint32_t ci = c0; ci < nc;) {
@@ -516,7 +540,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                         }
                         hcount += nb;
                         if (nb == 0) continue;
-                        const uint32_t ns = eval_sort<NCH>(A, w.base, nb, w.T(A)[A.L - 1], vsh);
+                        const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, w.T(A)[A.L - 1], vsh);
                         st_dist += nb;
                         merge_step(A, w, A.L, 0, ns, true);
                     }
@@ -529,7 +553,7 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                     // (d) cross-cell hop
                     const uint32_t cn = next_cell(A, cl, nc, ci + 1);
                     if (cn < nc) {
-                        nb = cross_hop<NCH>(A, w, cl[cn], hcount, st_dist, st_cross);
+                        nb = cross_hop<NCH, BYTES>(A, w, cl[cn], hcount, st_dist, st_cross);
                         ++st_hops;
                     }
                     ci = cn;
@@ -606,16 +630,23 @@ __global__ void merge_lists_kernel(const unsigned long long* __restrict__ keys, 
 
 typedef void (*KernelFn)(const SArgs);
 
-// Row lengths compiled with a fixed chunk count (d8 / 8); others use the generic kernel.
-KernelFn pick_kernel(uint32_t nch) {
+// Row lengths compiled with a fixed chunk count (fp16: d8 / 8, bytes: d16 / 16); others
+// use the generic kernel.
+KernelFn pick_kernel(uint32_t nch, bool bytes) {
+    if (bytes) {
+        switch (nch) {
+            case 8: return gmg_search_kernel<8, true>;
+            default: return gmg_search_kernel<0, true>;
+        }
+    }
     switch (nch) {
-        case 4: return gmg_search_kernel<4>;
-        case 8: return gmg_search_kernel<8>;
-        case 12: return gmg_search_kernel<12>;
-        case 16: return gmg_search_kernel<16>;
-        case 32: return gmg_search_kernel<32>;
-        case 96: return gmg_search_kernel<96>;
-        default: return gmg_search_kernel<0>;
+        case 4: return gmg_search_kernel<4, false>;
+        case 8: return gmg_search_kernel<8, false>;
+        case 12: return gmg_search_kernel<12, false>;
+        case 16: return gmg_search_kernel<16, false>;
+        case 32: return gmg_search_kernel<32, false>;
+        case 96: return gmg_search_kernel<96, false>;
+        default: return gmg_search_kernel<0, false>;
     }
 }
 
@@ -671,7 +702,14 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (p.qnum == 0) return GF_OK;
 
     SArgs A;
-    A.vec16 = d.vec16;
+    const bool bytes = d.codec != 0;
+    A.vec16 = bytes ? d.vec8 : d.vec16;
+    A.q32 = p.q32;
+    A.csc = d.csc;
+    A.cbi = d.cbi;
+    A.alpha = d.alpha;
+    A.xmask = d.codec == 1 ? 0x80808080u : 0u;
+    A.dim = d.dim;
     A.attrs = d.attrs;
     A.graph = view ? view->graph : d.graph;
     A.cross = view ? view->cross : d.cross;
@@ -698,7 +736,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.out_d = dist;
     A.stats = p.stats;
     A.qnum = p.qnum;
-    A.nch = d.d8 / 8;
+    A.nch = bytes ? d.d16 / 16 : d.d8 / 8;
     A.a = d.a;
     A.P = d.ncells;
     A.R = d.degree;
@@ -732,9 +770,9 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t sr = 32;
     while (sr > 1 && sr * row_bytes > 8192) sr >>= 1;
     A.stage_rows = sr;
-    make_layout(A, nch16);
+    make_layout(A, nch16, bytes);
 
-    KernelFn kern = pick_kernel(A.nch);
+    KernelFn kern = pick_kernel(A.nch, bytes);
     const int warps_per_block = 4;
     size_t smem = (size_t)warps_per_block * A.warp_words * 4;
     int dev = d.device;

@@ -78,6 +78,17 @@ typedef struct {
                               shard results merge by (distance, position) (gf_search_keys,
                               gf_merge_keys).  Not with host_graph or keep_fp32. */
     uint32_t n_shard_cells;
+    /* Stored row format.  0 = fp16 (half(x * f2h_factor)); 1 = int8 per-dimension affine
+     * (the out-of-core codec, production_adapter.cuh:286-383): codes = NULL quantises
+     * vectors * f2h_factor here (gf_quantize_i8_host), else codes / code_scales /
+     * code_zero_points are the quantised rows (n x dim, global order) and their parameters,
+     * e.g. from a .q file; 2 = uint8 rows (u8bin data, big_dataset_adapterV3.cuh:2802-2810)
+     * in codes, decoded scale * (q - zero_point), default scale 0.01 and zero point 0.
+     * Byte rows are compared with the fp32 query * f2h_factor (gf_search, orc_dist8). */
+    uint32_t codec;
+    const uint8_t* codes;
+    const float* code_scales;
+    const int32_t* code_zero_points;
 } gf_index_desc;
 
 /* Paths of the reference's index files (realdataset_search flags, README.md:101-170). */
@@ -93,6 +104,8 @@ typedef struct {
     float f2h_factor;         /* --f2h_factor */
     uint32_t keep_fp32;
     uint32_t host_graph;      /* as gf_index_desc.host_graph */
+    uint32_t codec;           /* as gf_index_desc.codec; 2 reads data_path as u8bin */
+    const char* quantized;    /* codec 1: .q file with the codes (NULL: quantise the data) */
     /* Uniform grid (normaldataset_search, normaldataset_search.cu:1748-2104), used when
      * grid is NULL: attribute j is cut into uniform_shape[j] equal slices of
      * [uniform_lo, uniform_hi) (the reference compiles shape {16} and [0, 1e6) in);
@@ -297,6 +310,27 @@ gf_status gf_read_fvecs(const char* path, float** data, uint32_t* n, uint32_t* d
 gf_status gf_write_fvecs(const char* path, const float* data, uint32_t n, uint32_t dim);
 /* u8bin: uint32 n, uint32 d, n*d uint8 (tools.cuh:108-150). */
 gf_status gf_read_u8bin(const char* path, uint8_t** data, uint32_t* n, uint32_t* dim);
+/* .q file: uint32 n, uint32 d, d float32 scales, d int32 zero points, n*d int8 codes
+ * (save_dataset_quantified / load_dataset_quantified, production_adapter.cuh:240-285).
+ * The reader allocates three arrays (gf_free each). */
+gf_status gf_read_q(const char* path, int8_t** codes, float** scales, int32_t** zero_points, uint32_t* n,
+                    uint32_t* dim);
+gf_status gf_write_q(const char* path, const int8_t* codes, const float* scales, const int32_t* zero_points,
+                     uint32_t n, uint32_t dim);
+/*
+ * Per-dimension affine int8 quantisation of data * alpha (the reference's host quantiser,
+ * production_adapter.cuh:316-337; its device kernel integer_production_kernal, :8-47,
+ * computes the same with round-half-even).  scale = (max - min) / 255, zero_point =
+ * round(-128 - min / scale), q = round(x / scale) + zero_point, both clamped to
+ * [-128, 127], round half away from zero, min / max starting from 100000 / -100000; a
+ * constant dimension gets scale 1.  gf_quantize_i8: device arrays (data n x dim, q_out
+ * n x dim, scales_out and zero_points_out dim), synchronises `stream`; _host: host arrays
+ * (q_out may be NULL to compute only the parameters).
+ */
+gf_status gf_quantize_i8(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q_out, float* scales_out,
+                         int32_t* zero_points_out, void* stream);
+gf_status gf_quantize_i8_host(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q_out,
+                              float* scales_out, int32_t* zero_points_out);
 /* attrs.bin: uint32 n, uint32 a, n*a int32 (tools.cuh:747-765). */
 gf_status gf_read_attrs(const char* path, int32_t** attrs, uint32_t* n, uint32_t* a);
 gf_status gf_write_attrs(const char* path, const int32_t* attrs, uint32_t n, uint32_t a);

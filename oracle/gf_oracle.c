@@ -23,6 +23,9 @@
  *   orc_search         gpu_graph.cu:3270-4131          select_path_contain_attr_filter_V2_
  *                                                      without_output_with_post_pre_filter
  *   orc_recall         tools.cuh:456-544               cal_recall_show_partition_multi_attrs
+ *   orc_quantize_i8    production_adapter.cuh:316-337  per-dimension affine int8 codec (host path of
+ *                                                      load_dataset_return_int8_arr_infile)
+ *   orc_dist8          big_dataset_adapterV3.cuh:852-863, 2802-2810  distances to int8 / uint8 rows
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
  *   - orc_dist16 / orc_dist32: squared L2 of two rows of padded length (a multiple of 8).
@@ -31,6 +34,9 @@
  *     s[j] = p[j] + p[j+4] (j<4), t[j] = s[j] + s[j+2] (j<2), result = t[0] + t[1].
  *     (Adjacent partials are the two halves of one packed two-wide fp32 register on the
  *     GPU, so every step is one packed instruction and the chunk loop needs no unrolling.)
+ *   - orc_dist8: the same eight partials over byte rows (d16 elements): x^ = scale[i] *
+ *     ((float)(row[i] ^ xmask) - bias[i]) (exact integer difference, one rounding), diff =
+ *     q[i] - x^ with q the fp32 query times f2h_factor (not rounded to fp16).
  *   - orc_dist_seq: squared L2 with one fma chain over d = 0..D-1 (used for the
  *     query-centroid distances of the cell ordering).
  * The reference accumulates candidate distances in fp16 (gpu_graph.cu:3394-3403) and
@@ -116,6 +122,50 @@ float orc_dist32(const float* q, const float* x, uint32_t d4) {
         p[i & 7] = fmaf(diff, diff, p[i & 7]);
     }
     return finish8(p);
+}
+
+/* byte rows of d16 elements; see the header for the formula */
+float orc_dist8(const float* q, const uint8_t* x, const float* scale, const float* bias, uint32_t xmask,
+                uint32_t d16) {
+    float p[8] = {0};
+    for (uint32_t i = 0; i < d16; ++i) {
+        float xh = scale[i] * ((float)(uint32_t)(x[i] ^ (uint8_t)xmask) - bias[i]);
+        float diff = q[i] - xh;
+        p[i & 7] = fmaf(diff, diff, p[i & 7]);
+    }
+    return finish8(p);
+}
+
+/*
+ * Per-dimension affine int8 quantisation, production_adapter.cuh:316-337 (the host path
+ * used with a .q file): x = data * alpha; per dimension min / max over all points starting
+ * from min = 100000, max = -100000 (as the reference); scale = (max - min) / 255;
+ * zero_point = round(-128 - min / scale) clamped to [-128, 127]; q = round(x / scale) +
+ * zero_point clamped to [-128, 127]; round = half away from zero (C round).  Where max ==
+ * min the reference divides by zero; here scale = 1 for such a dimension.
+ */
+void orc_quantize_i8(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q, float* scales,
+                     int32_t* zero_points) {
+    for (uint32_t j = 0; j < dim; ++j) {
+        float mn = 100000.0f, mx = -100000.0f;
+        for (uint32_t i = 0; i < n; ++i) {
+            float x = data[(size_t)i * dim + j] * alpha;
+            mn = fminf(mn, x);
+            mx = fmaxf(mx, x);
+        }
+        float scale = (mx - mn) / 255.0f;
+        if (!(scale > 0.0f)) scale = 1.0f;
+        int zp = (int)roundf(-128.0f - mn / scale);
+        zp = zp < -128 ? -128 : zp > 127 ? 127 : zp;
+        for (uint32_t i = 0; i < n; ++i) {
+            float x = data[(size_t)i * dim + j] * alpha;
+            int v = (int)roundf(x / scale) + zp;
+            v = v < -128 ? -128 : v > 127 ? 127 : v;
+            q[(size_t)i * dim + j] = (int8_t)v;
+        }
+        scales[j] = scale;
+        zero_points[j] = zp;
+    }
 }
 
 float orc_dist_seq(const float* q, const float* x, uint32_t dim) {
@@ -350,6 +400,12 @@ typedef struct {
     const uint32_t* cell_of; /* n: grid cell of each point (global_pid) */
     const uint32_t* graphs;  /* concatenated per-cell graphs, cell order, local ids */
     const uint32_t* cross;   /* n x (ncells * cross_e) local ids in the target cell */
+    /* byte-row codec (codec != 0): rows of d16 bytes, per-element scale and bias */
+    uint32_t codec;          /* 0 = fp16 rows (vec16), 1 = int8, 2 = uint8 (vec8) */
+    uint32_t d16;
+    const uint8_t* vec8;     /* n x d16 */
+    const float* scale;      /* d16 (0 past dim) */
+    const float* bias;       /* d16: zero_point + 128 (int8) or zero_point (uint8) */
 } orc_index;
 
 typedef struct {
@@ -428,15 +484,23 @@ typedef struct {
     const uint32_t* g_of;  /* position -> global id */
     const uint32_t* p_of;  /* global id -> position */
     const uint16_t* q16;   /* d8 */
+    const float* qv;       /* d16: fp32 query * f2h_factor, zero padded (byte codecs) */
     const float* lb;
     const float* rb;
     uint64_t* stats; /* n_dist, n_exp, n_cross, n_hops */
 } qctx;
 
+static inline float row_dist(const qctx* c, uint32_t g) {
+    const orc_index* ix = c->ix;
+    if (ix->codec == 0) return orc_dist16(c->q16, ix->vec16 + (size_t)g * ix->d8, ix->d8);
+    return orc_dist8(c->qv, ix->vec8 + (size_t)g * ix->d16, ix->scale, ix->bias, ix->codec == 1 ? 0x80u : 0u,
+                     ix->d16);
+}
+
 static inline ent evaluate(const qctx* c, uint32_t pos) {
     uint32_t g = c->g_of[pos];
     ent e;
-    e.d = orc_dist16(c->q16, c->ix->vec16 + (size_t)g * c->ix->d8, c->ix->d8);
+    e.d = row_dist(c, g);
     e.w = pos | (in_box(c->ix->attrs + (size_t)g * c->ix->a, c->lb, c->rb, c->ix->a) ? ORC_INRANGE : 0);
     c->stats[0]++;
     return e;
@@ -502,7 +566,7 @@ static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, u
                 uint32_t g = c->g_of[pos];
                 if (!in_box(ix->attrs + (size_t)g * ix->a, c->lb, c->rb, ix->a)) continue;
                 c->stats[0]++;
-                orc_pair v = {orc_dist16(c->q16, ix->vec16 + (size_t)g * ix->d8, ix->d8), pos};
+                orc_pair v = {row_dist(c, g), pos};
                 topk_insert(best, &nb, K, v);
             }
         }
@@ -686,10 +750,12 @@ void orc_search(const orc_index* ix, const orc_params* p, const float* queries, 
     {
         uint64_t st[4] = {0, 0, 0, 0};
         uint16_t* q16 = (uint16_t*)malloc(sizeof(uint16_t) * ix->d8);
+        float* qv = (float*)calloc(ix->d16 > dim ? ix->d16 : dim, sizeof(float));
 #pragma omp for schedule(dynamic, 1)
         for (long q = 0; q < (long)qnum; ++q) {
             orc_f2h(queries + (size_t)q * dim, 1, dim, ix->d8, alpha, q16);
-            qctx c = {ix, seg, g_of, p_of, q16, lb + q * ix->a, rb + q * ix->a, st};
+            for (uint32_t i = 0; i < dim; ++i) qv[i] = queries[(size_t)q * dim + i] * alpha;
+            qctx c = {ix, seg, g_of, p_of, q16, qv, lb + q * ix->a, rb + q * ix->a, st};
             int exact = route_exact(ix, p, counts[q], box_counts ? box_counts[q] : ix->n);
             search_one(&c, p, cells + offsets[q], counts[q], exact, entry, ids_out + (size_t)q * p->K,
                        dist_out + (size_t)q * p->K);
@@ -697,6 +763,7 @@ void orc_search(const orc_index* ix, const orc_params* p, const float* queries, 
 #pragma omp critical
         for (int i = 0; i < 4; ++i) tot[i] += st[i];
         free(q16);
+        free(qv);
     }
     if (stats)
         for (int i = 0; i < 4; ++i) stats[i] += tot[i];
@@ -732,6 +799,7 @@ void orc_search_batched(const orc_index* ix, const orc_params* p, const float* q
     {
         uint64_t st[4] = {0, 0, 0, 0};
         uint16_t* q16 = (uint16_t*)malloc(sizeof(uint16_t) * ix->d8);
+        float* qv = (float*)calloc(ix->d16 > dim ? ix->d16 : dim, sizeof(float));
         uint32_t* sub = (uint32_t*)malloc(sizeof(uint32_t) * (ix->ncells ? ix->ncells : 1));
         uint32_t* bid = (uint32_t*)malloc(sizeof(uint32_t) * K);
         float* bd = (float*)malloc(sizeof(float) * K);
@@ -741,7 +809,8 @@ void orc_search_batched(const orc_index* ix, const orc_params* p, const float* q
 #pragma omp for schedule(dynamic, 1)
         for (long q = 0; q < (long)qnum; ++q) {
             orc_f2h(queries + (size_t)q * dim, 1, dim, ix->d8, alpha, q16);
-            qctx c = {ix, seg, g_of, p_of, q16, lb + q * ix->a, rb + q * ix->a, st};
+            for (uint32_t i = 0; i < dim; ++i) qv[i] = queries[(size_t)q * dim + i] * alpha;
+            qctx c = {ix, seg, g_of, p_of, q16, qv, lb + q * ix->a, rb + q * ix->a, st};
             const uint32_t* cl = cells + offsets[q];
             int exact = route_exact(ix, p, counts[q], box_counts ? box_counts[q] : ix->n);
             for (uint32_t k = 0; k < K; ++k) run[k] = (ent){INFINITY, ORC_EMPTY};
@@ -764,6 +833,7 @@ void orc_search_batched(const orc_index* ix, const orc_params* p, const float* q
 #pragma omp critical
         for (int i = 0; i < 4; ++i) tot[i] += st[i];
         free(q16);
+        free(qv);
         free(sub);
         free(bid);
         free(bd);

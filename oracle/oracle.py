@@ -32,7 +32,9 @@ _L = None
 class OrcIndex(C.Structure):
     _fields_ = [("n", C.c_uint32), ("d8", C.c_uint32), ("a", C.c_uint32), ("ncells", C.c_uint32),
                 ("degree", C.c_uint32), ("cross_e", C.c_uint32), ("vec16", C.c_void_p), ("attrs", C.c_void_p),
-                ("cell_of", C.c_void_p), ("graphs", C.c_void_p), ("cross", C.c_void_p)]
+                ("cell_of", C.c_void_p), ("graphs", C.c_void_p), ("cross", C.c_void_p),
+                ("codec", C.c_uint32), ("d16", C.c_uint32), ("vec8", C.c_void_p), ("scale", C.c_void_p),
+                ("bias", C.c_void_p)]
 
 
 class OrcParams(C.Structure):
@@ -50,6 +52,9 @@ def lib() -> C.CDLL:
         _L.orc_dist16.argtypes = [P, P, U]
         _L.orc_dist32.restype = C.c_float
         _L.orc_dist32.argtypes = [P, P, U]
+        _L.orc_dist8.restype = C.c_float
+        _L.orc_dist8.argtypes = [P, P, P, P, U, U]
+        _L.orc_quantize_i8.argtypes = [P, U, U, C.c_float, P, P, P]
         _L.orc_dist_seq.restype = C.c_float
         _L.orc_dist_seq.argtypes = [P, P, U]
         _L.orc_f2h.argtypes = [P, U, U, U, C.c_float, P]
@@ -161,13 +166,46 @@ def order_cells(queries, centroids, hist, counts, offsets, cells):
     return cells, top4
 
 
+def quantize_i8(data, alpha: float = 1.0):
+    """orc_quantize_i8: (q int8 n x dim, scales fp32 dim, zero_points int32 dim)."""
+    data = _c(data, np.float32)
+    n, dim = data.shape
+    q = np.zeros((n, dim), np.int8)
+    sc = np.zeros(dim, np.float32)
+    zp = np.zeros(dim, np.int32)
+    lib().orc_quantize_i8(_p(data), n, dim, alpha, _p(q), _p(sc), _p(zp))
+    return q, sc, zp
+
+
+def byte_rows(q, scales, zero_points, codec: int):
+    """Byte rows padded to a multiple of 16 with per-element scale and bias (orc_dist8);
+    codec 1 = int8 (bias = zero_point + 128), 2 = uint8 (bias = zero_point)."""
+    q = np.ascontiguousarray(q)
+    n, dim = q.shape
+    d16 = (dim + 15) // 16 * 16
+    rows = np.zeros((n, d16), np.uint8)
+    rows[:, :dim] = q.view(np.uint8)
+    sc = np.zeros(d16, np.float32)
+    bias = np.zeros(d16, np.float32)
+    sc[:dim] = scales
+    bias[:dim] = np.asarray(zero_points, np.float32) + (128.0 if codec == 1 else 0.0)
+    return rows, sc, bias, d16
+
+
+def dist8(q, row, scale, bias, codec: int) -> float:
+    return lib().orc_dist8(_p(_c(q, np.float32)), _p(_c(row, np.uint8)), _p(_c(scale, np.float32)),
+                           _p(_c(bias, np.float32)), 0x80 if codec == 1 else 0, len(row))
+
+
 def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells, entry, *, L, K, width=1,
            max_iter=10000, postfilter=0xFFFFFFFF, prefilter=0.0, box_counts=None, alpha=1.0, threads=0,
-           batches=None):
+           batches=None, codec=0, codes=None, scales=None, zero_points=None):
     """Beam search restatement; index_arrays: an indexbuild.GmgArrays (reference layout).
 
     With `batches` (a list of cell lists), the batched driver orc_search_batched runs
-    instead: each batch is searched on its own and the results merged."""
+    instead: each batch is searched on its own and the results merged.  codec 1 / 2:
+    distances to int8 / uint8 rows `codes` (n x dim, global order) with per-dimension
+    `scales` and `zero_points` (orc_dist8) instead of fp16 rows."""
     vectors = _c(vectors, np.float32)
     n, dim = vectors.shape
     d8 = (dim + 7) // 8 * 8
@@ -179,6 +217,9 @@ def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells
     ncells = int(np.prod(index_arrays.grid))
     ix = OrcIndex(n, d8, attrs.shape[1], ncells, index_arrays.degree, index_arrays.cross_e,
                   _p(vec16), _p(attrs), _p(cell_of), _p(graphs), _p(cross))
+    if codec:
+        rows, sc8, bias8, d16 = byte_rows(codes, scales, zero_points, codec)
+        ix.codec, ix.d16, ix.vec8, ix.scale, ix.bias = codec, d16, _p(rows), _p(sc8), _p(bias8)
     entry = _c(entry, np.uint32)
     prm = OrcParams(L, K, width, max_iter, postfilter, prefilter, len(entry))
     queries = _c(queries, np.float32)

@@ -3,12 +3,16 @@
 // vectors for the oracle:
 //   bf       naive_brute_force_with_filter (gpu_graph.cu:10782-10812), one call per query
 //   cluster  load_clustering (tools.cuh:569-602): centroids and the cell x cluster histogram
+//   quant    load_dataset_return_int8_arr_infile (production_adapter.cuh:286-383): its host
+//            quantiser writes the .q file before any device copy; without a GPU the device
+//            copies that follow fail and are ignored by the reference's own error handling
 // Built by oracle/Makefile (target ref_golden) into oracle/_ref/; never linked into the
 // product.  Input/output files are plain little-endian arrays described below.
 #include <unordered_map>
 #include <unordered_set>
 
 #include "gpu_graph.cu"
+#include "production_adapter.cuh"
 
 #include <cstdio>
 #include <cstdlib>
@@ -63,6 +67,19 @@ int main(int argc, char** argv) {
         write_u32(argv[5], h);
         return 0;
     }
-    fprintf(stderr, "usage: bf data attrs queries ranges k out | cluster data labels centroids hist\n");
+    if (mode == "quant" && argc == 5) {
+        // quant data.fvecs alpha out.q   (out.q must not exist)
+        float* data = nullptr;
+        unsigned num = 0, dim = 0;
+        int8_t* q = nullptr;
+        float* scales = nullptr;
+        int* zps = nullptr;
+        smart::production_adapter::load_dataset_return_int8_arr_infile(std::string(argv[2]), std::string(argv[4]),
+                                                                       data, num, dim, (float)atof(argv[3]), q,
+                                                                       scales, zps);
+        return 0;
+    }
+    fprintf(stderr, "usage: bf data attrs queries ranges k out | cluster data labels centroids hist | "
+                    "quant data alpha out.q\n");
     return 2;
 }

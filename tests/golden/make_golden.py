@@ -11,6 +11,9 @@ the GPU box never runs this script, it only reads the .npz files it writes.
                       `make -C oracle ref_golden REF=<checkout>`)
   golden_cluster.npz  load_clustering (tools.cuh:569-602) run the same way: centroids and
                       the cell x cluster histogram (cells = i / 62500 in the reference)
+  golden_quant.npz    the reference's host int8 quantiser (production_adapter.cuh:316-337,
+                      via load_dataset_return_int8_arr_infile) run the same way: the .q file
+                      it writes (codes, scales, zero points)
 
 Inputs are seeded synthetic arrays written next to the outputs.
 """
@@ -91,6 +94,29 @@ def golden_bf_and_cluster(ref_bin: Path) -> None:
     np.savez_compressed(HERE / "golden_cluster.npz", labels=labels, centroids=cent, hist=hist)
 
 
+def golden_quant(ref_bin: Path) -> None:
+    import garfield_b200 as gf
+    rng = np.random.default_rng(31)
+    # mixture-like data in [0, 255] with a clipped tail, a constant-free set of dimensions,
+    # values on rounding boundaries, and a negative range (zero point clamping)
+    x = np.clip(rng.normal(100, 40, size=(700, 24)), 0, 255).astype(np.float32)
+    x[:, 3] = rng.integers(0, 256, size=700).astype(np.float32)
+    x[:, 5] = np.round(x[:, 5]) + 0.5
+    x[:, 7] = -x[:, 7] - 10.0
+    out = {}
+    with tempfile.TemporaryDirectory() as td:
+        t = Path(td)
+        gf.write_fvecs(t / "d.fvecs", x)
+        for name, alpha in (("a1", 1.0), ("a05", 0.5), ("a3", 3.0)):
+            qpath = t / f"{name}.q"
+            subprocess.run([str(ref_bin), "quant", str(t / "d.fvecs"), repr(alpha), str(qpath)], check=True,
+                           capture_output=True)
+            codes, sc, zp = gf.read_q(qpath)
+            out[f"{name}_codes"], out[f"{name}_scales"], out[f"{name}_zps"] = codes, sc, zp
+            out[f"{name}_alpha"] = np.float32(alpha)
+    np.savez_compressed(HERE / "golden_quant.npz", data=x, **out)
+
+
 def main() -> None:
     ref = Path(sys.argv[1]) if len(sys.argv) > 1 else None
     if ref is None or not (ref / "indexbuild" / "tools.py").exists():
@@ -100,6 +126,7 @@ def main() -> None:
     if not ref_bin.exists():
         subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref_golden", f"REF={ref}"], check=True)
     golden_bf_and_cluster(ref_bin)
+    golden_quant(ref_bin)
     print("golden fixtures written to", HERE)
 
 

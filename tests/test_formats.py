@@ -79,3 +79,18 @@ def test_errors(tmp_path):
     with pytest.raises(gf.GarfieldError) as e:
         gf.read_grid(p)
     assert e.value.status == 3
+
+
+def test_q_file_round_trip(tmp_path):
+    rng = np.random.default_rng(4)
+    codes = rng.integers(-128, 128, size=(37, 20)).astype(np.int8)
+    sc = rng.random(20).astype(np.float32)
+    zp = rng.integers(-128, 128, size=20).astype(np.int32)
+    gf.write_q(tmp_path / "x.q", codes, sc, zp)
+    c2, s2, z2 = gf.read_q(tmp_path / "x.q")
+    assert np.array_equal(c2, codes) and np.array_equal(s2, sc) and np.array_equal(z2, zp)
+    raw = (tmp_path / "x.q").read_bytes()
+    (tmp_path / "bad.q").write_bytes(raw[:-1])
+    with pytest.raises(gf.GarfieldError) as e:
+        gf.read_q(tmp_path / "bad.q")
+    assert e.value.status == 3
