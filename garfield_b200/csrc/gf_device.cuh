@@ -57,6 +57,11 @@ __device__ __forceinline__ f2x mul2(f2x a, f2x b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+__device__ __forceinline__ f2x fma2(f2x a, f2x b, f2x c) {  // a * b + c, fused, per half
+    f2x r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 __device__ __forceinline__ f2x add2(f2x a, f2x b) {
     f2x r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -105,12 +110,14 @@ __device__ __forceinline__ float byte_f23(uint32_t w, uint32_t e) {
 }
 
 // Canonical squared distance (oracle orc_dist8) of a byte row staged in shared memory
-// (nch chunks of 16 bytes, swizzled by stage_slot with key r): element i decodes to
-// x^ = scale[i] * (byte ^ xmask - bias[i]), computed as ((2^23 + byte) - (2^23 + bias))
-// * scale with the exact integer difference; diff = q[i] - x^; partial i mod 8.  q2, s2,
-// b2: the query, scales and 2^23 + bias as fp32 pairs.
+// (nch chunks of 16 bytes, swizzled by stage_slot with key r): element i contributes
+// diff = fma(-scale[i], byte ^ xmask - bias[i], q[i]) to partial i mod 8, the integer
+// difference computed exactly as (2^23 + byte) - (2^23 + bias).  The decoded value is not
+// rounded on its own: ptxas contracts a packed multiply followed by a packed subtract into
+// one fused operation even when both carry .rn, so the fused form is the defined one and
+// is written as such.  q2, ns2, b2: the query, -scale and 2^23 + bias as fp32 pairs.
 template <int NCH>
-__device__ __forceinline__ float dist8_staged(const uint4* srow, const f2x* q2, const f2x* s2, const f2x* b2,
+__device__ __forceinline__ float dist8_staged(const uint4* srow, const f2x* q2, const f2x* ns2, const f2x* b2,
                                               uint32_t xmask, uint32_t nch_rt, uint32_t r) {
     const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
     const uint32_t key = r & 15u;
@@ -124,8 +131,8 @@ __device__ __forceinline__ float dist8_staged(const uint4* srow, const f2x* q2, 
             const uint32_t word = w[j >> 1], e = (j & 1) * 2;
             const f2x u = pack2(byte_f23(word, e), byte_f23(word, e + 1));
             const uint32_t k = c * 8 + j;  // pair index in the row
-            const f2x xh = mul2(sub2(u, b2[k]), s2[k]);
-            p[j & 3] = sqacc2(sub2(q2[k], xh), p[j & 3]);
+            const f2x d = fma2(sub2(u, b2[k]), ns2[k], q2[k]);
+            p[j & 3] = sqacc2(d, p[j & 3]);
         }
     }
     return finish8(p[0], p[1], p[2], p[3]);

@@ -349,9 +349,9 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
                 const uint32_t pos = sharded ? row_pos[r] : (uint32_t)r;
                 std::memcpy(&rows8[r * d.d16], codes + (size_t)i2g[pos] * d.dim, d.dim);
             }
-            std::vector<float> sc(d.d16, 0.0f), bi(d.d16, 8388608.0f);
+            std::vector<float> sc(d.d16, 0.0f), bi(d.d16, 8388608.0f);  // sc holds -scale
             for (uint32_t j = 0; j < d.dim; ++j) {
-                sc[j] = d.scales_h[j];
+                sc[j] = -d.scales_h[j];
                 bi[j] = 8388608.0f + (float)(d.zps_h[j] + (d.codec == 1 ? 128 : 0));
             }
             cudaError_t e = cudaMemcpy(d.vec8, rows8.data(), rows8.size(), cudaMemcpyHostToDevice);

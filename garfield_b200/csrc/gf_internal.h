@@ -47,7 +47,7 @@ struct DeviceIndex {
     // byte codecs (codec 1 = int8, 2 = uint8): rows of d16 bytes, decoded scale * (q - zp)
     uint32_t codec = 0, d16 = 0;
     uint4* vec8 = nullptr;       // rows x d16 bytes
-    float* csc = nullptr;        // d16 per-element scale (0 past dim)
+    float* csc = nullptr;        // d16 per-element -scale (0 past dim)
     float* cbi = nullptr;        // d16 per-element 2^23 + bias (bias = zp + 128 for int8, zp for uint8)
     std::vector<float> scales_h; // dim
     std::vector<int32_t> zps_h;  // dim
@@ -84,6 +84,7 @@ void free_batch_state(BatchState* b);
 
 struct Plan {
     gf_index* idx = nullptr;
+    int device = 0;  // the index's device, kept so that destroying the plan never reads the index
     uint32_t max_q = 0, qnum = 0;
     bool planned = false;
     float prefilter = 0.0f;

@@ -90,6 +90,7 @@ extern "C" gf_status gf_search_noalloc(gf_index* idx, const float* queries, cons
     gf_plan plan;
     Plan& p = plan.p;
     p.idx = idx;
+    p.device = d.device;
     p.max_q = qnum;
     Carver cv{scratch};
     const size_t Q = qnum;

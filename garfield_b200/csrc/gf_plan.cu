@@ -440,6 +440,7 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
     gf_plan* pl = new gf_plan();
     Plan& p = pl->p;
     p.idx = idx;
+    p.device = d.device;
     p.max_q = max_queries;
     const size_t Q = max_queries;
     cudaError_t e = cudaSuccess;
@@ -484,7 +485,7 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
 
 gf_status gf_plan_destroy(gf_plan* plan) {
     if (!plan) return GF_OK;
-    DeviceGuard2 guard(plan->p.idx->d.device);
+    DeviceGuard2 guard(plan->p.device);
     free_plan(plan->p);
     delete plan;
     return GF_OK;
@@ -502,7 +503,7 @@ gf_status gf_plan_read(gf_plan* plan, uint32_t* counts, uint32_t* offsets, uint3
     if (!plan) return fail(GF_ERR_ARG, "null plan");
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "plan not built");
-    DeviceGuard2 guard(p.idx->d.device);
+    DeviceGuard2 guard(p.device);
     GF_CUDA(cudaStreamSynchronize(p.stream));
     const uint32_t q = p.qnum;
     if (q == 0) return GF_OK;
@@ -531,7 +532,7 @@ gf_status gf_search(gf_index* idx, gf_plan* plan, const gf_search_params* params
 gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out) {
     if (!plan || !out) return fail(GF_ERR_ARG, "null argument");
     Plan& p = plan->p;
-    DeviceGuard2 guard(p.idx->d.device);
+    DeviceGuard2 guard(p.device);
     unsigned long long v[8];
     GF_CUDA(cudaStreamSynchronize(p.stream));
     GF_CUDA(cudaMemcpy(v, p.stats, sizeof(v), cudaMemcpyDeviceToHost));

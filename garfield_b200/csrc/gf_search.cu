@@ -35,7 +35,7 @@ struct SArgs {
     const uint32_t* __restrict__ i2g;
     const uint4* __restrict__ q16;
     const float* __restrict__ q32;    // fp32 queries (byte codecs: times alpha, fp32)
-    const float* __restrict__ csc;    // byte codecs: per-element scale (d16)
+    const float* __restrict__ csc;    // byte codecs: per-element -scale (d16)
     const float* __restrict__ cbi;    // byte codecs: per-element 2^23 + bias (d16)
     float alpha;
     uint32_t xmask, dim;
@@ -62,7 +62,7 @@ struct SArgs {
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, warp_words;
     // word offsets inside a warp's shared-memory slice
-    uint32_t o_sc, o_bi;  // byte codecs: scale and 2^23 + bias pairs
+    uint32_t o_sc, o_bi;  // byte codecs: -scale and 2^23 + bias pairs
     uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
         o_picks, o_stage, o_hash;
 };

@@ -165,7 +165,8 @@ gf_status gf_index_destroy(gf_index* idx);
 
 /* ----------------------------------------------------------------- plan */
 
-/* Plan buffers for up to max_queries queries. */
+/* Plan buffers for up to max_queries queries.  A plan may be destroyed before or after
+ * its index; every other call needs the index alive. */
 gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out);
 gf_status gf_plan_destroy(gf_plan* plan);
 

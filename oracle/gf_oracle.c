@@ -34,9 +34,10 @@
  *     s[j] = p[j] + p[j+4] (j<4), t[j] = s[j] + s[j+2] (j<2), result = t[0] + t[1].
  *     (Adjacent partials are the two halves of one packed two-wide fp32 register on the
  *     GPU, so every step is one packed instruction and the chunk loop needs no unrolling.)
- *   - orc_dist8: the same eight partials over byte rows (d16 elements): x^ = scale[i] *
- *     ((float)(row[i] ^ xmask) - bias[i]) (exact integer difference, one rounding), diff =
- *     q[i] - x^ with q the fp32 query times f2h_factor (not rounded to fp16).
+ *   - orc_dist8: the same eight partials over byte rows (d16 elements): diff =
+ *     fma(-scale[i], (float)(row[i] ^ xmask) - bias[i], q[i]), i.e. q - scale * (code -
+ *     bias) with one rounding (the integer difference is exact); q is the fp32 query times
+ *     f2h_factor (not rounded to fp16).
  *   - orc_dist_seq: squared L2 with one fma chain over d = 0..D-1 (used for the
  *     query-centroid distances of the cell ordering).
  * The reference accumulates candidate distances in fp16 (gpu_graph.cu:3394-3403) and
@@ -129,8 +130,7 @@ float orc_dist8(const float* q, const uint8_t* x, const float* scale, const floa
                 uint32_t d16) {
     float p[8] = {0};
     for (uint32_t i = 0; i < d16; ++i) {
-        float xh = scale[i] * ((float)(uint32_t)(x[i] ^ (uint8_t)xmask) - bias[i]);
-        float diff = q[i] - xh;
+        float diff = fmaf(-scale[i], (float)(uint32_t)(x[i] ^ (uint8_t)xmask) - bias[i], q[i]);
         p[i & 7] = fmaf(diff, diff, p[i & 7]);
     }
     return finish8(p);

@@ -166,3 +166,13 @@ def test_f2h_factor(small):
                                       c.offsets, c.cells, c.entry(c.ix.degree), L=64, K=10, alpha=0.01)
     assert np.array_equal(as_u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
     g.close()
+
+
+def test_plan_may_outlive_its_index(small):
+    """Destroying a plan after its index (as a garbage collector may order them) leaves no
+    error behind: the next index builds."""
+    g = make_index(small)
+    plan = g.plan(8)
+    g.close()
+    plan.close()
+    make_index(small).close()
