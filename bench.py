@@ -39,7 +39,9 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-L_SWEEP = [16, 24, 32, 40, 48, 64, 80, 96, 128, 160, 192, 256, 320, 384, 512]
+# the reference's ef sweep (realdataset_search.cu:2757-2760), ascending, L >= k
+L_SWEEP = [10, 15, 20, 25, 30, 35, 40, 45, 50, 55, 60, 70, 80, 90, 100, 120, 140, 160, 180, 200, 250, 300, 400,
+           500, 600, 700, 800, 900, 1000, 1100, 1400, 1700]
 
 
 def log(*a):

@@ -73,7 +73,8 @@ class _SearchParams(C.Structure):
 
 
 class _SearchStats(C.Structure):
-    _fields_ = [(n, C.c_uint64) for n in ("n_dist", "n_exp", "n_cross", "n_hops", "n_exact", "n_queries")]
+    _fields_ = [(n, C.c_uint64) for n in ("n_dist", "n_exp", "n_cross", "n_hops", "n_exact", "n_queries",
+                                          "n_timeouts")]
 
 
 class _IndexInfo(C.Structure):

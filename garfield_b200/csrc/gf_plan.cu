@@ -542,6 +542,7 @@ gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out) {
     out->n_hops = v[3];
     out->n_exact = v[4];
     out->n_queries = v[5];
+    out->n_timeouts = v[7];
     return GF_OK;
 }
 
@@ -590,6 +591,9 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
             (e = cudaMemcpyAsync(dist_host, ddist, 4ull * qnum * P.k, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
             break;
         e = cudaStreamSynchronize(s);
+        unsigned long long to = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&to, p.stats + 7, sizeof(to), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && to) st = fail(GF_ERR_TIMEOUT, "row staging wait ran out in the search kernel");
     } while (0);
     if (st != GF_OK) return st;
     if (e != cudaSuccess) return cuda_fail(e, "gf_search_host");

@@ -60,11 +60,11 @@ struct SArgs {
     uint32_t nslots, xstride;
     uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
     float prefilter;
-    uint32_t hs, hshift, bcap, stage_rows, warp_words;
+    uint32_t hs, hshift, bcap, stage_rows, stage_stride, warp_words;
     // word offsets inside a warp's shared-memory slice
     uint32_t o_sc, o_bi;  // byte codecs: -scale and 2^23 + bias pairs
     uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
-        o_picks, o_stage, o_hash;
+        o_picks, o_stage, o_hash, o_mbar;
 };
 
 // Shared-memory layout of one warp, in 32-bit words, every region 16-byte aligned.
@@ -92,7 +92,8 @@ void make_layout(SArgs& A, uint32_t nch16, bool bytes) {
     A.o_ed = take(2 * A.bcap);
     A.o_t0w = A.o_t1w = A.o_r0w = A.o_r1w = A.o_bw = A.o_ew = 0;
     A.o_picks = take(32);
-    A.o_stage = take(A.stage_rows * nch16 * 4);
+    A.o_mbar = take(4);  // staging mbarrier (8 bytes), its phase bit, the warp's abort flag
+    A.o_stage = take(A.stage_rows * A.stage_stride * 4);
     A.o_hash = take(A.hs);
     A.warp_words = o;
 }
@@ -117,50 +118,70 @@ struct W {
 
 __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 1u << (32 - __clz(x - 1)); }
 
+// Bounded wait for a staging batch: polls of the mbarrier before the warp gives up,
+// counts a timeout in stats[7] and stops evaluating (the host reports GF_ERR_TIMEOUT).
+constexpr uint32_t kStageWaitPolls = 1u << 22;
+
 // Distances + range flags of the positions P[0..nb); the keys below `thr` (the list's
 // worst entry, or kEmptyKey for no bound) are written sorted to B[0..ns), padded with
 // empty keys to a power of two >= 32; returns ns.  A key at or above the list's worst
 // entry cannot enter the list, so dropping it before the sort leaves every merge result
-// unchanged.  Rows are staged through shared memory with cp.async, stage_rows at a time,
-// chunk c of staged row r at stage_slot(c, r); each lane computes the distance of one
-// staged row.  At most 32 survivors are sorted in registers, more in shared memory.
-// Kept out of line: one copy of the distance loop and sort network serves the entry
-// set, the beam rounds, the hop and the exact route.
+// unchanged.  Rows are staged through shared memory stage_rows at a time, one bulk (TMA)
+// copy per row issued by the lane that evaluates it, completion on the warp's mbarrier;
+// staged rows lie stage_stride chunks apart (an odd number, so lanes reading the same
+// chunk of consecutive rows hit different bank groups).  At most 32 survivors are sorted in
+// registers, more in shared memory.  Kept out of line: one copy of the distance loop and
+// sort network serves the entry set, the beam rounds, the hop and the exact route.
 template <int NCH, bool BYTES>
 __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr, long long vsh) {
     const W w{base, 0u, 0u};
     const uint32_t lane = lane_id();
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
-    const uint32_t nch16 = (nch + 15u) & ~15u;
+    const uint32_t stride = A.stage_stride, row_bytes = nch * 16;
     const uint32_t* P = w.P(A);
     key_t* B = w.B(A);
     uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(w.base + A.o_mbar);
+    uint32_t* phase = w.base + A.o_mbar + 2;
+    uint32_t* abort = w.base + A.o_mbar + 3;
     const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
     const uint32_t SR = A.stage_rows;
     uint32_t ns = 0;
+    if (*abort) return 0;
     for (uint32_t r0 = 0; r0 < nb; r0 += SR) {
         const uint32_t rows = min(SR, nb - r0);
-        const uint32_t total = rows * nch;
-        for (uint32_t e = lane; e < total; e += 32) {
-            const uint32_t r = e / nch, c = e - r * nch;
-            const uint32_t pos = P[r0 + r];
-            cp_async16(stage + (size_t)r * nch16 + stage_slot(c, r), A.vec16 + (pos + vsh) * nch + c);
-        }
+        const uint32_t par = *phase;
+        fence_proxy_async_smem();  // the previous batch's reads of the staging area come first
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(bar, rows * row_bytes);
+        __syncwarp();
         bool inr = false;
         uint32_t pos = 0;
         if (lane < rows) {
             pos = P[r0 + lane];
+            bulk_g2s(stage + (size_t)lane * stride, A.vec16 + (pos + vsh) * nch, row_bytes, bar);
             inr = in_box(A.attrs, pos, A.a, w.lb(A), w.rb(A));
         }
-        cp_async_wait_all();
+        uint32_t polls = 0;
+        while (!mbar_try_wait(bar, par) && ++polls < kStageWaitPolls) {
+        }
+        const bool timed_out = __any_sync(kFull, polls >= kStageWaitPolls);
         __syncwarp();
+        if (lane == 0) {
+            *phase = par ^ 1u;
+            if (timed_out) {
+                *abort = 1u;
+                atomicAdd(A.stats + 7, 1ull);
+            }
+        }
+        __syncwarp();
+        if (timed_out) return 0;
         key_t k = kEmptyKey;
         if (lane < rows) {
-            const float d = BYTES ? dist8_staged<NCH>(stage + (size_t)lane * nch16, q2,
-                                                      reinterpret_cast<const f2x*>(w.base + A.o_sc),
-                                                      reinterpret_cast<const f2x*>(w.base + A.o_bi), A.xmask, nch,
-                                                      lane)
-                                  : dist16_staged<NCH>(stage + (size_t)lane * nch16, q2, nch, lane);
+            const uint4* srow = stage + (size_t)lane * stride;
+            const float d = BYTES ? dist8_staged<NCH>(srow, q2, reinterpret_cast<const f2x*>(w.base + A.o_sc),
+                                                      reinterpret_cast<const f2x*>(w.base + A.o_bi), A.xmask, nch, 0)
+                                  : dist16_staged<NCH>(srow, q2, nch, 0);
             k = make_key(d, pos, inr ? kKeyInRange : 0u);
         }
         const bool keep = k < thr;
@@ -412,6 +433,13 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
     const uint32_t lane = lane_id();
     uint32_t* const base = smem + (threadIdx.x >> 5) * A.warp_words;
     const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
+    if (lane == 0) {
+        mbar_init(reinterpret_cast<uint64_t*>(base + A.o_mbar), 1);
+        base[A.o_mbar + 2] = 0;  // phase
+        base[A.o_mbar + 3] = 0;  // abort
+        fence_mbar_init();
+    }
+    __syncwarp();
 
     for (;;) {
         uint32_t slot = 0;
@@ -764,11 +792,11 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t lg = 0;
     while ((1u << lg) < hs) ++lg;
     A.hshift = 32 - lg;
-    // staging: up to 32 rows, at most 8 KB per warp
+    // staging: up to 32 rows of an odd number of 16-byte chunks, at most 9 KB per warp
     const uint32_t nch16 = (A.nch + 15) / 16 * 16;
-    uint32_t row_bytes = nch16 * 16;
+    A.stage_stride = A.nch | 1u;
     uint32_t sr = 32;
-    while (sr > 1 && sr * row_bytes > 8192) sr >>= 1;
+    while (sr > 1 && sr * A.stage_stride * 16 > 9216) sr >>= 1;
     A.stage_rows = sr;
     make_layout(A, nch16, bytes);
 

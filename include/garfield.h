@@ -135,6 +135,8 @@ typedef struct {
     uint64_t n_hops;    /* cell-to-cell hops */
     uint64_t n_exact;   /* queries answered by the exact route */
     uint64_t n_queries;
+    uint64_t n_timeouts; /* row-staging waits that ran out (the warp then stopped; any
+                            nonzero value makes gf_search_host return GF_ERR_TIMEOUT) */
 } gf_search_stats;
 
 typedef struct {
