@@ -75,32 +75,26 @@ __device__ __forceinline__ float finish8(f2x a0, f2x a1, f2x a2, f2x a3) {
     return __fadd_rn(lo2(t), hi2(t));
 }
 
-// Slot of chunk c of staged row r: chunks are XOR-swizzled within groups of 16 so that
-// lanes reading chunk c of consecutive rows hit different shared-memory bank groups.
-__device__ __forceinline__ uint32_t stage_slot(uint32_t c, uint32_t r) { return (c & ~15u) | ((c ^ r) & 15u); }
+// Partial sums of one half of a staged row (oracle orc_dist16 / orc_dist8): the chunks
+// of parity `half` (16-byte chunks: 8 fp16 or 16 byte elements), element i feeding packed
+// partial pair (i mod 8) / 2.  Two lanes evaluate a row, one per half; the owner of half 0
+// adds the other half's partials (add2) and finishes the sum (finish8).  The chunk loop
+// stays rolled, which keeps the search kernel's instruction footprint small.
 
-// Canonical fp16 squared distance (oracle orc_dist16) of a row staged in shared memory
-// (nch chunks of 8 halves, swizzled by stage_slot with key r) against the query held as
-// fp32 pairs q2[c*4 .. c*4+3] = (q0,q1),(q2,q3),(q4,q5),(q6,q7) of chunk c.  Element i
-// of the row feeds partial i mod 8, so packed accumulator j takes pair j of every chunk
-// and the chunk loop stays rolled (four chunks per trip): a small loop body keeps the
-// search kernel's instruction footprint inside the instruction cache.
+// fp16 rows: the query is held as fp32 pairs q2[c*4 .. c*4+3] of chunk c.
 template <int NCH>
-__device__ __forceinline__ float dist16_staged(const uint4* srow, const f2x* q2, uint32_t nch_rt, uint32_t r) {
+__device__ __forceinline__ void half16(const uint4* srow, const f2x* q2, uint32_t nch_rt, uint32_t half, f2x* p) {
     const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
-    const uint32_t key = r & 15u;
-    f2x p0 = 0ull, p1 = 0ull, p2 = 0ull, p3 = 0ull;
-#pragma unroll 4
-    for (uint32_t c = 0; c < nch; ++c) {
-        const uint4 x = srow[c ^ key];  // == stage_slot(c, r)
+#pragma unroll 2
+    for (uint32_t c = half; c < nch; c += 2) {
+        const uint4 x = srow[c];
         const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q2 + c * 4);
         const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q2 + c * 4 + 2);
-        p0 = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), p0);
-        p1 = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), p1);
-        p2 = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), p2);
-        p3 = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), p3);
+        p[0] = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), p[0]);
+        p[1] = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), p[1]);
+        p[2] = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), p[2]);
+        p[3] = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), p[3]);
     }
-    return finish8(p0, p1, p2, p3);
 }
 
 // Byte element e (0..3) of w as the float 2^23 + byte (exact): the byte is placed under
@@ -109,33 +103,27 @@ __device__ __forceinline__ float byte_f23(uint32_t w, uint32_t e) {
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | e));
 }
 
-// Canonical squared distance (oracle orc_dist8) of a byte row staged in shared memory
-// (nch chunks of 16 bytes, swizzled by stage_slot with key r): element i contributes
-// diff = fma(-scale[i], byte ^ xmask - bias[i], q[i]) to partial i mod 8, the integer
-// difference computed exactly as (2^23 + byte) - (2^23 + bias).  The decoded value is not
-// rounded on its own: ptxas contracts a packed multiply followed by a packed subtract into
-// one fused operation even when both carry .rn, so the fused form is the defined one and
-// is written as such.  q2, ns2, b2: the query, -scale and 2^23 + bias as fp32 pairs.
+// Byte rows: element i contributes diff = fma(-scale[i], byte ^ xmask - bias[i], q[i]), the
+// integer difference computed exactly as (2^23 + byte) - (2^23 + bias).  The decoded value
+// is not rounded on its own: ptxas contracts a packed multiply followed by a packed subtract
+// into one fused operation even when both carry .rn, so the fused form is the defined one
+// and is written as such.  q2, ns2, b2: the query, -scale and 2^23 + bias as fp32 pairs.
 template <int NCH>
-__device__ __forceinline__ float dist8_staged(const uint4* srow, const f2x* q2, const f2x* ns2, const f2x* b2,
-                                              uint32_t xmask, uint32_t nch_rt, uint32_t r) {
+__device__ __forceinline__ void half8(const uint4* srow, const f2x* q2, const f2x* ns2, const f2x* b2, uint32_t xmask,
+                                      uint32_t nch_rt, uint32_t half, f2x* p) {
     const uint32_t nch = NCH ? (uint32_t)NCH : nch_rt;
-    const uint32_t key = r & 15u;
-    f2x p[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll 2
-    for (uint32_t c = 0; c < nch; ++c) {
-        const uint4 x = srow[c ^ key];
+    for (uint32_t c = half; c < nch; c += 2) {
+        const uint4 x = srow[c];
         const uint32_t w[4] = {x.x ^ xmask, x.y ^ xmask, x.z ^ xmask, x.w ^ xmask};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {  // element pairs 2j, 2j+1 of the chunk -> partial pair j % 4
             const uint32_t word = w[j >> 1], e = (j & 1) * 2;
             const f2x u = pack2(byte_f23(word, e), byte_f23(word, e + 1));
             const uint32_t k = c * 8 + j;  // pair index in the row
-            const f2x d = fma2(sub2(u, b2[k]), ns2[k], q2[k]);
-            p[j & 3] = sqacc2(d, p[j & 3]);
+            p[j & 3] = sqacc2(fma2(sub2(u, b2[k]), ns2[k], q2[k]), p[j & 3]);
         }
     }
-    return finish8(p[0], p[1], p[2], p[3]);
 }
 
 // Canonical fp32 squared distance (oracle orc_dist32) of a global row of nch float4
@@ -181,12 +169,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// Waits up to an implementation-defined time (suspend_ns is a hint) for the phase of
+// parity `parity` to complete; false when it has not completed yet.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
         : "memory");
     return ok != 0;
 }

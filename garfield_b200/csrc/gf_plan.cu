@@ -133,138 +133,133 @@ __global__ void box_count_kernel(const float* __restrict__ attrs, uint32_t n, ui
 
 // Four nearest centroids per query (dis_cal_tensor_core + select_topk_by_reduce_min,
 // tools.cuh:1399-1537), distances by one fma chain over d (oracle orc_dist_seq), ties
-// by centroid id.  Block (x, y): 32 queries x the y-th range of c_chunk centroids, in
-// 64-centroid tiles; thread t owns queries 4*(t%8)..+3 and centroids 4*(t/8)..+3 of the
-// tile; both tiles are stored dimension-major in shared memory so each step reads two
-// float4.  Each block writes the 4 best of its range per query to part (q, y); a second
-// kernel merges the ranges.
-constexpr uint32_t kTQ = 32, kTC = 64, kTD = 32;
-__global__ void __launch_bounds__(128) centroid_top4_kernel(const float* __restrict__ queries, uint32_t qnum,
+// by centroid id.  Block (x, y): 64 queries x the y-th range of c_chunk (<= 128)
+// centroids; thread t owns queries 8*(t%8)..+7 and centroids 4*(t/8)..+3 and keeps their
+// 32 distances in registers, each one sequential fma chain over the dimensions.  Query and
+// centroid tiles of kTD dimensions are staged dimension-major in shared memory (float4
+// global loads), so a step reads three float4 for 32 fused multiply-adds.  The finished
+// 64 x 128 distance tile goes through shared memory, where 4 threads per query select its
+// 4 best of the range (part (q, y)); a second kernel merges the ranges.
+constexpr uint32_t kTQ = 64, kTC = 128, kTD = 32;
+constexpr uint32_t kTileWords = kTD * (kTQ + kTC);
+__global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restrict__ queries, uint32_t qnum,
                                                             uint32_t dim, const float* __restrict__ cent,
                                                             uint32_t C, uint32_t c_chunk, float* __restrict__ part_d,
                                                             uint32_t* __restrict__ part_i) {
-    __shared__ __align__(16) float qt[kTD][kTQ];
-    __shared__ __align__(16) float ct[kTD][kTC];
-    __shared__ float md[kTQ][16][4];
-    __shared__ uint32_t mi[kTQ][16][4];
+    // staging tiles (qt: kTD x kTQ, ct: kTD x kTC), then the distance tile (kTQ x kTC)
+    __shared__ __align__(16) float sm[kTQ * kTC > kTileWords ? kTQ * kTC : kTileWords];
+    float* qt = sm;
+    float* ct = sm + kTD * kTQ;
     const uint32_t t = threadIdx.x, qg = t & 7, cg = t >> 3;
     const uint32_t q0 = blockIdx.x * kTQ;
     const uint32_t cbeg = blockIdx.y * c_chunk, cend = min(C, cbeg + c_chunk);
-    float bd[4][4];
-    uint32_t bi[4][4];
+    float acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            bd[i][r] = __int_as_float(0x7f800000);
-            bi[i][r] = kEmpty;
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    const bool vec = (dim & 3u) == 0;
+    for (uint32_t d0 = 0; d0 < dim; d0 += kTD) {
+        __syncthreads();
+        // rows x kTD/4 float4 groups; lanes take consecutive rows at the same dimensions,
+        // so the transposed shared-memory stores hit different banks
+        for (uint32_t e = t; e < (kTQ + kTC) * (kTD / 4); e += blockDim.x) {
+            const bool isq = e < kTQ * (kTD / 4);
+            const uint32_t e2 = isq ? e : e - kTQ * (kTD / 4);
+            const uint32_t rows = isq ? kTQ : kTC;
+            const uint32_t r = e2 % rows, dd = (e2 / rows) * 4;
+            const uint32_t g = (isq ? q0 : cbeg) + r, lim = isq ? qnum : cend;
+            const float* src = isq ? queries : cent;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (g < lim) {
+                const uint32_t d = d0 + dd;
+                if (vec && d + 3 < dim) {
+                    const float4 x = *reinterpret_cast<const float4*>(src + (size_t)g * dim + d);
+                    v[0] = x.x;
+                    v[1] = x.y;
+                    v[2] = x.z;
+                    v[3] = x.w;
+                } else {
+#pragma unroll
+                    for (uint32_t i = 0; i < 4; ++i)
+                        if (d + i < dim) v[i] = src[(size_t)g * dim + d + i];
+                }
+            }
+            float* dst = isq ? qt : ct;
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) dst[(dd + i) * rows + r] = v[i];
         }
-    for (uint32_t c0 = cbeg; c0 < cend; c0 += kTC) {
-        float acc[4][4];
+        __syncthreads();
+        const uint32_t dn = min(kTD, dim - d0);
+        for (uint32_t dd = 0; dd < dn; ++dd) {
+            const float4 qa4 = *reinterpret_cast<const float4*>(&qt[dd * kTQ + qg * 8]);
+            const float4 qb4 = *reinterpret_cast<const float4*>(&qt[dd * kTQ + qg * 8 + 4]);
+            const float4 cv = *reinterpret_cast<const float4*>(&ct[dd * kTC + cg * 4]);
+            const float qa[8] = {qa4.x, qa4.y, qa4.z, qa4.w, qb4.x, qb4.y, qb4.z, qb4.w};
+            const float ca[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-        for (uint32_t d0 = 0; d0 < dim; d0 += kTD) {
-            __syncthreads();
-            // lanes of a warp take consecutive rows at the same 4 dimensions, so the
-            // transposed shared-memory stores hit 32 different banks
-            for (uint32_t e = t; e < kTQ * (kTD / 4); e += blockDim.x) {
-                const uint32_t r = e % kTQ, dd = (e / kTQ) * 4;
-                const uint32_t q = q0 + r;
-#pragma unroll
-                for (uint32_t i = 0; i < 4; ++i) {
-                    const uint32_t d = d0 + dd + i;
-                    qt[dd + i][r] = (q < qnum && d < dim) ? queries[(size_t)q * dim + d] : 0.0f;
+                for (int j = 0; j < 4; ++j) {
+                    const float df = __fsub_rn(qa[i], ca[j]);
+                    acc[i][j] = __fmaf_rn(df, df, acc[i][j]);
                 }
-            }
-            for (uint32_t e = t; e < kTC * (kTD / 4); e += blockDim.x) {
-                const uint32_t r = e % kTC, dd = (e / kTC) * 4;
-                const uint32_t c = c0 + r;
-#pragma unroll
-                for (uint32_t i = 0; i < 4; ++i) {
-                    const uint32_t d = d0 + dd + i;
-                    ct[dd + i][r] = (c < cend && d < dim) ? cent[(size_t)c * dim + d] : 0.0f;
-                }
-            }
-            __syncthreads();
-            const uint32_t dn = min(kTD, dim - d0);
-            for (uint32_t dd = 0; dd < dn; ++dd) {
-                float4 qv = *reinterpret_cast<const float4*>(&qt[dd][qg * 4]);
-                float4 cv = *reinterpret_cast<const float4*>(&ct[dd][cg * 4]);
-                float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ca[4] = {cv.x, cv.y, cv.z, cv.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        float df = __fsub_rn(qa[i], ca[j]);
-                        acc[i][j] = __fmaf_rn(df, df, acc[i][j]);
-                    }
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t c = c0 + cg * 4 + j;
-            if (c >= cend) continue;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float dv = acc[i][j];
-                // insert (dv, c) into the sorted 4-list of query i
-                if (mkkey(dv, c) < mkkey(bd[i][3], bi[i][3])) {
-                    bd[i][3] = dv;
-                    bi[i][3] = c;
-#pragma unroll
-                    for (int r = 3; r > 0; --r) {
-                        if (mkkey(bd[i][r], bi[i][r]) < mkkey(bd[i][r - 1], bi[i][r - 1])) {
-                            float td = bd[i][r];
-                            bd[i][r] = bd[i][r - 1];
-                            bd[i][r - 1] = td;
-                            uint32_t ti = bi[i][r];
-                            bi[i][r] = bi[i][r - 1];
-                            bi[i][r - 1] = ti;
-                        }
-                    }
-                }
-            }
         }
     }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            md[qg * 4 + i][cg][r] = bd[i][r];
-            mi[qg * 4 + i][cg][r] = bi[i][r];
-        }
     __syncthreads();
-    if (t < kTQ && q0 + t < qnum) {
-        float fd[4];
-        uint32_t fi[4];
-        for (int r = 0; r < 4; ++r) {
-            fd[r] = __int_as_float(0x7f800000);
-            fi[r] = kEmpty;
-        }
-        for (uint32_t g = 0; g < 16; ++g)
-            for (int r = 0; r < 4; ++r) {
-                float dv = md[t][g][r];
-                uint32_t c = mi[t][g][r];
-                if (c == kEmpty) continue;
-                if (mkkey(dv, c) < mkkey(fd[3], fi[3])) {
-                    fd[3] = dv;
-                    fi[3] = c;
-                    for (int k = 3; k > 0 && mkkey(fd[k], fi[k]) < mkkey(fd[k - 1], fi[k - 1]); --k) {
-                        float td = fd[k];
-                        fd[k] = fd[k - 1];
-                        fd[k - 1] = td;
-                        uint32_t ti = fi[k];
-                        fi[k] = fi[k - 1];
-                        fi[k - 1] = ti;
-                    }
-                }
+    float* dt = sm;  // kTQ x kTC distances
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dt[(qg * 8 + i) * kTC + cg * 4 + j] = acc[i][j];
+    __syncthreads();
+    // 4 threads per query, 32 centroids each, then a 4-way merge over shuffles
+    const uint32_t ql = t >> 2, part = t & 3;
+    float bd[4];
+    uint32_t bi[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        bd[r] = __int_as_float(0x7f800000);
+        bi[r] = kEmpty;
+    }
+    auto insert = [&](float dv, uint32_t c) {
+        if (!(mkkey(dv, c) < mkkey(bd[3], bi[3]))) return;
+        bd[3] = dv;
+        bi[3] = c;
+#pragma unroll
+        for (int r = 3; r > 0; --r)
+            if (mkkey(bd[r], bi[r]) < mkkey(bd[r - 1], bi[r - 1])) {
+                const float td = bd[r];
+                bd[r] = bd[r - 1];
+                bd[r - 1] = td;
+                const uint32_t ti = bi[r];
+                bi[r] = bi[r - 1];
+                bi[r - 1] = ti;
             }
-        const size_t o = ((size_t)(q0 + t) * gridDim.y + blockIdx.y) * 4;
+    };
+    for (uint32_t k = 0; k < kTC / 4; ++k) {
+        const uint32_t cl = part * (kTC / 4) + ((k + ql) & (kTC / 4 - 1));  // rotation spreads banks
+        const uint32_t c = cbeg + cl;
+        if (c < cend) insert(dt[ql * kTC + cl], c);
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+        float od[4];
+        uint32_t oi[4];
+#pragma unroll
         for (int r = 0; r < 4; ++r) {
-            part_d[o + r] = fd[r];
-            part_i[o + r] = fi[r];
+            od[r] = __shfl_xor_sync(0xFFFFFFFFu, bd[r], o);
+            oi[r] = __shfl_xor_sync(0xFFFFFFFFu, bi[r], o);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+            if (oi[r] != kEmpty) insert(od[r], oi[r]);
+    }
+    if (part == 0 && q0 + ql < qnum) {
+        const size_t o = ((size_t)(q0 + ql) * gridDim.y + blockIdx.y) * 4;
+        for (int r = 0; r < 4; ++r) {
+            part_d[o + r] = bd[r];
+            part_i[o + r] = bi[r];
         }
     }
 }
@@ -345,7 +340,7 @@ uint32_t centroid_chunk(uint32_t C) {
 }
 
 uint32_t centroid_splits(uint32_t C) {
-    uint32_t S = (C + 127) / 128;
+    uint32_t S = (C + kTC - 1) / kTC;
     S = std::min(S, 32u);
     S = std::max(S, 1u);
     // all ranges non-empty
@@ -381,7 +376,7 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     if (d.C) {
         const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
         dim3 grid((qnum + kTQ - 1) / kTQ, S);
-        centroid_top4_kernel<<<grid, 128, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i);
+        centroid_top4_kernel<<<grid, 256, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i);
         centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, s>>>(qnum, S, p.part_d, p.part_i, p.top4);
         order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
     } else {

@@ -121,16 +121,17 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 // Bounded wait for a staging batch: polls of the mbarrier before the warp gives up,
 // counts a timeout in stats[7] and stops evaluating (the host reports GF_ERR_TIMEOUT).
 constexpr uint32_t kStageWaitPolls = 1u << 22;
+constexpr uint32_t kStageSuspendNs = 2000;  // suspend hint of each poll (a copy takes ~1-3 us)
 
 // Distances + range flags of the positions P[0..nb); the keys below `thr` (the list's
 // worst entry, or kEmptyKey for no bound) are written sorted to B[0..ns), padded with
 // empty keys to a power of two >= 32; returns ns.  A key at or above the list's worst
 // entry cannot enter the list, so dropping it before the sort leaves every merge result
-// unchanged.  Rows are staged through shared memory stage_rows at a time, one bulk (TMA)
-// copy per row issued by the lane that evaluates it, completion on the warp's mbarrier;
-// staged rows lie stage_stride chunks apart (an odd number, so lanes reading the same
-// chunk of consecutive rows hit different bank groups).  At most 32 survivors are sorted in
-// registers, more in shared memory.  Kept out of line: one copy of the distance loop and
+// unchanged.  Rows are staged through shared memory stage_rows (<= 16) at a time, one bulk
+// (TMA) copy per row, completion on the warp's mbarrier.  Staged rows lie stage_stride chunks apart (an odd number, so lanes reading the same chunk of consecutive rows hit
+// different bank groups).  Lanes r and r + 16 evaluate row r, one chunk parity each, and
+// lane r adds the two halves.  At most 32 survivors are sorted in registers, more in
+// shared memory.  Kept out of line: one copy of the distance loop and
 // sort network serves the entry set, the beam rounds, the hop and the exact route.
 template <int NCH, bool BYTES>
 __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint32_t nb, key_t thr, long long vsh) {
@@ -145,25 +146,32 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
     uint32_t* phase = w.base + A.o_mbar + 2;
     uint32_t* abort = w.base + A.o_mbar + 3;
     const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
-    const uint32_t SR = A.stage_rows;
+    const uint32_t SR = A.stage_rows, row = lane & 15u, half = lane >> 4;
     uint32_t ns = 0;
     if (*abort) return 0;
-    for (uint32_t r0 = 0; r0 < nb; r0 += SR) {
-        const uint32_t rows = min(SR, nb - r0);
-        const uint32_t par = *phase;
-        fence_proxy_async_smem();  // the previous batch's reads of the staging area come first
+    // copies of stage s (rows s*SR ..); returns the lane's in-range flag
+    auto issue = [&](uint32_t s) -> bool {
+        const uint32_t r0 = s * SR, rows = min(SR, nb - r0);
+        fence_proxy_async_smem();  // earlier reads of the staging area come before the copies
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(bar, rows * row_bytes);
         __syncwarp();
         bool inr = false;
-        uint32_t pos = 0;
         if (lane < rows) {
-            pos = P[r0 + lane];
+            const uint32_t pos = P[r0 + lane];
             bulk_g2s(stage + (size_t)lane * stride, A.vec16 + (pos + vsh) * nch, row_bytes, bar);
             inr = in_box(A.attrs, pos, A.a, w.lb(A), w.rb(A));
         }
+        return inr;
+    };
+    const uint32_t nst = (nb + SR - 1) / SR;
+    bool inr_next = nst ? issue(0) : false;
+    for (uint32_t s = 0; s < nst; ++s) {
+        const bool inr = inr_next;
+        const uint32_t r0 = s * SR, rows = min(SR, nb - r0);
+        const uint32_t par = *phase;
         uint32_t polls = 0;
-        while (!mbar_try_wait(bar, par) && ++polls < kStageWaitPolls) {
+        while (!mbar_try_wait(bar, par, kStageSuspendNs) && ++polls < kStageWaitPolls) {
         }
         const bool timed_out = __any_sync(kFull, polls >= kStageWaitPolls);
         __syncwarp();
@@ -175,20 +183,26 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
             }
         }
         __syncwarp();
-        if (timed_out) return 0;
-        key_t k = kEmptyKey;
-        if (lane < rows) {
-            const uint4* srow = stage + (size_t)lane * stride;
-            const float d = BYTES ? dist8_staged<NCH>(srow, q2, reinterpret_cast<const f2x*>(w.base + A.o_sc),
-                                                      reinterpret_cast<const f2x*>(w.base + A.o_bi), A.xmask, nch, 0)
-                                  : dist16_staged<NCH>(srow, q2, nch, 0);
-            k = make_key(d, pos, inr ? kKeyInRange : 0u);
+        if (timed_out) return 0;  // the buffers are not used again by this warp
+        f2x acc[4] = {0ull, 0ull, 0ull, 0ull};
+        if (row < rows) {
+            const uint4* srow = stage + (size_t)row * stride;
+            if (BYTES)
+                half8<NCH>(srow, q2, reinterpret_cast<const f2x*>(w.base + A.o_sc),
+                           reinterpret_cast<const f2x*>(w.base + A.o_bi), A.xmask, nch, half, acc);
+            else
+                half16<NCH>(srow, q2, nch, half, acc);
         }
+#pragma unroll
+        for (int m = 0; m < 4; ++m) acc[m] = add2(acc[m], __shfl_down_sync(kFull, acc[m], 16));
+        key_t k = kEmptyKey;
+        if (lane < rows) k = make_key(finish8(acc[0], acc[1], acc[2], acc[3]), P[r0 + lane], inr ? kKeyInRange : 0u);
         const bool keep = k < thr;
         const uint32_t msk = __ballot_sync(kFull, keep);
         if (keep) B[ns + __popc(msk & lanemask_lt())] = k;
         ns += __popc(msk);
         __syncwarp();
+        if (s + 1 < nst) inr_next = issue(s + 1);
     }
     if (ns <= 32) {
         if (ns) {
@@ -428,7 +442,7 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
 }
 
 template <int NCH, bool BYTES>
-__global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constant__ SArgs A) {
+__global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constant__ SArgs A) {
     extern __shared__ __align__(16) uint32_t smem[];
     const uint32_t lane = lane_id();
     uint32_t* const base = smem + (threadIdx.x >> 5) * A.warp_words;
@@ -554,11 +568,11 @@ __global__ void __launch_bounds__(128, 4) gmg_search_kernel(const __grid_constan
                             const uint32_t* picks = w.picks(A);
                             uint32_t* H = w.H(A);
                             for (uint32_t j0 = 0; j0 < total; j0 += 32) {
-                                uint32_t j = j0 + lane;
+                                const uint32_t j = j0 + lane;
                                 bool ok = false;
                                 uint32_t pos = kEmpty;
                                 if (j < total) {
-                                    uint32_t node = picks[j / A.R];
+                                    const uint32_t node = picks[j / A.R];
                                     pos = __ldg(A.graph + (gbase + (long long)node * A.R + (j % A.R)));
                                     if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
                                 }
@@ -792,11 +806,11 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t lg = 0;
     while ((1u << lg) < hs) ++lg;
     A.hshift = 32 - lg;
-    // staging: up to 32 rows of an odd number of 16-byte chunks, at most 9 KB per warp
+    // staging: up to 16 rows of an odd number of 16-byte chunks, at most 4.5 KB per warp
     const uint32_t nch16 = (A.nch + 15) / 16 * 16;
     A.stage_stride = A.nch | 1u;
-    uint32_t sr = 32;
-    while (sr > 1 && sr * A.stage_stride * 16 > 9216) sr >>= 1;
+    uint32_t sr = 16;
+    while (sr > 1 && sr * A.stage_stride * 16 > 4608) sr >>= 1;
     A.stage_rows = sr;
     make_layout(A, nch16, bytes);
 

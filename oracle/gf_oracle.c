@@ -28,13 +28,18 @@
  *   orc_dist8          big_dataset_adapterV3.cuh:852-863, 2802-2810  distances to int8 / uint8 rows
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
- *   - orc_dist16 / orc_dist32: squared L2 of two rows of padded length (a multiple of 8).
- *     Eight partial sums: element i feeds p[i mod 8], in increasing order of i, with one
- *     fused multiply-add p = fma(q-x, q-x, p) (q-x rounded to fp32 first).  Then
- *     s[j] = p[j] + p[j+4] (j<4), t[j] = s[j] + s[j+2] (j<2), result = t[0] + t[1].
+ *   - orc_dist32: squared L2 of two rows of padded length (a multiple of 4).  Eight
+ *     partial sums: element i feeds p[i mod 8], in increasing order of i, with one fused
+ *     multiply-add p = fma(q-x, q-x, p) (q-x rounded to fp32 first).  Then
+ *     s[j] = p[j] + p[j+4] (j<4), t[j] = s[j] + s[j+2] (j<2), result = t[0] + t[1] ("finish8").
  *     (Adjacent partials are the two halves of one packed two-wide fp32 register on the
  *     GPU, so every step is one packed instruction and the chunk loop needs no unrolling.)
- *   - orc_dist8: the same eight partials over byte rows (d16 elements): diff =
+ *   - orc_dist16 (search rows, fp16): the row is cut into 16-byte chunks of 8 elements;
+ *     chunks of even index feed partial set 0, odd chunks set 1, element i feeding
+ *     p[set][i mod 8] as above; then s[j] = p[0][j] + p[1][j] and finish8(s).  (On the GPU
+ *     two lanes share a row, one per chunk parity, and add their partials once.)
+ *   - orc_dist8: the same two partial sets over byte rows (d16 elements, 16-element
+ *     chunks, set = chunk index mod 2): diff =
  *     fma(-scale[i], (float)(row[i] ^ xmask) - bias[i], q[i]), i.e. q - scale * (code -
  *     bias) with one rounding (the integer difference is exact); q is the fp32 query times
  *     f2h_factor (not rounded to fp16).
@@ -105,14 +110,17 @@ static inline float finish8(const float p[8]) {
     return t[0] + t[1];
 }
 
-/* fp16 rows of d8 elements (d8 % 8 == 0). */
+/* fp16 rows of d8 elements (d8 % 8 == 0): two partial sets by chunk parity. */
 float orc_dist16(const uint16_t* q, const uint16_t* x, uint32_t d8) {
-    float p[8] = {0};
+    float p[2][8] = {{0}};
     for (uint32_t i = 0; i < d8; ++i) {
         float diff = f16_bits_to_f32(q[i]) - f16_bits_to_f32(x[i]);
-        p[i & 7] = fmaf(diff, diff, p[i & 7]);
+        float* ps = p[(i / 8) & 1];
+        ps[i & 7] = fmaf(diff, diff, ps[i & 7]);
     }
-    return finish8(p);
+    float s8[8];
+    for (int j = 0; j < 8; ++j) s8[j] = p[0][j] + p[1][j];
+    return finish8(s8);
 }
 
 /* fp32 rows of d4 elements (d4 % 4 == 0). */
@@ -128,12 +136,15 @@ float orc_dist32(const float* q, const float* x, uint32_t d4) {
 /* byte rows of d16 elements; see the header for the formula */
 float orc_dist8(const float* q, const uint8_t* x, const float* scale, const float* bias, uint32_t xmask,
                 uint32_t d16) {
-    float p[8] = {0};
+    float p[2][8] = {{0}};
     for (uint32_t i = 0; i < d16; ++i) {
         float diff = fmaf(-scale[i], (float)(uint32_t)(x[i] ^ (uint8_t)xmask) - bias[i], q[i]);
-        p[i & 7] = fmaf(diff, diff, p[i & 7]);
+        float* ps = p[(i / 16) & 1];
+        ps[i & 7] = fmaf(diff, diff, ps[i & 7]);
     }
-    return finish8(p);
+    float s8[8];
+    for (int j = 0; j < 8; ++j) s8[j] = p[0][j] + p[1][j];
+    return finish8(s8);
 }
 
 /*
