@@ -325,7 +325,9 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": int(bytes_step),
                      "counters": {k: int(v) for k, v in st.items()}},
         "clocks": clocks.summary(),
-        "gpu_launches": 7 * args.steps,  # per step: f2h, cell count, cell fill, centroid top-4, order, iota, search
+        # per step: f2h, cell count, cell fill, centroid top-4, centroid merge, cell order, iota,
+        # search (the CUB scan and radix-sort kernels of the planner are library launches)
+        "gpu_launches": 8 * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1)
