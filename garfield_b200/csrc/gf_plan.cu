@@ -153,11 +153,9 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
     const uint32_t t = threadIdx.x, qg = t & 7, cg = t >> 3;
     const uint32_t q0 = blockIdx.x * kTQ;
     const uint32_t cbeg = blockIdx.y * c_chunk, cend = min(C, cbeg + c_chunk);
-    float acc[8][4];
+    f2x acc2[8][2];  // (query i, centroid pair j) partial distances, fp32 pairs
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int i = 0; i < 8; ++i) acc2[i][0] = acc2[i][1] = 0ull;
     const bool vec = (dim & 3u) == 0;
     for (uint32_t d0 = 0; d0 < dim; d0 += kTD) {
         __syncthreads();
@@ -194,16 +192,15 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
         for (uint32_t dd = 0; dd < dn; ++dd) {
             const float4 qa4 = *reinterpret_cast<const float4*>(&qt[dd * kTQ + qg * 8]);
             const float4 qb4 = *reinterpret_cast<const float4*>(&qt[dd * kTQ + qg * 8 + 4]);
-            const float4 cv = *reinterpret_cast<const float4*>(&ct[dd * kTC + cg * 4]);
+            const ulonglong2 cv = *reinterpret_cast<const ulonglong2*>(&ct[dd * kTC + cg * 4]);
             const float qa[8] = {qa4.x, qa4.y, qa4.z, qa4.w, qb4.x, qb4.y, qb4.z, qb4.w};
-            const float ca[4] = {cv.x, cv.y, cv.z, cv.w};
+            // packed pairs of centroids (j, j+1): two independent IEEE operations each
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float df = __fsub_rn(qa[i], ca[j]);
-                    acc[i][j] = __fmaf_rn(df, df, acc[i][j]);
-                }
+            for (int i = 0; i < 8; ++i) {
+                const f2x qq = pack2(qa[i], qa[i]);
+                acc2[i][0] = sqacc2(sub2(qq, cv.x), acc2[i][0]);
+                acc2[i][1] = sqacc2(sub2(qq, cv.y), acc2[i][1]);
+            }
         }
     }
     __syncthreads();
@@ -211,7 +208,10 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) dt[(qg * 8 + i) * kTC + cg * 4 + j] = acc[i][j];
+        for (int j = 0; j < 2; ++j) {
+            dt[(qg * 8 + i) * kTC + cg * 4 + 2 * j] = lo2(acc2[i][j]);
+            dt[(qg * 8 + i) * kTC + cg * 4 + 2 * j + 1] = hi2(acc2[i][j]);
+        }
     __syncthreads();
     // 4 threads per query, 32 centroids each, then a 4-way merge over shuffles
     const uint32_t ql = t >> 2, part = t & 3;
