@@ -69,7 +69,7 @@ class _IndexFiles(C.Structure):
 
 class _SearchParams(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in
-                ("L", "k", "width", "max_iter", "n_entry", "postfilter", "hash_slots", "reserved")]
+                ("L", "k", "width", "max_iter", "n_entry", "postfilter", "hash_slots", "test_wait")]
 
 
 class _SearchStats(C.Structure):
@@ -186,10 +186,11 @@ class SearchParams:
     n_entry: int = 0          # 0 = graph degree
     postfilter: int = 0xFFFFFFFF
     hash_slots: int = 0       # 0 = automatic
+    test_wait: int = 0        # test hook: staging waits give up after this many polls and never complete
 
     def _c(self) -> _SearchParams:
         return _SearchParams(self.L, self.k, self.width, self.max_iter, self.n_entry, self.postfilter,
-                             self.hash_slots, 0)
+                             self.hash_slots, self.test_wait)
 
 
 # ------------------------------------------------------------------ index

@@ -489,7 +489,7 @@ void gf_search_defaults(gf_search_params* p) {
     p->n_entry = 0;  // 0 = graph degree
     p->postfilter = 0xFFFFFFFFu;
     p->hash_slots = 0;
-    p->reserved = 0;
+    p->test_wait = 0;
 }
 
 gf_status gf_index_create(const gf_index_desc* desc, int device, gf_index** out) {

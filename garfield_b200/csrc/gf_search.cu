@@ -61,6 +61,7 @@ struct SArgs {
     uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, stage_stride, warp_words;
+    uint32_t wait_polls, extra_tx;  // staging wait limit; test hook: bytes expected but never sent
     // word offsets inside a warp's shared-memory slice
     uint32_t o_sc, o_bi;  // byte codecs: -scale and 2^23 + bias pairs
     uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
@@ -120,7 +121,7 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 
 // Bounded wait for a staging batch: polls of the mbarrier before the warp gives up,
 // counts a timeout in stats[7] and stops evaluating (the host reports GF_ERR_TIMEOUT).
-constexpr uint32_t kStageWaitPolls = 1u << 22;
+constexpr uint32_t kStageWaitPolls = 1u << 19;  // with the suspend hint, about a second
 constexpr uint32_t kStageSuspendNs = 2000;  // suspend hint of each poll (a copy takes ~1-3 us)
 
 // Distances + range flags of the positions P[0..nb); the keys below `thr` (the list's
@@ -154,7 +155,7 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         const uint32_t r0 = s * SR, rows = min(SR, nb - r0);
         fence_proxy_async_smem();  // earlier reads of the staging area come before the copies
         __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(bar, rows * row_bytes);
+        if (lane == 0) mbar_arrive_expect_tx(bar, rows * row_bytes + A.extra_tx);
         __syncwarp();
         bool inr = false;
         if (lane < rows) {
@@ -171,9 +172,9 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         const uint32_t r0 = s * SR, rows = min(SR, nb - r0);
         const uint32_t par = *phase;
         uint32_t polls = 0;
-        while (!mbar_try_wait(bar, par, kStageSuspendNs) && ++polls < kStageWaitPolls) {
+        while (!mbar_try_wait(bar, par, kStageSuspendNs) && ++polls < A.wait_polls) {
         }
-        const bool timed_out = __any_sync(kFull, polls >= kStageWaitPolls);
+        const bool timed_out = __any_sync(kFull, polls >= A.wait_polls);
         __syncwarp();
         if (lane == 0) {
             *phase = par ^ 1u;
@@ -411,10 +412,11 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         nf -= take;
     }
     __syncwarp();
-    eval_sort<NCH, BYTES>(A, w.base, nb, kEmptyKey, cell_vsh(A, next));
+    // every key is below kEmptyKey, so ns == nb unless the warp stopped on a staging timeout
+    const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, kEmptyKey, cell_vsh(A, next));
     st_dist += nb;
-    const uint32_t ne = min(nb, A.n_entry);
-    const uint32_t nm = min(nb - ne, kHopSlots);
+    const uint32_t ne = min(ns, A.n_entry);
+    const uint32_t nm = min(ns - ne, kHopSlots);
     merge_step(A, w, A.L, ne, nm, false);
     // visited set of the next cell: its entry set + its points now in T
     hash_clear(H, A.hs);
@@ -528,8 +530,10 @@ __global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constan
                     }
                     __syncwarp();
                     hcount = nb;
-                    eval_sort<NCH, BYTES>(A, w.base, nb, kEmptyKey, cell_vsh(A, cell));
-                    st_dist += nb;
+                    // ns == nb unless the warp stopped on a staging timeout
+                    const uint32_t n0 = nb;
+                    nb = eval_sort<NCH, BYTES>(A, w.base, n0, kEmptyKey, cell_vsh(A, cell));
+                    st_dist += n0;
                 }
                 for (uint32_t ci = c0; ci < nc;) {
                     const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
@@ -791,6 +795,8 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.postfilter = P.postfilter;
     A.n = d.n;
     A.prefilter = p.prefilter;
+    A.wait_polls = P.test_wait ? P.test_wait : kStageWaitPolls;
+    A.extra_tx = P.test_wait ? 16u : 0u;
     uint32_t need = std::max<uint32_t>({P.width * d.degree, n_entry, kHopSlots * A.E, 64u});
     uint32_t bcap = 1;
     while (bcap < need) bcap <<= 1;

@@ -124,7 +124,11 @@ typedef struct {
     uint32_t n_entry;    /* entry points of the first cell (= degree in the reference) */
     uint32_t postfilter; /* --postfilter: queries with >= this many cells scan exactly */
     uint32_t hash_slots; /* visited-hash slots per query, power of two; 0 = automatic */
-    uint32_t reserved;
+    uint32_t test_wait;  /* 0 in normal use.  Test hook for the timeout path: a row-staging
+                            wait gives up after test_wait polls, and every staging batch
+                            expects 16 bytes more than it copies, so no wait completes; the
+                            warps stop, gf_search_stats.n_timeouts counts them and
+                            gf_search_host returns GF_ERR_TIMEOUT. */
 } gf_search_params;
 
 /* Per-search counters (device-side, summed over queries). */

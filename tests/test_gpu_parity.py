@@ -176,3 +176,22 @@ def test_plan_may_outlive_its_index(small):
     g.close()
     plan.close()
     make_index(small).close()
+
+
+def test_staging_wait_timeout_is_reported(small, g_small):
+    """The bounded row-staging wait: with the test hook no staging batch can complete, the
+    waits give up, the warps stop, the counter and gf_search_host report it, and the
+    context stays usable for the next search."""
+    c = small
+    plan = g_small.plan(c.ds.queries.shape[0])
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+    plan.search(gf.SearchParams(L=32, k=10, test_wait=64))
+    assert plan.stats()["n_timeouts"] > 0
+    with pytest.raises(gf.GarfieldError) as e:
+        g_small.search_host(c.ds.queries, c.ds.lo.astype(np.float32), c.ds.hi.astype(np.float32), plan,
+                            gf.SearchParams(L=32, k=10, test_wait=64))
+    assert e.value.status == 6
+    ids, dist = plan.search(gf.SearchParams(L=32, k=10))
+    assert plan.stats()["n_timeouts"] == 0
+    ref_ids, ref_d, _ = _oracle_search(c, L=32, K=10)
+    assert np.array_equal(as_u32(ids), ref_ids)
