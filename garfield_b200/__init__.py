@@ -74,7 +74,7 @@ class _SearchParams(C.Structure):
 
 class _SearchStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("n_dist", "n_exp", "n_cross", "n_hops", "n_exact", "n_queries",
-                                          "n_timeouts")]
+                                          "n_timeouts", "n_plan_fallbacks", "n_plan_reranked")]
 
 
 class _IndexInfo(C.Structure):

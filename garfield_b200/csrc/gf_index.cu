@@ -4,6 +4,7 @@
 // (tools.cuh:862-915), load_result of the global graph (tools.cuh:205-223), f2h
 // (tools.cuh:308-321), load_clustering (tools.cuh:569-602).
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <random>
@@ -75,7 +76,8 @@ static gf_status dalloc(T** p, size_t count, uint64_t* bytes) {
 static void free_index(DeviceIndex& d) {
     void* ptrs[] = {d.vec16,   d.vec32,   d.attrs,     d.graph,   d.cross,   d.i2g,     d.seg,
                     d.grid_d,  d.lq_d,    d.rq_d,      d.centroids, d.hist,  d.entry,   d.sh_slot,
-                    d.sh_gofs, d.sh_xofs, d.sh_vsh,    d.vec8,      d.csc,   d.cbi};
+                    d.sh_gofs, d.sh_xofs, d.sh_vsh,    d.vec8,      d.csc,   d.cbi,     d.cnorm,
+                    d.cmean};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);
@@ -327,6 +329,32 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         for (uint32_t c = 0; c < d.C; ++c)
             for (uint32_t k = 0; k < d.dim; ++k) centroids[(size_t)c * d.dim + k] /= (float)num[c];
     }
+    // tensor-core planner inputs: the centroids' mean m and, per centroid, the squared norm
+    // of c - m (fp32 differences, as the device forms them) and its square root
+    std::vector<float> cmean(d.C ? d.dim : 0, 0.0f), cnorm(2 * (size_t)d.C, 0.0f);
+    if (d.C) {
+        // mean over the finite centroids (an empty cluster's centroid is 0/0)
+        std::vector<double> msum(d.dim, 0.0);
+        uint32_t nfin = 0;
+        for (uint32_t c = 0; c < d.C; ++c) {
+            const float* cr = &centroids[(size_t)c * d.dim];
+            bool fin = true;
+            for (uint32_t k = 0; k < d.dim && fin; ++k) fin = std::isfinite(cr[k]);
+            if (!fin) continue;
+            ++nfin;
+            for (uint32_t k = 0; k < d.dim; ++k) msum[k] += cr[k];
+        }
+        for (uint32_t k = 0; k < d.dim; ++k) cmean[k] = nfin ? (float)(msum[k] / nfin) : 0.0f;
+        for (uint32_t c = 0; c < d.C; ++c) {
+            float acc = 0.0f;
+            for (uint32_t k = 0; k < d.dim; ++k) {
+                const float t = centroids[(size_t)c * d.dim + k] - cmean[k];
+                acc += t * t;
+            }
+            cnorm[2 * (size_t)c] = acc;
+            cnorm[2 * (size_t)c + 1] = std::sqrt(acc);
+        }
+    }
 
     DeviceGuard guard(device);
     gf_status st = GF_OK;
@@ -380,6 +408,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         if (d.C) {
             if (!chk(dalloc(&d.centroids, (size_t)d.C * d.dim, &d.bytes))) break;
             if (!chk(dalloc(&d.hist, (size_t)P * d.C, &d.bytes))) break;
+            if (!chk(dalloc(&d.cnorm, 2 * (size_t)d.C, &d.bytes))) break;
+            if (!chk(dalloc(&d.cmean, d.dim, &d.bytes))) break;
         }
         // fp32 rows in position order (temporary unless kept)
         uint64_t dummy = 0;
@@ -428,6 +458,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             {d.entry, d.entry_h.data(), d.entry_h.size() * 4},
             {d.centroids, centroids.data(), centroids.size() * 4},
             {d.hist, hist.data(), hist.size() * 4},
+            {d.cnorm, cnorm.data(), cnorm.size() * 4},
+            {d.cmean, cmean.data(), cmean.size() * 4},
             {d.sh_slot, sh_slot.data(), sh_slot.size() * 4},
             {d.sh_gofs, sh_gofs.data(), sh_gofs.size() * 8},
             {d.sh_xofs, sh_xofs.data(), sh_xofs.size() * 8},

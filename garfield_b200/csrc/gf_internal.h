@@ -75,6 +75,8 @@ struct DeviceIndex {
     float* lq_d = nullptr;
     float* rq_d = nullptr;
     float* centroids = nullptr;  // C x dim fp32
+    float* cnorm = nullptr;      // C x (|c - m|^2, |c - m|) of the centroids (tensor-core planner)
+    float* cmean = nullptr;      // dim: the centroids' mean m (tensor-core planner)
     uint32_t* hist = nullptr;    // ncells x C
     uint32_t* entry = nullptr;   // entry_h on device
 };
@@ -98,6 +100,7 @@ struct Plan {
     uint32_t* offsets = nullptr; // max_q
     uint32_t* cells = nullptr;   // max_q x ncells
     uint32_t* top4 = nullptr;    // max_q x 4
+    float* S = nullptr;          // max_q x centroid_tc_stride query-centroid products (tensor-core planner), or NULL
     float* part_d = nullptr;     // max_q x splits x 4 per-range centroid candidates
     uint32_t* part_i = nullptr;
     uint32_t* box = nullptr;     // max_q (box counts)
@@ -128,9 +131,14 @@ struct gf_plan {
 namespace gf {
 // gf_plan.cu
 uint32_t centroid_splits(uint32_t C);  // centroid ranges of the top-4 kernel
-uint32_t centroid_chunk(uint32_t C);   // centroids per range (multiple of 64)
+uint32_t centroid_chunk(uint32_t C);   // centroids per range (multiple of 128)
 gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
                        uint32_t qnum, float prefilter, cudaStream_t s);
+// gf_centroid_tc.cu
+bool centroid_tc_usable(const DeviceIndex& d);
+size_t centroid_tc_stride(const DeviceIndex& d);  // floats per row of the plan's S
+gf_status centroid_top4_tc(const DeviceIndex& d, const float* q32, uint32_t qnum, float* S, uint32_t* top4,
+                           uint32_t* counters, cudaStream_t s);
 // gf_search.cu
 // Restriction of one search launch to a set of cells ("slots"), whose graph rows and
 // cross-edge rows may lie anywhere in device memory (batched and out-of-core search).

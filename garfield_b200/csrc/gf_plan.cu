@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
     float bd[4];
     uint32_t bi[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        bd[r] = __int_as_float(0x7f800000);
+    for (int r = 0; r < 4; ++r) {  // all-ones key: above every distance, NaN (empty cluster) included
+        bd[r] = __int_as_float(0xffffffff);
         bi[r] = kEmpty;
     }
     auto insert = [&](float dv, uint32_t c) {
@@ -272,7 +272,7 @@ __global__ void centroid_merge_kernel(uint32_t qnum, uint32_t splits, const floa
     float fd[4];
     uint32_t fi[4];
     for (int r = 0; r < 4; ++r) {
-        fd[r] = __int_as_float(0x7f800000);
+        fd[r] = __int_as_float(0xffffffff);
         fi[r] = kEmpty;
     }
     for (uint32_t e = 0; e < splits * 4; ++e) {
@@ -373,7 +373,14 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     GF_CUDA(cub::DeviceScan::ExclusiveSum(p.scan_tmp, tmp, p.counts, p.offsets, (int)qnum, s));
     plan_fill_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts, p.offsets,
                                        p.cells);
-    if (d.C) {
+    // planner counters, read by gf_plan_stats: scratch[8] tensor-core waits that ran out,
+    // [9] queries that fell back to the exact centroid scan, [10] centroids re-ranked exactly
+    GF_CUDA(cudaMemsetAsync(p.scratch + 8, 0, 3 * sizeof(uint32_t), s));
+    if (d.C && p.S && centroid_tc_usable(d)) {  // tensor-core products + exact re-rank
+        gf_status st = centroid_top4_tc(d, p.q32, qnum, p.S, p.top4, p.scratch + 8, s);
+        if (st != GF_OK) return st;
+        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
+    } else if (d.C) {
         const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
         dim3 grid((qnum + kTQ - 1) / kTQ, S);
         centroid_top4_kernel<<<grid, 256, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i);
@@ -414,7 +421,7 @@ struct DeviceGuard2 {
 };
 
 void free_plan(Plan& p) {
-    void* ptrs[] = {p.q16, p.q32, p.lb, p.rb, p.counts, p.offsets, p.cells, p.top4, p.box, p.task, p.scratch,
+    void* ptrs[] = {p.S, p.q16, p.q32, p.lb, p.rb, p.counts, p.offsets, p.cells, p.top4, p.box, p.task, p.scratch,
                     p.stats, p.scan_tmp, p.part_d, p.part_i};
     for (void* x : ptrs)
         if (x) cudaFree(x);
@@ -450,6 +457,7 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
     A((void**)&p.offsets, Q * 4);
     A((void**)&p.cells, Q * d.ncells * 4);
     A((void**)&p.top4, Q * 16);
+    if (centroid_tc_usable(d)) A((void**)&p.S, Q * centroid_tc_stride(d) * 4);
     A((void**)&p.part_d, Q * centroid_splits(d.C) * 16);
     A((void**)&p.part_i, Q * centroid_splits(d.C) * 16);
     A((void**)&p.box, Q * 4);
@@ -537,7 +545,11 @@ gf_status gf_search_stats_read(gf_plan* plan, gf_search_stats* out) {
     out->n_hops = v[3];
     out->n_exact = v[4];
     out->n_queries = v[5];
-    out->n_timeouts = v[7];
+    uint32_t pc[3];
+    GF_CUDA(cudaMemcpy(pc, p.scratch + 8, sizeof(pc), cudaMemcpyDeviceToHost));
+    out->n_timeouts = v[7] + pc[0];
+    out->n_plan_fallbacks = pc[1];
+    out->n_plan_reranked = pc[2];
     return GF_OK;
 }
 
@@ -587,8 +599,10 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
             break;
         e = cudaStreamSynchronize(s);
         unsigned long long to = 0;
+        uint32_t pto = 0;
         if (e == cudaSuccess) e = cudaMemcpy(&to, p.stats + 7, sizeof(to), cudaMemcpyDeviceToHost);
-        if (e == cudaSuccess && to) st = fail(GF_ERR_TIMEOUT, "row staging wait ran out in the search kernel");
+        if (e == cudaSuccess) e = cudaMemcpy(&pto, p.scratch + 8, sizeof(pto), cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && (to || pto)) st = fail(GF_ERR_TIMEOUT, "a bounded device wait ran out");
     } while (0);
     if (st != GF_OK) return st;
     if (e != cudaSuccess) return cuda_fail(e, "gf_search_host");

@@ -140,7 +140,12 @@ typedef struct {
     uint64_t n_exact;   /* queries answered by the exact route */
     uint64_t n_queries;
     uint64_t n_timeouts; /* row-staging waits that ran out (the warp then stopped; any
-                            nonzero value makes gf_search_host return GF_ERR_TIMEOUT) */
+                            nonzero value makes gf_search_host return GF_ERR_TIMEOUT), plus
+                            tensor-core waits of the planner that ran out */
+    uint64_t n_plan_fallbacks; /* queries whose 4 nearest centroids the tensor-core planner
+                            could not narrow below its candidate cap (exact scan instead) */
+    uint64_t n_plan_reranked; /* centroids the tensor-core planner re-ranked with the exact
+                            distance (those its error bound could not rule out) */
 } gf_search_stats;
 
 typedef struct {

@@ -214,7 +214,14 @@ typedef struct {
     uint32_t id;
 } orc_pair;
 
-static inline int pair_less(orc_pair x, orc_pair y) { return x.d < y.d || (x.d == y.d && x.id < y.id); }
+/* (distance, id) order; a NaN distance (the 0/0 centroid of an empty cluster, as
+ * load_clustering tools.cuh:600-603 computes it) ranks after every number, NaNs by id --
+ * the order of the device keys, whose NaN bit pattern is above +inf. */
+static inline int pair_less(orc_pair x, orc_pair y) {
+    const int xn = isnan(x.d), yn = isnan(y.d);
+    if (xn || yn) return xn ? (yn && x.id < y.id) : 1;
+    return x.d < y.d || (x.d == y.d && x.id < y.id);
+}
 
 /* Insert into a sorted list of capacity k holding *n items; keeps the k smallest. */
 static inline void topk_insert(orc_pair* list, uint32_t* n, uint32_t k, orc_pair v) {

@@ -175,3 +175,27 @@ def test_batched_search_properties(small, odd):
         ids5, _, _ = oracle.search(*args, L=16, K=10, postfilter=1, batches=[[0]])
         in0 = np.isin(ids5, np.flatnonzero(c.ix.cell_of == 0)) | (ids5 == oracle.EMPTY)
         assert in0.all()
+
+
+def test_nan_centroid_ranks_last():
+    """An empty cluster's 0/0 centroid ranks after every real centroid whatever its id
+    (pair_less orders NaN distances after numbers, NaNs by id)."""
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((6, 8)).astype(np.float32)
+    cent = rng.standard_normal((7, 8)).astype(np.float32)
+    for gap in (0, 2, 6):
+        c2 = cent.copy()
+        c2[gap] = np.nan
+        hist = np.ones((1, 7), np.uint32)
+        counts = np.ones(6, np.uint32)
+        offsets = np.arange(6, dtype=np.uint32)
+        cells = np.zeros(6, np.uint32)
+        _, top4 = oracle.order_cells(q, c2, hist, counts, offsets, cells)
+        assert not (top4 == gap).any()
+        d = ((q[:, None, :] - c2[None]) ** 2).sum(-1)
+        d[:, gap] = np.inf
+        assert np.array_equal(top4, np.argsort(d, axis=1, kind="stable")[:, :4].astype(np.uint32))
+    c3 = np.full((5, 8), np.nan, np.float32)
+    c3[1] = 0.0
+    _, top4 = oracle.order_cells(q, c3, np.ones((1, 5), np.uint32), counts, offsets, cells)
+    assert (top4 == np.array([1, 0, 2, 3], np.uint32)).all()
