@@ -322,14 +322,13 @@ __device__ __forceinline__ float chain_dists(const float* __restrict__ q, const 
 }
 
 // Error-bound constants of one query (see the file comment).  For a centroid with centred
-// squared norm cn (and norm ncn) and approximate distance dt:
+// squared norm cn (norm ncn) and approximate distance dt, |canonical - dt| stays within
 //   E = k_prod ncn + k_norm (qn + cn) + k_cent (nq + ncn)^2 + k_dt |dt|
+// (products, norms and their sum, centring, the subtraction forming dt) before the
+// canonical chain's own relative error g_can.  With (nq + ncn)^2 <= 2 (qn + cn) and
+// |dt| <= (2 + 2 a_inner)(qn + cn) this is at most  B ncn + D (qn + cn).
 struct Bound {
-    float qn, k_prod, k_norm, k_cent, k_dt, nq, up, dn;
-    __device__ __forceinline__ float err(float cn, float ncn, float dt) const {
-        const float t = nq + ncn;
-        return k_prod * ncn + k_norm * (qn + cn) + k_cent * t * t + k_dt * fabsf(dt);
-    }
+    float B, D, up, dn;
 };
 
 __device__ __forceinline__ Bound make_bound(float qn, uint32_t dim) {
@@ -339,15 +338,15 @@ __device__ __forceinline__ Bound make_bound(float qn, uint32_t dim) {
     // fp32 accumulation of 3 * dim products, its term doubled in case the tensor cores
     // truncate instead of rounding
     const float a_inner = 3.01f * 9.5367432e-7f + 2.0f * (float)(3 * dim + 2) * u * 1.003f;
+    const float s = 1.05f;                    // slack for the roundings of the bound's own arithmetic
+    const float k_prod = 2.0f * a_inner * sqrtf(qn);  // 2 S
+    const float k_norm = gD + 2.0f * u;       // both squared norms and the sum qn + cn
+    const float k_cent = 2.1f * u;            // rounding of the centring subtractions
+    const float k_dt = 2.0f * u;              // the subtraction forming dt
+    const float g_can = gD + 2.0f * u;        // the canonical chain against the exact distance
     Bound b;
-    b.qn = qn;
-    b.nq = sqrtf(qn);
-    const float s = 1.05f;  // slack for the roundings of the bound's own arithmetic
-    b.k_prod = s * 2.0f * a_inner * b.nq;  // 2 S
-    b.k_norm = s * (gD + 2.0f * u);        // both squared norms and the sum qn + cn
-    b.k_cent = s * 2.1f * u;               // rounding of the centring subtractions
-    b.k_dt = s * 2.0f * u;                 // the subtraction forming dt
-    const float g_can = gD + 2.0f * u;     // the canonical chain against the exact distance
+    b.B = s * k_prod;
+    b.D = s * (k_norm + 2.0f * k_cent + (2.0f + 2.0f * a_inner) * k_dt);
     b.up = (1.0f + g_can) * (1.0f + 4.0f * u);
     b.dn = (1.0f - g_can) * (1.0f - 4.0f * u);
     return b;
@@ -366,6 +365,7 @@ __global__ void __launch_bounds__(128) centroid_select_kernel(const float* __res
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t q = blockIdx.x * 4 + warp;
     if (q >= qnum) return;
+    const float kInf = __int_as_float(0x7f800000);
     const float* qv = Q + (size_t)q * dim;
     float qn = 0.0f;  // centred squared norm
     for (uint32_t d = lane; d < dim; d += 32) {
@@ -376,29 +376,59 @@ __global__ void __launch_bounds__(128) centroid_select_kernel(const float* __res
     for (int o = 16; o > 0; o >>= 1) qn = __fadd_rn(qn, __shfl_xor_sync(kFull, qn, o));
     const Bound b = make_bound(qn, dim);
     const float* Sq = S + (size_t)q * s_stride;
-    // pass 1: U = 4th smallest upper bound
-    key_t ubk[4] = {kEmptyKey, kEmptyKey, kEmptyKey, kEmptyKey};
+    float* ws = rr_smem + warp * kRrWarpFloats;
+    // pass 1: every lane keeps its 4 smallest upper bounds; lower bounds are stashed in the
+    // warp's staging area when they fit (a NaN centroid's as +inf: it is kept only when
+    // U = +inf, i.e. when fewer than 4 centroids have numbers)
+    const bool stash = C <= kRrWarpFloats;
+    float t0 = kInf, t1 = kInf, t2 = kInf, t3 = kInf;
     for (uint32_t c = lane; c < C; c += 32) {
         const float2 cn = cnorm[c];
-        const float dt = (qn + cn.x) - 2.0f * Sq[c];
-        float ub = (dt + b.err(cn.x, cn.y, dt)) * b.up;
-        // a NaN (empty cluster, non-finite input) bounds nothing: +inf, never a small U
-        ub = ub >= 0.0f ? ub : (ub < 0.0f ? 0.0f : __int_as_float(0x7f800000));
-        top4_insert(ubk, make_key(ub, c, 0));
+        const float qc = qn + cn.x;
+        const float dt = __fmaf_rn(-2.0f, Sq[c], qc);
+        const float E = __fmaf_rn(b.B, cn.y, b.D * qc);
+        float ub = (dt + E) * b.up;
+        ub = ub >= 0.0f ? ub : (ub < 0.0f ? 0.0f : kInf);  // NaN bounds nothing: +inf
+        if (stash) ws[c] = isnan(cn.x) ? kInf : (dt - E) * b.dn;
+        if (ub < t3) {
+            t3 = ub;
+            if (t3 < t2) { const float x = t2; t2 = t3; t3 = x; }
+            if (t2 < t1) { const float x = t1; t1 = t2; t2 = x; }
+            if (t1 < t0) { const float x = t0; t0 = t1; t1 = x; }
+        }
     }
-    top4_warp(ubk);
-    const float U = ubk[3] == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(ubk[3]);
-    // pass 2: candidates whose lower bound does not exceed U
+    // U = 4th smallest over the warp: four rounds of popping the warp minimum (the bounds
+    // are >= +0, so their bit patterns order like the values)
+    uint32_t Ub = 0;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        Ub = __reduce_min_sync(kFull, __float_as_uint(t0));
+        const uint32_t win = __ffs(__ballot_sync(kFull, __float_as_uint(t0) == Ub)) - 1;
+        if (lane == win) {
+            t0 = t1;
+            t1 = t2;
+            t2 = t3;
+            t3 = kInf;
+        }
+    }
+    const float U = __uint_as_float(Ub);
+    __syncwarp();
+    // pass 2: candidates whose lower bound does not exceed U (a NaN bound is kept)
     uint32_t nc = 0;
     for (uint32_t c0 = 0; c0 < C; c0 += 32) {
         const uint32_t c = c0 + lane;
         bool keep = false;
         if (c < C) {
-            const float2 cn = cnorm[c];
-            const float dt = (qn + cn.x) - 2.0f * Sq[c];
-            // a NaN centroid (empty cluster) ranks after every number: never among the 4
-            // nearest while 4 candidates with numbers exist (checked below)
-            keep = !isnan(cn.x) && !((dt - b.err(cn.x, cn.y, dt)) * b.dn > U);  // a NaN bound is kept
+            float lb;
+            if (stash) {
+                lb = ws[c];
+            } else {
+                const float2 cn = cnorm[c];
+                const float qc = qn + cn.x;
+                const float dt = __fmaf_rn(-2.0f, Sq[c], qc);
+                lb = isnan(cn.x) ? kInf : (dt - __fmaf_rn(b.B, cn.y, b.D * qc)) * b.dn;
+            }
+            keep = !(lb > U);
         }
         const uint32_t m = __ballot_sync(kFull, keep);
         const uint32_t at = nc + __popc(m & lanemask_lt());
@@ -407,27 +437,42 @@ __global__ void __launch_bounds__(128) centroid_select_kernel(const float* __res
     }
     __syncwarp();
     // re-rank every centroid when the bound kept too many, when fewer than 4 candidates
-    // remain (fewer than 4 centroids with numbers) or when the query is not finite
-    const bool scan_all = nc > kMaxCand || nc < 4 || !(fabsf(qn) < __int_as_float(0x7f800000));
+    // remain or when the query is not finite
+    const bool scan_all = nc > kMaxCand || nc < 4 || !(fabsf(qn) < kInf);
     if (lane == 0) {
         if (scan_all) atomicAdd(counters + 1, 1u);
         atomicAdd(counters + 2, scan_all ? C : nc);
     }
     const uint32_t n = scan_all ? C : nc;
-    // exact re-rank, 32 candidates at a time (lane i: candidate g0 + i)
-    key_t best[4] = {kEmptyKey, kEmptyKey, kEmptyKey, kEmptyKey};
     const uint32_t* cw = cand[warp];
-    for (uint32_t g0 = 0; g0 < n; g0 += 32) {
-        const uint32_t ng = min(32u, n - g0);
-        auto id = [&](uint32_t i) { return scan_all ? g0 + i : cw[g0 + i]; };
-        const float acc = chain_dists(qv, Cm, dim, ng, id, rr_smem + warp * kRrWarpFloats, lane);
-        if (lane < ng) top4_insert(best, make_key(acc, id(lane), 0));
-    }
-    top4_warp(best);
-    key_t mine = best[0];
+    key_t mine;
+    if (n <= 32) {  // one candidate per lane: four rounds of popping the warp's smallest key
+        auto id = [&](uint32_t i) { return scan_all ? i : cw[i]; };
+        const float acc = chain_dists(qv, Cm, dim, n, id, ws, lane);
+        key_t k = lane < n ? make_key(acc, id(lane), 0) : kEmptyKey;
+        mine = kEmptyKey;
 #pragma unroll
-    for (uint32_t r = 1; r < 4; ++r)
-        if (lane == r) mine = best[r];
+        for (uint32_t r = 0; r < 4; ++r) {
+            const uint32_t hi = (uint32_t)(k >> 32), lo = (uint32_t)k;
+            const uint32_t mh = __reduce_min_sync(kFull, hi);
+            const uint32_t ml = __reduce_min_sync(kFull, hi == mh ? lo : 0xFFFFFFFFu);
+            if (lane == r) mine = ((key_t)mh << 32) | ml;
+            if (hi == mh && lo == ml) k = kEmptyKey;
+        }
+    } else {  // 32 candidates at a time (lane i: candidate g0 + i), per-lane lists merged
+        key_t best[4] = {kEmptyKey, kEmptyKey, kEmptyKey, kEmptyKey};
+        for (uint32_t g0 = 0; g0 < n; g0 += 32) {
+            const uint32_t ng = min(32u, n - g0);
+            auto id = [&](uint32_t i) { return scan_all ? g0 + i : cw[g0 + i]; };
+            const float acc = chain_dists(qv, Cm, dim, ng, id, ws, lane);
+            if (lane < ng) top4_insert(best, make_key(acc, id(lane), 0));
+        }
+        top4_warp(best);
+        mine = best[0];
+#pragma unroll
+        for (uint32_t r = 1; r < 4; ++r)
+            if (lane == r) mine = best[r];
+    }
     if (lane < 4) top4[(size_t)q * 4 + lane] = mine == kEmptyKey ? kEmpty : key_pos(mine);
 }
 
