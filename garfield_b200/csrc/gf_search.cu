@@ -62,6 +62,7 @@ struct SArgs {
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, stage_stride, warp_words;
     uint32_t wait_polls, extra_tx;  // staging wait limit; test hook: bytes expected but never sent
+    uint32_t graph_bulk;            // neighbour rows are fetched with bulk copies (R * 4 a multiple of 16)
     // word offsets inside a warp's shared-memory slice
     uint32_t o_sc, o_bi;  // byte codecs: -scale and 2^23 + bias pairs
     uint32_t o_q, o_lb, o_rb, o_t0d, o_t0w, o_t1d, o_t1w, o_r0d, o_r0w, o_r1d, o_r1w, o_bd, o_bw, o_ed, o_ew,
@@ -124,6 +125,29 @@ __device__ __forceinline__ uint32_t next_pow2(uint32_t x) { return x <= 1 ? 1 : 
 constexpr uint32_t kStageWaitPolls = 1u << 19;  // with the suspend hint, about a second
 constexpr uint32_t kStageSuspendNs = 2000;  // suspend hint of each poll (a copy takes ~1-3 us)
 
+// Bounded wait for the copies counted on the warp's staging mbarrier, then the phase bit
+// flips.  A wait that runs out stops the warp: the abort flag is set, stats[7] counts it
+// and true is returned (the staging buffers are not used again by this warp).
+__device__ __forceinline__ bool stage_wait(const SArgs& A, uint32_t* base) {
+    uint64_t* bar = reinterpret_cast<uint64_t*>(base + A.o_mbar);
+    uint32_t* phase = base + A.o_mbar + 2;
+    const uint32_t par = *phase;
+    uint32_t polls = 0;
+    while (!mbar_try_wait(bar, par, kStageSuspendNs) && ++polls < A.wait_polls) {
+    }
+    const bool timed_out = __any_sync(kFull, polls >= A.wait_polls);
+    __syncwarp();
+    if (lane_id() == 0) {
+        *phase = par ^ 1u;
+        if (timed_out) {
+            base[A.o_mbar + 3] = 1u;
+            atomicAdd(A.stats + 7, 1ull);
+        }
+    }
+    __syncwarp();
+    return timed_out;
+}
+
 // Distances + range flags of the positions P[0..nb); the keys below `thr` (the list's
 // worst entry, or kEmptyKey for no bound) are written sorted to B[0..ns), padded with
 // empty keys to a power of two >= 32; returns ns.  A key at or above the list's worst
@@ -144,7 +168,6 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
     key_t* B = w.B(A);
     uint4* stage = reinterpret_cast<uint4*>(w.base + A.o_stage);
     uint64_t* bar = reinterpret_cast<uint64_t*>(w.base + A.o_mbar);
-    uint32_t* phase = w.base + A.o_mbar + 2;
     uint32_t* abort = w.base + A.o_mbar + 3;
     const f2x* q2 = reinterpret_cast<const f2x*>(w.base + A.o_q);
     const uint32_t SR = A.stage_rows, row = lane & 15u, half = lane >> 4;
@@ -170,21 +193,7 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
     for (uint32_t s = 0; s < nst; ++s) {
         const bool inr = inr_next;
         const uint32_t r0 = s * SR, rows = min(SR, nb - r0);
-        const uint32_t par = *phase;
-        uint32_t polls = 0;
-        while (!mbar_try_wait(bar, par, kStageSuspendNs) && ++polls < A.wait_polls) {
-        }
-        const bool timed_out = __any_sync(kFull, polls >= A.wait_polls);
-        __syncwarp();
-        if (lane == 0) {
-            *phase = par ^ 1u;
-            if (timed_out) {
-                *abort = 1u;
-                atomicAdd(A.stats + 7, 1ull);
-            }
-        }
-        __syncwarp();
-        if (timed_out) return 0;  // the buffers are not used again by this warp
+        if (stage_wait(A, w.base)) return 0;
         f2x acc[4] = {0ull, 0ull, 0ull, 0ull};
         if (row < rows) {
             const uint4* srow = stage + (size_t)row * stride;
@@ -329,6 +338,15 @@ __device__ __forceinline__ void append(uint32_t* P, uint32_t& nb, bool ok, uint3
     uint32_t msk = __ballot_sync(kFull, ok);
     if (ok) P[nb + __popc(msk & lanemask_lt())] = pos;
     nb += __popc(msk);
+}
+
+// Neighbour rows of the np picks into G with plain loads (graphs whose rows are not a
+// multiple of 16 bytes; others use one bulk copy per row).
+__device__ __noinline__ void copy_rows(const SArgs& A, uint32_t* G, const uint32_t* picks, uint32_t np,
+                                       long long gbase) {
+    for (uint32_t j = lane_id(); j < np * A.R; j += 32)
+        G[j] = __ldg(A.graph + (gbase + (long long)picks[j / A.R] * A.R + (j % A.R)));
+    __syncwarp();
 }
 
 // Exact route (gpu_graph.cu:3788-4022): every in-range point of the query's cells.
@@ -571,16 +589,37 @@ __global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constan
                         {
                             const uint32_t* picks = w.picks(A);
                             uint32_t* H = w.H(A);
-                            for (uint32_t j0 = 0; j0 < total; j0 += 32) {
-                                const uint32_t j = j0 + lane;
-                                bool ok = false;
-                                uint32_t pos = kEmpty;
-                                if (j < total) {
-                                    const uint32_t node = picks[j / A.R];
-                                    pos = __ldg(A.graph + (gbase + (long long)node * A.R + (j % A.R)));
-                                    if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+                            // the picks' neighbour rows, staged in B (free between a merge
+                            // and the next evaluation): one bulk copy per row and one wait
+                            uint32_t* G = reinterpret_cast<uint32_t*>(w.B(A));
+                            bool have = !w.base[A.o_mbar + 3];
+                            if (have) {
+                                if (A.graph_bulk) {
+                                    fence_proxy_async_smem();
+                                    __syncwarp();
+                                    if (lane == 0)
+                                        mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(w.base + A.o_mbar),
+                                                              np * A.R * 4 + A.extra_tx);
+                                    __syncwarp();
+                                    if (lane < np)
+                                        bulk_g2s(G + lane * A.R, A.graph + (gbase + (long long)picks[lane] * A.R),
+                                                 A.R * 4, reinterpret_cast<uint64_t*>(w.base + A.o_mbar));
+                                    have = !stage_wait(A, w.base);
+                                } else {
+                                    copy_rows(A, G, picks, np, gbase);
                                 }
-                                append(w.P(A), nb, ok, pos);
+                            }
+                            if (have) {
+                                for (uint32_t j0 = 0; j0 < total; j0 += 32) {
+                                    const uint32_t j = j0 + lane;
+                                    bool ok = false;
+                                    uint32_t pos = kEmpty;
+                                    if (j < total) {
+                                        pos = G[j];
+                                        if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+                                    }
+                                    append(w.P(A), nb, ok, pos);
+                                }
                             }
                             __syncwarp();
                         }
@@ -797,6 +836,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.prefilter = p.prefilter;
     A.wait_polls = P.test_wait ? P.test_wait : kStageWaitPolls;
     A.extra_tx = P.test_wait ? 16u : 0u;
+    A.graph_bulk = (d.degree * 4) % 16 == 0 ? 1u : 0u;
     uint32_t need = std::max<uint32_t>({P.width * d.degree, n_entry, kHopSlots * A.E, 64u});
     uint32_t bcap = 1;
     while (bcap < need) bcap <<= 1;

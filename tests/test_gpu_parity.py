@@ -195,3 +195,21 @@ def test_staging_wait_timeout_is_reported(small, g_small):
     assert plan.stats()["n_timeouts"] == 0
     ref_ids, ref_d, _ = _oracle_search(c, L=32, K=10)
     assert np.array_equal(as_u32(ids), ref_ids)
+
+
+def test_graph_rows_not_a_multiple_of_16_bytes():
+    """Degree 18 (72-byte rows): the picks' neighbour rows are read with plain loads instead
+    of bulk copies; results and counters still equal the oracle's."""
+    from conftest import Case
+    c = Case(8000, 48, 30, 200, (2, 2), 0.2, R=18, E=2, C=30, seed=41)
+    assert c.ix.degree % 4 != 0
+    g = make_index(c)
+    plan = g.plan(c.ds.queries.shape[0])
+    plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+    for L, width in ((32, 1), (64, 4)):
+        ids, dist = plan.search(gf.SearchParams(L=L, k=10, width=width))
+        st = plan.stats()
+        ref_ids, ref_d, ref_st = _oracle_search(c, L=L, K=10, width=width)
+        assert np.array_equal(as_u32(ids), ref_ids)
+        assert np.array_equal(dist.cpu().numpy(), ref_d)
+        assert st["n_exp"] == ref_st[1] and st["n_cross"] == ref_st[2] and st["n_hops"] == ref_st[3]
