@@ -17,6 +17,8 @@ length in a fixed sweep whose recall on the ground-truth sample reaches the targ
                                                             per scheduled batch of B cells (row a17)
   torchrun ... bench.py --mode sharded                     cell-sharded index over the ranks, keys
                                                             all-gathered over NCCL and merged (row e)
+  python bench.py --mode bruteforce                        exact filtered k-NN of all queries: tensor-core
+                                                            pass vs the CUDA-core kernel
   python bench.py --impl reference-cuda                     the reference's own CUDA binary: prints
                                                             "unavailable" (it faults on B200, see
                                                             REF_CUDA_FAULT)
@@ -421,6 +423,111 @@ def run_out_of_core(args):
     print(json.dumps(out), flush=True)
 
 
+def peak_tensor() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured (cuBLAS bf16 burst; fp16 runs at the same rate)"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def run_bruteforce(args):
+    """Exact filtered k-NN mode (gf_bruteforce, the GPU ground truth): config-2 data, all 10k
+    queries, k = 10.  Times the tensor-core pass (query x point products on tcgen05 with a
+    proven error bound, exact re-rank, CUDA-core answer for unproven queries) beside the
+    CUDA-core kernel on the same inputs, and checks that both return the same ids and
+    distances.  The roofline is the tensor pipe: executed MMA FLOPs per second."""
+    import torch
+    import garfield_b200 as gf
+    from garfield_b200 import indexbuild, synth
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    lq, rq, _, cell_of = indexbuild.quantile_grid(ds.attrs, ds.grid)
+    n, D = ds.vectors.shape
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=np.asarray(ds.grid, np.uint32),
+                            l_quant=lq, r_quant=rq, cell_of=cell_of, graphs=np.zeros((n, 1), np.uint32), degree=1,
+                            keep_fp32=True, device=local)
+    qnum = ds.queries.shape[0]
+    qd = torch.from_numpy(ds.queries).to(device)
+    lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
+    hid = torch.from_numpy(ds.hi.astype(np.float32)).to(device)
+    stream = torch.cuda.Stream(device)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
+    stats = torch.zeros(3, dtype=torch.int32, device=device)
+
+    def timed(path, steps, warmup):
+        for _ in range(warmup):
+            index.bruteforce(qd, lod, hid, 10, stream=stream, path=path, stats=stats)
+        stream.synchronize()
+        ms = []
+        with ClockSampler(local) as clocks:
+            for i in range(steps):
+                with torch.cuda.stream(stream):
+                    flush.fill_(float(i))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                ids, dist = index.bruteforce(qd, lod, hid, 10, stream=stream, path=path, stats=stats)
+                b.record(stream)
+                b.synchronize()
+                ms.append(a.elapsed_time(b))
+        return ids, dist, float(np.mean(ms)), stats.cpu().numpy().copy(), clocks.summary()
+
+    t_ids, t_d, t_ms, st, clocks = timed(2, args.steps, args.warmup)
+    c_ids, c_d, c_ms, _, _ = timed(1, 1, 1)
+    same = bool(torch.equal(t_ids, c_ids) and torch.equal(t_d, c_d))
+    # end to end: host queries and boxes in pinned memory, ids back to the host
+    qh, lh, hh = (torch.from_numpy(x).pin_memory() for x in (ds.queries, ds.lo.astype(np.float32),
+                                                              ds.hi.astype(np.float32)))
+    qg, lg, hg = torch.empty_like(qd), torch.empty_like(lod), torch.empty_like(hid)
+    ih = torch.empty((qnum, 10), dtype=torch.int32).pin_memory()
+    e_ms = []
+    for i in range(max(args.warmup, 1) + args.steps):
+        with torch.cuda.stream(stream):
+            flush.fill_(float(i))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            qg.copy_(qh, non_blocking=True)
+            lg.copy_(lh, non_blocking=True)
+            hg.copy_(hh, non_blocking=True)
+            ids, _ = index.bruteforce(qg, lg, hg, 10, stream=stream)
+            ih.copy_(ids, non_blocking=True)
+            b.record(stream)
+        b.synchronize()
+        if i >= max(args.warmup, 1):
+            e_ms.append(a.elapsed_time(b))
+    assert torch.equal(ih, t_ids.cpu())
+    products = int(st[2])
+    dp = (D + 15) // 16 * 16
+    flops = 2.0 * products * 128 * 128 * dp
+    achieved = flops / (t_ms / 1e3) / 1e12
+    peak, peak_kind = peak_tensor()
+    out = {"metric": "exact filtered k-NN queries/s (1M x 128, 2 attrs, 10% sel., k=10)",
+           "value": round(qnum / (t_ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f16 products, f32 accumulate, f32 exact re-rank",
+           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
+           "config": {"workload": "config2 brute force: 1M x 128 fp32, 10k queries, sel 10%, k=10",
+                      "l2": "flushed (256 MiB write) between timed steps",
+                      "cuda_core_ms_per_step": round(c_ms, 3), "speedup_vs_cuda_cores": round(c_ms / t_ms, 2),
+                      "identical_to_cuda_cores": same, "fallback_queries": int(st[0]), "timeouts": int(st[1]),
+                      "tile_products": products, "dense_products": ((qnum + 127) // 128) * ((n + 127) // 128)},
+           "e2e": {"value": round(qnum / (float(np.mean(e_ms)) / 1e3), 1), "unit": "queries/s",
+                   "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(ih.nbytes)},
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(achieved / peak, 4), "traffic": None, "kernel": "bf_tc_kernel (whole call timed)",
+                        "peak_kind": peak_kind, "flops_per_step": flops},
+           "clocks": clocks,
+           # morton, 3 radix-sort passes are CUB's; prep, boxes, tiles, tc, merge, CUDA-core list
+           "gpu_launches": 6 * args.steps}
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1)
+    print(json.dumps(out), flush=True)
+
+
 def run_sharded(args):
     """Cell-sharded mode (row e, strong scaling): rank r of N holds the cells
     dist.shard_cells(grid, N)[r] only; a step plans all queries on every rank, searches them
@@ -596,13 +703,15 @@ def main():
     ap.add_argument("--cache", default="/tmp/gf_cache")
     ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
-    ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core", "sharded"])
+    ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core", "sharded", "bruteforce"])
     ap.add_argument("--batch-cells", dest="batch_cells", type=int, default=4)
     args = ap.parse_args()
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
     elif args.impl == "ours" and args.mode == "sharded":
         run_sharded(args)
+    elif args.impl == "ours" and args.mode == "bruteforce":
+        run_bruteforce(args)
     elif args.impl == "reference":
         run_reference_cpu(args)
     elif args.impl == "reference-cuda":

@@ -72,6 +72,10 @@ class _SearchParams(C.Structure):
                 ("L", "k", "width", "max_iter", "n_entry", "postfilter", "hash_slots", "test_wait")]
 
 
+class _BfParams(C.Structure):
+    _fields_ = [("path", C.c_uint32), ("test_fallback_every", C.c_uint32), ("stats_out", C.c_void_p)]
+
+
 class _SearchStats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("n_dist", "n_exp", "n_cross", "n_hops", "n_exact", "n_queries",
                                           "n_timeouts", "n_plan_fallbacks", "n_plan_reranked")]
@@ -121,6 +125,7 @@ def lib() -> C.CDLL:
         "gf_schedule_batches_host": (C.c_int, [_U32, _U32, _P, _P, _P, _U32, _P, _P, _PTR(_U32),
                                                _PTR(C.c_uint64)]),
         "gf_bruteforce": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _P]),
+        "gf_bruteforce_ex": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _PTR(_BfParams), _P]),
         "gf_free": (None, [_P]),
         "gf_read_fvecs": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
         "gf_write_fvecs": (C.c_int, [C.c_char_p, _P, _U32, _U32]),
@@ -312,14 +317,25 @@ class Index:
                                    _stream_ptr(stream)), "gf_merge_keys")
         return ids, dist
 
-    def bruteforce(self, queries, lb, rb, k: int, stream=None):
-        """Exact filtered k-NN on the device; returns (ids, dists) CUDA tensors."""
+    def bruteforce(self, queries, lb, rb, k: int, stream=None, path: int = 0, test_fallback_every: int = 0,
+                   stats=None):
+        """Exact filtered k-NN on the device; returns (ids, dists) CUDA tensors.
+
+        path: 0 automatic (tensor cores when available), 1 CUDA cores, 2 tensor cores.
+        stats: optional int32 CUDA tensor of 3 words (queries answered by the CUDA-core
+        kernel after the tensor-core pass, waits that ran out, 128 x 128 tile products)."""
         import torch
         q = queries.shape[0]
         ids = torch.empty((q, k), dtype=torch.int32, device=queries.device)
         dist = torch.empty((q, k), dtype=torch.float32, device=queries.device)
-        _check(lib().gf_bruteforce(self._h, _dev_ptr(queries), _dev_ptr(lb), _dev_ptr(rb), q, k,
-                                   _dev_ptr(ids), _dev_ptr(dist), _stream_ptr(stream)), "gf_bruteforce")
+        if path == 0 and test_fallback_every == 0 and stats is None:
+            _check(lib().gf_bruteforce(self._h, _dev_ptr(queries), _dev_ptr(lb), _dev_ptr(rb), q, k,
+                                       _dev_ptr(ids), _dev_ptr(dist), _stream_ptr(stream)), "gf_bruteforce")
+        else:
+            prm = _BfParams(path, test_fallback_every, _dev_ptr(stats).value if stats is not None else None)
+            _check(lib().gf_bruteforce_ex(self._h, _dev_ptr(queries), _dev_ptr(lb), _dev_ptr(rb), q, k,
+                                          _dev_ptr(ids), _dev_ptr(dist), C.byref(prm), _stream_ptr(stream)),
+                   "gf_bruteforce_ex")
         return ids, dist
 
     def search(self, queries, lb, rb, params: SearchParams | None = None, prefilter: float = 0.0,

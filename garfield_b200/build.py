@@ -22,7 +22,7 @@ BUILD = ROOT / "_build"
 LIB = PKG / "libgarfield_b200.so"
 BIN = PKG / "bin"
 
-LIB_SOURCES = ["gf_index.cu", "gf_io.cpp", "gf_plan.cu", "gf_search.cu", "gf_bruteforce.cu", "gf_noalloc.cu", "gf_batch.cu", "gf_schedule.cpp", "gf_codec.cu", "gf_centroid_tc.cu"]
+LIB_SOURCES = ["gf_index.cu", "gf_io.cpp", "gf_plan.cu", "gf_search.cu", "gf_bruteforce.cu", "gf_noalloc.cu", "gf_batch.cu", "gf_schedule.cpp", "gf_codec.cu", "gf_centroid_tc.cu", "gf_bf_tc.cu"]
 CLI_SOURCES = ["gf_cli.cpp"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

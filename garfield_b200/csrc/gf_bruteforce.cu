@@ -22,9 +22,12 @@ __global__ void __launch_bounds__(256) bruteforce_kernel(const float4* __restric
                                                          uint32_t a, const float* __restrict__ queries, uint32_t dim,
                                                          const float* __restrict__ lb, const float* __restrict__ rb,
                                                          uint32_t k, uint32_t* __restrict__ ids,
-                                                         float* __restrict__ dists) {
+                                                         float* __restrict__ dists, const uint32_t* __restrict__ qlist,
+                                                         const uint32_t* __restrict__ qcount) {
     extern __shared__ __align__(16) float sm[];
-    const uint32_t q = blockIdx.x, lane = lane_id(), w = threadIdx.x >> 5;
+    // with a query list, block b answers query qlist[b] (blocks past *qcount have none)
+    if (qlist && blockIdx.x >= *qcount) return;
+    const uint32_t q = qlist ? qlist[blockIdx.x] : blockIdx.x, lane = lane_id(), w = threadIdx.x >> 5;
     float4* qs = reinterpret_cast<float4*>(sm);                 // nch
     float* sl = sm + nch * 4;                                   // a
     float* sr = sl + kMaxAttr;                                  // a
@@ -141,10 +144,17 @@ __global__ void __launch_bounds__(256) bruteforce_kernel(const float4* __restric
 }  // namespace
 
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
-                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s) {
+                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm) {
     DeviceIndex& d = idx->d;
     if (!d.vec32) return fail(GF_ERR_STATE, "index was created without keep_fp32");
     if (k == 0 || k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");
+    gf_bf_params P{};
+    if (prm) P = *prm;
+    if (P.path > 2) return fail(GF_ERR_ARG, "path must be 0, 1 or 2");
+    const bool tc = P.path != 1 && bf_tc_usable(d, k);
+    if (P.path == 2 && !tc)
+        return fail(GF_ERR_ARG, "tensor-core brute force needs keep_fp32, dim <= 256, finite rows and k <= 16");
+    if (P.stats_out) GF_CUDA(cudaMemsetAsync(P.stats_out, 0, 3 * sizeof(uint32_t), s));
     if (qnum == 0) return GF_OK;
     if (!queries || !lb || !rb || !ids) return fail(GF_ERR_ARG, "null argument");
     const uint32_t nch = d.d4 / 4;
@@ -154,10 +164,30 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device);
     if (smem > (size_t)max_optin) return fail(GF_ERR_ARG, "k or dim too large for the brute-force kernel");
     GF_CUDA(cudaFuncSetAttribute(bruteforce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k, ids,
-                                              dist);
-    GF_CUDA(cudaGetLastError());
-    return GF_OK;
+    if (!tc) {
+        bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k,
+                                                  ids, dist, nullptr, nullptr);
+        GF_CUDA(cudaGetLastError());
+        return GF_OK;
+    }
+    // tensor-core pass, then the CUDA-core kernel for the queries it could not prove
+    uint32_t* w = nullptr;  // [0] fallback count, [1] timeouts, [2] tile products, [3..] fallback list
+    GF_CUDA(cudaMallocAsync((void**)&w, sizeof(uint32_t) * (3 + (size_t)qnum), s));
+    gf_status st = GF_OK;
+    cudaError_t e = cudaMemsetAsync(w, 0, 3 * sizeof(uint32_t), s);
+    if (e != cudaSuccess) st = cuda_fail(e, "brute-force counters");
+    if (st == GF_OK)
+        st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, w + 3, w, P.test_fallback_every, w + 1, w + 2, s);
+    if (st == GF_OK) {
+        bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k,
+                                                  ids, dist, w + 3, w);
+        e = cudaGetLastError();
+        if (e == cudaSuccess && P.stats_out)
+            e = cudaMemcpyAsync(P.stats_out, w, 3 * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) st = cuda_fail(e, "brute force");
+    }
+    cudaFreeAsync(w, s);
+    return st;
 }
 
 }  // namespace gf

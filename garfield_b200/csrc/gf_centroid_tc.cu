@@ -209,7 +209,15 @@ __global__ void __launch_bounds__(128) centroid_dot_tc_kernel(const float* __res
             uint32_t v[32];
             tmem_ld16(taddr + cb, v);
             tmem_ld16(taddr + cb + 16, v + 16);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            // the wait names the loaded registers so that no use of them is scheduled before it
+            asm volatile("tcgen05.wait::ld.sync.aligned;"
+                         : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]),
+                           "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]),
+                           "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]),
+                           "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]),
+                           "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+                         :
+                         : "memory");
 #pragma unroll
             for (uint32_t j = 0; j < 32; ++j) stg[lane * 33 + j] = __uint_as_float(v[j]);
             __syncwarp();

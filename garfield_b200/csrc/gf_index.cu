@@ -82,6 +82,7 @@ static void free_index(DeviceIndex& d) {
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);
     if (d.cross_h) cudaFreeHost(d.cross_h);
+    free_bf_tc(d);
 }
 
 // Deterministic entry local ids: std::mt19937 with its default seed (as the reference,
@@ -474,6 +475,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             }
         }
         if (st != GF_OK) break;
+        if (d.vec32 && (st = bf_tc_prepare(d)) != GF_OK) break;  // fp16 tiles of the tensor-core brute force
         cudaError_t e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) st = cuda_fail(e, "index build");

@@ -79,6 +79,18 @@ struct DeviceIndex {
     float* cmean = nullptr;      // dim: the centroids' mean m (tensor-core planner)
     uint32_t* hist = nullptr;    // ncells x C
     uint32_t* entry = nullptr;   // entry_h on device
+    // tensor-core brute force (gf_bf_tc.cu): centred, scaled fp16 copy of the fp32 rows in
+    // 128-point tcgen05 tiles, per point (1 - kappa)|x~|^2, per tile attribute bounds
+    bool bf_ok = false;
+    uint32_t bf_dp = 0, bf_tiles = 0;   // padded row length (multiple of 16), point tiles
+    float bf_scale = 1.0f, bf_dmax = 0.0f;  // power-of-two scale s, largest residual |x - x^|
+    void* bf_x = nullptr;        // bf_tiles x 128 x bf_dp halves
+    float* bf_px = nullptr;      // bf_tiles x 128 (+inf past n)
+    float* bf_mean = nullptr;    // dim
+    float* bf_tbox = nullptr;    // bf_tiles x 2 x a8: attribute bounds per tile (a8 = a rounded up to 4)
+    float* bf_attrs = nullptr;   // bf_tiles x 128 x a (NaN past n)
+    uint32_t* bf_rowpos = nullptr; // bf_tiles x 128: position of each row (rows in attribute Morton order)
+    float* bf_arange = nullptr;  // 2 x a: attribute origin and inverse extent (Morton codes)
 };
 
 struct BatchState;  // gf_batch.cu: buffers, streams and events of gf_search_batched
@@ -166,7 +178,16 @@ gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t tota
                      cudaStream_t s);
 // gf_bruteforce.cu
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
-                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s);
+                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm = nullptr);
+// gf_bf_tc.cu
+gf_status bf_tc_prepare(DeviceIndex& d);  // at index creation, after vec32 and attrs
+void free_bf_tc(DeviceIndex& d);
+bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
+// Tensor-core pass: writes the proven queries' results and appends the others to
+// fb_list / fb_cnt (answered afterwards by the CUDA-core kernel).
+gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
+                    uint32_t* ids, float* dist, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
+                    uint32_t* timeouts, uint32_t* products, cudaStream_t s);
 // gf_codec.cu
 void quantize_i8_host(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q, float* scales,
                       int32_t* zps);

@@ -616,4 +616,11 @@ gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, co
     return gf::bruteforce(idx, queries, lb, rb, qnum, k, ids_out, dist_out, (cudaStream_t)stream);
 }
 
+gf_status gf_bruteforce_ex(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                           uint32_t k, uint32_t* ids_out, float* dist_out, const gf_bf_params* params, void* stream) {
+    if (!idx) return fail(GF_ERR_ARG, "null index");
+    DeviceGuard2 guard(idx->d.device);
+    return gf::bruteforce(idx, queries, lb, rb, qnum, k, ids_out, dist_out, (cudaStream_t)stream, params);
+}
+
 }  // extern "C"

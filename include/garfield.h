@@ -295,6 +295,31 @@ gf_status gf_schedule_batches_host(uint32_t ncells, uint32_t qnum, const uint32_
 gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
                         uint32_t k, uint32_t* ids_out, float* dist_out, void* stream);
 
+/* Options of gf_bruteforce_ex (all zero = gf_bruteforce's behaviour). */
+typedef struct {
+    uint32_t path;       /* 0 = automatic: the tensor-core pass when the index has its fp16 tiles
+                            (keep_fp32, dim <= 256, finite rows) and k <= 16, else CUDA cores;
+                            1 = CUDA cores only; 2 = tensor cores (GF_ERR_ARG when unavailable) */
+    uint32_t test_fallback_every; /* 0 in normal use.  Test hook: queries whose index is a
+                            multiple of this value skip the tensor-core proof and are answered
+                            by the CUDA-core kernel, as unproven queries are */
+    uint32_t* stats_out; /* optional device array of 3 words, written on the stream: queries
+                            answered by the CUDA-core kernel after the tensor-core pass,
+                            tensor-core waits that ran out (their queries are among the former),
+                            and (128-query tile, 128-point tile) products multiplied */
+} gf_bf_params;
+
+/*
+ * gf_bruteforce with options.  Same results on every path: on the tensor cores each query's
+ * points are ranked by an fp16 product with a proven error bound, the 32 best are re-ranked
+ * with the canonical fp32 distance, and a query whose result the bound cannot prove is
+ * answered again by the CUDA-core kernel.  The dense query x point contraction replaces the
+ * fp16 distance scan of prefiltering_and_bruteforce / dis_cal_reduce (brute_force.cuh:252-405).
+ * Allocates its working memory on the stream (cudaMallocAsync).
+ */
+gf_status gf_bruteforce_ex(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
+                           uint32_t k, uint32_t* ids_out, float* dist_out, const gf_bf_params* params, void* stream);
+
 /*
  * Plan + search of one batch without allocating memory.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory at query time
