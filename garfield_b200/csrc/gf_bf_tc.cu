@@ -1068,6 +1068,14 @@ std::vector<float> attr_range(const DeviceIndex& d) {
 }  // namespace
 
 void free_bf_tc(DeviceIndex& d) {
+    if (d.bf_ws_ev) {
+        cudaEventSynchronize(d.bf_ws_ev);
+        cudaEventDestroy(d.bf_ws_ev);
+        d.bf_ws_ev = nullptr;
+    }
+    if (d.bf_ws) cudaFree(d.bf_ws);
+    d.bf_ws = nullptr;
+    d.bf_ws_bytes = 0;
     void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean, d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_arange};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -1168,8 +1176,52 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
 
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k) { return d.bf_ok && k >= 1 && k <= kMaxK; }
 
+namespace {
+// Working memory of one call, carved in this order from `base` (sizes only when base is NULL).
+void carve_ws(const DeviceIndex& d, uint32_t qnum, size_t tmp_sort, unsigned char* base, size_t* used, void** p) {
+    const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM, dp = d.bf_dp, a = d.a;
+    Carve c{base};
+    p[0] = c.take<unsigned long long>(qnum);  // keys
+    p[1] = c.take<unsigned long long>(qnum);  // keys sorted
+    p[2] = c.take<uint32_t>(qnum);            // iota
+    p[3] = c.take<uint32_t>(qnum);            // sorted queries
+    p[4] = c.take<unsigned char>(tmp_sort);
+    p[5] = c.take<uint32_t>(qpad);            // perm
+    p[6] = c.take<uint32_t>(qpad);            // flag
+    p[7] = c.take<float>(qpad);               // pq
+    p[8] = c.take<float>(qpad);               // dq
+    p[9] = c.take<__half>((size_t)qpad * dp);
+    p[10] = c.take<float>((size_t)qtiles * a);
+    p[11] = c.take<float>((size_t)qtiles * a);
+    p[12] = c.take<float>((size_t)qtiles * 4 * a);
+    p[13] = c.take<float>((size_t)qtiles * 4 * a);
+    p[14] = c.take<uint32_t>((size_t)qtiles * d.bf_tiles);
+    p[15] = c.take<uint32_t>(qtiles);
+    p[16] = c.take<uint2>((size_t)qpad * kLists * kM);
+    p[17] = c.take<uint32_t>((size_t)qpad * kLists + qpad);  // list counts, then row fallbacks
+    p[18] = nullptr;
+    p[19] = c.take<uint32_t>(qpad);            // published thresholds
+    p[20] = c.take<uint32_t>(qtiles + 1 + 2);  // prefix of the tile counts, then W and G
+    *used = c.used;
+}
+
+size_t sort_tmp_bytes(uint32_t qnum) {
+    size_t tmp_sort = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, tmp_sort, (unsigned long long*)nullptr, (unsigned long long*)nullptr,
+                                    (uint32_t*)nullptr, (uint32_t*)nullptr, (int)qnum);
+    return tmp_sort;
+}
+}  // namespace
+
+size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum) {
+    void* P[21];
+    size_t used = 0;
+    carve_ws(d, qnum, sort_tmp_bytes(qnum), nullptr, &used, P);
+    return used;
+}
+
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
-                    uint32_t* ids, float* dist, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
+                    uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
                     uint32_t* timeouts, uint32_t* products, cudaStream_t s) {
     DeviceIndex& d = idx->d;
     const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM;
@@ -1184,39 +1236,10 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     const TcLayout Lo = tc_layout(dp, stages, a);
     if (Lo.total > kSmemLimit) return fail(GF_ERR_ARG, "tensor-core brute force: shared memory");
 
-    size_t tmp_sort = 0;
-    cub::DeviceRadixSort::SortPairs(nullptr, tmp_sort, (unsigned long long*)nullptr, (unsigned long long*)nullptr,
-                                    (uint32_t*)nullptr, (uint32_t*)nullptr, (int)qnum);
-    auto carve = [&](Carve& c, void** p) {
-        p[0] = c.take<unsigned long long>(qnum);  // keys
-        p[1] = c.take<unsigned long long>(qnum);  // keys sorted
-        p[2] = c.take<uint32_t>(qnum);        // iota
-        p[3] = c.take<uint32_t>(qnum);        // sorted queries
-        p[4] = c.take<unsigned char>(tmp_sort);
-        p[5] = c.take<uint32_t>(qpad);        // perm
-        p[6] = c.take<uint32_t>(qpad);        // flag
-        p[7] = c.take<float>(qpad);           // pq
-        p[8] = c.take<float>(qpad);           // dq
-        p[9] = c.take<__half>((size_t)qpad * dp);
-        p[10] = c.take<float>((size_t)qtiles * a);
-        p[11] = c.take<float>((size_t)qtiles * a);
-        p[12] = c.take<float>((size_t)qtiles * 4 * a);
-        p[13] = c.take<float>((size_t)qtiles * 4 * a);
-        p[14] = c.take<uint32_t>((size_t)qtiles * d.bf_tiles);
-        p[15] = c.take<uint32_t>(qtiles);
-        p[16] = c.take<uint2>((size_t)qpad * kLists * kM);
-        p[17] = c.take<uint32_t>((size_t)qpad * kLists + qpad);  // list counts, then row fallbacks
-        p[18] = nullptr;
-        p[19] = c.take<uint32_t>(qpad);        // published thresholds
-        p[20] = c.take<uint32_t>(qtiles + 1 + 2);  // prefix of the tile counts, then W and G
-    };
-    Carve sizing;
+    size_t tmp_sort = sort_tmp_bytes(qnum);
     void* P[21];
-    carve(sizing, P);
-    unsigned char* ws = nullptr;
-    GF_CUDA(cudaMallocAsync((void**)&ws, sizing.used, s));
-    Carve cv{ws};
-    carve(cv, P);
+    size_t used = 0;
+    carve_ws(d, qnum, tmp_sort, static_cast<unsigned char*>(ws), &used, P);
     unsigned long long *keys = (unsigned long long*)P[0], *keys2 = (unsigned long long*)P[1];
     uint32_t *iota = (uint32_t*)P[2], *sorted = (uint32_t*)P[3];
     uint32_t *perm = (uint32_t*)P[5], *flag = (uint32_t*)P[6];
@@ -1302,7 +1325,6 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     const size_t msmem = sizeof(float) * 8 * d.d4;
     bf_merge_kernel<<<(qpad + 7) / 8, 256, msmem, s>>>(M);
     ck(cudaGetLastError(), "bf kernels");
-    ck(cudaFreeAsync(ws, s), "bf workspace");
     return st;
 }
 

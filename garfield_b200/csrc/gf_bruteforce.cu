@@ -6,6 +6,7 @@
 // and their canonical fp32 distances computed thread-per-point; each warp keeps a
 // sorted top-k list in shared memory, merged at the end.  Order: (distance, global id).
 #include <algorithm>
+#include <mutex>
 
 #include "gf_device.cuh"
 #include "gf_internal.h"
@@ -170,14 +171,28 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
         GF_CUDA(cudaGetLastError());
         return GF_OK;
     }
-    // tensor-core pass, then the CUDA-core kernel for the queries it could not prove
-    uint32_t* w = nullptr;  // [0] fallback count, [1] timeouts, [2] tile products, [3..] fallback list
-    GF_CUDA(cudaMallocAsync((void**)&w, sizeof(uint32_t) * (3 + (size_t)qnum), s));
+    // tensor-core pass, then the CUDA-core kernel for the queries it could not prove; working
+    // memory: the pass's, then [0] fallback count, [1] timeouts, [2] tile products, [3..] list
+    const size_t tc_bytes = (bf_tc_ws_bytes(d, qnum) + 255) & ~size_t(255);
+    const size_t need = tc_bytes + sizeof(uint32_t) * (3 + (size_t)qnum);
+    std::lock_guard<std::mutex> lock(*d.bf_mu);
+    if (!d.bf_ws_ev) GF_CUDA(cudaEventCreateWithFlags(&d.bf_ws_ev, cudaEventDisableTiming));
+    if (d.bf_ws_bytes < need) {
+        GF_CUDA(cudaEventSynchronize(d.bf_ws_ev));  // the last call that used the buffer is done
+        if (d.bf_ws) cudaFree(d.bf_ws);
+        d.bf_ws = nullptr;
+        d.bf_ws_bytes = 0;
+        GF_CUDA(cudaMalloc(&d.bf_ws, need));
+        d.bf_ws_bytes = need;
+    }
+    GF_CUDA(cudaStreamWaitEvent(s, d.bf_ws_ev, 0));  // calls on other streams that share the buffer
+    uint32_t* w = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(d.bf_ws) + tc_bytes);
     gf_status st = GF_OK;
     cudaError_t e = cudaMemsetAsync(w, 0, 3 * sizeof(uint32_t), s);
     if (e != cudaSuccess) st = cuda_fail(e, "brute-force counters");
     if (st == GF_OK)
-        st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, w + 3, w, P.test_fallback_every, w + 1, w + 2, s);
+        st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, d.bf_ws, w + 3, w, P.test_fallback_every, w + 1, w + 2,
+                       s);
     if (st == GF_OK) {
         bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k,
                                                   ids, dist, w + 3, w);
@@ -186,7 +201,8 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
             e = cudaMemcpyAsync(P.stats_out, w, 3 * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s);
         if (e != cudaSuccess) st = cuda_fail(e, "brute force");
     }
-    cudaFreeAsync(w, s);
+    const cudaError_t er = cudaEventRecord(d.bf_ws_ev, s);
+    if (st == GF_OK && er != cudaSuccess) st = cuda_fail(er, "brute-force event");
     return st;
 }
 

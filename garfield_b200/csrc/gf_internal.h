@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -91,6 +93,12 @@ struct DeviceIndex {
     float* bf_attrs = nullptr;   // bf_tiles x 128 x a (NaN past n)
     uint32_t* bf_rowpos = nullptr; // bf_tiles x 128: position of each row (rows in attribute Morton order)
     float* bf_arange = nullptr;  // 2 x a: attribute origin and inverse extent (Morton codes)
+    // working memory of gf_bruteforce, kept between calls and grown on demand; the event
+    // orders calls on different streams, the mutex guards the buffer's replacement
+    void* bf_ws = nullptr;
+    size_t bf_ws_bytes = 0;
+    cudaEvent_t bf_ws_ev = nullptr;
+    std::shared_ptr<std::mutex> bf_mu = std::make_shared<std::mutex>();
 };
 
 struct BatchState;  // gf_batch.cu: buffers, streams and events of gf_search_batched
@@ -185,8 +193,9 @@ void free_bf_tc(DeviceIndex& d);
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
 // Tensor-core pass: writes the proven queries' results and appends the others to
 // fb_list / fb_cnt (answered afterwards by the CUDA-core kernel).
+size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum);  // working memory of bf_tc_run
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
-                    uint32_t* ids, float* dist, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
+                    uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
                     uint32_t* timeouts, uint32_t* products, cudaStream_t s);
 // gf_codec.cu
 void quantize_i8_host(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q, float* scales,

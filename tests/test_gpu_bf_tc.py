@@ -116,3 +116,24 @@ def test_tc_large_matches_cuda_cores():
     ref_ids, ref_d = oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[:64], ds.lo[:64], ds.hi[:64], 10)
     assert np.array_equal(t_ids[:64], ref_ids) and np.array_equal(t_d[:64], ref_d)
     g.close()
+
+
+def test_tc_calls_on_two_streams_share_the_working_memory():
+    ds = synth.make(20000, 64, 40, 400, (2, 2), 0.1, seed=13, stratified=False)
+    g = bf_index(ds.vectors, ds.attrs, (2, 2))
+    q, lo, hi = dev(ds.queries), dev(ds.lo), dev(ds.hi)
+    ref1 = g.bruteforce(q[:150].contiguous(), lo[:150].contiguous(), hi[:150].contiguous(), 10, path=2)
+    ref2 = g.bruteforce(q[150:].contiguous(), lo[150:].contiguous(), hi[150:].contiguous(), 10, path=2)
+    torch.cuda.synchronize()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    a = (q[:150].contiguous(), lo[:150].contiguous(), hi[:150].contiguous())
+    b = (q[150:].contiguous(), lo[150:].contiguous(), hi[150:].contiguous())
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s1):
+        r1 = g.bruteforce(*a, 10, stream=s1, path=2)
+    with torch.cuda.stream(s2):
+        r2 = g.bruteforce(*b, 10, stream=s2, path=2)
+    torch.cuda.synchronize()
+    for got, ref in ((r1, ref1), (r2, ref2)):
+        assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
+    g.close()
