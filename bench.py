@@ -187,8 +187,9 @@ def run_ours(args):
     index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
                             r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
                             cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, keep_fp32=True,
-                            device=local)
-    log(f"device index {index.device_bytes / 2**30:.2f} GiB in {time.time() - t0:.1f}s")
+                            cross_spokesman=args.cross_spokesman, device=local)
+    log(f"device index {index.device_bytes / 2**30:.2f} GiB in {time.time() - t0:.1f}s, "
+        f"cross rows {index.cross_rows} of {index.n}")
     qnum = ds.queries.shape[0]
     qd = torch.from_numpy(ds.queries).to(device)
     lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
@@ -304,7 +305,7 @@ def run_ours(args):
     # roofline of the search kernel: algorithmic bytes from the device counters
     D, a_attr = ds.vectors.shape[1], ds.attrs.shape[1]
     bytes_step = (st["n_dist"] * (((D + 7) // 8 * 8) * 2 + a_attr * 4) + st["n_exp"] * ix.degree * 4 +
-                  st["n_cross"] * ix.cross_e * 4)
+                  st["n_cross"] * (ix.cross_e * 4 + (4 if args.cross_spokesman else 0)))
     kern_s = float(np.mean(search_ms)) / 1e3
     achieved = bytes_step / kern_s / 1e9
     peak, peak_kind = peak_hbm()
@@ -318,7 +319,9 @@ def run_ours(args):
                    "L": L, "width": args.width, "recall_at_10": round(recall, 4), "recall_sample": S,
                    "l2": "flushed (256 MiB write) between timed steps", "parallelism": f"replicas x{world}",
                    "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
-                   "sweep": sweep},
+                   "sweep": sweep,
+                   "cross_edges": (f"spokesman rows only: {index.cross_rows} of {index.n} (compress_global_graph_extreme)"
+                                   if args.cross_spokesman else "full")},
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                 "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * 10 * 4)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -705,6 +708,8 @@ def main():
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
     ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core", "sharded", "bruteforce"])
     ap.add_argument("--batch-cells", dest="batch_cells", type=int, default=4)
+    ap.add_argument("--cross-spokesman", dest="cross_spokesman", action="store_true",
+                    help="keep the cross-cell edges of spokesmen only (row f2 of the scope table)")
     args = ap.parse_args()
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)

@@ -51,7 +51,7 @@ class _IndexDesc(C.Structure):
         ("f2h_factor", C.c_float), ("keep_fp32", C.c_uint32), ("host_graph", C.c_uint32),
         ("shard_cells", C.c_void_p), ("n_shard_cells", C.c_uint32),
         ("codec", C.c_uint32), ("codes", C.c_void_p), ("code_scales", C.c_void_p),
-        ("code_zero_points", C.c_void_p),
+        ("code_zero_points", C.c_void_p), ("cross_spokesman", C.c_uint32),
     ]
 
 
@@ -84,7 +84,7 @@ class _SearchStats(C.Structure):
 class _IndexInfo(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in
                 ("n", "dim", "n_attr", "n_cells", "degree", "cross_e", "n_clusters", "d_stored",
-                 "min_cell_size")] + [("device_bytes", C.c_uint64)]
+                 "min_cell_size", "cross_rows")] + [("device_bytes", C.c_uint64)]
 
 
 _LIB = None
@@ -142,6 +142,10 @@ def lib() -> C.CDLL:
         "gf_write_ranges": (C.c_int, [C.c_char_p, _P, _P, _U32, _U32]),
         "gf_read_labels": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32)]),
         "gf_read_grid": (C.c_int, [C.c_char_p, _PTR(_U32), _PTR(_U32), _PTR(_P), _PTR(_P), _PTR(_P), _PTR(_P)]),
+        "gf_spokesman_host": (C.c_int, [_U32, _U32, _P, _U32, _P, _P, _P, _PTR(_U32)]),
+        "gf_write_spokesman_graph": (C.c_int, [C.c_char_p, _U32, _U32, _U32, _P, _P, _P, _P]),
+        "gf_read_spokesman_graph": (C.c_int, [C.c_char_p, _PTR(_U32), _PTR(_U32), _PTR(_U32), _PTR(_P), _PTR(_P),
+                                              _PTR(_P), _PTR(_P)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -212,11 +216,13 @@ class Index:
         self.n_cells, self.degree, self.cross_e = info.n_cells, info.degree, info.cross_e
         self.n_clusters, self.min_cell_size = info.n_clusters, info.min_cell_size
         self.device_bytes = info.device_bytes
+        self.cross_rows = info.cross_rows
 
     @classmethod
     def create(cls, *, vectors, attrs, grid, l_quant, r_quant, cell_of, graphs, degree, cross=None,
                cross_e=0, labels=None, f2h_factor=1.0, keep_fp32=True, host_graph=False, shard_cells=None,
-               codec=0, codes=None, code_scales=None, code_zero_points=None, device=0) -> "Index":
+               codec=0, codes=None, code_scales=None, code_zero_points=None, cross_spokesman=False,
+               device=0) -> "Index":
         """Build from host arrays in the reference's layout (see gf_index_desc).  With
         host_graph the graphs and cross edges stay in pinned host memory (search with
         Plan.search_batched); with shard_cells the device holds only those cells (a shard
@@ -246,6 +252,7 @@ class Index:
             d.shard_cells, d.n_shard_cells = _np_ptr(shard), len(shard)
             d.keep_fp32 = 0
         d.codec = codec
+        d.cross_spokesman = 1 if cross_spokesman else 0
         keep = []
         if codes is not None:
             codes = np.ascontiguousarray(codes).view(np.uint8)
@@ -597,6 +604,59 @@ def read_grid(path):
     grid = _take(g, a.value, np.uint32)
     tot = int(grid.sum())
     return grid, _take(lq, tot, np.int32), _take(rq, tot, np.int32), _take(co, n.value, np.uint32)
+
+
+def spokesman(cell_sizes, graphs):
+    """gf_spokesman_host: (spokesman position, spokesman rank, number of spokesmen) of every
+    position (cell order) from the per-cell graphs (n x R local ids, rows in cell order)."""
+    sizes = np.ascontiguousarray(cell_sizes, np.uint32)
+    g = np.ascontiguousarray(graphs, np.uint32)
+    n = g.shape[0]
+    spk = np.zeros(n, np.uint32)
+    rank = np.zeros(n, np.uint32)
+    ns = C.c_uint32()
+    _check(lib().gf_spokesman_host(n, len(sizes), _np_ptr(sizes), g.shape[1], _np_ptr(g), _np_ptr(spk), _np_ptr(rank),
+                                   C.byref(ns)), "gf_spokesman_host")
+    return spk, rank, ns.value
+
+
+def compress_cross(cell_of, graphs, cross, cross_e: int):
+    """The reference's compressed cross graph (compress_global_graph_extreme, tools.cuh:917-1010)
+    from index arrays in the reference layout (global order): returns (center_num, col_offset,
+    center_pos, edges) with center_pos indexed by position (cell order) and edges
+    n_cells x n_spokesmen x E local ids, as gf_write_spokesman_graph writes them."""
+    cell_of = np.asarray(cell_of, np.uint32)
+    P = int(cell_of.max()) + 1
+    order = np.argsort(cell_of, kind="stable")                    # position -> global id
+    sizes = np.bincount(cell_of, minlength=P).astype(np.uint32)
+    spk, rank, ns = spokesman(sizes, np.asarray(graphs, np.uint32))
+    heads = np.nonzero(spk == np.arange(len(spk)))[0]              # spokesman positions, rank order
+    seg = np.concatenate([[0], np.cumsum(sizes)])
+    center_num = np.array([((heads >= seg[c]) & (heads < seg[c + 1])).sum() for c in range(P)], np.uint32)
+    col_offset = np.concatenate([[0], np.cumsum(center_num)[:-1]]).astype(np.uint32)
+    x = np.asarray(cross, np.uint32).reshape(len(cell_of), P, cross_e)[order[heads]]  # ns x P x E
+    edges = np.ascontiguousarray(x.transpose(1, 0, 2))
+    return center_num, col_offset, rank.astype(np.uint32), edges
+
+
+def write_spokesman_graph(path, center_num, col_offset, center_pos, edges) -> None:
+    cn = np.ascontiguousarray(center_num, np.uint32)
+    co = np.ascontiguousarray(col_offset, np.uint32)
+    cp = np.ascontiguousarray(center_pos, np.uint32)
+    e = np.ascontiguousarray(edges, np.uint32)
+    _check(lib().gf_write_spokesman_graph(str(path).encode(), len(cp), len(cn), e.shape[2], _np_ptr(cn), _np_ptr(co),
+                                          _np_ptr(cp), _np_ptr(e)), "gf_write_spokesman_graph")
+
+
+def read_spokesman_graph(path):
+    n, P, E = C.c_uint32(), C.c_uint32(), C.c_uint32()
+    a, b, c, d = C.c_void_p(), C.c_void_p(), C.c_void_p(), C.c_void_p()
+    _check(lib().gf_read_spokesman_graph(str(path).encode(), C.byref(n), C.byref(P), C.byref(E), C.byref(a),
+                                         C.byref(b), C.byref(c), C.byref(d)), "gf_read_spokesman_graph")
+    cn = _take(a, P.value, np.uint32)
+    total = int(cn.sum())
+    return (cn, _take(b, P.value, np.uint32), _take(c, n.value, np.uint32),
+            _take(d, P.value * total * E.value, np.uint32).reshape(P.value, total, E.value))
 
 
 def recall(res: np.ndarray, gt: np.ndarray) -> float:

@@ -86,6 +86,7 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "gf_search_batched before gf_plan_queries");
     if (d.sharded) return fail(GF_ERR_STATE, "gf_search_batched on a shard: search it with gf_search_keys");
+    if (d.spk_rank) return fail(GF_ERR_STATE, "gf_search_batched on spokesman-compressed cross edges: use gf_search");
     gf_search_params P;
     gf_search_defaults(&P);
     if (prm) P = *prm;

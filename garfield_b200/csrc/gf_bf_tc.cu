@@ -1166,6 +1166,9 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
         d.bf_scale = s;
         d.bf_dp = dp;
         d.bf_tiles = tiles;
+        d.bytes += sizeof(float) * d.dim + sizeof(__half) * (size_t)npad * dp + sizeof(float) * npad +
+                   sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a) + sizeof(float) * (size_t)npad * d.a +
+                   sizeof(uint32_t) * (size_t)npad + sizeof(float) * 2 * d.a;
         d.bf_ok = std::isfinite(d.bf_dmax);
     } while (0);
     if (sum) cudaFree(sum);

@@ -77,12 +77,44 @@ static void free_index(DeviceIndex& d) {
     void* ptrs[] = {d.vec16,   d.vec32,   d.attrs,     d.graph,   d.cross,   d.i2g,     d.seg,
                     d.grid_d,  d.lq_d,    d.rq_d,      d.centroids, d.hist,  d.entry,   d.sh_slot,
                     d.sh_gofs, d.sh_xofs, d.sh_vsh,    d.vec8,      d.csc,   d.cbi,     d.cnorm,
-                    d.cmean};
+                    d.cmean,   d.spk_rank};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);
     if (d.cross_h) cudaFreeHost(d.cross_h);
     free_bf_tc(d);
+}
+
+// compress_global_graph_extreme (tools.cuh:917-935): positions in cell order; a point that is
+// still its own spokesman claims, in its graph row's order, every neighbour of higher position
+// that is still its own spokesman.  rank = index of the spokesman among all spokesmen in
+// position order (the reference's center_pos, tools.cuh:978-986).
+void spokesman_assign(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,
+                      const uint32_t* graphs, uint32_t* spk, uint32_t* rank, uint32_t* n_spk) {
+    for (uint32_t i = 0; i < n; ++i) spk[i] = i;
+    uint32_t off = 0;
+    for (uint32_t c = 0; c < n_cells; ++c) {
+        const uint32_t sz = cell_sizes[c];
+        for (uint32_t j = 0; j < sz; ++j) {
+            const uint32_t i = off + j;
+            if (spk[i] != i) continue;
+            for (uint32_t k = 0; k < degree; ++k) {
+                const uint32_t loc = graphs[(size_t)i * degree + k];
+                if (loc >= sz) continue;  // not a point of this cell
+                const uint32_t x = off + loc;
+                if (spk[x] == x && x > i) spk[x] = i;
+            }
+        }
+        off += sz;
+    }
+    uint32_t cnt = 0;
+    std::vector<uint32_t> r(rank ? 0 : n);
+    uint32_t* rk = rank ? rank : r.data();
+    for (uint32_t i = 0; i < n; ++i) {
+        if (spk[i] == i) rk[i] = cnt++;
+        else rk[i] = rk[spk[i]];  // spk[i] < i: its rank is already known
+    }
+    if (n_spk) *n_spk = cnt;
 }
 
 // Deterministic entry local ids: std::mt19937 with its default seed (as the reference,
@@ -123,6 +155,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         return fail(GF_ERR_ARG, "int8 codes need their scales and zero points");
     if (sharded && (ds->host_graph || ds->keep_fp32))
         return fail(GF_ERR_ARG, "a shard cannot keep host graphs or fp32 vectors");
+    if (ds->cross_spokesman && (sharded || ds->host_graph))
+        return fail(GF_ERR_ARG, "spokesman-compressed cross edges need a whole device-resident index");
     uint64_t ncells = 1, nq = 0;
     for (uint32_t j = 0; j < ds->n_attr; ++j) {
         if (ds->grid[j] == 0) return fail(GF_ERR_ARG, "zero grid size");
@@ -297,6 +331,22 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             }
         }
     }
+    d.cross_rows = n;
+    std::vector<uint32_t> spk_rank;
+    if (ds->cross_spokesman && E) {
+        // keep the rows of spokesmen only; a position reads the row of its spokesman's rank
+        std::vector<uint32_t> spk(n), sizes(P);
+        spk_rank.resize(n);
+        for (uint32_t c = 0; c < P; ++c) sizes[c] = d.seg_h[c + 1] - d.seg_h[c];
+        uint32_t ns = 0;
+        spokesman_assign(n, P, sizes.data(), R, ds->graphs, spk.data(), spk_rank.data(), &ns);
+        const size_t rowlen = (size_t)P * E;
+        std::vector<uint32_t> comp((size_t)ns * rowlen);
+        for (uint32_t p = 0; p < n; ++p)
+            if (spk[p] == p) std::memcpy(&comp[(size_t)spk_rank[p] * rowlen], &cross[(size_t)p * rowlen], rowlen * 4);
+        cross.swap(comp);
+        d.cross_rows = ns;
+    }
     std::vector<float> attrs((size_t)n * d.a);
     for (uint32_t p = 0; p < n; ++p)
         std::memcpy(&attrs[(size_t)p * d.a], ds->attrs + (size_t)i2g[p] * d.a, sizeof(float) * d.a);
@@ -394,6 +444,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         if (!chk(dalloc(&d.attrs, (size_t)n * d.a, &d.bytes))) break;
         if (!d.host_graph && !chk(dalloc(&d.graph, graph.size(), &d.bytes))) break;
         if (!d.host_graph && E && !chk(dalloc(&d.cross, cross.size(), &d.bytes))) break;
+        if (!spk_rank.empty() && !chk(dalloc(&d.spk_rank, spk_rank.size(), &d.bytes))) break;
         if (sharded) {
             if (!chk(dalloc(&d.sh_slot, sh_slot.size(), &d.bytes))) break;
             if (!chk(dalloc(&d.sh_gofs, sh_gofs.size(), &d.bytes))) break;
@@ -451,6 +502,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             {d.attrs, attrs.data(), attrs.size() * 4},
             {d.graph, graph.data(), graph.size() * 4},
             {d.cross, cross.data(), cross.size() * 4},
+            {d.spk_rank, spk_rank.data(), spk_rank.size() * 4},
             {d.i2g, i2g.data(), i2g.size() * 4},
             {d.seg, d.seg_h.data(), d.seg_h.size() * 4},
             {d.grid_d, d.grid.data(), d.grid.size() * 4},
@@ -542,6 +594,7 @@ gf_status gf_index_info_get(const gf_index* idx, gf_index_info* out) {
     out->n_clusters = d.C;
     out->d_stored = d.d8;
     out->min_cell_size = d.min_cell;
+    out->cross_rows = d.cross_rows;
     out->device_bytes = d.bytes;
     return GF_OK;
 }

@@ -56,7 +56,9 @@ struct DeviceIndex {
     float4* vec32 = nullptr;     // n x d4 fp32 (optional)
     float* attrs = nullptr;      // n x a
     uint32_t* graph = nullptr;   // n x degree positions (NULL when host_graph)
-    uint32_t* cross = nullptr;   // n x (ncells*E) positions (NULL when host_graph)
+    uint32_t* cross = nullptr;   // cross_rows x (ncells*E) positions (NULL when host_graph)
+    uint32_t cross_rows = 0;     // n, or the number of spokesmen (cross_spokesman)
+    uint32_t* spk_rank = nullptr; // n: row of each position's cross edges (spokesman rank), or NULL
     // host_graph: graphs and cross edges stay in pinned host memory and are copied to the
     // device per batch of cells (gf_search_batched)
     bool host_graph = false;
@@ -197,6 +199,10 @@ size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum);  // working memory o
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
                     uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
                     uint32_t* timeouts, uint32_t* products, cudaStream_t s);
+// gf_index.cu: greedy spokesman assignment (compress_global_graph_extreme, tools.cuh:917-935);
+// graphs: n x degree local ids, rows in position (cell) order
+void spokesman_assign(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,
+                      const uint32_t* graphs, uint32_t* spk, uint32_t* rank, uint32_t* n_spk);
 // gf_codec.cu
 void quantize_i8_host(const float* data, uint32_t n, uint32_t dim, float alpha, int8_t* q, float* scales,
                       int32_t* zps);

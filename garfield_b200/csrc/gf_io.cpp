@@ -237,6 +237,82 @@ gf_status gf_write_u32mat(const char* path, const uint32_t* data, uint32_t n, ui
     return wr(fl, data, 4ull * n * k, path);
 }
 
+gf_status gf_write_spokesman_graph(const char* path, uint32_t n, uint32_t n_cells, uint32_t e,
+                                   const uint32_t* center_num, const uint32_t* col_offset, const uint32_t* center_pos,
+                                   const uint32_t* edges) {
+    if (!center_num || !col_offset || !center_pos || !edges) return fail(GF_ERR_ARG, "null array");
+    uint64_t total = 0;
+    for (uint32_t c = 0; c < n_cells; ++c) total += center_num[c];
+    File fl;
+    TRY(open_write(fl, path));
+    uint32_t h[3] = {n, n_cells, e};
+    TRY(wr(fl, h, 12, path));
+    TRY(wr(fl, center_num, 4ull * n_cells, path));
+    TRY(wr(fl, col_offset, 4ull * n_cells, path));
+    TRY(wr(fl, center_pos, 4ull * n, path));
+    return wr(fl, edges, 4ull * total * e * n_cells, path);
+}
+
+gf_status gf_read_spokesman_graph(const char* path, uint32_t* n, uint32_t* n_cells, uint32_t* e, uint32_t** center_num,
+                                  uint32_t** col_offset, uint32_t** center_pos, uint32_t** edges) {
+    File fl;
+    long long size;
+    TRY(open_read(fl, path, &size));
+    uint32_t h[3];
+    if (size < 12) return fail(GF_ERR_FORMAT, std::string("compressed graph too short ") + path);
+    TRY(rd(fl, h, 12, path));
+    const uint64_t head = 12 + 8ull * h[1] + 4ull * h[0];
+    if ((uint64_t)size < head) return fail(GF_ERR_FORMAT, std::string("compressed graph too short ") + path);
+    std::vector<uint32_t> cn(h[1]), co(h[1]);
+    TRY(rd(fl, cn.data(), 4ull * h[1], path));
+    TRY(rd(fl, co.data(), 4ull * h[1], path));
+    uint64_t total = 0;
+    for (uint32_t c = 0; c < h[1]; ++c) {
+        if (co[c] != total) return fail(GF_ERR_FORMAT, std::string("compressed graph offsets ") + path);
+        total += cn[c];
+    }
+    if ((uint64_t)size != head + 4ull * total * h[2] * h[1])
+        return fail(GF_ERR_FORMAT, std::string("compressed graph size mismatch ") + path);
+    uint32_t* a = xmalloc<uint32_t>(h[1]);
+    uint32_t* b = xmalloc<uint32_t>(h[1]);
+    uint32_t* c = xmalloc<uint32_t>(h[0]);
+    uint32_t* d = xmalloc<uint32_t>((size_t)total * h[2] * h[1]);
+    if (!a || !b || !c || !d) {
+        free(a), free(b), free(c), free(d);
+        return fail(GF_ERR_OOM, "host allocation");
+    }
+    std::memcpy(a, cn.data(), 4ull * h[1]);
+    std::memcpy(b, co.data(), 4ull * h[1]);
+    if (rd(fl, c, 4ull * h[0], path) != GF_OK || rd(fl, d, 4ull * total * h[2] * h[1], path) != GF_OK) {
+        free(a), free(b), free(c), free(d);
+        return GF_ERR_FORMAT;
+    }
+    for (uint32_t i = 0; i < h[0]; ++i)
+        if (c[i] >= total) {
+            free(a), free(b), free(c), free(d);
+            return fail(GF_ERR_FORMAT, std::string("spokesman rank out of range ") + path);
+        }
+    *n = h[0];
+    *n_cells = h[1];
+    *e = h[2];
+    *center_num = a;
+    *col_offset = b;
+    *center_pos = c;
+    *edges = d;
+    return GF_OK;
+}
+
+gf_status gf_spokesman_host(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,
+                            const uint32_t* graphs, uint32_t* spokesman_out, uint32_t* rank_out,
+                            uint32_t* n_spokesmen_out) {
+    if (!cell_sizes || !graphs || !spokesman_out) return fail(GF_ERR_ARG, "null array");
+    uint64_t sum = 0;
+    for (uint32_t c = 0; c < n_cells; ++c) sum += cell_sizes[c];
+    if (sum != n) return fail(GF_ERR_ARG, "cell sizes do not add up to n");
+    gf::spokesman_assign(n, n_cells, cell_sizes, degree, graphs, spokesman_out, rank_out, n_spokesmen_out);
+    return GF_OK;
+}
+
 gf_status gf_read_ranges(const char* path, uint32_t qnum, uint32_t a, int32_t* l_out, int32_t* r_out) {
     File fl;
     long long size;

@@ -33,6 +33,7 @@ struct SArgs {
     const uint32_t* __restrict__ cross;
     const uint32_t* __restrict__ seg;
     const uint32_t* __restrict__ i2g;
+    const uint32_t* __restrict__ spk;  // cross-edge row of each position (spokesman rank), or NULL
     const uint4* __restrict__ q16;
     const float* __restrict__ q32;    // fp32 queries (byte codecs: times alpha, fp32)
     const float* __restrict__ csc;    // byte codecs: per-element -scale (d16)
@@ -321,7 +322,11 @@ __device__ __forceinline__ long long graph_base(const SArgs& A, uint32_t cell, u
 
 // Element offset from A.cross of the cross edges of position src toward cell `next`.
 __device__ __forceinline__ long long cross_row(const SArgs& A, uint32_t src, uint32_t next) {
-    if (!A.slot) return (long long)src * A.P * A.E + (long long)next * A.E;
+    if (!A.slot) {
+        // spokesman-compressed edges: the row of the point's spokesman
+        const uint32_t row = A.spk ? __ldg(A.spk + src) : src;
+        return (long long)row * A.P * A.E + (long long)next * A.E;
+    }
     uint32_t lo = 0, hi = A.P;  // A.seg[lo] <= src < A.seg[hi]
     while (hi - lo > 1) {
         const uint32_t mid = (lo + hi) >> 1;
@@ -807,6 +812,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.xstride = view ? view->xstride : 0;
     A.seg = d.seg;
     A.i2g = d.i2g;
+    A.spk = view ? nullptr : d.spk_rank;
     A.q16 = p.q16;
     A.lb = p.lb;
     A.rb = p.rb;

@@ -89,6 +89,10 @@ typedef struct {
     const uint8_t* codes;
     const float* code_scales;
     const int32_t* code_zero_points;
+    /* 1 = store the cross-cell edges of spokesmen only (the "extreme" compression of
+     * compress_global_graph_extreme, tools.cuh:917-1010; see gf_spokesman_host): a point's
+     * hop into another cell uses its spokesman's edges.  Not with host_graph or shard_cells. */
+    uint32_t cross_spokesman;
 } gf_index_desc;
 
 /* Paths of the reference's index files (realdataset_search flags, README.md:101-170). */
@@ -152,6 +156,7 @@ typedef struct {
     uint32_t n, dim, n_attr, n_cells, degree, cross_e, n_clusters;
     uint32_t d_stored;       /* stored row length (dim rounded up to 8) */
     uint32_t min_cell_size;  /* entry ids are drawn below this */
+    uint32_t cross_rows;     /* points whose cross-cell edges are stored (n, or the spokesmen) */
     uint64_t device_bytes;   /* device memory held by the index */
 } gf_index_info;
 
@@ -338,9 +343,31 @@ gf_status gf_search_noalloc(gf_index* idx, const float* queries, const float* lb
                             float prefilter, const gf_search_params* params, uint32_t* ids_out, float* dist_out,
                             void* stream);
 
+/*
+ * Spokesman assignment of the cross-edge compression (compress_global_graph_extreme,
+ * tools.cuh:917-935): positions in cell order (cell c holds cell_sizes[c] points, rows of
+ * `graphs` in that order, entries local ids); a point that is still its own spokesman
+ * claims, in its graph row's order, every neighbour of higher position that is still its
+ * own spokesman.  spokesman_out[pos] = the spokesman's position; rank_out[pos] (optional) =
+ * the spokesman's rank among all spokesmen in position order (the reference's center_pos).
+ */
+gf_status gf_spokesman_host(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,
+                            const uint32_t* graphs, uint32_t* spokesman_out, uint32_t* rank_out,
+                            uint32_t* n_spokesmen_out);
+
 /* ------------------------------------------------------ file formats (host) */
 /* Readers allocate with malloc; release with gf_free. */
 void gf_free(void* p);
+
+/* Compressed cross-cell graph (save_global_graph_extreme / load_global_graph_extreme,
+ * tools.cuh:1012-1065): uint32 n, n_cells, E; n_cells spokesmen per cell; n_cells offsets
+ * (prefix of the former); n ranks (center_pos, the spokesman rank of each position); then
+ * n_cells x n_spokesmen x E local ids: block c holds the spokesmen's E edges into cell c. */
+gf_status gf_write_spokesman_graph(const char* path, uint32_t n, uint32_t n_cells, uint32_t e,
+                                   const uint32_t* center_num, const uint32_t* col_offset, const uint32_t* center_pos,
+                                   const uint32_t* edges);
+gf_status gf_read_spokesman_graph(const char* path, uint32_t* n, uint32_t* n_cells, uint32_t* e, uint32_t** center_num,
+                                  uint32_t** col_offset, uint32_t** center_pos, uint32_t** edges);
 
 /* .fvecs: per row int32 d then d float32 (tools.cuh:85-106). */
 gf_status gf_read_fvecs(const char* path, float** data, uint32_t* n, uint32_t* dim);

@@ -26,6 +26,8 @@
  *   orc_quantize_i8    production_adapter.cuh:316-337  per-dimension affine int8 codec (host path of
  *                                                      load_dataset_return_int8_arr_infile)
  *   orc_dist8          big_dataset_adapterV3.cuh:852-863, 2802-2810  distances to int8 / uint8 rows
+ *   orc_spokesman      tools.cuh:917-935, 978-986      spokesman assignment of the cross-edge
+ *                                                      compression (compress_global_graph_extreme)
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
  *   - orc_dist32: squared L2 of two rows of padded length (a multiple of 4).  Eight
@@ -266,6 +268,40 @@ void orc_bruteforce(const float* data4, uint32_t n, uint32_t d4, const float* at
         }
         free(list);
     }
+}
+
+/* ------------------------------------------------- cross-edge compression */
+
+/*
+ * tools.cuh:917-935, 978-986 (compress_global_graph_extreme): spokesman of every position
+ * (cells in order, sizes[c] points each, graph rows in position order holding local ids).
+ * Scanning positions in order, a point that is still its own spokesman makes every
+ * neighbour k of its row (in row order) with position > its own and still its own spokesman
+ * a follower.  rank[p] = number of spokesmen at positions before p's spokesman.  Returns
+ * the number of spokesmen.
+ */
+uint32_t orc_spokesman(const uint32_t* sizes, uint32_t ncells, const uint32_t* graphs, uint32_t degree, uint32_t* spk,
+                       uint32_t* rank) {
+    uint32_t n = 0;
+    for (uint32_t c = 0; c < ncells; ++c) n += sizes[c];
+    for (uint32_t i = 0; i < n; ++i) spk[i] = i;
+    uint32_t off = 0;
+    for (uint32_t c = 0; c < ncells; ++c) {
+        for (uint32_t j = 0; j < sizes[c]; ++j) {
+            const uint32_t i = off + j;
+            if (spk[i] != i) continue;
+            for (uint32_t k = 0; k < degree; ++k) {
+                const uint32_t loc = graphs[(size_t)i * degree + k];
+                if (loc >= sizes[c]) continue;
+                const uint32_t x = off + loc;
+                if (spk[x] == x && x > i) spk[x] = i;
+            }
+        }
+        off += sizes[c];
+    }
+    uint32_t cnt = 0;
+    for (uint32_t i = 0; i < n; ++i) rank[i] = spk[i] == i ? cnt++ : rank[spk[i]];
+    return cnt;
 }
 
 /* ------------------------------------------------------------- planning */

@@ -55,6 +55,8 @@ def lib() -> C.CDLL:
         _L.orc_dist8.restype = C.c_float
         _L.orc_dist8.argtypes = [P, P, P, P, U, U]
         _L.orc_quantize_i8.argtypes = [P, U, U, C.c_float, P, P, P]
+        _L.orc_spokesman.argtypes = [P, U, P, U, P, P]
+        _L.orc_spokesman.restype = U
         _L.orc_dist_seq.restype = C.c_float
         _L.orc_dist_seq.argtypes = [P, P, U]
         _L.orc_f2h.argtypes = [P, U, U, U, C.c_float, P]
@@ -164,6 +166,29 @@ def order_cells(queries, centroids, hist, counts, offsets, cells):
     lib().orc_order_cells(_p(queries), queries.shape[0], queries.shape[1], _p(centroids), centroids.shape[0],
                           _p(hist), _p(counts), _p(offsets), _p(cells), _p(top4))
     return cells, top4
+
+
+def spokesman(sizes, graphs):
+    """tools.cuh:917-935 (compress_global_graph_extreme): (spokesman position, rank, count)
+    of every position; graphs are n x R local ids with rows in position (cell) order."""
+    sizes = np.ascontiguousarray(sizes, np.uint32)
+    g = np.ascontiguousarray(graphs, np.uint32)
+    spk = np.zeros(g.shape[0], np.uint32)
+    rank = np.zeros(g.shape[0], np.uint32)
+    ns = lib().orc_spokesman(_p(sizes), len(sizes), _p(g), g.shape[1], _p(spk), _p(rank))
+    return spk, rank, int(ns)
+
+
+def expand_spokesman_cross(cell_of, graphs, cross):
+    """Cross edges as a spokesman-compressed index uses them, in the reference layout
+    (global order): the row of every point is replaced by its spokesman's row."""
+    cell_of = np.asarray(cell_of, np.uint32)
+    order = np.argsort(cell_of, kind="stable")  # position -> global id
+    sizes = np.bincount(cell_of, minlength=int(cell_of.max()) + 1)
+    spk, _, _ = spokesman(sizes, np.asarray(graphs, np.uint32))
+    out = np.empty_like(np.asarray(cross))
+    out[order] = np.asarray(cross)[order[spk]]
+    return out
 
 
 def quantize_i8(data, alpha: float = 1.0):

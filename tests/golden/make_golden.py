@@ -14,6 +14,10 @@ the GPU box never runs this script, it only reads the .npz files it writes.
   golden_quant.npz    the reference's host int8 quantiser (production_adapter.cuh:316-337,
                       via load_dataset_return_int8_arr_infile) run the same way: the .q file
                       it writes (codes, scales, zero points)
+  golden_spokesman.npz the reference's cross-graph compression compress_global_graph_extreme
+                      and its writer save_global_graph_extreme (tools.cuh:917-1038) run on the
+                      CPU by oracle/_ref/ref_spokesman (`make -C oracle ref_spokesman REF=...`):
+                      the compressed-graph file it writes, for seeded per-cell graphs
 
 Inputs are seeded synthetic arrays written next to the outputs.
 """
@@ -117,6 +121,30 @@ def golden_quant(ref_bin: Path) -> None:
     np.savez_compressed(HERE / "golden_quant.npz", data=x, **out)
 
 
+def golden_spokesman(ref_bin: Path) -> None:
+    rng = np.random.default_rng(20261207)
+    sizes = np.array([700, 500, 650, 400, 3], np.uint32)
+    R, E = 8, 2
+    n, P = int(sizes.sum()), len(sizes)
+    graphs = np.concatenate([rng.integers(0, s, size=(s, R)) for s in sizes]).astype(np.uint32)
+    cross_t = np.stack([rng.integers(0, sizes[c], size=(n, E)) for c in range(P)]).astype(np.uint32)
+    with tempfile.TemporaryDirectory() as td:
+        t = Path(td)
+        graphs.tofile(t / "g.u32")
+        sizes.tofile(t / "s.u32")
+        cross_t.tofile(t / "x.u32")
+        subprocess.run([str(ref_bin), str(t / "g.u32"), str(t / "s.u32"), str(t / "x.u32"), str(R), str(E),
+                        str(t / "out.bin")], check=True, capture_output=True)
+        raw = np.fromfile(t / "out.bin", np.uint32)
+    hn, hp, he = (int(v) for v in raw[:3])
+    cn = raw[3:3 + hp]
+    co = raw[3 + hp:3 + 2 * hp]
+    cp = raw[3 + 2 * hp:3 + 2 * hp + hn]
+    edges = raw[3 + 2 * hp + hn:].reshape(hp, int(cn.sum()), he)
+    np.savez_compressed(HERE / "golden_spokesman.npz", sizes=sizes, graphs=graphs, cross_t=cross_t, degree=R, e=E,
+                        center_num=cn, col_offset=co, center_pos=cp, edges=edges, raw=raw)
+
+
 def main() -> None:
     ref = Path(sys.argv[1]) if len(sys.argv) > 1 else None
     if ref is None or not (ref / "indexbuild" / "tools.py").exists():
@@ -127,6 +155,10 @@ def main() -> None:
         subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref_golden", f"REF={ref}"], check=True)
     golden_bf_and_cluster(ref_bin)
     golden_quant(ref_bin)
+    spk_bin = ROOT / "oracle" / "_ref" / "ref_spokesman"
+    if not spk_bin.exists():
+        subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref_spokesman", f"REF={ref}"], check=True)
+    golden_spokesman(spk_bin)
     print("golden fixtures written to", HERE)
 
 
