@@ -531,6 +531,71 @@ def run_bruteforce(args):
     print(json.dumps(out), flush=True)
 
 
+def run_fullgraph(args):
+    """Full-graph post-filter ablation (row f4): the reference's baseline that searches
+    assemble_edges' graph of the whole index and applies the box only at the end
+    (full_graph_search.cuh:179-997), on config 2 beside the cell-by-cell search: recall at
+    each L of the sweep and QPS (plan + search) for both."""
+    import torch
+    import garfield_b200 as gf
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    ds, ix = dataset_and_index(args, device)
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, keep_fp32=True,
+                            device=local)
+    index.assemble(ix.cross_e)
+    qnum = ds.queries.shape[0]
+    qd = torch.from_numpy(ds.queries).to(device)
+    lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
+    hid = torch.from_numpy(ds.hi.astype(np.float32)).to(device)
+    S = min(args.gt_sample, qnum)
+    gt = index.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), 10)[0]
+    gt = gt.cpu().numpy().view(np.uint32)
+    stream = torch.cuda.Stream(device)
+    plan = index.plan(qnum)
+    width = args.width or 4
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
+    res = {}
+    for name in ("cell_by_cell", "full_graph_postfilter"):
+        def step(L):
+            plan.build(qd, lod, hid, 0.0, stream)
+            p = gf.SearchParams(L=L, k=10, width=width)
+            return plan.search(p, stream) if name == "cell_by_cell" else plan.search_fullgraph(p, stream)
+        sweep = []
+        for L in L_SWEEP[:12]:
+            with torch.cuda.stream(stream):
+                ids, _ = step(L)
+            stream.synchronize()
+            sweep.append((L, round(gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt), 4)))
+        L40 = 40
+        for _ in range(args.warmup):
+            with torch.cuda.stream(stream):
+                step(L40)
+        ms = []
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.fill_(float(i))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                step(L40)
+                b.record(stream)
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        res[name] = {"qps_at_L40": round(qnum / (float(np.mean(ms)) / 1e3), 1),
+                     "ms_per_step_at_L40": round(float(np.mean(ms)), 4), "sweep": sweep}
+    out = {"metric": "recall@10 and QPS of the full-graph post-filter ablation vs the cell-by-cell search (1M x 128)",
+           "value": res["full_graph_postfilter"]["qps_at_L40"], "unit": "queries/s", "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["full_graph_postfilter"]["ms_per_step_at_L40"],
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
+           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
+           "config": {"workload": "config2, full-graph ablation (assemble_edges, reserve = E)", "width": width,
+                      "recall_sample": S, "l2": "flushed (256 MiB write) between timed steps", **res}}
+    print(json.dumps(out), flush=True)
+
+
 def run_sharded(args):
     """Cell-sharded mode (row e, strong scaling): rank r of N holds the cells
     dist.shard_cells(grid, N)[r] only; a step plans all queries on every rank, searches them
@@ -706,7 +771,8 @@ def main():
     ap.add_argument("--cache", default="/tmp/gf_cache")
     ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
-    ap.add_argument("--mode", default="in-memory", choices=["in-memory", "out-of-core", "sharded", "bruteforce"])
+    ap.add_argument("--mode", default="in-memory",
+                    choices=["in-memory", "out-of-core", "sharded", "bruteforce", "fullgraph"])
     ap.add_argument("--batch-cells", dest="batch_cells", type=int, default=4)
     ap.add_argument("--cross-spokesman", dest="cross_spokesman", action="store_true",
                     help="keep the cross-cell edges of spokesmen only (row f2 of the scope table)")
@@ -717,6 +783,8 @@ def main():
         run_sharded(args)
     elif args.impl == "ours" and args.mode == "bruteforce":
         run_bruteforce(args)
+    elif args.impl == "ours" and args.mode == "fullgraph":
+        run_fullgraph(args)
     elif args.impl == "reference":
         run_reference_cpu(args)
     elif args.impl == "reference-cuda":

@@ -126,6 +126,8 @@ def lib() -> C.CDLL:
                                                _PTR(C.c_uint64)]),
         "gf_bruteforce": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _P]),
         "gf_bruteforce_ex": (C.c_int, [_P, _P, _P, _P, _U32, _U32, _P, _P, _PTR(_BfParams), _P]),
+        "gf_index_assemble": (C.c_int, [_P, _U32]),
+        "gf_search_fullgraph": (C.c_int, [_P, _P, _PTR(_SearchParams), _P, _P, _P]),
         "gf_free": (None, [_P]),
         "gf_read_fvecs": (C.c_int, [C.c_char_p, _PTR(_P), _PTR(_U32), _PTR(_U32)]),
         "gf_write_fvecs": (C.c_int, [C.c_char_p, _P, _U32, _U32]),
@@ -311,6 +313,10 @@ class Index:
         _check(lib().gf_index_entry_points(self._h, n, _np_ptr(out)), "gf_index_entry_points")
         return out
 
+    def assemble(self, reserve: int = 2) -> None:
+        """gf_index_assemble: the full-graph ablation's graph (assemble_edges) on the device."""
+        _check(lib().gf_index_assemble(self._h, reserve), "gf_index_assemble")
+
     def plan(self, max_queries: int) -> "Plan":
         return Plan(self, max_queries)
 
@@ -425,6 +431,21 @@ class Plan:
         cp = params._c()
         _check(lib().gf_search(self.index._h, self._h, C.byref(cp), _dev_ptr(ids), _dev_ptr(dist),
                                _stream_ptr(stream)), "gf_search")
+        return ids, dist
+
+    def search_fullgraph(self, params: SearchParams | None = None, stream=None, ids=None, dist=None):
+        """gf_search_fullgraph: the full-graph post-filter ablation over the index's assembled
+        graph (Index.assemble first)."""
+        import torch
+        params = params or SearchParams()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if ids is None:
+            ids = torch.empty((self.qnum, params.k), dtype=torch.int32, device=dev)
+        if dist is None:
+            dist = torch.empty((self.qnum, params.k), dtype=torch.float32, device=dev)
+        cp = params._c()
+        _check(lib().gf_search_fullgraph(self.index._h, self._h, C.byref(cp), _dev_ptr(ids), _dev_ptr(dist),
+                                         _stream_ptr(stream)), "gf_search_fullgraph")
         return ids, dist
 
     def search_batched(self, batches, params: SearchParams | None = None, stream=None, ids=None, dist=None):

@@ -77,7 +77,7 @@ static void free_index(DeviceIndex& d) {
     void* ptrs[] = {d.vec16,   d.vec32,   d.attrs,     d.graph,   d.cross,   d.i2g,     d.seg,
                     d.grid_d,  d.lq_d,    d.rq_d,      d.centroids, d.hist,  d.entry,   d.sh_slot,
                     d.sh_gofs, d.sh_xofs, d.sh_vsh,    d.vec8,      d.csc,   d.cbi,     d.cnorm,
-                    d.cmean,   d.spk_rank};
+                    d.cmean,   d.spk_rank, d.fgraph, d.fentry};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (d.graph_h) cudaFreeHost(d.graph_h);

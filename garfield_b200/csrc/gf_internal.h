@@ -59,6 +59,11 @@ struct DeviceIndex {
     uint32_t* cross = nullptr;   // cross_rows x (ncells*E) positions (NULL when host_graph)
     uint32_t cross_rows = 0;     // n, or the number of spokesmen (cross_spokesman)
     uint32_t* spk_rank = nullptr; // n: row of each position's cross edges (spokesman rank), or NULL
+    // full-graph ablation (gf_index_assemble): n x fdeg positions, entry positions
+    uint32_t* fgraph = nullptr;
+    uint32_t fdeg = 0, fentry_n = 0;
+    uint32_t* fentry = nullptr;
+    std::vector<uint32_t> fentry_h;
     // host_graph: graphs and cross edges stay in pinned host memory and are copied to the
     // device per batch of cells (gf_search_batched)
     bool host_graph = false;
@@ -181,7 +186,7 @@ struct CellView {
     bool accumulate_stats = false;      // add to the plan's counters instead of resetting them
 };
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
-                 cudaStream_t s, const CellView* view = nullptr);
+                 cudaStream_t s, const CellView* view = nullptr, bool fullgraph = false);
 CellView shard_view(const DeviceIndex& d);
 // run keys -> ids (via position -> global id) and distances
 gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t total, uint32_t* ids, float* dist,

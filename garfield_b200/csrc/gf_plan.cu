@@ -340,6 +340,7 @@ uint32_t centroid_chunk(uint32_t C) {
 }
 
 uint32_t centroid_splits(uint32_t C) {
+    if (C == 0) return 1;  // no clusters: cells keep their id order
     uint32_t S = (C + kTC - 1) / kTC;
     S = std::min(S, 32u);
     S = std::max(S, 1u);

@@ -14,6 +14,8 @@
 // arithmetic.  The range predicate is evaluated alongside and kept as a flag bit, so
 // evictions and the final filter need no further attribute reads.
 #include <algorithm>
+#include <random>
+#include <vector>
 #include <cstdio>
 
 #include "gf_device.cuh"
@@ -683,6 +685,198 @@ __global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constan
     }
 }
 
+// Full-graph post-filter search (full_graph_search_postfiltering, full_graph_search.cuh:
+// 179-593): the same warp-per-query beam rounds as gmg_search_kernel, over the assembled
+// graph (A.graph, A.R entries per row) of the whole index -- no cell walk, no hops, no
+// recycle list; the box is applied once, to the final list.  Entry set: A.entry holds
+// positions.
+template <int NCH, bool BYTES>
+__global__ void __launch_bounds__(128, 5) fullgraph_kernel(const __grid_constant__ SArgs A) {
+    extern __shared__ __align__(16) uint32_t smem[];
+    const uint32_t lane = lane_id();
+    uint32_t* const base = smem + (threadIdx.x >> 5) * A.warp_words;
+    const uint32_t nch = NCH ? (uint32_t)NCH : A.nch;
+    if (lane == 0) {
+        mbar_init(reinterpret_cast<uint64_t*>(base + A.o_mbar), 1);
+        base[A.o_mbar + 2] = 0;
+        base[A.o_mbar + 3] = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    for (;;) {
+        uint32_t slot = 0;
+        if (lane == 0) slot = atomicAdd(A.queue, 1u);
+        slot = __shfl_sync(kFull, slot, 0);
+        if (slot >= A.qnum) break;
+        const uint32_t q = A.task[slot];
+        if (BYTES) {
+            float* qf = reinterpret_cast<float*>(base + A.o_q);
+            float* sc = reinterpret_cast<float*>(base + A.o_sc);
+            float* bi = reinterpret_cast<float*>(base + A.o_bi);
+            for (uint32_t i = lane; i < nch * 16; i += 32) {
+                qf[i] = i < A.dim ? __fmul_rn(A.q32[(size_t)q * A.dim + i], A.alpha) : 0.0f;
+                sc[i] = A.csc[i];
+                bi[i] = A.cbi[i];
+            }
+        } else {
+            f2x* q2 = reinterpret_cast<f2x*>(base + A.o_q);
+            for (uint32_t c = lane; c < nch; c += 32) {
+                const uint4 v = A.q16[(size_t)q * nch + c];
+                q2[c * 4 + 0] = h2_to_f2x(v.x);
+                q2[c * 4 + 1] = h2_to_f2x(v.y);
+                q2[c * 4 + 2] = h2_to_f2x(v.z);
+                q2[c * 4 + 3] = h2_to_f2x(v.w);
+            }
+        }
+        if (lane < A.a) {
+            base[A.o_lb + lane] = __float_as_uint(A.lb[(size_t)q * A.a + lane]);
+            base[A.o_rb + lane] = __float_as_uint(A.rb[(size_t)q * A.a + lane]);
+        }
+        __syncwarp();
+        uint32_t st_dist = 0, st_exp = 0;
+        W w{base, 0u, 0u};
+        for (uint32_t i = lane; i < A.L; i += 32) w.T(A)[i] = kEmptyKey;
+        hash_clear(w.H(A), A.hs);
+        uint32_t nb = 0;
+        for (uint32_t i0 = 0; i0 < A.n_entry; i0 += 32) {
+            const uint32_t i = i0 + lane;
+            bool ok = false;
+            uint32_t pos = 0;
+            if (i < A.n_entry) {
+                pos = A.entry[i];
+                ok = pos < A.n && hash_insert(w.H(A), A.hs, A.hshift, pos);
+            }
+            append(w.P(A), nb, ok, pos);
+        }
+        __syncwarp();
+        uint32_t hcount = nb;
+        {
+            const uint32_t n0 = nb;
+            nb = eval_sort<NCH, BYTES>(A, w.base, n0, kEmptyKey, 0);
+            st_dist += n0;
+        }
+        merge_step(A, w, A.L, 0, nb, false);
+        for (uint32_t it = 0; it < A.max_iter; ++it) {
+            uint32_t np = 0;
+            {
+                key_t* T = w.T(A);
+                uint32_t* picks = w.picks(A);
+                for (uint32_t i0 = 0; i0 < A.L && np < A.W; i0 += 32) {
+                    const uint32_t i = i0 + lane;
+                    const key_t k = i < A.L ? T[i] : kEmptyKey;
+                    uint32_t msk = __ballot_sync(kFull, (k & kKeyExplored) == 0);
+                    while (msk && np < A.W) {
+                        const uint32_t b = __ffs(msk) - 1;
+                        msk &= msk - 1;
+                        if (lane == b) {
+                            T[i] = k | kKeyExplored;
+                            picks[np] = key_pos(k);
+                        }
+                        ++np;
+                    }
+                }
+                __syncwarp();
+            }
+            if (np == 0) break;
+            st_exp += np;
+            const uint32_t total = np * A.R;
+            if (hcount + total > (A.hs >> 1)) hcount = hash_rebuild(A, w, 0, A.n);
+            nb = 0;
+            {
+                const uint32_t* picks = w.picks(A);
+                uint32_t* H = w.H(A);
+                uint32_t* G = reinterpret_cast<uint32_t*>(w.B(A));
+                bool have = !w.base[A.o_mbar + 3];
+                if (have) {
+                    if (A.graph_bulk) {
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive_expect_tx(reinterpret_cast<uint64_t*>(w.base + A.o_mbar),
+                                                  np * A.R * 4 + A.extra_tx);
+                        __syncwarp();
+                        if (lane < np)
+                            bulk_g2s(G + lane * A.R, A.graph + (long long)picks[lane] * A.R, A.R * 4,
+                                     reinterpret_cast<uint64_t*>(w.base + A.o_mbar));
+                        have = !stage_wait(A, w.base);
+                    } else {
+                        copy_rows(A, G, picks, np, 0);
+                    }
+                }
+                if (have) {
+                    for (uint32_t j0 = 0; j0 < total; j0 += 32) {
+                        const uint32_t j = j0 + lane;
+                        bool ok = false;
+                        uint32_t pos = kEmpty;
+                        if (j < total) {
+                            pos = G[j];
+                            if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
+                        }
+                        append(w.P(A), nb, ok, pos);
+                    }
+                }
+                __syncwarp();
+            }
+            hcount += nb;
+            if (nb == 0) continue;
+            const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, w.T(A)[A.L - 1], 0);
+            st_dist += nb;
+            merge_step(A, w, A.L, 0, ns, false);
+        }
+        // post-filter: the in-range entries of the final list, in order
+        {
+            const key_t* T = w.T(A);
+            key_t* Tn = w.Tn(A);
+            uint32_t nin = 0;
+            for (uint32_t i0 = 0; i0 < A.L; i0 += 32) {
+                const uint32_t i = i0 + lane;
+                const key_t k = i < A.L ? T[i] : kEmptyKey;
+                const bool ok = k != kEmptyKey && (k & kKeyInRange);
+                const uint32_t msk = __ballot_sync(kFull, ok);
+                if (ok) Tn[nin + __popc(msk & lanemask_lt())] = k;
+                nin += __popc(msk);
+            }
+            __syncwarp();
+            write_result(A, q, Tn, nin);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            atomicAdd(A.stats + 0, (unsigned long long)st_dist);
+            atomicAdd(A.stats + 1, (unsigned long long)st_exp);
+            atomicAdd(A.stats + 5, 1ull);
+        }
+    }
+}
+
+// Assembled graph of the full-graph search (assemble_edges, full_graph_search.cuh:984-997):
+// row of position p, slot j * reserve + e: in p's own cell the e-th entry of its graph row,
+// in every other cell j its e-th cross edge (positions; kEmpty where absent).
+__global__ void assemble_kernel(const uint32_t* __restrict__ graph, const uint32_t* __restrict__ cross,
+                                const uint32_t* __restrict__ spk, const uint32_t* __restrict__ seg, uint32_t n,
+                                uint32_t P, uint32_t R, uint32_t E, uint32_t reserve, uint32_t* __restrict__ out) {
+    const uint64_t D = (uint64_t)P * reserve, total = (uint64_t)n * D;
+    for (uint64_t idx = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t pos = (uint32_t)(idx / D), slot = (uint32_t)(idx % D), j = slot / reserve, e = slot % reserve;
+        uint32_t lo = 0, hi = P;  // seg[lo] <= pos < seg[hi]: the own cell
+        while (hi - lo > 1) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (seg[mid] <= pos)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        uint32_t v = kEmpty;
+        if (j == lo) {
+            if (e < R) v = graph[(size_t)pos * R + e];
+        } else if (e < E && cross) {
+            const uint32_t row = spk ? spk[pos] : pos;
+            v = cross[(size_t)row * P * E + (size_t)j * E + e];
+        }
+        out[idx] = v;
+    }
+}
+
 __global__ void run_to_ids_kernel(const unsigned long long* __restrict__ run, uint32_t total,
                                   const uint32_t* __restrict__ i2g, uint32_t* ids, float* dist) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -740,6 +934,15 @@ KernelFn pick_kernel(uint32_t nch, bool bytes) {
     }
 }
 
+KernelFn pick_fullgraph(uint32_t nch, bool bytes) {
+    if (bytes) return nch == 8 ? fullgraph_kernel<8, true> : fullgraph_kernel<0, true>;
+    switch (nch) {
+        case 16: return fullgraph_kernel<16, false>;
+        case 8: return fullgraph_kernel<8, false>;
+        default: return fullgraph_kernel<0, false>;
+    }
+}
+
 }  // namespace
 
 CellView shard_view(const DeviceIndex& d) {
@@ -756,10 +959,12 @@ CellView shard_view(const DeviceIndex& d) {
 }
 
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
-                 cudaStream_t s, const CellView* view) {
+                 cudaStream_t s, const CellView* view, bool fullgraph) {
     DeviceIndex& d = idx->d;
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "gf_search before gf_plan_queries");
+    if (fullgraph && (view || !d.fgraph))
+        return fail(GF_ERR_STATE, "full-graph search needs the assembled graph (gf_index_assemble)");
     gf_search_params P;
     gf_search_defaults(&P);
     if (prm) P = *prm;
@@ -767,9 +972,9 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (P.L < P.k || P.L > 4096) return fail(GF_ERR_ARG, "L must be k..4096");
     if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
     uint32_t n_entry = P.n_entry ? P.n_entry : d.degree;
-    n_entry = std::min<uint32_t>(n_entry, (uint32_t)d.entry_h.size());
+    n_entry = std::min<uint32_t>(n_entry, fullgraph ? d.fentry_n : (uint32_t)d.entry_h.size());
     if (!ids && !(view && view->run)) return fail(GF_ERR_ARG, "null ids_out");
-    if (!view && d.sharded) {
+    if (!view && d.sharded && !fullgraph) {
         // a shard: search its cells through its view, merge into the plan's running keys
         const size_t need = (size_t)p.qnum * P.k;
         if (need > p.run_cap) {
@@ -821,7 +1026,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.cells = p.cells;
     A.box = p.prefilter > 0.0f ? p.box : nullptr;
     A.task = p.task;
-    A.entry = d.entry;
+    A.entry = fullgraph ? d.fentry : d.entry;
     A.queue = p.scratch;
     A.out_ids = ids;
     A.out_d = dist;
@@ -842,8 +1047,15 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.prefilter = p.prefilter;
     A.wait_polls = P.test_wait ? P.test_wait : kStageWaitPolls;
     A.extra_tx = P.test_wait ? 16u : 0u;
-    A.graph_bulk = (d.degree * 4) % 16 == 0 ? 1u : 0u;
-    uint32_t need = std::max<uint32_t>({P.width * d.degree, n_entry, kHopSlots * A.E, 64u});
+    if (fullgraph) {  // one graph over the whole index: the assembled rows, no cross edges
+        A.graph = d.fgraph;
+        A.R = d.fdeg;
+        A.cross = nullptr;
+        A.E = 0;
+        A.spk = nullptr;
+    }
+    A.graph_bulk = (A.R * 4) % 16 == 0 ? 1u : 0u;
+    uint32_t need = std::max<uint32_t>({P.width * A.R, n_entry, kHopSlots * A.E, 64u});
     uint32_t bcap = 1;
     while (bcap < need) bcap <<= 1;
     A.bcap = bcap;
@@ -866,7 +1078,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.stage_rows = sr;
     make_layout(A, nch16, bytes);
 
-    KernelFn kern = pick_kernel(A.nch, bytes);
+    KernelFn kern = fullgraph ? pick_fullgraph(A.nch, bytes) : pick_kernel(A.nch, bytes);
     const int warps_per_block = 4;
     size_t smem = (size_t)warps_per_block * A.warp_words * 4;
     int dev = d.device;
@@ -899,6 +1111,69 @@ gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t tota
 }  // namespace gf
 
 using namespace gf;
+
+extern "C" gf_status gf_index_assemble(gf_index* idx, uint32_t reserve) {
+    if (!idx) return fail(GF_ERR_ARG, "null index");
+    DeviceIndex& d = idx->d;
+    if (d.sharded || d.host_graph) return fail(GF_ERR_STATE, "the assembled graph needs a whole device-resident index");
+    if (reserve == 0 || reserve > 16) return fail(GF_ERR_ARG, "reserve must be 1..16");
+    if ((uint64_t)d.ncells * reserve > 4096) return fail(GF_ERR_ARG, "cells x reserve above 4096");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d.device);
+    gf_status st = GF_OK;
+    do {
+        if (d.fgraph) {
+            cudaFree(d.fgraph);
+            d.fgraph = nullptr;
+        }
+        const uint32_t D = d.ncells * reserve;
+        cudaError_t e = cudaMalloc((void**)&d.fgraph, std::max<size_t>((size_t)d.n * D, 1) * 4);
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "assembled graph");
+            break;
+        }
+        assemble_kernel<<<148 * 8, 256>>>(d.graph, d.cross, d.spk_rank, d.seg, d.n, d.ncells, d.degree, d.E,
+                                          reserve, d.fgraph);
+        // entry positions over the whole index: std::mt19937 default seed, draw % n, distinct
+        std::mt19937 rng;
+        std::vector<uint32_t> ent;
+        const uint32_t want = std::min<uint32_t>(std::max<uint32_t>(D, 64), d.n);
+        std::vector<uint8_t> seen(d.n, 0);
+        while (ent.size() < want) {
+            const uint32_t t = (uint32_t)(rng() % d.n);
+            if (!seen[t]) {
+                seen[t] = 1;
+                ent.push_back(t);
+            }
+        }
+        if (d.fentry) cudaFree(d.fentry);
+        d.fentry = nullptr;
+        e = cudaMalloc((void**)&d.fentry, std::max<size_t>(ent.size(), 1) * 4);
+        if (e == cudaSuccess) e = cudaMemcpy(d.fentry, ent.data(), ent.size() * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "assembled graph");
+            break;
+        }
+        d.fdeg = D;
+        d.fentry_n = (uint32_t)ent.size();
+        d.fentry_h = ent;
+    } while (0);
+    if (prev >= 0) cudaSetDevice(prev);
+    return st;
+}
+
+extern "C" gf_status gf_search_fullgraph(gf_index* idx, gf_plan* plan, const gf_search_params* params,
+                                         uint32_t* ids_out, float* dist_out, void* stream) {
+    if (!idx || !plan || plan->p.idx != idx) return fail(GF_ERR_ARG, "plan does not belong to this index");
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(idx->d.device);
+    gf_status st = search(idx, plan, params, ids_out, dist_out, (cudaStream_t)stream, nullptr, true);
+    if (prev >= 0) cudaSetDevice(prev);
+    return st;
+}
 
 extern "C" gf_status gf_search_keys(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint64_t* keys_out,
                                     void* stream) {

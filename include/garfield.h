@@ -291,6 +291,21 @@ gf_status gf_schedule_batches_host(uint32_t ncells, uint32_t qnum, const uint32_
                                    uint32_t* batch_sizes_out, uint32_t* n_batches_out, uint64_t* splits_out);
 
 /*
+ * Full-graph post-filter search, the reference's ablation baseline
+ * (full_graph_search_postfiltering over assemble_edges' graph, full_graph_search.cuh:179-997).
+ * gf_index_assemble builds the graph on the device: per point `reserve` neighbours per cell
+ * (its first `reserve` cell-graph neighbours in its own cell, its first `reserve` cross edges
+ * into every other cell; the reference uses reserve = 2) and the entry points (positions,
+ * std::mt19937 default seed, draw % n, distinct).  gf_search_fullgraph searches a planned
+ * batch (gf_plan_queries) over that graph of the whole index with the same beam rounds as
+ * gf_search, without the cell walk or the recycle list, and applies the box to the final
+ * list only.  Results as gf_search.
+ */
+gf_status gf_index_assemble(gf_index* idx, uint32_t reserve);
+gf_status gf_search_fullgraph(gf_index* idx, gf_plan* plan, const gf_search_params* params, uint32_t* ids_out,
+                              float* dist_out, void* stream);
+
+/*
  * Exact filtered k-NN: every point whose attributes lie inside the query's box competes;
  * squared L2 on the fp32 vectors; (distance, global id) order.  Replaces
  * naive_brute_force_with_filter (gpu_graph.cu:10782) and prefiltering_and_bruteforce

@@ -28,6 +28,8 @@
  *   orc_dist8          big_dataset_adapterV3.cuh:852-863, 2802-2810  distances to int8 / uint8 rows
  *   orc_spokesman      tools.cuh:917-935, 978-986      spokesman assignment of the cross-edge
  *                                                      compression (compress_global_graph_extreme)
+ *   orc_assemble       full_graph_search.cuh:984-997   assemble_edges (the full-graph ablation's graph)
+ *   orc_search_fullgraph full_graph_search.cuh:179-593 full_graph_search_postfiltering
  *
  * Fixed evaluation orders ("canonical distances"), shared with the CUDA kernels:
  *   - orc_dist32: squared L2 of two rows of padded length (a multiple of 4).  Eight
@@ -760,6 +762,141 @@ static void search_one(const qctx* c, const orc_params* p, const uint32_t* cl, u
     free(tmp);
     free(seen);
     free(touched);
+}
+
+/* Forward declaration (defined below). */
+static void make_positions(const orc_index* ix, uint32_t** seg_out, uint32_t** g_out, uint32_t** p_out);
+
+/*
+ * full_graph_search.cuh:984-997 (assemble_edges): one row per point, `reserve` neighbours
+ * per cell -- in the point's own cell the first `reserve` entries of its cell-graph row,
+ * in every other cell its first `reserve` cross edges -- slot j*reserve + e for cell j.
+ * Rows and entries are positions (the reference writes global ids, rows by global id);
+ * an entry that is not a point of its cell is ORC_EMPTY.  out: n x (ncells*reserve).
+ */
+void orc_assemble(const orc_index* ix, uint32_t reserve, uint32_t* out) {
+    uint32_t *seg, *g_of, *p_of;
+    make_positions(ix, &seg, &g_of, &p_of);
+    const uint32_t P = ix->ncells, R = ix->degree, E = ix->cross_e, D = P * reserve;
+    for (uint32_t pos = 0; pos < ix->n; ++pos) {
+        const uint32_t g = g_of[pos], own = ix->cell_of[g];
+        for (uint32_t j = 0; j < P; ++j) {
+            const uint32_t base = seg[j], sz = seg[j + 1] - seg[j];
+            for (uint32_t e = 0; e < reserve; ++e) {
+                uint32_t loc = ORC_EMPTY;
+                if (j == own)
+                    loc = e < R ? ix->graphs[(size_t)pos * R + e] : ORC_EMPTY;
+                else
+                    loc = e < E ? ix->cross[(size_t)g * P * E + (size_t)j * E + e] : ORC_EMPTY;
+                out[(size_t)pos * D + (size_t)j * reserve + e] = loc < sz ? base + loc : ORC_EMPTY;
+            }
+        }
+    }
+    free(seg);
+    free(g_of);
+    free(p_of);
+}
+
+/*
+ * full_graph_search.cuh:179-593 (full_graph_search_postfiltering): beam search over the
+ * assembled graph `fg` (orc_assemble, `deg` entries per row) of the whole index, filtered
+ * by the box only at the end.  The entry set is entry_pos[0..n_entry) (positions); list T
+ * of L entries; each round expands the first `width` unexplored entries of T (width 1 in the
+ * reference, :394-418), evaluates their not-yet-seen neighbours, sorts and merges them into
+ * T (:421-511, no recycle list); the search stops when T has no unexplored entry or after
+ * max_iter rounds.  The in-range entries of T in list order give the K results (:579-592).
+ */
+void orc_search_fullgraph(const orc_index* ix, const orc_params* p, const uint32_t* fg, uint32_t deg,
+                          const float* queries, uint32_t dim, float alpha, const float* lb, const float* rb,
+                          uint32_t qnum, const uint32_t* entry_pos, uint32_t* ids_out, float* dist_out,
+                          uint64_t* stats, int threads) {
+    uint32_t *seg, *g_of, *p_of;
+    make_positions(ix, &seg, &g_of, &p_of);
+    uint64_t tot[4] = {0, 0, 0, 0};
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#endif
+#pragma omp parallel
+    {
+        uint64_t st[4] = {0, 0, 0, 0};
+        const uint32_t L = p->L, K = p->K, width = p->width ? p->width : 1;
+        uint32_t bcap = width * deg > p->n_entry ? width * deg : p->n_entry;
+        uint16_t* q16 = (uint16_t*)malloc(sizeof(uint16_t) * ix->d8);
+        float* qv = (float*)calloc(ix->d16 > dim ? ix->d16 : dim, sizeof(float));
+        ent* T = (ent*)malloc(sizeof(ent) * L);
+        ent* B = (ent*)malloc(sizeof(ent) * bcap);
+        ent* tmp = (ent*)malloc(sizeof(ent) * (L + bcap));
+        uint8_t* seen = (uint8_t*)calloc(ix->n ? ix->n : 1, 1);
+        uint32_t* touched = (uint32_t*)malloc(sizeof(uint32_t) * (L + bcap) * 64);
+#pragma omp for schedule(dynamic, 1)
+        for (long q = 0; q < (long)qnum; ++q) {
+            orc_f2h(queries + (size_t)q * dim, 1, dim, ix->d8, alpha, q16);
+            for (uint32_t i = 0; i < dim; ++i) qv[i] = queries[(size_t)q * dim + i] * alpha;
+            qctx c = {ix, seg, g_of, p_of, q16, qv, lb + q * ix->a, rb + q * ix->a, st};
+            uint32_t nt = 0, nbt = 0;
+            for (uint32_t i = 0; i < L; ++i) T[i] = (ent){INFINITY, ORC_EMPTY};
+            for (uint32_t i = 0; i < p->n_entry; ++i) {
+                const uint32_t pos = entry_pos[i];
+                if (pos >= ix->n || seen[pos]) continue;
+                seen[pos] = 1;
+                touched[nt++] = pos;
+                B[nbt++] = evaluate(&c, pos);
+            }
+            ent_sort(B, nbt);
+            merge_into(T, L, B, nbt, NULL, 0, tmp);
+            for (uint32_t it = 0; it < p->max_iter; ++it) {
+                uint32_t picked[64], np = 0;
+                for (uint32_t i = 0; i < L && np < width; ++i)
+                    if (T[i].w != ORC_EMPTY && !(T[i].w & ORC_EXPLORED)) {
+                        T[i].w |= ORC_EXPLORED;
+                        picked[np++] = T[i].w & ORC_POSMASK;
+                    }
+                if (np == 0) break;
+                st[1] += np;
+                nbt = 0;
+                for (uint32_t k = 0; k < np; ++k)
+                    for (uint32_t j = 0; j < deg; ++j) {
+                        const uint32_t pos = fg[(size_t)picked[k] * deg + j];
+                        if (pos == ORC_EMPTY || seen[pos]) continue;
+                        seen[pos] = 1;
+                        if (nt < (L + bcap) * 64) touched[nt++] = pos;
+                        B[nbt++] = evaluate(&c, pos);
+                    }
+                ent_sort(B, nbt);
+                merge_into(T, L, B, nbt, NULL, 0, tmp);
+            }
+            uint32_t o = 0;
+            for (uint32_t i = 0; i < L && o < K; ++i)
+                if (T[i].w != ORC_EMPTY && (T[i].w & ORC_INRANGE)) {
+                    ids_out[(size_t)q * K + o] = g_of[T[i].w & ORC_POSMASK];
+                    dist_out[(size_t)q * K + o] = T[i].d;
+                    ++o;
+                }
+            for (; o < K; ++o) {
+                ids_out[(size_t)q * K + o] = ORC_EMPTY;
+                dist_out[(size_t)q * K + o] = INFINITY;
+            }
+            if (nt < (L + bcap) * 64) {
+                for (uint32_t k = 0; k < nt; ++k) seen[touched[k]] = 0;
+            } else {
+                memset(seen, 0, ix->n);
+            }
+        }
+#pragma omp critical
+        for (int i = 0; i < 4; ++i) tot[i] += st[i];
+        free(q16);
+        free(qv);
+        free(T);
+        free(B);
+        free(tmp);
+        free(seen);
+        free(touched);
+    }
+    if (stats)
+        for (int i = 0; i < 4; ++i) stats[i] += tot[i];
+    free(seg);
+    free(g_of);
+    free(p_of);
 }
 
 /* Cell-major positions (tools.cuh:862-889 get_idx_mapper): seg[c] .. seg[c+1]-1 are the

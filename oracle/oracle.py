@@ -70,6 +70,9 @@ def lib() -> C.CDLL:
                                   P, P, P, P, C.c_int]
         _L.orc_search_batched.argtypes = [C.POINTER(OrcIndex), C.POINTER(OrcParams), P, U, C.c_float, P, P, U, P,
                                           P, P, P, P, P, U, P, P, P, C.c_int]
+        _L.orc_assemble.argtypes = [C.POINTER(OrcIndex), U, P]
+        _L.orc_search_fullgraph.argtypes = [C.POINTER(OrcIndex), C.POINTER(OrcParams), P, U, P, U, C.c_float, P, P,
+                                            U, P, P, P, P, C.c_int]
         _L.orc_recall.restype = C.c_double
         _L.orc_recall.argtypes = [P, U, P, U, U]
     return _L
@@ -266,6 +269,49 @@ def search(index_arrays, vectors, attrs, queries, lo, hi, counts, offsets, cells
         lib().orc_search_batched(C.byref(ix), C.byref(prm), _p(queries), dim, alpha, _p(lo), _p(hi), qn,
                                  _p(counts), _p(offsets), _p(cells), _p(box), _p(entry), _p(batch_of), len(batches),
                                  _p(ids), _p(dist), _p(stats), threads)
+    return ids, dist, stats
+
+
+def _orc_index(index_arrays, vectors, attrs, alpha):
+    vectors = _c(vectors, np.float32)
+    n, dim = vectors.shape
+    d8 = (dim + 7) // 8 * 8
+    keep = dict(vec16=f2h(vectors, d8, alpha), attrs=_c(attrs, np.float32),
+                cell_of=_c(index_arrays.cell_of, np.uint32), graphs=_c(index_arrays.graphs, np.uint32),
+                cross=_c(index_arrays.cross, np.uint32))
+    ix = OrcIndex(n, d8, keep["attrs"].shape[1], int(np.prod(index_arrays.grid)), index_arrays.degree,
+                  index_arrays.cross_e, _p(keep["vec16"]), _p(keep["attrs"]), _p(keep["cell_of"]),
+                  _p(keep["graphs"]), _p(keep["cross"]))
+    return ix, keep
+
+
+def assemble(index_arrays, reserve: int = 2):
+    """full_graph_search.cuh:984-997 (assemble_edges): the full-graph ablation's graph,
+    n x (cells * reserve) positions, rows in position order."""
+    n = len(index_arrays.cell_of)
+    zeros = np.zeros((n, 1), np.float32)
+    ix, keep = _orc_index(index_arrays, zeros, np.zeros((n, 1), np.float32), 1.0)
+    out = np.zeros((n, ix.ncells * reserve), np.uint32)
+    lib().orc_assemble(C.byref(ix), reserve, _p(out))
+    return out
+
+
+def search_fullgraph(index_arrays, vectors, attrs, queries, lo, hi, entry_pos, *, L, K, width=1, reserve=2,
+                     max_iter=10000, alpha=1.0, threads=0):
+    """full_graph_search_postfiltering (full_graph_search.cuh:179-593) over assemble()'s
+    graph of the whole index, box applied at the end; entry_pos are positions."""
+    ix, keep = _orc_index(index_arrays, vectors, attrs, alpha)
+    fg = assemble(index_arrays, reserve)
+    entry = _c(entry_pos, np.uint32)
+    prm = OrcParams(L, K, width, max_iter, 0xFFFFFFFF, 0.0, len(entry))
+    queries = _c(queries, np.float32)
+    lo, hi = _c(lo, np.float32), _c(hi, np.float32)
+    qn, dim = queries.shape
+    ids = np.zeros((qn, K), np.uint32)
+    dist = np.zeros((qn, K), np.float32)
+    stats = np.zeros(4, np.uint64)
+    lib().orc_search_fullgraph(C.byref(ix), C.byref(prm), _p(fg), fg.shape[1], _p(queries), dim, alpha, _p(lo),
+                               _p(hi), qn, _p(entry), _p(ids), _p(dist), _p(stats), threads)
     return ids, dist, stats
 
 

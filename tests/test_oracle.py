@@ -199,3 +199,25 @@ def test_nan_centroid_ranks_last():
     c3[1] = 0.0
     _, top4 = oracle.order_cells(q, c3, np.ones((1, 5), np.uint32), counts, offsets, cells)
     assert (top4 == np.array([1, 0, 2, 3], np.uint32)).all()
+
+
+def test_assemble_restates_assemble_edges():
+    """orc_assemble (full_graph_search.cuh:984-997) on a hand-checked slot layout: own cell's
+    first `reserve` graph neighbours in the own slot block, first `reserve` cross edges in the
+    others, all as positions."""
+    from conftest import Case
+    c = Case(3000, 16, 10, 4, (2, 2), 0.2, R=8, E=2, C=10, seed=5)
+    fg = oracle.assemble(c.ix, 2)
+    order = np.argsort(c.ix.cell_of, kind="stable")
+    seg = np.concatenate([[0], np.cumsum(np.bincount(c.ix.cell_of, minlength=4))])
+    for pos in (0, 5, 1500, 2999):
+        g = order[pos]
+        own = int(c.ix.cell_of[g])
+        for j in range(4):
+            for e in range(2):
+                v = fg[pos, j * 2 + e]
+                if j == own:
+                    loc = c.ix.graphs[pos, e]
+                else:
+                    loc = c.ix.cross[g, j * 2 + e]
+                assert v == seg[j] + loc
