@@ -21,7 +21,7 @@
 //     copies of the point chunks into a ring of shared-memory stages and the tcgen05.mma
 //     (kind::f16, M = N = 128, fp32 accumulation) of each tile into one of four TMEM
 //     accumulators; eight epilogue warps read the accumulators (tcgen05.ld, one query per
-//     TMEM lane, two warps per lane quarter splitting the columns) and form
+//     TMEM lane, two warps per lane quarter taking alternate tiles) and form
 //     a = px - 2 S; a thread keeps its query's 32 smallest a among in-box points (sorted, in
 //     shared memory) -- a point is tested against the box only when a is below the list's
 //     current 32nd value, which after the first few tiles is rare;
@@ -647,13 +647,14 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
+        // a tile is read by the four epilogue warps of its parity (one per TMEM lane quarter)
         for (uint32_t i = 0; i < kAcc; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], kEpiWarps);
+            mbar_init(&tempty[i], kEpiWarps / 2);
         }
         for (uint32_t i = 0; i < kMeta; ++i) {
             mbar_init(&mfull[i], 1);
-            mbar_init(&mempty[i], kEpiWarps);
+            mbar_init(&mempty[i], kEpiWarps / 2);
         }
         mbar_init(aload, 1);
         mbar_init(afree, 1);
@@ -794,6 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
         __syncwarp();
     } else {
         // -------------------------------------------------------------- epilogue warps
+        // warp: TMEM lane quarter qq (rows 32 qq ..), tiles of parity h
         const uint32_t ew = warp - 2, qq = warp & 3u, h = ew >> 2;
         const uint32_t row = qq * 32 + lane, owner = ew * 32 + lane;
         bool ok = true;
@@ -823,6 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             float thr = __int_as_float(0x7f800000);
             uint32_t pub = __ldcg(A.thr_g + r);
             for (; t < seg_end; ++t) {
+                if ((t & 1u) != h) continue;  // the other warp of this lane quarter takes this tile
                 const uint32_t b = t % kAcc, m = t % kMeta;
                 ok = bwait(&mfull[m], (t / kMeta) & 1u, stop) && bwait(&tfull[b], (t / kAcc) & 1u, stop);
                 if (!__all_sync(kFull, ok)) {
@@ -853,15 +856,16 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                         mine = mine & (tlo[j] <= bu) & (bl <= thi[j]);
                         inside = inside & (bl <= tlo[j]) & (thi[j] <= bu);
                     }
-                    const uint32_t taddr = tmem + ((qq * 32u) << 16) + b * kBN + h * 64;
+                    const uint32_t taddr = tmem + ((qq * 32u) << 16) + b * kBN;
                     uint32_t v[2][32];
                     __syncwarp();  // tcgen05.ld is warp-collective
                     tmem_ld32(taddr, v[0]);
                     tmem_wait_ld(v[0]);
 #pragma unroll
-                    for (uint32_t g = 0; g < 2; ++g) {
-                        const uint32_t col = h * 64 + g * 32;
-                        if (g == 0) tmem_ld32(taddr + 32, v[1]);  // overlaps the work on the first 32
+                    for (uint32_t g = 0; g < 4; ++g) {
+                        const uint32_t col = g * 32, cur = g & 1u;
+                        // the next 32 columns load while these are processed
+                        if (g + 1 < 4) tmem_ld32(taddr + col + 32, v[cur ^ 1u]);
                         uint32_t mask = 0;
                         float av[32];
                         if (mine) {
@@ -869,10 +873,10 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
 #pragma unroll
                             for (uint32_t j4 = 0; j4 < 8; ++j4) {
                                 const float4 p4 = pm[j4];
-                                av[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[g][4 * j4 + 0]), p4.x);
-                                av[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[g][4 * j4 + 1]), p4.y);
-                                av[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[g][4 * j4 + 2]), p4.z);
-                                av[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[g][4 * j4 + 3]), p4.w);
+                                av[4 * j4 + 0] = fmaf(-2.0f, __uint_as_float(v[cur][4 * j4 + 0]), p4.x);
+                                av[4 * j4 + 1] = fmaf(-2.0f, __uint_as_float(v[cur][4 * j4 + 1]), p4.y);
+                                av[4 * j4 + 2] = fmaf(-2.0f, __uint_as_float(v[cur][4 * j4 + 2]), p4.z);
+                                av[4 * j4 + 3] = fmaf(-2.0f, __uint_as_float(v[cur][4 * j4 + 3]), p4.w);
                             }
                             // points below the threshold (four independent partial masks)
                             uint32_t m4[4] = {0u, 0u, 0u, 0u};
@@ -912,9 +916,9 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                             }
                         }
                         if (thr < before) atomicMin(A.thr_g + r, f2ord(thr));
-                        if (g == 0) {
+                        if (g + 1 < 4) {
                             __syncwarp();
-                            tmem_wait_ld(v[1]);
+                            tmem_wait_ld(v[cur ^ 1u]);
                         }
                     }
                 }
@@ -925,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                     mbar_arrive(&mempty[m]);
                 }
             }
-            // this segment's list of row r (slot slot_id, column half h)
+            // this segment's list of row r (slot slot_id, tile parity h)
             heap_sort(n, owner, la, lp);
             if (slot_id < kSlots) {
                 const uint32_t l = slot_id * 2 + h;
