@@ -73,7 +73,8 @@ class _SearchParams(C.Structure):
 
 
 class _BfParams(C.Structure):
-    _fields_ = [("path", C.c_uint32), ("test_fallback_every", C.c_uint32), ("stats_out", C.c_void_p)]
+    _fields_ = [("path", C.c_uint32), ("test_fallback_every", C.c_uint32), ("test_wait", C.c_uint32),
+                ("stats_out", C.c_void_p)]
 
 
 class _SearchStats(C.Structure):
@@ -331,7 +332,7 @@ class Index:
         return ids, dist
 
     def bruteforce(self, queries, lb, rb, k: int, stream=None, path: int = 0, test_fallback_every: int = 0,
-                   stats=None):
+                   stats=None, test_wait: int = 0):
         """Exact filtered k-NN on the device; returns (ids, dists) CUDA tensors.
 
         path: 0 automatic (tensor cores when available), 1 CUDA cores, 2 tensor cores.
@@ -341,11 +342,11 @@ class Index:
         q = queries.shape[0]
         ids = torch.empty((q, k), dtype=torch.int32, device=queries.device)
         dist = torch.empty((q, k), dtype=torch.float32, device=queries.device)
-        if path == 0 and test_fallback_every == 0 and stats is None:
+        if path == 0 and test_fallback_every == 0 and stats is None and test_wait == 0:
             _check(lib().gf_bruteforce(self._h, _dev_ptr(queries), _dev_ptr(lb), _dev_ptr(rb), q, k,
                                        _dev_ptr(ids), _dev_ptr(dist), _stream_ptr(stream)), "gf_bruteforce")
         else:
-            prm = _BfParams(path, test_fallback_every, _dev_ptr(stats).value if stats is not None else None)
+            prm = _BfParams(path, test_fallback_every, test_wait, _dev_ptr(stats).value if stats is not None else None)
             _check(lib().gf_bruteforce_ex(self._h, _dev_ptr(queries), _dev_ptr(lb), _dev_ptr(rb), q, k,
                                           _dev_ptr(ids), _dev_ptr(dist), C.byref(prm), _stream_ptr(stream)),
                    "gf_bruteforce_ex")

@@ -120,9 +120,9 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t* v) {
                  : "memory");
 }
 
-// Bounded wait on a phase; false when it ran out or the CTA is stopping.
-__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t par, const volatile uint32_t* stop) {
-    for (uint32_t p = 0; p < kPolls; ++p) {
+// Bounded wait on a phase (at most `polls` polls); false when it ran out or the CTA is stopping.
+__device__ __forceinline__ bool bwait(uint64_t* bar, uint32_t par, const volatile uint32_t* stop, uint32_t polls) {
+    for (uint32_t p = 0; p < polls; ++p) {
         if (mbar_try_wait(bar, par, 1000)) return true;
         if (*stop) return false;
     }
@@ -496,6 +496,8 @@ struct TcArgs {
     uint32_t* cand_n;        // rows x kLists (0 = empty, kEmpty = list not valid)
     uint32_t* timeouts;
     uint32_t qtiles, tiles, a, a8, dp, nck, stages;
+    uint32_t polls;     // bound of every barrier wait
+    uint32_t extra_tx;  // test hook: bytes the query-tile load expects but never receives
 };
 
 // CTA c of G takes the tile products [W c / G, W (c + 1) / G) of the query-tile-major
@@ -688,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             return __shfl_sync(kFull, my_tile, t & 31u);
         };
         auto load_a = [&](uint32_t qt) {
-            mbar_arrive_expect_tx(aload, kBM * A.dp * 2);
+            mbar_arrive_expect_tx(aload, kBM * A.dp * 2 + A.extra_tx);
             for (uint32_t ch = 0; ch < A.nck; ++ch)
                 bulk_g2s(sm + Lo.a_off + ch * kChunkBytes, A.at + (size_t)qt * kBM * A.dp + (size_t)ch * (kBM * kKC),
                          chunk_bytes(ch), aload);
@@ -702,13 +704,13 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             while (A.pre[cq + 1] <= lo + t) ++cq;
             if (cq != qprev) {
                 // a new query tile: its rows replace A once the MMAs of the previous one are done
-                ok = __all_sync(kFull, bwait(afree, (na - 1) & 1u, stop));
+                ok = __all_sync(kFull, bwait(afree, (na - 1) & 1u, stop, A.polls));
                 if (!ok) break;
                 if (lane == 0) load_a(cq);
                 ++na;
             }
             const uint32_t m = t % kMeta;
-            if (t >= kMeta && !(ok = __all_sync(kFull, bwait(&mempty[m], ((t / kMeta) - 1) & 1u, stop)))) break;
+            if (t >= kMeta && !(ok = __all_sync(kFull, bwait(&mempty[m], ((t / kMeta) - 1) & 1u, stop, A.polls)))) break;
             if (lane == 0) {
                 fence_proxy_async_smem();  // the epilogue's reads of this slot come before the copy
                 unsigned char* slot = sm + Lo.meta_off + m * Lo.meta_bytes;
@@ -721,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             ++nm;
             for (uint32_t ch = 0; ch < A.nck; ++ch, ++i) {
                 const uint32_t st = i % A.stages;
-                if (i >= A.stages && !(ok = __all_sync(kFull, bwait(&empty[st], ((i / A.stages) - 1) & 1u, stop))))
+                if (i >= A.stages && !(ok = __all_sync(kFull, bwait(&empty[st], ((i / A.stages) - 1) & 1u, stop, A.polls))))
                     break;
                 if (lane == 0) {
                     const uint32_t bytes = chunk_bytes(ch);
@@ -738,17 +740,17 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             for (uint32_t st = 0; st < A.stages && st < i; ++st) {
                 const uint32_t last = st + ((i - 1 - st) / A.stages) * A.stages;
                 uint32_t p = 0;
-                while (!mbar_try_wait(&full[st], (last / A.stages) & 1u, 1000) && ++p < kPolls) {
+                while (!mbar_try_wait(&full[st], (last / A.stages) & 1u, 1000) && ++p < A.polls) {
                 }
             }
             for (uint32_t m = 0; m < kMeta && m < nm; ++m) {
                 const uint32_t last = m + ((nm - 1 - m) / kMeta) * kMeta;
                 uint32_t p = 0;
-                while (!mbar_try_wait(&mfull[m], (last / kMeta) & 1u, 1000) && ++p < kPolls) {
+                while (!mbar_try_wait(&mfull[m], (last / kMeta) & 1u, 1000) && ++p < A.polls) {
                 }
             }
             uint32_t p = 0;
-            while (!mbar_try_wait(aload, (na - 1) & 1u, 1000) && ++p < kPolls) {
+            while (!mbar_try_wait(aload, (na - 1) & 1u, 1000) && ++p < A.polls) {
             }
         }
         __syncwarp();
@@ -764,14 +766,14 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                 const uint32_t qprev = cq;
                 while (A.pre[cq + 1] <= lo + t) ++cq;
                 if (t == 0 || cq != qprev) {
-                    if (!(ok = bwait(aload, na & 1u, stop))) break;
+                    if (!(ok = bwait(aload, na & 1u, stop, A.polls))) break;
                     ++na;
                 }
-                if (t >= kAcc && !(ok = bwait(&tempty[b], ((t / kAcc) - 1) & 1u, stop))) break;
+                if (t >= kAcc && !(ok = bwait(&tempty[b], ((t / kAcc) - 1) & 1u, stop, A.polls))) break;
                 tc_fence_after();
                 for (uint32_t ch = 0; ch < A.nck; ++ch, ++i) {
                     const uint32_t st = i % A.stages;
-                    if (!(ok = bwait(&full[st], (i / A.stages) & 1u, stop))) break;
+                    if (!(ok = bwait(&full[st], (i / A.stages) & 1u, stop, A.polls))) break;
                     tc_fence_after();
                     const uint32_t ksteps = min(kKC, A.dp - ch * kKC) / 16;
                     const uint32_t a0 = smem_u32(sA + ch * kChunkBytes), b0 = smem_u32(sB + st * kChunkBytes);
@@ -788,9 +790,9 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             // every MMA has completed before TMEM is released
             mma_commit(drain);
             uint32_t p = 0;
-            while (!mbar_try_wait(drain, 0, 1000) && ++p < kPolls) {
+            while (!mbar_try_wait(drain, 0, 1000) && ++p < A.polls) {
             }
-            if (p >= kPolls) *stop = 1u;
+            if (p >= A.polls) *stop = 1u;
         }
         __syncwarp();
     } else {
@@ -827,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             for (; t < seg_end; ++t) {
                 if ((t & 1u) != h) continue;  // the other warp of this lane quarter takes this tile
                 const uint32_t b = t % kAcc, m = t % kMeta;
-                ok = bwait(&mfull[m], (t / kMeta) & 1u, stop) && bwait(&tfull[b], (t / kAcc) & 1u, stop);
+                ok = bwait(&mfull[m], (t / kMeta) & 1u, stop, A.polls) && bwait(&tfull[b], (t / kAcc) & 1u, stop, A.polls);
                 if (!__all_sync(kFull, ok)) {
                     ok = false;
                     break;
@@ -1229,7 +1231,7 @@ size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum) {
 
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
                     uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
-                    uint32_t* timeouts, uint32_t* products, cudaStream_t s) {
+                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s) {
     DeviceIndex& d = idx->d;
     const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM;
     const uint32_t dp = d.bf_dp, nck = (dp + kKC - 1) / kKC, a = d.a;
@@ -1294,6 +1296,8 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     T.sched = sched;
     T.row_fb = row_fb;
     T.qtiles = qtiles;
+    T.polls = test_wait ? test_wait : kPolls;
+    T.extra_tx = test_wait ? 16u : 0u;
     T.cand = cand;
     T.cand_n = cand_n;
     T.timeouts = timeouts;

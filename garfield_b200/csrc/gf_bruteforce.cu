@@ -191,8 +191,8 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     cudaError_t e = cudaMemsetAsync(w, 0, 3 * sizeof(uint32_t), s);
     if (e != cudaSuccess) st = cuda_fail(e, "brute-force counters");
     if (st == GF_OK)
-        st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, d.bf_ws, w + 3, w, P.test_fallback_every, w + 1, w + 2,
-                       s);
+        st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, d.bf_ws, w + 3, w, P.test_fallback_every, P.test_wait,
+                       w + 1, w + 2, s);
     if (st == GF_OK) {
         bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k,
                                                   ids, dist, w + 3, w);

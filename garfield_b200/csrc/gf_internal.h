@@ -203,7 +203,7 @@ bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
 size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum);  // working memory of bf_tc_run
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
                     uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
-                    uint32_t* timeouts, uint32_t* products, cudaStream_t s);
+                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s);
 // gf_index.cu: greedy spokesman assignment (compress_global_graph_extreme, tools.cuh:917-935);
 // graphs: n x degree local ids, rows in position (cell) order
 void spokesman_assign(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,

@@ -323,6 +323,11 @@ typedef struct {
     uint32_t test_fallback_every; /* 0 in normal use.  Test hook: queries whose index is a
                             multiple of this value skip the tensor-core proof and are answered
                             by the CUDA-core kernel, as unproven queries are */
+    uint32_t test_wait;  /* 0 in normal use.  Test hook for the timeout path: every barrier wait
+                            of the tensor-core pass gives up after test_wait polls and each query
+                            tile's load expects 16 bytes more than it copies, so every CTA stops;
+                            stats_out[1] counts them and all queries are answered by the CUDA-core
+                            kernel (the results stay exact) */
     uint32_t* stats_out; /* optional device array of 3 words, written on the stream: queries
                             answered by the CUDA-core kernel after the tensor-core pass,
                             tensor-core waits that ran out (their queries are among the former),

@@ -137,3 +137,19 @@ def test_tc_calls_on_two_streams_share_the_working_memory():
     for got, ref in ((r1, ref1), (r2, ref2)):
         assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
     g.close()
+
+
+def test_tc_wait_timeout_is_reported_and_answered_exactly():
+    """Test hook: every tensor-core wait gives up after a few thousand polls and the query-tile
+    loads never complete, so every CTA stops; the stops are counted and all queries are answered
+    by the CUDA-core kernel, exactly.  The next call on the same context is normal."""
+    ds = synth.make(20000, 64, 40, 300, (2, 2), 0.15, seed=17, stratified=False)
+    g = bf_index(ds.vectors, ds.attrs, (2, 2))
+    ref_ids, ref_d = oracle.bruteforce(ds.vectors, ds.attrs, ds.queries, ds.lo, ds.hi, 10)
+    ids, dist, st = run(g, ds.queries, ds.lo, ds.hi, 10, path=2, test_wait=4096)
+    assert st[1] > 0 and st[0] == ds.queries.shape[0], st
+    assert np.array_equal(ids, ref_ids) and np.array_equal(dist, ref_d)
+    ids, dist, st = run(g, ds.queries, ds.lo, ds.hi, 10, path=2)
+    assert st[1] == 0 and st[0] <= ds.queries.shape[0] // 4, st
+    assert np.array_equal(ids, ref_ids) and np.array_equal(dist, ref_d)
+    g.close()
