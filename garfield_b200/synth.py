@@ -96,10 +96,13 @@ class Dataset:
 
 def make(n: int, dim: int, n_centers: int, qnum: int, grid: tuple[int, ...], selectivity: float,
          domain: int = 10000, sigma: float = 20.0, seed: int = DEFAULT_SEED, stratified: bool = True,
-         normalize: bool = False, center_hi: float = 255.0) -> Dataset:
+         normalize: bool = False, center_hi: float = 255.0, sphere: bool = False) -> Dataset:
     rv = np.random.default_rng(seed)
-    vectors, centers, labels = gaussian_mixture(n, dim, n_centers, sigma, rv, hi=center_hi,
-                                                clip_min=None if normalize else 0.0, normalize=normalize)
+    if sphere:
+        vectors, centers, labels = sphere_mixture(n, dim, n_centers, sigma, rv)
+    else:
+        vectors, centers, labels = gaussian_mixture(n, dim, n_centers, sigma, rv, hi=center_hi,
+                                                    clip_min=None if normalize else 0.0, normalize=normalize)
     ra = np.random.default_rng(seed + 1)
     if stratified:
         attrs, cell_of = stratified_uniform_attrs(n, grid, domain, ra)
@@ -115,8 +118,53 @@ def make(n: int, dim: int, n_centers: int, qnum: int, grid: tuple[int, ...], sel
                         sigma=sigma, seed=seed))
 
 
-# Benchmark configurations; configs 3-5 follow
-# the same generators with their own shapes.
+def sphere_mixture(n: int, dim: int, n_centers: int, sigma: float, rng: np.random.Generator,
+                   centers: np.ndarray | None = None, chunk: int = 1 << 18):
+    """Unit-normalised mixture: centers are N(0, 1)^dim directions scaled to norm 1, a point
+    is its center plus N(0, sigma^2) noise per coordinate, normalised to norm 1 afterwards."""
+    if centers is None:
+        centers = rng.standard_normal((n_centers, dim), dtype=np.float32)
+        centers /= np.maximum(np.linalg.norm(centers, axis=1, keepdims=True), 1e-12)
+    return gaussian_mixture(n, dim, centers.shape[0], sigma, rng, centers=centers, clip_min=None,
+                            normalize=True, chunk=chunk)
+
+
+def zipf_attr(n: int, domain: int, s: float, rng: np.random.Generator) -> np.ndarray:
+    """Bounded Zipf on [0, domain): P(v) proportional to (v + 1)^-s, by inverse CDF."""
+    w = np.arange(1, domain + 1, dtype=np.float64) ** -s
+    cdf = np.cumsum(w)
+    cdf /= cdf[-1]
+    v = np.searchsorted(cdf, rng.random(n), side="right")
+    return np.minimum(v, domain - 1).astype(np.int32)
+
+
+def cluster_attr(labels: np.ndarray, n_centers: int, domain: int, rng: np.random.Generator) -> np.ndarray:
+    """An attribute correlated with the mixture component: a uniform integer inside the
+    component's own band [label, label + 1) * domain / n_centers."""
+    u = rng.random(labels.shape[0])
+    return np.minimum(np.floor((labels + u) * (domain / n_centers)), domain - 1).astype(np.int32)
+
+
+def quantile_boxes(attrs: np.ndarray, qnum: int, selectivity: float, rng: np.random.Generator):
+    """Closed boxes drawn in rank space: in every dimension the side spans
+    selectivity^(1/a) of the points (by rank), placed uniformly; bounds are the attribute
+    values at the two end ranks.  On skewed attributes (Zipf) ties widen a side, so the
+    selectivity is approximate."""
+    n, a = attrs.shape
+    side = max(1, min(n, int(round(n * selectivity ** (1.0 / a)))))
+    lo = np.empty((qnum, a), np.int32)
+    hi = np.empty((qnum, a), np.int32)
+    for j in range(a):
+        srt = np.sort(attrs[:, j])
+        st = rng.integers(0, n - side + 1, size=qnum)
+        lo[:, j] = srt[st]
+        hi[:, j] = srt[st + side - 1]
+    return lo, hi
+
+
+# Benchmark configurations (BASELINE.json configs[0] .. configs[4]).  Configs 3-5 take the
+# point count, query count and center count as arguments so that tests can draw the same
+# distributions at a size the oracle finishes in seconds.
 def config1(seed: int = DEFAULT_SEED, n: int = 100_000, qnum: int = 1000) -> Dataset:
     """100k x 128, 100-center mixture, 2 uniform attributes, 1000 queries, ~10% boxes."""
     return make(n, 128, 100, qnum, (4, 4), 0.10, seed=seed, stratified=False)
@@ -125,3 +173,43 @@ def config1(seed: int = DEFAULT_SEED, n: int = 100_000, qnum: int = 1000) -> Dat
 def config2(seed: int = DEFAULT_SEED, selectivity: float = 0.10, n: int = 1_000_000, qnum: int = 10_000) -> Dataset:
     """1M x 128, 1000-center mixture, 2 attributes on a 4x4 grid, 10k queries."""
     return make(n, 128, 1000, qnum, (4, 4), selectivity, seed=seed, stratified=True)
+
+
+def config3(seed: int = DEFAULT_SEED, n: int = 10_000_000, qnum: int = 100_000, n_centers: int = 10_000,
+            selectivity: float = 0.05) -> Dataset:
+    """10M x 96 unit-normalised mixture (sigma 0.1 per coordinate before normalisation);
+    attributes U[0, 10000), Zipf(1.1) on [0, 10000) and the component's band; 4x4x4 grid;
+    100k queries from the mixture with rank-space 3-D boxes of ~5% selectivity."""
+    domain = 10000
+    rv = np.random.default_rng(seed)
+    vectors, centers, labels = sphere_mixture(n, 96, n_centers, 0.1, rv)
+    ra = np.random.default_rng(seed + 1)
+    attrs = np.stack([ra.integers(0, domain, size=n, dtype=np.int64).astype(np.int32),
+                      zipf_attr(n, domain, 1.1, ra), cluster_attr(labels, n_centers, domain, ra)], 1)
+    rq = np.random.default_rng(seed + 2)
+    queries, _, _ = sphere_mixture(qnum, 96, n_centers, 0.1, rq, centers=centers)
+    lo, hi = quantile_boxes(attrs, qnum, selectivity, np.random.default_rng(seed + 3))
+    return Dataset(vectors, attrs, queries, lo, hi, (4, 4, 4), None,
+                   dict(n=n, dim=96, n_centers=n_centers, qnum=qnum, selectivity=selectivity, domain=domain,
+                        sigma=0.1, seed=seed, k=100, R=32, E=0))
+
+
+def config4(seed: int = DEFAULT_SEED, n: int = 1_000_000, qnum: int = 10_000, n_centers: int = 2000,
+            selectivity: float = 0.02, sigma: float = 0.02) -> Dataset:
+    """1M x 768 unit-normalised embedding-like mixture (sigma 0.02 per coordinate: noise of
+    norm ~0.55 around unit centers); 2 attributes U[0, 2^20) on an 8x8 grid; 10k queries
+    with ~2% boxes."""
+    return make(n, 768, n_centers, qnum, (8, 8), selectivity, domain=1 << 20, sigma=sigma, seed=seed,
+                stratified=False, normalize=True, sphere=True)
+
+
+def config5(seed: int = DEFAULT_SEED, n: int = 1_000_000_000, qnum: int = 100_000, n_centers: int = 100_000,
+            selectivity: float = 0.01):
+    """1B x 128 uint8 (the config-1 mixture rounded and clipped to [0, 255]); 2 attributes
+    U[0, 10000) on a 16x16 grid; 100k queries with ~1% boxes.  Returns the Dataset (fp32
+    vectors) and the uint8 rows."""
+    ds = make(n, 128, n_centers, qnum, (16, 16), selectivity, seed=seed, stratified=True)
+    codes = np.clip(np.rint(ds.vectors), 0, 255).astype(np.uint8)
+    ds.vectors = codes.astype(np.float32)
+    ds.meta.update(k=10, R=32, E=2)
+    return ds, codes

@@ -36,12 +36,16 @@ def pytest_collection_modifyitems(config, items):
 class Case:
     """A small synthetic dataset with its index (reference layout) and oracle plan."""
 
-    def __init__(self, n, dim, centers, qnum, grid, sel, R, E, C, seed, sigma=20.0, stratified=True, domain=10000):
+    def __init__(self, n, dim, centers, qnum, grid, sel, R, E, C, seed, sigma=20.0, stratified=True, domain=10000,
+                 ds=None, k=10, device="cpu"):
         from garfield_b200 import indexbuild, synth
         import oracle
-        self.ds = synth.make(n, dim, centers, qnum, grid, sel, domain=domain, sigma=sigma, seed=seed,
-                             stratified=stratified)
-        self.ix = indexbuild.build(self.ds.vectors, self.ds.attrs, grid, R=R, E=E, C=C, seed=seed, device="cpu")
+        if ds is None:
+            ds = synth.make(n, dim, centers, qnum, grid, sel, domain=domain, sigma=sigma, seed=seed,
+                            stratified=stratified)
+        self.ds = ds
+        grid = tuple(ds.grid)
+        self.ix = indexbuild.build(self.ds.vectors, self.ds.attrs, grid, R=R, E=E, C=C, seed=seed, device=device)
         self.grid = grid
         self.ncells = int(np.prod(grid))
         self.counts, self.offsets, self.cells_unordered = oracle.plan_cells(self.ds.lo, self.ds.hi, self.ix.grid,
@@ -49,8 +53,9 @@ class Case:
         self.centroids, self.hist = oracle.cluster_info(self.ds.vectors, self.ix.labels, self.ix.cell_of, self.ncells)
         self.cells, self.top4 = oracle.order_cells(self.ds.queries, self.centroids, self.hist, self.counts,
                                                    self.offsets, self.cells_unordered)
+        self.k = k
         self.gt, self.gt_d = oracle.bruteforce(self.ds.vectors, self.ds.attrs, self.ds.queries, self.ds.lo,
-                                               self.ds.hi, 10)
+                                               self.ds.hi, k)
 
     def entry(self, n):
         """The library's entry sequence: std::mt19937 default seed, draw % range, distinct."""
