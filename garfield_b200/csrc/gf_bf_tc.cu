@@ -66,7 +66,8 @@ constexpr uint32_t kAcc = 4;           // TMEM accumulators of kBN columns
 constexpr uint32_t kMeta = 8;          // tile metadata slots (copies run up to kMeta tiles ahead)
 constexpr uint32_t kSlots = 16;        // CTAs that may share one query tile (2 lists each)
 constexpr uint32_t kLists = 2 * kSlots; // lists per query, merged by one warp
-constexpr uint32_t kMaxDp = 256;
+constexpr uint32_t kMaxDp = 1024;
+constexpr uint32_t kResidentDp = 256;  // query tiles up to this width stay in shared memory
 constexpr uint32_t kMaxK = 16;
 constexpr uint32_t kPolls = 1u << 20;
 constexpr uint32_t kSmemLimit = 227 * 1024;
@@ -496,6 +497,7 @@ struct TcArgs {
     uint32_t* cand_n;        // rows x kLists (0 = empty, kEmpty = list not valid)
     uint32_t* timeouts;
     uint32_t qtiles, tiles, a, a8, dp, nck, stages;
+    uint32_t stream_a;  // 1: the query tile's chunks are copied into every stage beside the point chunk
     uint32_t polls;     // bound of every barrier wait
     uint32_t extra_tx;  // test hook: bytes the query-tile load expects but never receives
 };
@@ -539,17 +541,22 @@ __host__ __device__ inline uint32_t tbox_stride(uint32_t a) { return (a + 3) / 4
 // Shared-memory layout of bf_tc_kernel (byte offsets from a 1024-aligned base).  A meta slot
 // holds a tile's px (128 floats), its rows' positions (128), its points' attributes (128 x a
 // floats) and the tile's attribute bounds (2 x a8 floats).
+// With stream_a (rows wider than kResidentDp) there is no resident query tile: a stage holds
+// the query tile's chunk (first kChunkBytes) and the point tile's chunk of the same K range.
 struct TcLayout {
-    uint32_t a_off, b_off, meta_off, meta_bytes, la_off, lp_off, box_off, bar_off, total;
+    uint32_t a_off, b_off, stage_bytes, meta_off, meta_bytes, la_off, lp_off, box_off, bar_off, total;
 };
-__host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint32_t a) {
+__host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint32_t a, uint32_t stream_a) {
     TcLayout L;
     uint32_t o = 0;
     L.a_off = o;
-    o += kBM * dp * 2;
-    o = (o + 1023u) & ~1023u;
+    if (!stream_a) {
+        o += kBM * dp * 2;
+        o = (o + 1023u) & ~1023u;
+    }
     L.b_off = o;
-    o += stages * kChunkBytes;
+    L.stage_bytes = stream_a ? 2 * kChunkBytes : kChunkBytes;
+    o += stages * L.stage_bytes;
     L.meta_off = o;
     L.meta_bytes = kBN * 4 * (2 + a) + 8 * tbox_stride(a);
     o += kMeta * L.meta_bytes;
@@ -602,7 +609,7 @@ template <int NA>
 __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constant__ TcArgs A) {
     extern __shared__ unsigned char bf_smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(bf_smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a);
+    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a, A.stream_a);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lo.bar_off);
     uint64_t* full = bars;
     uint64_t* empty = full + A.stages;
@@ -697,12 +704,12 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
         };
         bool ok = true;
         uint32_t cq = qt0, na = 1, i = 0, nm = 0;  // A loads, chunks and metadata slots issued
-        if (lane == 0) load_a(qt0);
+        if (lane == 0 && !A.stream_a) load_a(qt0);
         for (uint32_t t = 0; ok && t < T; ++t) {
             const uint32_t tile = tile_of(t);
             const uint32_t qprev = cq;
             while (A.pre[cq + 1] <= lo + t) ++cq;
-            if (cq != qprev) {
+            if (cq != qprev && !A.stream_a) {
                 // a new query tile: its rows replace A once the MMAs of the previous one are done
                 ok = __all_sync(kFull, bwait(afree, (na - 1) & 1u, stop, A.polls));
                 if (!ok) break;
@@ -727,9 +734,15 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                     break;
                 if (lane == 0) {
                     const uint32_t bytes = chunk_bytes(ch);
-                    mbar_arrive_expect_tx(&full[st], bytes);
-                    bulk_g2s(sm + Lo.b_off + st * kChunkBytes, A.xt + tile * tile_halves + (size_t)ch * (kBN * kKC),
-                             bytes, &full[st]);
+                    unsigned char* stg = sm + Lo.b_off + st * Lo.stage_bytes;
+                    if (A.stream_a) {
+                        mbar_arrive_expect_tx(&full[st], 2 * bytes + A.extra_tx);
+                        bulk_g2s(stg, A.at + (size_t)cq * kBM * A.dp + (size_t)ch * (kBM * kKC), bytes, &full[st]);
+                        stg += kChunkBytes;
+                    } else {
+                        mbar_arrive_expect_tx(&full[st], bytes);
+                    }
+                    bulk_g2s(stg, A.xt + tile * tile_halves + (size_t)ch * (kBN * kKC), bytes, &full[st]);
                 }
             }
         }
@@ -750,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                 }
             }
             uint32_t p = 0;
-            while (!mbar_try_wait(aload, (na - 1) & 1u, 1000) && ++p < A.polls) {
+            while (!A.stream_a && !mbar_try_wait(aload, (na - 1) & 1u, 1000) && ++p < A.polls) {
             }
         }
         __syncwarp();
@@ -765,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                 const uint32_t b = t % kAcc;
                 const uint32_t qprev = cq;
                 while (A.pre[cq + 1] <= lo + t) ++cq;
-                if (t == 0 || cq != qprev) {
+                if (!A.stream_a && (t == 0 || cq != qprev)) {
                     if (!(ok = bwait(aload, na & 1u, stop, A.polls))) break;
                     ++na;
                 }
@@ -776,7 +789,9 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                     if (!(ok = bwait(&full[st], (i / A.stages) & 1u, stop, A.polls))) break;
                     tc_fence_after();
                     const uint32_t ksteps = min(kKC, A.dp - ch * kKC) / 16;
-                    const uint32_t a0 = smem_u32(sA + ch * kChunkBytes), b0 = smem_u32(sB + st * kChunkBytes);
+                    const uint32_t sst = smem_u32(sB + st * Lo.stage_bytes);
+                    const uint32_t a0 = A.stream_a ? sst : smem_u32(sA + ch * kChunkBytes);
+                    const uint32_t b0 = A.stream_a ? sst + kChunkBytes : sst;
                     for (uint32_t s = 0; s < ksteps; ++s)
                         mma_f16(tmem + b * kBN, kmajor_desc(a0 + s * 2 * kColBytes, kColBytes, 128),
                                 kmajor_desc(b0 + s * 2 * kColBytes, kColBytes, 128), (ch | s) ? 1u : 0u);
@@ -784,7 +799,8 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                 }
                 if (!ok) break;
                 mma_commit(&tfull[b]);
-                if (t + 1 == T || A.pre[cq + 1] <= lo + t + 1) mma_commit(afree);  // last tile of this query tile
+                if (!A.stream_a && (t + 1 == T || A.pre[cq + 1] <= lo + t + 1))
+                    mma_commit(afree);  // last tile of this query tile
             }
             if (!ok) *stop = 1u;
             // every MMA has completed before TMEM is released
@@ -1240,9 +1256,10 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     const uint32_t grid = (uint32_t)std::max(1, nsm);  // persistent: one CTA per SM
 
     // stages of the point-chunk ring: as many as fit (at least 2)
+    const uint32_t stream = dp > kResidentDp ? 1u : 0u;
     uint32_t stages = 8;
-    while (stages > 2 && tc_layout(dp, stages, a).total > kSmemLimit) --stages;
-    const TcLayout Lo = tc_layout(dp, stages, a);
+    while (stages > 2 && tc_layout(dp, stages, a, stream).total > kSmemLimit) --stages;
+    const TcLayout Lo = tc_layout(dp, stages, a, stream);
     if (Lo.total > kSmemLimit) return fail(GF_ERR_ARG, "tensor-core brute force: shared memory");
 
     size_t tmp_sort = sort_tmp_bytes(qnum);
@@ -1306,6 +1323,7 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     T.dp = dp;
     T.nck = nck;
     T.stages = stages;
+    T.stream_a = stream;
     void (*kern)(TcArgs) = a == 1 ? bf_tc_kernel<1> : a == 2 ? bf_tc_kernel<2> : a == 3 ? bf_tc_kernel<3>
                          : a == 4 ? bf_tc_kernel<4> : bf_tc_kernel<0>;
     ck(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Lo.total), "bf smem");

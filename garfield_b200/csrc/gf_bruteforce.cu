@@ -154,7 +154,7 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     if (P.path > 2) return fail(GF_ERR_ARG, "path must be 0, 1 or 2");
     const bool tc = P.path != 1 && bf_tc_usable(d, k);
     if (P.path == 2 && !tc)
-        return fail(GF_ERR_ARG, "tensor-core brute force needs keep_fp32, dim <= 256, finite rows and k <= 16");
+        return fail(GF_ERR_ARG, "tensor-core brute force needs keep_fp32, dim <= 1024, finite rows and k <= 16");
     if (P.stats_out) GF_CUDA(cudaMemsetAsync(P.stats_out, 0, 3 * sizeof(uint32_t), s));
     if (qnum == 0) return GF_OK;
     if (!queries || !lb || !rb || !ids) return fail(GF_ERR_ARG, "null argument");

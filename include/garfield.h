@@ -318,7 +318,7 @@ gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, co
 /* Options of gf_bruteforce_ex (all zero = gf_bruteforce's behaviour). */
 typedef struct {
     uint32_t path;       /* 0 = automatic: the tensor-core pass when the index has its fp16 tiles
-                            (keep_fp32, dim <= 256, finite rows) and k <= 16, else CUDA cores;
+                            (keep_fp32, dim <= 1024, finite rows) and k <= 16, else CUDA cores;
                             1 = CUDA cores only; 2 = tensor cores (GF_ERR_ARG when unavailable) */
     uint32_t test_fallback_every; /* 0 in normal use.  Test hook: queries whose index is a
                             multiple of this value skip the tensor-core proof and are answered

@@ -48,11 +48,22 @@ def check(ds, g, k, path=2, max_fallback_frac=0.25, **kw):
 
 
 @pytest.mark.parametrize("dim,grid,k", [(128, (4, 4), 10), (128, (4, 4), 1), (128, (4, 4), 16), (100, (2, 2, 2), 10),
-                                        (256, (3, 2), 5), (16, (4,), 10)])
+                                        (256, (3, 2), 5), (16, (4,), 10), (384, (4, 4), 10), (1000, (2, 2), 7),
+                                        (1024, (2, 2), 16)])
 def test_tc_matches_oracle(dim, grid, k):
     ds = synth.make(30000, dim, 60, 700, grid, 0.1, seed=101 + dim + k, stratified=False)
     g = bf_index(ds.vectors, ds.attrs, grid)
     check(ds, g, k)
+    g.close()
+
+
+def test_tc_wide_unit_norm_rows():
+    """768-dim unit-normalised rows on an 8x8 grid (the shape of configuration 4): query
+    chunks are streamed beside the point chunks instead of staying in shared memory."""
+    ds = synth.config4(seed=43, n=30000, qnum=700, n_centers=40)
+    g = bf_index(ds.vectors, ds.attrs, ds.grid)
+    st = check(ds, g, 10, max_fallback_frac=0.05)
+    assert st[2] > 0
     g.close()
 
 
