@@ -163,7 +163,7 @@ def cpu_baseline(ds, sample: int, threads: int) -> dict:
     oracle.bruteforce(ds.vectors, ds.attrs, q, ds.lo[:sample], ds.hi[:sample], 10, threads)
     dt = time.perf_counter() - t0
     return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} config-2 queries, exact filtered scan over all {ds.vectors.shape[0]} points "
+            "sample": f"{sample} queries, exact filtered scan over all {ds.vectors.shape[0]} points "
                       f"({dt:.1f}s)"}
 
 
@@ -448,7 +448,12 @@ def run_bruteforce(args):
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    if args.config == 4:
+        ds = synth.config4(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+        shape = f"{args.n // 10**6}M x 768 unit-norm, 2 attrs on 8x8, {args.sel:.0%} sel., k=10"
+    else:
+        ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+        shape = f"{args.n // 10**6}M x 128, 2 attrs, {args.sel:.0%} sel., k=10"
     lq, rq, _, cell_of = indexbuild.quantile_grid(ds.attrs, ds.grid)
     n, D = ds.vectors.shape
     index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=np.asarray(ds.grid, np.uint32),
@@ -508,12 +513,13 @@ def run_bruteforce(args):
     flops = 2.0 * products * 128 * 128 * dp
     achieved = flops / (t_ms / 1e3) / 1e12
     peak, peak_kind = peak_tensor()
-    out = {"metric": "exact filtered k-NN queries/s (1M x 128, 2 attrs, 10% sel., k=10)",
+    out = {"metric": f"exact filtered k-NN queries/s ({shape})",
            "value": round(qnum / (t_ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f16 products, f32 accumulate, f32 exact re-rank",
-           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
-           "config": {"workload": "config2 brute force: 1M x 128 fp32, 10k queries, sel 10%, k=10",
+           "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
+           "config": {"workload": f"config{args.config} brute force: {n} x {D} fp32, {qnum} queries, "
+                                  f"sel {args.sel:.0%}, k=10",
                       "l2": "flushed (256 MiB write) between timed steps",
                       "cuda_core_ms_per_step": round(c_ms, 3), "speedup_vs_cuda_cores": round(c_ms / t_ms, 2),
                       "identical_to_cuda_cores": same, "fallback_queries": int(st[0]), "timeouts": int(st[1]),
@@ -754,7 +760,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
-    ap.add_argument("--sel", type=float, default=0.10)
+    ap.add_argument("--sel", type=float, default=None)  # default: 0.10 (config 2), 0.02 (config 4)
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4])  # data shape of --mode bruteforce
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
     ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4, 8
@@ -777,6 +784,10 @@ def main():
     ap.add_argument("--cross-spokesman", dest="cross_spokesman", action="store_true",
                     help="keep the cross-cell edges of spokesmen only (row f2 of the scope table)")
     args = ap.parse_args()
+    if args.sel is None:
+        args.sel = 0.02 if args.config == 4 else 0.10
+    if args.config != 2 and args.mode != "bruteforce":
+        ap.error("--config 4 applies to --mode bruteforce")
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
     elif args.impl == "ours" and args.mode == "sharded":
