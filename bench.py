@@ -41,6 +41,10 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# data shape of each --config (config 3 runs at --n points)
+SHAPES = {2: "1M x 128, 2 attrs, 10% sel.", 3: "config-3 shape: 96-dim unit-norm, 3 attrs (uniform, Zipf, component), "
+          "5% sel.", 4: "1M x 768 unit-norm, 2 attrs on 8x8, 2% sel."}
+
 # the reference's ef sweep (realdataset_search.cu:2757-2760), ascending, L >= k
 L_SWEEP = [10, 15, 20, 25, 30, 35, 40, 45, 50, 55, 60, 70, 80, 90, 100, 120, 140, 160, 180, 200, 250, 300, 400,
            500, 600, 700, 800, 900, 1000, 1100, 1400, 1700]
@@ -121,13 +125,20 @@ def peak_hbm() -> tuple[float, str]:
 # --------------------------------------------------------------------------- data
 
 def dataset_and_index(args, device):
-    """Config-2 synthetic dataset and its index (cached per process tree under --cache)."""
+    """Synthetic dataset of --config's shape and its index (cached per process tree under
+    --cache).  Config 3 keeps its ratio of 1000 points per mixture component at any --n."""
     import torch
     from garfield_b200 import indexbuild, synth
     t0 = time.time()
-    ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    if args.config == 3:
+        ds = synth.config3(seed=args.seed, n=args.n, qnum=args.qnum, n_centers=max(10, args.n // 1000),
+                           selectivity=args.sel)
+    elif args.config == 4:
+        ds = synth.config4(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    else:
+        ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
     log(f"dataset {ds.vectors.shape} in {time.time() - t0:.1f}s")
-    key = f"cfg2_n{args.n}_s{args.seed}_R{args.R}_E{args.E}_C{args.C}.npz"
+    key = f"cfg{args.config}_n{args.n}_s{args.seed}_R{args.R}_E{args.E}_C{args.C}.npz"
     cache = Path(args.cache) / key if args.cache else None
     if cache is not None and cache.exists():
         z = np.load(cache)
@@ -153,14 +164,14 @@ def dataset_and_index(args, device):
     return ds, ix
 
 
-def cpu_baseline(ds, sample: int, threads: int) -> dict:
+def cpu_baseline(ds, sample: int, threads: int, k: int = 10) -> dict:
     """The oracle's exact filtered scan (naive_brute_force_with_filter restated) on host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     q = ds.queries[:sample]
-    oracle.bruteforce(ds.vectors, ds.attrs, q[:4], ds.lo[:4], ds.hi[:4], 10, threads)  # warm
+    oracle.bruteforce(ds.vectors, ds.attrs, q[:4], ds.lo[:4], ds.hi[:4], k, threads)  # warm
     t0 = time.perf_counter()
-    oracle.bruteforce(ds.vectors, ds.attrs, q, ds.lo[:sample], ds.hi[:sample], 10, threads)
+    oracle.bruteforce(ds.vectors, ds.attrs, q, ds.lo[:sample], ds.hi[:sample], k, threads)
     dt = time.perf_counter() - t0
     return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
             "sample": f"{sample} queries, exact filtered scan over all {ds.vectors.shape[0]} points "
@@ -197,28 +208,29 @@ def run_ours(args):
     # ground truth on a sample (exact, GPU brute force)
     S = min(args.gt_sample, qnum)
     t0 = time.time()
-    gt_ids, _ = index.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), 10)
+    K = args.k
+    gt_ids, _ = index.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), K)
     gt = gt_ids.cpu().numpy().view(np.uint32)
     log(f"ground truth for {S} queries in {time.time() - t0:.1f}s")
     stream = torch.cuda.Stream(device)
     plan = index.plan(qnum)
-    ids = torch.empty((qnum, 10), dtype=torch.int32, device=device)
-    dist_t = torch.empty((qnum, 10), dtype=torch.float32, device=device)
+    ids = torch.empty((qnum, K), dtype=torch.int32, device=device)
+    dist_t = torch.empty((qnum, K), dtype=torch.float32, device=device)
 
     def step(L, width):
         plan.build(qd, lod, hid, 0.0, stream)
-        plan.search(gf.SearchParams(L=L, k=10, width=width), stream, ids=ids, dist=dist_t)
+        plan.search(gf.SearchParams(L=L, k=K, width=width), stream, ids=ids, dist=dist_t)
 
     def find_L(width):
         """Smallest L of the sweep whose recall reaches the target at this width."""
         sweep = []
-        for L in ([args.L] if args.L else L_SWEEP):
+        for L in ([args.L] if args.L else [x for x in L_SWEEP if x >= K]):
             with torch.cuda.stream(stream):
                 step(L, width)
             stream.synchronize()
             r = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)
             sweep.append((L, round(r, 4)))
-            log(f"width={width} L={L} recall@10={r:.4f}")
+            log(f"width={width} L={L} recall@{K}={r:.4f}")
             if r >= args.target:
                 return L, r, sweep
         return sweep[-1][0], sweep[-1][1], sweep
@@ -262,7 +274,7 @@ def run_ours(args):
                 ev[i][0].record(stream)
                 plan.build(qd, lod, hid, 0.0, stream)
                 ev[i][1].record(stream)
-                plan.search(gf.SearchParams(L=L, k=10, width=args.width), stream, ids=ids, dist=dist_t)
+                plan.search(gf.SearchParams(L=L, k=K, width=args.width), stream, ids=ids, dist=dist_t)
                 ev[i][2].record(stream)
         stream.synchronize()
     torch.cuda.synchronize()
@@ -282,7 +294,7 @@ def run_ours(args):
     lh = torch.from_numpy(ds.lo.astype(np.float32)).pin_memory().numpy()
     hh = torch.from_numpy(ds.hi.astype(np.float32)).pin_memory().numpy()
     e2e_plan = index.plan(qnum)
-    params = gf.SearchParams(L=L, k=10, width=args.width)
+    params = gf.SearchParams(L=L, k=K, width=args.width)
     for _ in range(args.warmup):
         index.search_host(qh, lh, hh, e2e_plan, params, stream=stream)
     e_ms = []
@@ -310,20 +322,22 @@ def run_ours(args):
     achieved = bytes_step / kern_s / 1e9
     peak, peak_kind = peak_hbm()
     out = {
-        "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
+        "metric": f"QPS at recall@{K}>={args.target} ({SHAPES[args.config]})",
         "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
-        "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
-        "config": {"workload": "config2: 1M x 128 fp32, 4x4 grid, R=32, E=2, C=1000, 10k queries, sel 10%, k=10",
-                   "L": L, "width": args.width, "recall_at_10": round(recall, 4), "recall_sample": S,
+        "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
+        "config": {"workload": (f"config{args.config}: {ds.vectors.shape[0]} x {D} fp32, grid "
+                                f"{'x'.join(str(int(g)) for g in ix.grid)}, R={ix.degree}, E={ix.cross_e}, C={args.C}, "
+                                f"{qnum} queries, sel {args.sel:.0%}, k={K}"),
+                   "L": L, "width": args.width, f"recall_at_{K}": round(recall, 4), "recall_sample": S,
                    "l2": "flushed (256 MiB write) between timed steps", "parallelism": f"replicas x{world}",
                    "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
                    "sweep": sweep,
                    "cross_edges": (f"spokesman rows only: {index.cross_rows} of {index.n} (compress_global_graph_extreme)"
                                    if args.cross_spokesman else "full")},
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
-                "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * 10 * 4)},
+                "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * K * 4)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
                      "kernel": "gmg_search_kernel", "peak_kind": peak_kind,
@@ -335,7 +349,7 @@ def run_ours(args):
         "gpu_launches": 8 * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1)
+        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1, K)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -761,13 +775,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--sel", type=float, default=None)  # default: 0.10 (config 2), 0.02 (config 4)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4])  # data shape of --mode bruteforce
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])  # data shape (in-memory, bruteforce)
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
     ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4, 8
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--qnum", type=int, default=10_000)
-    ap.add_argument("--R", type=int, default=32)
+    ap.add_argument("--R", type=int, default=None)  # default: 32, 64 for config 4
     ap.add_argument("--E", type=int, default=2)
     ap.add_argument("--C", type=int, default=1000)
     ap.add_argument("--seed", type=int, default=20261201)
@@ -785,9 +799,12 @@ def main():
                     help="keep the cross-cell edges of spokesmen only (row f2 of the scope table)")
     args = ap.parse_args()
     if args.sel is None:
-        args.sel = 0.02 if args.config == 4 else 0.10
-    if args.config != 2 and args.mode != "bruteforce":
-        ap.error("--config 4 applies to --mode bruteforce")
+        args.sel = {2: 0.10, 3: 0.05, 4: 0.02}[args.config]
+    args.k = 100 if args.config == 3 else 10
+    if args.R is None:
+        args.R = 64 if args.config == 4 else 32
+    if args.config != 2 and args.mode not in ("in-memory", "bruteforce") or args.config == 3 and args.mode != "in-memory":
+        ap.error("--config 3 applies to the in-memory mode, --config 4 to in-memory and bruteforce")
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
     elif args.impl == "ours" and args.mode == "sharded":
