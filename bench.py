@@ -217,9 +217,12 @@ def run_ours(args):
     ids = torch.empty((qnum, K), dtype=torch.int32, device=device)
     dist_t = torch.empty((qnum, K), dtype=torch.float32, device=device)
 
+    def sp(L, width):
+        return gf.SearchParams(L=L, k=K, width=width, exact_tc=args.exact_tc)
+
     def step(L, width):
-        plan.build(qd, lod, hid, 0.0, stream)
-        plan.search(gf.SearchParams(L=L, k=K, width=width), stream, ids=ids, dist=dist_t)
+        plan.build(qd, lod, hid, args.prefilter, stream)
+        plan.search(sp(L, width), stream, ids=ids, dist=dist_t)
 
     def find_L(width):
         """Smallest L of the sweep whose recall reaches the target at this width."""
@@ -272,9 +275,9 @@ def run_ours(args):
             with torch.cuda.stream(stream):
                 flush.fill_(float(i))
                 ev[i][0].record(stream)
-                plan.build(qd, lod, hid, 0.0, stream)
+                plan.build(qd, lod, hid, args.prefilter, stream)
                 ev[i][1].record(stream)
-                plan.search(gf.SearchParams(L=L, k=K, width=args.width), stream, ids=ids, dist=dist_t)
+                plan.search(sp(L, args.width), stream, ids=ids, dist=dist_t)
                 ev[i][2].record(stream)
         stream.synchronize()
     torch.cuda.synchronize()
@@ -294,16 +297,16 @@ def run_ours(args):
     lh = torch.from_numpy(ds.lo.astype(np.float32)).pin_memory().numpy()
     hh = torch.from_numpy(ds.hi.astype(np.float32)).pin_memory().numpy()
     e2e_plan = index.plan(qnum)
-    params = gf.SearchParams(L=L, k=K, width=args.width)
+    params = sp(L, args.width)
     for _ in range(args.warmup):
-        index.search_host(qh, lh, hh, e2e_plan, params, stream=stream)
+        index.search_host(qh, lh, hh, e2e_plan, params, prefilter=args.prefilter, stream=stream)
     e_ms = []
     for i in range(args.steps):
         with torch.cuda.stream(stream):
             flush.fill_(float(i))
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        res_ids, _ = index.search_host(qh, lh, hh, e2e_plan, params, stream=stream)
+        res_ids, _ = index.search_host(qh, lh, hh, e2e_plan, params, prefilter=args.prefilter, stream=stream)
         b.record(stream)
         b.synchronize()
         e_ms.append(a.elapsed_time(b))
@@ -333,6 +336,8 @@ def run_ours(args):
                    "L": L, "width": args.width, f"recall_at_{K}": round(recall, 4), "recall_sample": S,
                    "l2": "flushed (256 MiB write) between timed steps", "parallelism": f"replicas x{world}",
                    "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
+                   "prefilter": args.prefilter, "exact_route": ("tensor-core exact scan" if args.exact_tc
+                                                                else "fp16 warp scan"), "n_exact": int(st["n_exact"]),
                    "sweep": sweep,
                    "cross_edges": (f"spokesman rows only: {index.cross_rows} of {index.n} (compress_global_graph_extreme)"
                                    if args.cross_spokesman else "full")},
@@ -462,7 +467,12 @@ def run_bruteforce(args):
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if args.config == 4:
+    K = args.k
+    if args.config == 3:
+        ds = synth.config3(seed=args.seed, n=args.n, qnum=args.qnum, n_centers=max(10, args.n // 1000),
+                           selectivity=args.sel)
+        shape = f"{args.n // 10**6}M x 96 unit-norm, 3 attrs on 4x4x4, {args.sel:.0%} sel., k=100"
+    elif args.config == 4:
         ds = synth.config4(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
         shape = f"{args.n // 10**6}M x 768 unit-norm, 2 attrs on 8x8, {args.sel:.0%} sel., k=10"
     else:
@@ -483,7 +493,7 @@ def run_bruteforce(args):
 
     def timed(path, steps, warmup):
         for _ in range(warmup):
-            index.bruteforce(qd, lod, hid, 10, stream=stream, path=path, stats=stats)
+            index.bruteforce(qd, lod, hid, K, stream=stream, path=path, stats=stats)
         stream.synchronize()
         ms = []
         with ClockSampler(local) as clocks:
@@ -492,7 +502,7 @@ def run_bruteforce(args):
                     flush.fill_(float(i))
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                ids, dist = index.bruteforce(qd, lod, hid, 10, stream=stream, path=path, stats=stats)
+                ids, dist = index.bruteforce(qd, lod, hid, K, stream=stream, path=path, stats=stats)
                 b.record(stream)
                 b.synchronize()
                 ms.append(a.elapsed_time(b))
@@ -505,7 +515,7 @@ def run_bruteforce(args):
     qh, lh, hh = (torch.from_numpy(x).pin_memory() for x in (ds.queries, ds.lo.astype(np.float32),
                                                               ds.hi.astype(np.float32)))
     qg, lg, hg = torch.empty_like(qd), torch.empty_like(lod), torch.empty_like(hid)
-    ih = torch.empty((qnum, 10), dtype=torch.int32).pin_memory()
+    ih = torch.empty((qnum, K), dtype=torch.int32).pin_memory()
     e_ms = []
     for i in range(max(args.warmup, 1) + args.steps):
         with torch.cuda.stream(stream):
@@ -515,7 +525,7 @@ def run_bruteforce(args):
             qg.copy_(qh, non_blocking=True)
             lg.copy_(lh, non_blocking=True)
             hg.copy_(hh, non_blocking=True)
-            ids, _ = index.bruteforce(qg, lg, hg, 10, stream=stream)
+            ids, _ = index.bruteforce(qg, lg, hg, K, stream=stream)
             ih.copy_(ids, non_blocking=True)
             b.record(stream)
         b.synchronize()
@@ -533,7 +543,7 @@ def run_bruteforce(args):
            "vs_baseline": None, "dtype": "f16 products, f32 accumulate, f32 exact re-rank",
            "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
            "config": {"workload": f"config{args.config} brute force: {n} x {D} fp32, {qnum} queries, "
-                                  f"sel {args.sel:.0%}, k=10",
+                                  f"sel {args.sel:.0%}, k={K}",
                       "l2": "flushed (256 MiB write) between timed steps",
                       "cuda_core_ms_per_step": round(c_ms, 3), "speedup_vs_cuda_cores": round(c_ms / t_ms, 2),
                       "identical_to_cuda_cores": same, "fallback_queries": int(st[0]), "timeouts": int(st[1]),
@@ -547,7 +557,7 @@ def run_bruteforce(args):
            # morton, 3 radix-sort passes are CUB's; prep, boxes, tiles, tc, merge, CUDA-core list
            "gpu_launches": 6 * args.steps}
     if not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1)
+        out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1, K)
     print(json.dumps(out), flush=True)
 
 
@@ -776,6 +786,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--sel", type=float, default=None)  # default: 0.10 (config 2), 0.02 (config 4)
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])  # data shape (in-memory, bruteforce)
+    ap.add_argument("--prefilter", type=float, default=0.0)  # --prefilter: box share at or below -> exact route
+    ap.add_argument("--exact-tc", dest="exact_tc", type=int, default=0)  # exact route on the tensor cores
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
     ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4, 8
@@ -803,8 +815,8 @@ def main():
     args.k = 100 if args.config == 3 else 10
     if args.R is None:
         args.R = 64 if args.config == 4 else 32
-    if args.config != 2 and args.mode not in ("in-memory", "bruteforce") or args.config == 3 and args.mode != "in-memory":
-        ap.error("--config 3 applies to the in-memory mode, --config 4 to in-memory and bruteforce")
+    if args.config != 2 and args.mode not in ("in-memory", "bruteforce"):
+        ap.error("--config 3 and 4 apply to the in-memory and bruteforce modes")
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
     elif args.impl == "ours" and args.mode == "sharded":

@@ -88,6 +88,7 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
     if (d.sharded) return fail(GF_ERR_STATE, "gf_search_batched on a shard: search it with gf_search_keys");
     if (d.spk_rank) return fail(GF_ERR_STATE, "gf_search_batched on spokesman-compressed cross edges: use gf_search");
     gf_search_params P;
+    if (prm && prm->exact_tc) return fail(GF_ERR_ARG, "exact_tc applies to gf_search and gf_search_host");
     gf_search_defaults(&P);
     if (prm) P = *prm;
     if (P.k == 0 || P.k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");

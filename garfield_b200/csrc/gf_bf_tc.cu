@@ -22,10 +22,11 @@
 //     (kind::f16, M = N = 128, fp32 accumulation) of each tile into one of four TMEM
 //     accumulators; eight epilogue warps read the accumulators (tcgen05.ld, one query per
 //     TMEM lane, two warps per lane quarter taking alternate tiles) and form
-//     a = px - 2 S; a thread keeps its query's 32 smallest a among in-box points (sorted, in
-//     shared memory) -- a point is tested against the box only when a is below the list's
-//     current 32nd value, which after the first few tiles is rare;
-//  5. bf_merge_kernel (a warp per query): merges the lists, re-ranks the 32 smallest a with
+//     a = px - 2 S; a thread keeps its query's KM smallest a among in-box points (a heap in
+//     shared memory; KM = 32 for k <= 16, 128 with one warp per lane quarter for k <= 128)
+//     -- a point is tested against the box only when a is below the list's current KM-th
+//     value, which after the first few tiles is rare;
+//  5. bf_merge_kernel (a warp per query): merges the lists, re-ranks the KM smallest a with
 //     the canonical fp32 distance (dist32, oracle orc_dist32) and proves the result: every
 //     point left out has a >= a*, hence a canonical distance >= LB(a*) (the error bound
 //     below); when LB(a*) is not above the k-th re-ranked distance, or the query could not
@@ -58,17 +59,26 @@ constexpr uint32_t kBN = 128;          // points per tile (accumulator columns)
 constexpr uint32_t kKC = 64;           // elements per K chunk (8 core-matrix columns)
 constexpr uint32_t kChunkBytes = kBN * kKC * 2;  // 16 KB
 constexpr uint32_t kColBytes = kBN * 16;         // one 16-byte core-matrix column of 128 rows
-constexpr uint32_t kM = 32;            // candidates kept per list
-constexpr uint32_t kEpiWarps = 8;
-constexpr uint32_t kOwners = kEpiWarps * 32;
-constexpr uint32_t kThreads = 64 + kOwners;  // producer warp, MMA warp, epilogue warps
 constexpr uint32_t kAcc = 4;           // TMEM accumulators of kBN columns
 constexpr uint32_t kMeta = 8;          // tile metadata slots (copies run up to kMeta tiles ahead)
-constexpr uint32_t kSlots = 16;        // CTAs that may share one query tile (2 lists each)
-constexpr uint32_t kLists = 2 * kSlots; // lists per query, merged by one warp
+constexpr uint32_t kSlots = 16;        // CTAs that may share one query tile
+// Candidate lists of one query row.  Shallow (k <= 16): 32 entries; two epilogue warps per
+// TMEM lane quarter take alternate tiles (8 epilogue warps, 2 lists per query and CTA).
+// Deep (16 < k <= 128): 128 entries; one warp per lane quarter takes every tile (4 epilogue
+// warps, 1 list per query and CTA), so that the lists still fit in shared memory.
+template <bool DEEP>
+struct Lists {
+    static constexpr uint32_t KM = DEEP ? 128 : 32;   // candidates kept per list
+    static constexpr uint32_t NPAR = DEEP ? 1 : 2;    // tile parities
+    static constexpr uint32_t EW = 4 * NPAR;          // epilogue warps
+    static constexpr uint32_t OWN = 32 * EW;          // list owners (epilogue threads)
+    static constexpr uint32_t THREADS = 64 + OWN;     // producer warp, MMA warp, epilogue warps
+    static constexpr uint32_t LISTS = kSlots * NPAR;  // lists per query, merged by one warp
+};
+constexpr uint32_t kMaxKShallow = 16;
 constexpr uint32_t kMaxDp = 1024;
 constexpr uint32_t kResidentDp = 256;  // query tiles up to this width stay in shared memory
-constexpr uint32_t kMaxK = 16;
+constexpr uint32_t kMaxK = 128;
 constexpr uint32_t kPolls = 1u << 20;
 constexpr uint32_t kSmemLimit = 227 * 1024;
 
@@ -256,8 +266,8 @@ __global__ void bf_convert_kernel(const float* __restrict__ x, uint32_t n, uint3
 // empty tile gets lo > hi; unused entries lo = -inf, hi = +inf), and the tile-padded attribute
 // copy (NaN past n, so no padding point is ever inside a box).
 __global__ void bf_tilebox_kernel(const float* __restrict__ attrs, uint32_t n, uint32_t a, uint32_t a8,
-                                  uint32_t tiles, const uint32_t* __restrict__ order, float* __restrict__ tbox,
-                                  float* __restrict__ pattrs, uint32_t* __restrict__ rowpos) {
+                                  uint32_t tiles, const uint32_t* order, float* __restrict__ tbox,
+                                  float* __restrict__ pattrs, uint32_t* rowpos) {  // order may alias rowpos
     const uint32_t lane = lane_id();
     const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= tiles) return;
@@ -291,28 +301,32 @@ __global__ void bf_tilebox_kernel(const float* __restrict__ attrs, uint32_t n, u
 // ------------------------------------------------------------------ per-call kernels
 
 // Morton code of the box centre (the points' code of the same attribute space).
+// Queries left out by the mask get the largest key: they sort behind every other query, so
+// the trailing query tiles hold only them and meet no point tile.
 __global__ void bf_morton_kernel(const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum, uint32_t a,
                                  const float* __restrict__ alo, const float* __restrict__ ainv,
-                                 unsigned long long* keys, uint32_t* vals) {
+                                 const uint32_t* __restrict__ qmask, unsigned long long* keys, uint32_t* vals) {
     const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
     if (q >= qnum) return;
     float c[kMaxAttr];
     for (uint32_t j = 0; j < a; ++j) c[j] = 0.5f * (lb[(size_t)q * a + j] + rb[(size_t)q * a + j]);
-    keys[q] = attr_morton(c, a, alo, ainv);
+    keys[q] = (qmask && !qmask[q]) ? ~0ull : attr_morton(c, a, alo, ainv);
     vals[q] = q;
 }
 
 // One warp per sorted row r < qpad: the tiled fp16 query, pq, delta_q and the routing flag
 // (1 = no query, 2 = the query cannot be handled on the tensor cores).
 __global__ void bf_prep_kernel(const float* __restrict__ queries, uint32_t qnum, uint32_t dim, uint32_t dp,
-                               const uint32_t* __restrict__ sorted, uint32_t qpad, const float* __restrict__ m, float s,
+                               const uint32_t* __restrict__ sorted, const uint32_t* __restrict__ qmask, uint32_t qpad,
+                               const float* __restrict__ m, float s,
                                double one_minus_kappa, uint32_t* __restrict__ perm, __half* __restrict__ at,
                                float* __restrict__ pq, float* __restrict__ dq, uint32_t* __restrict__ flag,
                                uint32_t* __restrict__ thr_g) {
     const uint32_t lane = lane_id();
     const uint32_t r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= qpad) return;
-    const uint32_t q = r < qnum ? sorted[r] : kEmpty;
+    uint32_t q = r < qnum ? sorted[r] : kEmpty;
+    if (q != kEmpty && qmask && !qmask[q]) q = kEmpty;  // left out: a row without a query
     __half* tile = at + (size_t)(r / kBM) * kBM * dp;
     const uint32_t row = r % kBM;
     double nq = 0.0, d2 = 0.0;
@@ -420,25 +434,27 @@ __global__ void bf_tiles_kernel(const float* __restrict__ tbox, uint32_t a8, uin
     }
 }
 
-// Per-thread candidate list: a max-heap of up to kM (a, position) entries in shared memory
-// (entry i of owner o at i * kOwners + o), so that an insertion costs at most log2(kM) steps
-// whatever its rank -- the same for every lane of a warp.  heap_push: n < kM entries; the
+// Per-thread candidate list: a max-heap of up to KM (a, position) entries in shared memory
+// (entry i of owner o at i * OWN + o), so that an insertion costs at most log2(KM) steps
+// whatever its rank -- the same for every lane of a warp.  heap_push: n < KM entries; the
 // entry sifts up.  heap_replace: a full heap whose root (its largest a) is above aj; the root
 // is replaced and sifts down.
+template <uint32_t OWN>
 __device__ __forceinline__ void heap_push(float aj, uint32_t pos, uint32_t n, uint32_t owner, float* la, uint32_t* lp) {
     uint32_t i = n;
 #pragma unroll 1
     while (i > 0) {
         const uint32_t p = (i - 1) >> 1;
-        const float ap = la[p * kOwners + owner];
+        const float ap = la[p * OWN + owner];
         if (!(ap < aj)) break;
-        la[i * kOwners + owner] = ap;
-        lp[i * kOwners + owner] = lp[p * kOwners + owner];
+        la[i * OWN + owner] = ap;
+        lp[i * OWN + owner] = lp[p * OWN + owner];
         i = p;
     }
-    la[i * kOwners + owner] = aj;
-    lp[i * kOwners + owner] = pos;
+    la[i * OWN + owner] = aj;
+    lp[i * OWN + owner] = pos;
 }
+template <uint32_t OWN>
 __device__ __forceinline__ void heap_sift_down(float aj, uint32_t pos, uint32_t n, uint32_t owner, float* la,
                                                uint32_t* lp) {
     uint32_t i = 0;
@@ -446,32 +462,33 @@ __device__ __forceinline__ void heap_sift_down(float aj, uint32_t pos, uint32_t 
     for (;;) {
         uint32_t c = 2 * i + 1;
         if (c >= n) break;
-        float ac = la[c * kOwners + owner];
+        float ac = la[c * OWN + owner];
         if (c + 1 < n) {
-            const float a2 = la[(c + 1) * kOwners + owner];
+            const float a2 = la[(c + 1) * OWN + owner];
             if (a2 > ac) {
                 ac = a2;
                 ++c;
             }
         }
         if (!(ac > aj)) break;
-        la[i * kOwners + owner] = ac;
-        lp[i * kOwners + owner] = lp[c * kOwners + owner];
+        la[i * OWN + owner] = ac;
+        lp[i * OWN + owner] = lp[c * OWN + owner];
         i = c;
     }
-    la[i * kOwners + owner] = aj;
-    lp[i * kOwners + owner] = pos;
+    la[i * OWN + owner] = aj;
+    lp[i * OWN + owner] = pos;
 }
 // Heap of n entries -> ascending order in place (heapsort).
+template <uint32_t OWN>
 __device__ __noinline__ void heap_sort(uint32_t n, uint32_t owner, float* la, uint32_t* lp) {
     for (uint32_t end = n; end > 1; --end) {
-        const float top = la[0 * kOwners + owner];
-        const uint32_t tp = lp[0 * kOwners + owner];
-        const float x = la[(end - 1) * kOwners + owner];
-        const uint32_t xp = lp[(end - 1) * kOwners + owner];
-        heap_sift_down(x, xp, end - 1, owner, la, lp);
-        la[(end - 1) * kOwners + owner] = top;
-        lp[(end - 1) * kOwners + owner] = tp;
+        const float top = la[0 * OWN + owner];
+        const uint32_t tp = lp[0 * OWN + owner];
+        const float x = la[(end - 1) * OWN + owner];
+        const uint32_t xp = lp[(end - 1) * OWN + owner];
+        heap_sift_down<OWN>(x, xp, end - 1, owner, la, lp);
+        la[(end - 1) * OWN + owner] = top;
+        lp[(end - 1) * OWN + owner] = tp;
     }
 }
 
@@ -493,8 +510,8 @@ struct TcArgs {
     const uint32_t* sched;   // [0] total tile products W, [1] CTAs that take work G
     uint32_t* thr_g;         // per sorted row: smallest published list threshold (ordered bits)
     uint32_t* row_fb;        // per sorted row: 1 = answer on the CUDA cores
-    uint2* cand;             // rows x kLists x kM (a bits, position)
-    uint32_t* cand_n;        // rows x kLists (0 = empty, kEmpty = list not valid)
+    uint2* cand;             // rows x LISTS x KM (a bits, position)
+    uint32_t* cand_n;        // rows x LISTS (0 = empty, kEmpty = list not valid)
     uint32_t* timeouts;
     uint32_t qtiles, tiles, a, a8, dp, nck, stages;
     uint32_t stream_a;  // 1: the query tile's chunks are copied into every stage beside the point chunk
@@ -546,7 +563,8 @@ __host__ __device__ inline uint32_t tbox_stride(uint32_t a) { return (a + 3) / 4
 struct TcLayout {
     uint32_t a_off, b_off, stage_bytes, meta_off, meta_bytes, la_off, lp_off, box_off, bar_off, total;
 };
-__host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint32_t a, uint32_t stream_a) {
+__host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint32_t a, uint32_t stream_a, uint32_t km,
+                                              uint32_t own) {
     TcLayout L;
     uint32_t o = 0;
     L.a_off = o;
@@ -561,11 +579,11 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint
     L.meta_bytes = kBN * 4 * (2 + a) + 8 * tbox_stride(a);
     o += kMeta * L.meta_bytes;
     L.la_off = o;
-    o += kM * kOwners * 4;
+    o += km * own * 4;
     L.lp_off = o;
-    o += kM * kOwners * 4;
+    o += km * own * 4;
     L.box_off = o;
-    o += 2 * a * kOwners * 4;
+    o += 2 * a * own * 4;
     L.bar_off = o;
     o += (2 * stages + 2 * kAcc + 2 * kMeta + 3) * 8 + 16;
     L.total = o + 1024;  // room to align the base
@@ -574,21 +592,21 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint
 
 // The owner's box: NA attributes in registers (NA = 0: a attributes read from shared memory).
 // Tests combine with & (no short-circuit branches).
-template <int NA>
+template <int NA, uint32_t OWN>
 struct OwnBox {
     float lo[NA > 0 ? NA : 1], hi[NA > 0 ? NA : 1];
     __device__ __forceinline__ void load(const float* blo, const float* bhi, uint32_t owner) {
 #pragma unroll
         for (int e = 0; e < NA; ++e) {
-            lo[e] = blo[e * kOwners + owner];
-            hi[e] = bhi[e * kOwners + owner];
+            lo[e] = blo[e * OWN + owner];
+            hi[e] = bhi[e * OWN + owner];
         }
     }
     __device__ __forceinline__ float l(uint32_t e, const float* blo, uint32_t owner) const {
-        return NA > 0 ? lo[e] : blo[e * kOwners + owner];
+        return NA > 0 ? lo[e] : blo[e * OWN + owner];
     }
     __device__ __forceinline__ float u(uint32_t e, const float* bhi, uint32_t owner) const {
-        return NA > 0 ? hi[e] : bhi[e * kOwners + owner];
+        return NA > 0 ? hi[e] : bhi[e * OWN + owner];
     }
     // point attributes pa[0..a) inside the box
     __device__ __forceinline__ bool has(const float* pa, uint32_t a, const float* blo, const float* bhi,
@@ -599,17 +617,18 @@ struct OwnBox {
             for (int e = 0; e < NA; ++e) in = in & (pa[e] >= lo[e]) & (pa[e] <= hi[e]);
         } else {
             for (uint32_t e = 0; e < a; ++e)
-                in = in & (pa[e] >= blo[e * kOwners + owner]) & (pa[e] <= bhi[e * kOwners + owner]);
+                in = in & (pa[e] >= blo[e * OWN + owner]) & (pa[e] <= bhi[e * OWN + owner]);
         }
         return in;
     }
 };
 
-template <int NA>
-__global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constant__ TcArgs A) {
+template <int NA, bool DEEP>
+__global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __grid_constant__ TcArgs A) {
+    using C = Lists<DEEP>;
     extern __shared__ unsigned char bf_smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(bf_smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a, A.stream_a);
+    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a, A.stream_a, C::KM, C::OWN);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lo.bar_off);
     uint64_t* full = bars;
     uint64_t* empty = full + A.stages;
@@ -625,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
     float* la = reinterpret_cast<float*>(sm + Lo.la_off);
     uint32_t* lp = reinterpret_cast<uint32_t*>(sm + Lo.lp_off);
     float* blo = reinterpret_cast<float*>(sm + Lo.box_off);
-    float* bhi = blo + A.a * kOwners;
+    float* bhi = blo + A.a * C::OWN;
     const uint32_t a = NA > 0 ? (uint32_t)NA : A.a;
 
     const uint32_t warp = threadIdx.x >> 5, lane = lane_id();
@@ -659,11 +678,11 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
         // a tile is read by the four epilogue warps of its parity (one per TMEM lane quarter)
         for (uint32_t i = 0; i < kAcc; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], kEpiWarps / 2);
+            mbar_init(&tempty[i], 4);
         }
         for (uint32_t i = 0; i < kMeta; ++i) {
             mbar_init(&mfull[i], 1);
-            mbar_init(&mempty[i], kEpiWarps / 2);
+            mbar_init(&mempty[i], 4);
         }
         mbar_init(aload, 1);
         mbar_init(afree, 1);
@@ -828,10 +847,10 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             bool valid = A.flag[r] == 0;  // a query handled here with a box that is not empty
             for (uint32_t j = 0; valid && j < a; ++j) valid = A.lb[(size_t)q * a + j] <= A.rb[(size_t)q * a + j];
             for (uint32_t j = 0; j < a; ++j) {
-                blo[j * kOwners + owner] = valid ? A.lb[(size_t)q * a + j] : __int_as_float(0x7f800000);
-                bhi[j * kOwners + owner] = valid ? A.rb[(size_t)q * a + j] : -__int_as_float(0x7f800000);
+                blo[j * C::OWN + owner] = valid ? A.lb[(size_t)q * a + j] : __int_as_float(0x7f800000);
+                bhi[j * C::OWN + owner] = valid ? A.rb[(size_t)q * a + j] : -__int_as_float(0x7f800000);
             }
-            OwnBox<NA> box;
+            OwnBox<NA, C::OWN> box;
             box.load(blo, bhi, owner);
             float glo[kMaxAttr], ghi[kMaxAttr];  // union box of this warp's 32 rows (warp-uniform)
 #pragma unroll
@@ -843,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
             float thr = __int_as_float(0x7f800000);
             uint32_t pub = __ldcg(A.thr_g + r);
             for (; t < seg_end; ++t) {
-                if ((t & 1u) != h) continue;  // the other warp of this lane quarter takes this tile
+                if (C::NPAR == 2 && (t & 1u) != h) continue;  // the other warp of this lane quarter takes it
                 const uint32_t b = t % kAcc, m = t % kMeta;
                 ok = bwait(&mfull[m], (t / kMeta) & 1u, stop, A.polls) && bwait(&tfull[b], (t / kAcc) & 1u, stop, A.polls);
                 if (!__all_sync(kFull, ok)) {
@@ -851,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                     break;
                 }
                 // a tighter threshold published by another list of this query (any full list's
-                // largest entry bounds the query's 32 smallest); the next one is fetched now
+                // largest entry bounds the query's KM smallest); the next one is fetched now
                 thr = fminf(thr, ord2f(pub));
                 pub = __ldcg(A.thr_g + r);
                 tc_fence_after();
@@ -923,11 +942,11 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                                 for (uint32_t jj = 1; jj < 32; ++jj) aj = j == jj ? av[jj] : aj;
                                 if (aj < thr) {
                                     const uint32_t pos = mpos[col + j];
-                                    if (n < kM) {
-                                        heap_push(aj, pos, n, owner, la, lp);
-                                        if (++n == kM) thr = fminf(thr, la[owner]);
+                                    if (n < C::KM) {
+                                        heap_push<C::OWN>(aj, pos, n, owner, la, lp);
+                                        if (++n == C::KM) thr = fminf(thr, la[owner]);
                                     } else {
-                                        heap_sift_down(aj, pos, kM, owner, la, lp);
+                                        heap_sift_down<C::OWN>(aj, pos, C::KM, owner, la, lp);
                                         thr = fminf(thr, la[owner]);
                                     }
                                 }
@@ -948,13 +967,13 @@ __global__ void __launch_bounds__(kThreads, 1) bf_tc_kernel(const __grid_constan
                 }
             }
             // this segment's list of row r (slot slot_id, tile parity h)
-            heap_sort(n, owner, la, lp);
+            heap_sort<C::OWN>(n, owner, la, lp);
             if (slot_id < kSlots) {
-                const uint32_t l = slot_id * 2 + h;
-                uint2* out = A.cand + ((size_t)r * kLists + l) * kM;
+                const uint32_t l = slot_id * C::NPAR + h;
+                uint2* out = A.cand + ((size_t)r * C::LISTS + l) * C::KM;
                 for (uint32_t k = 0; k < n; ++k)
-                    out[k] = make_uint2(__float_as_uint(la[k * kOwners + owner]), lp[k * kOwners + owner]);
-                A.cand_n[(size_t)r * kLists + l] = (ok && !*stop) ? n : kEmpty;
+                    out[k] = make_uint2(__float_as_uint(la[k * C::OWN + owner]), lp[k * C::OWN + owner]);
+                A.cand_n[(size_t)r * C::LISTS + l] = (ok && !*stop) ? n : kEmpty;
             } else {
                 A.row_fb[r] = 1u;  // more CTAs than list slots met this query tile
             }
@@ -996,8 +1015,13 @@ struct MergeArgs {
     double eta;
 };
 
-// One warp per sorted row: merge, exact re-rank, proof (see the file comment).
+// One warp per sorted row: merge, exact re-rank, proof (see the file comment).  The KM
+// smallest a of the merged lists are re-ranked (KM / 32 per lane); the k smallest canonical
+// keys are the answer when the bound proves that no point left out can beat the k-th.
+template <bool DEEP>
 __global__ void __launch_bounds__(256) bf_merge_kernel(const __grid_constant__ MergeArgs M) {
+    using C = Lists<DEEP>;
+    constexpr uint32_t NR = C::KM / 32;  // re-ranked candidates per lane
     extern __shared__ __align__(16) float mq[];
     const uint32_t lane = lane_id(), w = threadIdx.x >> 5;
     const uint32_t r = blockIdx.x * (blockDim.x >> 5) + w;
@@ -1005,42 +1029,89 @@ __global__ void __launch_bounds__(256) bf_merge_kernel(const __grid_constant__ M
     const uint32_t q = M.perm[r];
     if (q == kEmpty) return;
     bool fallback = M.flag[r] != 0 || M.row_fb[r] != 0 || (M.test_every && q % M.test_every == 0);
-    const uint32_t nl = kLists;
+    const uint32_t nl = C::LISTS;
     const uint32_t cnt = lane < nl ? M.cand_n[(size_t)r * nl + lane] : 0u;
     fallback = fallback || __any_sync(kFull, cnt == kEmpty);
     if (!fallback) {
         float4* qs = reinterpret_cast<float4*>(mq + (size_t)w * M.nch * 4);
         float* qf = reinterpret_cast<float*>(qs);
         for (uint32_t i = lane; i < M.nch * 4; i += 32) qf[i] = i < M.dim ? M.queries[(size_t)q * M.dim + i] : 0.0f;
-        const uint2* lst = M.cand + ((size_t)r * nl + lane) * kM;
+        const uint2* lst = M.cand + ((size_t)r * nl + (lane < nl ? lane : 0u)) * C::KM;
         uint32_t hd = 0;
         const uint32_t inf_o = f2ord(__int_as_float(0x7f800000));
         uint32_t head = (lane < nl && cnt > 0) ? f2ord(__uint_as_float(lst[0].x)) : inf_o;
-        const uint32_t lthr = (lane < nl && cnt == kM) ? f2ord(__uint_as_float(lst[kM - 1].x)) : inf_o;
+        const uint32_t lthr = (lane < nl && cnt == C::KM) ? f2ord(__uint_as_float(lst[C::KM - 1].x)) : inf_o;
         uint32_t astar = __reduce_min_sync(kFull, lthr);
-        uint32_t mypos = kEmpty, npick = 0;
-        for (; npick < 32; ++npick) {
+        uint32_t mypos[NR];
+#pragma unroll
+        for (uint32_t i = 0; i < NR; ++i) mypos[i] = kEmpty;
+        uint32_t npick = 0;
+        for (; npick < C::KM; ++npick) {
             const uint32_t mn = __reduce_min_sync(kFull, head);
             if (mn == inf_o) break;
             const uint32_t win = __ffs(__ballot_sync(kFull, head == mn)) - 1;
             const uint32_t p = __shfl_sync(kFull, lane == win ? lst[hd].y : 0u, win);
-            if (lane == npick) mypos = p;
+            if (lane == (npick & 31u)) {
+#pragma unroll
+                for (uint32_t i = 0; i < NR; ++i)
+                    if (i == (npick >> 5)) mypos[i] = p;
+            }
             if (lane == win) {
                 ++hd;
                 head = hd < cnt ? f2ord(__uint_as_float(lst[hd].x)) : inf_o;
             }
         }
-        if (npick == 32) astar = min(astar, __reduce_min_sync(kFull, head));
+        if (npick == C::KM) astar = min(astar, __reduce_min_sync(kFull, head));
         __syncwarp();
-        key_t key = kEmptyKey;
-        if (lane < npick) {
-            const float c = dist32(M.vec32 + (size_t)mypos * M.nch, qs, M.nch);
-            key = ((key_t)__float_as_uint(c) << 32) | __ldg(M.i2g + mypos);
+        key_t key[NR];
+#pragma unroll
+        for (uint32_t i = 0; i < NR; ++i) {
+            key[i] = kEmptyKey;
+            if (i * 32 + lane < npick) {
+                const float c = dist32(M.vec32 + (size_t)mypos[i] * M.nch, qs, M.nch);
+                key[i] = ((key_t)__float_as_uint(c) << 32) | __ldg(M.i2g + mypos[i]);
+            }
         }
-        key = warp_sort32_key(key);
+        // res[i] of lane l: the (32 i + l)-th smallest key; kth: the k-th smallest
+        key_t res[NR], kth;
+        if (NR == 1) {
+            res[0] = warp_sort32_key(key[0]);
+            kth = __shfl_sync(kFull, res[0], M.k - 1);
+        } else {
+            // the lane's keys ascending, then k rounds that take the warp's smallest head
+#pragma unroll
+            for (uint32_t i = 0; i < NR; ++i)
+#pragma unroll
+                for (uint32_t j = 0; j + 1 < NR - i; ++j)
+                    if (key[j] > key[j + 1]) {
+                        const key_t t = key[j];
+                        key[j] = key[j + 1];
+                        key[j + 1] = t;
+                    }
+#pragma unroll
+            for (uint32_t i = 0; i < NR; ++i) res[i] = kEmptyKey;
+            kth = kEmptyKey;
+            for (uint32_t i = 0; i < M.k; ++i) {
+                const uint32_t hi = __reduce_min_sync(kFull, (uint32_t)(key[0] >> 32));
+                const uint32_t lo = __reduce_min_sync(kFull, (uint32_t)(key[0] >> 32) == hi ? (uint32_t)key[0] : ~0u);
+                const key_t mn = ((key_t)hi << 32) | lo;
+                kth = mn;
+                if (mn == kEmptyKey) break;
+                if (lane == (i & 31u)) {
+#pragma unroll
+                    for (uint32_t j = 0; j < NR; ++j)
+                        if (j == (i >> 5)) res[j] = mn;
+                }
+                const uint32_t win = __ffs(__ballot_sync(kFull, key[0] == mn)) - 1;
+                if (lane == win) {
+#pragma unroll
+                    for (uint32_t j = 0; j + 1 < NR; ++j) key[j] = key[j + 1];
+                    key[NR - 1] = kEmptyKey;
+                }
+            }
+        }
         if (astar != inf_o) {
             // some point was left out: it must provably lose to the k-th re-ranked one
-            const key_t kth = __shfl_sync(kFull, key, M.k - 1);
             bool proven = false;
             if (kth != kEmptyKey) {
                 const double as = (double)ord2f(astar);
@@ -1052,9 +1123,16 @@ __global__ void __launch_bounds__(256) bf_merge_kernel(const __grid_constant__ M
             }
             fallback = !proven;
         }
-        if (!fallback && lane < M.k) {
-            M.ids[(size_t)q * M.k + lane] = key == kEmptyKey ? kEmpty : (uint32_t)key;
-            if (M.dists) M.dists[(size_t)q * M.k + lane] = key == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(key);
+        if (!fallback) {
+#pragma unroll
+            for (uint32_t i = 0; i < NR; ++i) {
+                const uint32_t j = i * 32 + lane;
+                if (j < M.k) {
+                    M.ids[(size_t)q * M.k + j] = res[i] == kEmptyKey ? kEmpty : (uint32_t)res[i];
+                    if (M.dists)
+                        M.dists[(size_t)q * M.k + j] = res[i] == kEmptyKey ? __int_as_float(0x7f800000) : key_dist(res[i]);
+                }
+            }
         }
     }
     if (fallback && lane == 0) M.fb_list[atomicAdd(M.fb_cnt, 1u)] = q;
@@ -1203,8 +1281,12 @@ bool bf_tc_usable(const DeviceIndex& d, uint32_t k) { return d.bf_ok && k >= 1 &
 
 namespace {
 // Working memory of one call, carved in this order from `base` (sizes only when base is NULL).
-void carve_ws(const DeviceIndex& d, uint32_t qnum, size_t tmp_sort, unsigned char* base, size_t* used, void** p) {
+void carve_ws(const DeviceIndex& d, uint32_t qnum, uint32_t k, size_t tmp_sort, unsigned char* base, size_t* used,
+              void** p) {
     const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM, dp = d.bf_dp, a = d.a;
+    const bool deep = k > kMaxKShallow;
+    const size_t lists = deep ? Lists<true>::LISTS : Lists<false>::LISTS;
+    const size_t km = deep ? Lists<true>::KM : Lists<false>::KM;
     Carve c{base};
     p[0] = c.take<unsigned long long>(qnum);  // keys
     p[1] = c.take<unsigned long long>(qnum);  // keys sorted
@@ -1222,8 +1304,8 @@ void carve_ws(const DeviceIndex& d, uint32_t qnum, size_t tmp_sort, unsigned cha
     p[13] = c.take<float>((size_t)qtiles * 4 * a);
     p[14] = c.take<uint32_t>((size_t)qtiles * d.bf_tiles);
     p[15] = c.take<uint32_t>(qtiles);
-    p[16] = c.take<uint2>((size_t)qpad * kLists * kM);
-    p[17] = c.take<uint32_t>((size_t)qpad * kLists + qpad);  // list counts, then row fallbacks
+    p[16] = c.take<uint2>((size_t)qpad * lists * km);
+    p[17] = c.take<uint32_t>((size_t)qpad * lists + qpad);  // list counts, then row fallbacks
     p[18] = nullptr;
     p[19] = c.take<uint32_t>(qpad);            // published thresholds
     p[20] = c.take<uint32_t>(qtiles + 1 + 2);  // prefix of the tile counts, then W and G
@@ -1238,16 +1320,17 @@ size_t sort_tmp_bytes(uint32_t qnum) {
 }
 }  // namespace
 
-size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum) {
+size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum, uint32_t k) {
     void* P[21];
     size_t used = 0;
-    carve_ws(d, qnum, sort_tmp_bytes(qnum), nullptr, &used, P);
+    carve_ws(d, qnum, k, sort_tmp_bytes(qnum), nullptr, &used, P);
     return used;
 }
 
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
                     uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
-                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s) {
+                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s,
+                    const uint32_t* qmask) {
     DeviceIndex& d = idx->d;
     const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM;
     const uint32_t dp = d.bf_dp, nck = (dp + kKC - 1) / kKC, a = d.a;
@@ -1255,17 +1338,21 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, d.device);
     const uint32_t grid = (uint32_t)std::max(1, nsm);  // persistent: one CTA per SM
 
-    // stages of the point-chunk ring: as many as fit (at least 2)
-    const uint32_t stream = dp > kResidentDp ? 1u : 0u;
+    // list depth; stages of the chunk ring: as many as fit (at least 2); the query tile stays
+    // in shared memory when it is at most kResidentDp wide and two stages still fit beside it
+    const bool deep = k > kMaxKShallow;
+    const uint32_t km = deep ? Lists<true>::KM : Lists<false>::KM, own = deep ? Lists<true>::OWN : Lists<false>::OWN;
+    const uint32_t nlists = deep ? Lists<true>::LISTS : Lists<false>::LISTS;
+    const uint32_t stream = (dp > kResidentDp || tc_layout(dp, 2, a, 0, km, own).total > kSmemLimit) ? 1u : 0u;
     uint32_t stages = 8;
-    while (stages > 2 && tc_layout(dp, stages, a, stream).total > kSmemLimit) --stages;
-    const TcLayout Lo = tc_layout(dp, stages, a, stream);
+    while (stages > 2 && tc_layout(dp, stages, a, stream, km, own).total > kSmemLimit) --stages;
+    const TcLayout Lo = tc_layout(dp, stages, a, stream, km, own);
     if (Lo.total > kSmemLimit) return fail(GF_ERR_ARG, "tensor-core brute force: shared memory");
 
     size_t tmp_sort = sort_tmp_bytes(qnum);
     void* P[21];
     size_t used = 0;
-    carve_ws(d, qnum, tmp_sort, static_cast<unsigned char*>(ws), &used, P);
+    carve_ws(d, qnum, k, tmp_sort, static_cast<unsigned char*>(ws), &used, P);
     unsigned long long *keys = (unsigned long long*)P[0], *keys2 = (unsigned long long*)P[1];
     uint32_t *iota = (uint32_t*)P[2], *sorted = (uint32_t*)P[3];
     uint32_t *perm = (uint32_t*)P[5], *flag = (uint32_t*)P[6];
@@ -1275,7 +1362,7 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     uint32_t *tl = (uint32_t*)P[14], *tl_cnt = (uint32_t*)P[15];
     uint2* cand = (uint2*)P[16];
     uint32_t* cand_n = (uint32_t*)P[17];
-    uint32_t* row_fb = cand_n + (size_t)qpad * kLists;
+    uint32_t* row_fb = cand_n + (size_t)qpad * nlists;
     uint32_t* thr_g = (uint32_t*)P[19];
     uint32_t* pre = (uint32_t*)P[20];
     uint32_t* sched = pre + qtiles + 1;
@@ -1284,12 +1371,13 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     auto ck = [&](cudaError_t e, const char* what) {
         if (e != cudaSuccess && st == GF_OK) st = cuda_fail(e, what);
     };
-    ck(cudaMemsetAsync(cand_n, 0, sizeof(uint32_t) * ((size_t)qpad * kLists + qpad), s), "bf lists");
-    bf_morton_kernel<<<(qnum + 255) / 256, 256, 0, s>>>(lb, rb, qnum, a, d.bf_arange, d.bf_arange + a, keys, iota);
+    ck(cudaMemsetAsync(cand_n, 0, sizeof(uint32_t) * ((size_t)qpad * nlists + qpad), s), "bf lists");
+    bf_morton_kernel<<<(qnum + 255) / 256, 256, 0, s>>>(lb, rb, qnum, a, d.bf_arange, d.bf_arange + a, qmask, keys,
+                                                         iota);
     ck(cub::DeviceRadixSort::SortPairs(P[4], tmp_sort, keys, keys2, iota, sorted, (int)qnum, 0, 64, s), "bf sort");
     const double omk = 1.0 - kappa_of(dp);
-    bf_prep_kernel<<<(qpad + 7) / 8, 256, 0, s>>>(queries, qnum, d.dim, dp, sorted, qpad, d.bf_mean, d.bf_scale, omk,
-                                                  perm, at, pq, dq, flag, thr_g);
+    bf_prep_kernel<<<(qpad + 7) / 8, 256, 0, s>>>(queries, qnum, d.dim, dp, sorted, qmask, qpad, d.bf_mean,
+                                                  d.bf_scale, omk, perm, at, pq, dq, flag, thr_g);
     bf_boxes_kernel<<<qtiles, kBM, 0, s>>>(lb, rb, a, perm, flag, tq_lo, tq_hi, g_lo, g_hi);
     bf_tiles_kernel<<<qtiles, 256, 0, s>>>(d.bf_tbox, tbox_stride(a), d.bf_tiles, a, tq_lo, tq_hi, tl, tl_cnt, products);
     bf_sched_kernel<<<1, 32, 0, s>>>(tl_cnt, qtiles, grid, pre, sched);
@@ -1324,10 +1412,13 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     T.nck = nck;
     T.stages = stages;
     T.stream_a = stream;
-    void (*kern)(TcArgs) = a == 1 ? bf_tc_kernel<1> : a == 2 ? bf_tc_kernel<2> : a == 3 ? bf_tc_kernel<3>
-                         : a == 4 ? bf_tc_kernel<4> : bf_tc_kernel<0>;
+    void (*kern)(TcArgs) =
+        deep ? (a == 1 ? bf_tc_kernel<1, true> : a == 2 ? bf_tc_kernel<2, true> : a == 3 ? bf_tc_kernel<3, true>
+                : a == 4 ? bf_tc_kernel<4, true> : bf_tc_kernel<0, true>)
+             : (a == 1 ? bf_tc_kernel<1, false> : a == 2 ? bf_tc_kernel<2, false> : a == 3 ? bf_tc_kernel<3, false>
+                : a == 4 ? bf_tc_kernel<4, false> : bf_tc_kernel<0, false>);
     ck(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Lo.total), "bf smem");
-    kern<<<grid, kThreads, Lo.total, s>>>(T);
+    kern<<<grid, deep ? Lists<true>::THREADS : Lists<false>::THREADS, Lo.total, s>>>(T);
     MergeArgs M;
     M.cand = cand;
     M.cand_n = cand_n;
@@ -1352,7 +1443,10 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     M.dmax = d.bf_dmax;
     M.eta = (d.d4 / 8.0 + 16.0) * 0x1p-23;
     const size_t msmem = sizeof(float) * 8 * d.d4;
-    bf_merge_kernel<<<(qpad + 7) / 8, 256, msmem, s>>>(M);
+    if (deep)
+        bf_merge_kernel<true><<<(qpad + 7) / 8, 256, msmem, s>>>(M);
+    else
+        bf_merge_kernel<false><<<(qpad + 7) / 8, 256, msmem, s>>>(M);
     ck(cudaGetLastError(), "bf kernels");
     return st;
 }

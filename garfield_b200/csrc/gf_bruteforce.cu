@@ -145,7 +145,8 @@ __global__ void __launch_bounds__(256) bruteforce_kernel(const float4* __restric
 }  // namespace
 
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
-                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm) {
+                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm,
+                     const uint32_t* qmask) {
     DeviceIndex& d = idx->d;
     if (!d.vec32) return fail(GF_ERR_STATE, "index was created without keep_fp32");
     if (k == 0 || k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");
@@ -153,8 +154,9 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     if (prm) P = *prm;
     if (P.path > 2) return fail(GF_ERR_ARG, "path must be 0, 1 or 2");
     const bool tc = P.path != 1 && bf_tc_usable(d, k);
+    if (qmask && !tc) return fail(GF_ERR_STATE, "a query mask needs the tensor-core pass");
     if (P.path == 2 && !tc)
-        return fail(GF_ERR_ARG, "tensor-core brute force needs keep_fp32, dim <= 1024, finite rows and k <= 16");
+        return fail(GF_ERR_ARG, "tensor-core brute force needs keep_fp32, dim <= 1024, finite rows and k <= 128");
     if (P.stats_out) GF_CUDA(cudaMemsetAsync(P.stats_out, 0, 3 * sizeof(uint32_t), s));
     if (qnum == 0) return GF_OK;
     if (!queries || !lb || !rb || !ids) return fail(GF_ERR_ARG, "null argument");
@@ -173,7 +175,7 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     }
     // tensor-core pass, then the CUDA-core kernel for the queries it could not prove; working
     // memory: the pass's, then [0] fallback count, [1] timeouts, [2] tile products, [3..] list
-    const size_t tc_bytes = (bf_tc_ws_bytes(d, qnum) + 255) & ~size_t(255);
+    const size_t tc_bytes = (bf_tc_ws_bytes(d, qnum, k) + 255) & ~size_t(255);
     const size_t need = tc_bytes + sizeof(uint32_t) * (3 + (size_t)qnum);
     std::lock_guard<std::mutex> lock(*d.bf_mu);
     if (!d.bf_ws_ev) GF_CUDA(cudaEventCreateWithFlags(&d.bf_ws_ev, cudaEventDisableTiming));
@@ -192,7 +194,7 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
     if (e != cudaSuccess) st = cuda_fail(e, "brute-force counters");
     if (st == GF_OK)
         st = bf_tc_run(idx, queries, lb, rb, qnum, k, ids, dist, d.bf_ws, w + 3, w, P.test_fallback_every, P.test_wait,
-                       w + 1, w + 2, s);
+                       w + 1, w + 2, s, qmask);
     if (st == GF_OK) {
         bruteforce_kernel<<<qnum, 256, smem, s>>>(d.vec32, d.attrs, d.i2g, d.n, nch, d.a, queries, d.dim, lb, rb, k,
                                                   ids, dist, w + 3, w);

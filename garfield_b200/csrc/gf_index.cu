@@ -576,6 +576,7 @@ void gf_search_defaults(gf_search_params* p) {
     p->postfilter = 0xFFFFFFFFu;
     p->hash_slots = 0;
     p->test_wait = 0;
+    p->exact_tc = 0;
 }
 
 gf_status gf_index_create(const gf_index_desc* desc, int device, gf_index** out) {

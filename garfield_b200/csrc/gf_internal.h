@@ -142,6 +142,7 @@ struct Plan {
     size_t io_bytes = 0;
     BatchState* batch = nullptr;  // created by the first gf_search_batched
     unsigned long long* run = nullptr;  // running keys of searches on a shard index
+    uint32_t* xmark = nullptr;          // max_q: queries answered by the tensor-core exact scan (exact_tc)
     size_t run_cap = 0;
 };
 
@@ -192,18 +193,22 @@ CellView shard_view(const DeviceIndex& d);
 gf_status finish_run(gf_index* idx, const unsigned long long* run, uint32_t total, uint32_t* ids, float* dist,
                      cudaStream_t s);
 // gf_bruteforce.cu
+// qmask (device, qnum words, or NULL): only queries q with qmask[q] != 0 are answered (tensor-core
+// path only); the others' rows of ids / dist are left untouched
 gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum,
-                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm = nullptr);
+                     uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm = nullptr,
+                     const uint32_t* qmask = nullptr);
 // gf_bf_tc.cu
 gf_status bf_tc_prepare(DeviceIndex& d);  // at index creation, after vec32 and attrs
 void free_bf_tc(DeviceIndex& d);
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
 // Tensor-core pass: writes the proven queries' results and appends the others to
 // fb_list / fb_cnt (answered afterwards by the CUDA-core kernel).
-size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum);  // working memory of bf_tc_run
+size_t bf_tc_ws_bytes(const DeviceIndex& d, uint32_t qnum, uint32_t k);  // working memory of bf_tc_run
 gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const float* rb, uint32_t qnum, uint32_t k,
                     uint32_t* ids, float* dist, void* ws, uint32_t* fb_list, uint32_t* fb_cnt, uint32_t test_every,
-                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s);
+                    uint32_t test_wait, uint32_t* timeouts, uint32_t* products, cudaStream_t s,
+                    const uint32_t* qmask = nullptr);
 // gf_index.cu: greedy spokesman assignment (compress_global_graph_extreme, tools.cuh:917-935);
 // graphs: n x degree local ids, rows in position (cell) order
 void spokesman_assign(uint32_t n, uint32_t n_cells, const uint32_t* cell_sizes, uint32_t degree,

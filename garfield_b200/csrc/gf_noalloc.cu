@@ -81,6 +81,8 @@ extern "C" gf_status gf_search_noalloc(gf_index* idx, const float* queries, cons
     if (!queries || !lb || !rb || !ids_out) return fail(GF_ERR_ARG, "null argument");
     DeviceIndex& d = idx->d;
     if (d.sharded || d.host_graph) return fail(GF_ERR_STATE, "gf_search_noalloc needs a whole device-resident index");
+    if (params && params->exact_tc)
+        return fail(GF_ERR_ARG, "exact_tc needs the tensor-core pass's working memory (use gf_search)");
     DeviceGuard3 guard(d.device);
     unsigned char* scratch = nullptr;
     gf_status st = scratch_address(d.device, &scratch);

@@ -427,6 +427,8 @@ void free_plan(Plan& p) {
     for (void* x : ptrs)
         if (x) cudaFree(x);
     if (p.io) cudaFree(p.io);
+    if (p.xmark) cudaFree(p.xmark);
+    if (p.run) cudaFree(p.run);
     free_batch_state(p.batch);
     p.batch = nullptr;
 }

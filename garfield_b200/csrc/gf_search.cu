@@ -48,6 +48,7 @@ struct SArgs {
     const uint32_t* __restrict__ offsets;
     const uint32_t* __restrict__ cells;
     const uint32_t* __restrict__ box;  // box counts (only when prefilter > 0)
+    const uint32_t* __restrict__ skip = nullptr;  // queries answered by the tensor-core exact scan
     const uint32_t* __restrict__ task;
     const uint32_t* __restrict__ entry;
     uint32_t* queue;
@@ -488,6 +489,7 @@ __global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constan
         slot = __shfl_sync(kFull, slot, 0);
         if (slot >= A.qnum) break;
         const uint32_t q = A.task[slot];
+        if (A.skip && A.skip[q]) continue;  // answered by the tensor-core exact scan
         const uint32_t nc = A.counts[q];
         const uint32_t* cl = A.cells + A.offsets[q];
         // query row (fp16 -> fp32 element pairs) and box
@@ -958,6 +960,29 @@ CellView shard_view(const DeviceIndex& d) {
     return v;
 }
 
+namespace {
+// Queries of a whole-index search that take the exact route (the search kernel's rule:
+// a non-empty cell list and >= postfilter cells or a box share <= prefilter) are marked for
+// the tensor-core exact scan (gf_search_params.exact_tc); their number goes to n_exact and
+// n_queries.
+__global__ void mark_exact_kernel(const uint32_t* __restrict__ counts, const uint32_t* __restrict__ box, uint32_t n,
+                                  uint32_t qnum, uint32_t postfilter, float prefilter, uint32_t* __restrict__ mark,
+                                  unsigned long long* stats) {
+    const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+    bool ex = false;
+    if (q < qnum) {
+        const uint32_t nc = counts[q];
+        ex = nc > 0 && (nc >= postfilter || (box && (float)((double)box[q] / (double)n) <= prefilter));
+        mark[q] = ex ? 1u : 0u;
+    }
+    const uint32_t b = __ballot_sync(kFull, ex);
+    if (lane_id() == 0 && b) {
+        atomicAdd(stats + 4, (unsigned long long)__popc(b));  // n_exact
+        atomicAdd(stats + 5, (unsigned long long)__popc(b));  // n_queries (the search kernel skips them)
+    }
+}
+}  // namespace
+
 gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint32_t* ids, float* dist,
                  cudaStream_t s, const CellView* view, bool fullgraph) {
     DeviceIndex& d = idx->d;
@@ -971,6 +996,12 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (P.k == 0 || P.k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");
     if (P.L < P.k || P.L > 4096) return fail(GF_ERR_ARG, "L must be k..4096");
     if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
+    if (P.exact_tc) {
+        if (view || fullgraph || d.sharded || d.host_graph)
+            return fail(GF_ERR_ARG, "exact_tc applies to gf_search / gf_search_host on a whole device-resident index");
+        if (!bf_tc_usable(d, P.k))
+            return fail(GF_ERR_STATE, "exact_tc needs an index with keep_fp32 rows (dim <= 1024, finite) and k <= 128");
+    }
     uint32_t n_entry = P.n_entry ? P.n_entry : d.degree;
     n_entry = std::min<uint32_t>(n_entry, fullgraph ? d.fentry_n : (uint32_t)d.entry_h.size());
     if (!ids && !(view && view->run)) return fail(GF_ERR_ARG, "null ids_out");
@@ -1095,6 +1126,17 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     blocks = std::min(blocks, need_blocks);
     GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
     if (!(view && view->accumulate_stats)) GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
+    if (P.exact_tc) {
+        // exact-route queries: the tensor-core exact scan writes their rows, the search kernel
+        // skips them
+        if (!p.xmark) GF_CUDA(cudaMalloc((void**)&p.xmark, sizeof(uint32_t) * std::max<uint32_t>(p.max_q, 1)));
+        mark_exact_kernel<<<(p.qnum + 255) / 256, 256, 0, s>>>(p.counts, A.box, d.n, p.qnum, P.postfilter,
+                                                                p.prefilter, p.xmark, p.stats);
+        GF_CUDA(cudaGetLastError());
+        gf_status st = bruteforce(idx, p.q32, p.lb, p.rb, p.qnum, P.k, ids, dist, s, nullptr, p.xmark);
+        if (st != GF_OK) return st;
+        A.skip = p.xmark;
+    }
     kern<<<blocks, 128, smem, s>>>(A);
     GF_CUDA(cudaGetLastError());
     return GF_OK;

@@ -133,6 +133,14 @@ typedef struct {
                             expects 16 bytes more than it copies, so no wait completes; the
                             warps stop, gf_search_stats.n_timeouts counts them and
                             gf_search_host returns GF_ERR_TIMEOUT. */
+    uint32_t exact_tc;   /* 0 = the reference's exact route (fp16 distances over the in-box points
+                            of the query's cells, gpu_graph.cu:3788-4022).  1 = queries that take
+                            the exact route (postfilter, plan prefilter) are answered by the
+                            tensor-core exact scan of gf_bruteforce instead: canonical fp32
+                            distances of the fp32 rows, ids ordered by (distance, global id).
+                            Needs keep_fp32, dim <= 1024 and k <= 128; gf_search and
+                            gf_search_host only (GF_ERR_ARG for batched, sharded, full-graph and
+                            no-allocation searches). */
 } gf_search_params;
 
 /* Per-search counters (device-side, summed over queries). */
@@ -318,7 +326,7 @@ gf_status gf_bruteforce(gf_index* idx, const float* queries, const float* lb, co
 /* Options of gf_bruteforce_ex (all zero = gf_bruteforce's behaviour). */
 typedef struct {
     uint32_t path;       /* 0 = automatic: the tensor-core pass when the index has its fp16 tiles
-                            (keep_fp32, dim <= 1024, finite rows) and k <= 16, else CUDA cores;
+                            (keep_fp32, dim <= 1024, finite rows) and k <= 128, else CUDA cores;
                             1 = CUDA cores only; 2 = tensor cores (GF_ERR_ARG when unavailable) */
     uint32_t test_fallback_every; /* 0 in normal use.  Test hook: queries whose index is a
                             multiple of this value skip the tensor-core proof and are answered

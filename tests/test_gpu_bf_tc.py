@@ -57,6 +57,26 @@ def test_tc_matches_oracle(dim, grid, k):
     g.close()
 
 
+@pytest.mark.parametrize("dim,grid,k,max_fb", [(128, (4, 4), 17, 0.1), (128, (4, 4), 100, 0.1), (256, (2, 2), 50, 0.1),
+                                               (1000, (2, 2), 64, 0.1), (64, (2, 2), 128, 1.0)])
+def test_tc_deep_lists(dim, grid, k, max_fb):
+    """k > 16: lists of 128 candidates, one epilogue warp per TMEM lane quarter; k = 128
+    leaves no margin for the proof, so most queries go to the CUDA cores (still exact)."""
+    ds = synth.make(30000, dim, 60, 700, grid, 0.1, seed=201 + dim + k, stratified=False)
+    g = bf_index(ds.vectors, ds.attrs, grid)
+    check(ds, g, k, max_fallback_frac=max_fb)
+    g.close()
+
+
+def test_tc_config3_shape_k100():
+    """96-dim unit vectors, 3 attributes (uniform, Zipf, component band), k = 100."""
+    ds = synth.config3(seed=33, n=60000, qnum=700, n_centers=60)
+    g = bf_index(ds.vectors, ds.attrs, ds.grid)
+    st = check(ds, g, 100, max_fallback_frac=0.05)
+    assert st[2] > 0
+    g.close()
+
+
 def test_tc_wide_unit_norm_rows():
     """768-dim unit-normalised rows on an 8x8 grid (the shape of configuration 4): query
     chunks are streamed beside the point chunks instead of staying in shared memory."""
@@ -72,12 +92,12 @@ def test_tc_fallback_hook_and_automatic_path():
     g = bf_index(ds.vectors, ds.attrs, (2, 2))
     st = check(ds, g, 10, test_fallback_every=3, max_fallback_frac=1.0)
     assert st[0] >= len([q for q in range(300) if q % 3 == 0])
-    # the automatic path (k <= 16 with fp16 tiles) agrees with the CUDA-core path
+    # the automatic path (k <= 128 with fp16 tiles) agrees with the CUDA-core path
     a_ids, a_d, _ = run(g, ds.queries, ds.lo, ds.hi, 10)
     c_ids, c_d, cst = run(g, ds.queries, ds.lo, ds.hi, 10, path=1)
     assert np.array_equal(a_ids, c_ids) and np.array_equal(a_d, c_d) and cst[0] == 0
     with pytest.raises(RuntimeError):
-        g.bruteforce(dev(ds.queries), dev(ds.lo), dev(ds.hi), 17, path=2)
+        g.bruteforce(dev(ds.queries), dev(ds.lo), dev(ds.hi), 129, path=2)  # past the deep lists
     g.close()
 
 

@@ -109,7 +109,8 @@ def test_config3_shape(c3):
     ids = check_search(c, plan, 1024, 8, 100)
     check_filter(c, ids)
     assert oracle.recall(ids, c.gt) >= 0.97
-    check_bruteforce(c, g, 100)
+    st = check_bruteforce(c, g, 100)
+    assert st[2] > 0 and st[0] <= 0.05 * c.ds.queries.shape[0]  # deep lists on the tensor cores
     plan.close()
     g.close()
 
