@@ -42,8 +42,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 # data shape of each --config (config 3 runs at --n points)
-SHAPES = {2: "1M x 128, 2 attrs, 10% sel.", 3: "config-3 shape: 96-dim unit-norm, 3 attrs (uniform, Zipf, component), "
-          "5% sel.", 4: "1M x 768 unit-norm, 2 attrs on 8x8, 2% sel."}
+SHAPES = {2: "1M x 128, 2 attrs, {sel:.0%} sel.",
+          3: "config-3 shape: 96-dim unit-norm, 3 attrs (uniform, Zipf, component), {sel:.0%} sel.",
+          4: "1M x 768 unit-norm, 2 attrs on 8x8, {sel:.0%} sel."}
 
 # the reference's ef sweep (realdataset_search.cu:2757-2760), ascending, L >= k
 L_SWEEP = [10, 15, 20, 25, 30, 35, 40, 45, 50, 55, 60, 70, 80, 90, 100, 120, 140, 160, 180, 200, 250, 300, 400,
@@ -325,7 +326,7 @@ def run_ours(args):
     achieved = bytes_step / kern_s / 1e9
     peak, peak_kind = peak_hbm()
     out = {
-        "metric": f"QPS at recall@{K}>={args.target} ({SHAPES[args.config]})",
+        "metric": f"QPS at recall@{K}>={args.target} ({SHAPES[args.config].format(sel=args.sel)})",
         "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",

@@ -267,10 +267,25 @@ __global__ void bf_convert_kernel(const float* __restrict__ x, uint32_t n, uint3
 // copy (NaN past n, so no padding point is ever inside a box).
 __global__ void bf_tilebox_kernel(const float* __restrict__ attrs, uint32_t n, uint32_t a, uint32_t a8,
                                   uint32_t tiles, const uint32_t* order, float* __restrict__ tbox,
-                                  float* __restrict__ pattrs, uint32_t* rowpos) {  // order may alias rowpos
+                                  float* __restrict__ pattrs, uint32_t* rowpos,  // order may alias rowpos
+                                  uint32_t* __restrict__ tcnt) {
     const uint32_t lane = lane_id();
     const uint32_t t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= tiles) return;
+    {  // points of the tile whose attributes are all numbers (a NaN is inside no box)
+        uint32_t c = 0;
+        for (uint32_t r = lane; r < kBN; r += 32) {
+            const uint32_t p = t * kBN + r;
+            bool ok = p < n;
+            for (uint32_t j = 0; ok && j < a; ++j) {
+                const float v = attrs[(size_t)order[p] * a + j];
+                ok = v == v;
+            }
+            c += ok;
+        }
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(kFull, c, o);
+        if (lane == 0) tcnt[t] = c;
+    }
     for (uint32_t r = lane; r < kBN; r += 32) {
         const uint32_t p = t * kBN + r;
         rowpos[p] = p < n ? order[p] : kEmpty;
@@ -1176,21 +1191,77 @@ void free_bf_tc(DeviceIndex& d) {
     if (d.bf_ws) cudaFree(d.bf_ws);
     d.bf_ws = nullptr;
     d.bf_ws_bytes = 0;
-    void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean, d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_arange};
+    void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean, d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_arange, d.bf_tcnt};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     d.bf_x = nullptr;
     d.bf_px = d.bf_mean = d.bf_tbox = d.bf_attrs = d.bf_arange = nullptr;
-    d.bf_rowpos = nullptr;
+    d.bf_rowpos = d.bf_tcnt = nullptr;
     d.bf_ok = false;
+    d.at_ok = false;
+}
+
+// Attribute tiles (every index): rows in the Morton order of their attributes, 128 per
+// tile, each tile's attribute bounds and the tile-padded attribute copy.  Used by the
+// tensor-core brute force and by the plan's box counts.
+gf_status attr_tiles_prepare(DeviceIndex& d) {
+    d.at_ok = false;
+    if (d.n == 0 || d.a == 0 || d.a > kMaxAttr) return GF_OK;
+    const uint32_t tiles = (d.n + kBN - 1) / kBN, npad = tiles * kBN;
+    gf_status st = GF_OK;
+    auto ck = [&](cudaError_t e, const char* what) {
+        if (e != cudaSuccess && st == GF_OK) st = cuda_fail(e, what);
+        return st == GF_OK;
+    };
+    do {
+        if (!ck(cudaMalloc((void**)&d.bf_tbox, sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a)), "tile bounds"))
+            break;
+        if (!ck(cudaMalloc((void**)&d.bf_attrs, sizeof(float) * (size_t)npad * d.a), "tile attributes")) break;
+        if (!ck(cudaMalloc((void**)&d.bf_rowpos, sizeof(uint32_t) * (size_t)npad), "tile positions")) break;
+        if (!ck(cudaMalloc((void**)&d.bf_arange, sizeof(float) * 2 * d.a), "attribute range")) break;
+        if (!ck(cudaMalloc((void**)&d.bf_tcnt, sizeof(uint32_t) * tiles), "tile counts")) break;
+        {
+            std::vector<float> ar = attr_range(d);
+            if (!ck(cudaMemcpy(d.bf_arange, ar.data(), sizeof(float) * 2 * d.a, cudaMemcpyHostToDevice), "range"))
+                break;
+        }
+        // row order: Morton order of the points' attributes
+        unsigned long long *k0 = nullptr, *k1 = nullptr;
+        uint32_t* v0 = nullptr;
+        void* tmp = nullptr;
+        size_t tb = 0;
+        cub::DeviceRadixSort::SortPairs(nullptr, tb, k0, k1, v0, v0, (int)d.n);
+        bool good = ck(cudaMalloc((void**)&k0, 8 * (size_t)d.n), "tile sort") &&
+                    ck(cudaMalloc((void**)&k1, 8 * (size_t)d.n), "tile sort") &&
+                    ck(cudaMalloc((void**)&v0, 4 * (size_t)d.n), "tile sort") &&
+                    ck(cudaMalloc(&tmp, std::max<size_t>(tb, 16)), "tile sort");
+        if (good) {
+            bf_point_keys_kernel<<<(d.n + 255) / 256, 256>>>(d.attrs, d.n, d.a, d.bf_arange, d.bf_arange + d.a, k0, v0);
+            ck(cub::DeviceRadixSort::SortPairs(tmp, tb, k0, k1, v0, d.bf_rowpos, (int)d.n), "tile sort");
+            // rowpos: sorted positions, then padding marks past n
+            bf_tilebox_kernel<<<(tiles + 7) / 8, 256>>>(d.attrs, d.n, d.a, tbox_stride(d.a), tiles, d.bf_rowpos,
+                                                        d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_tcnt);
+            ck(cudaGetLastError(), "tile bounds");
+            ck(cudaDeviceSynchronize(), "tile sort");
+        }
+        for (void* pp : {(void*)k0, (void*)k1, (void*)v0, tmp})
+            if (pp) cudaFree(pp);
+        if (st != GF_OK) break;
+        d.bf_tiles = tiles;
+        d.bytes += sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a) + sizeof(float) * (size_t)npad * d.a +
+                   sizeof(uint32_t) * (size_t)npad + sizeof(float) * 2 * d.a + sizeof(uint32_t) * tiles;
+        d.at_ok = true;
+    } while (0);
+    if (st != GF_OK) free_bf_tc(d);
+    return st;
 }
 
 gf_status bf_tc_prepare(DeviceIndex& d) {
     d.bf_ok = false;
-    if (!d.vec32 || d.n == 0) return GF_OK;
+    if (!d.vec32 || d.n == 0 || !d.at_ok) return GF_OK;
     const uint32_t dp = (d.dim + 15) / 16 * 16;
     if (dp > kMaxDp) return GF_OK;  // wider rows use the CUDA-core kernel
-    const uint32_t tiles = (d.n + kBN - 1) / kBN, npad = tiles * kBN;
+    const uint32_t tiles = d.bf_tiles, npad = tiles * kBN;
     const float* x = reinterpret_cast<const float*>(d.vec32);
     double* sum = nullptr;
     uint32_t* words = nullptr;
@@ -1205,37 +1276,6 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
         if (!ck(cudaMalloc((void**)&d.bf_mean, sizeof(float) * d.dim), "bf mean")) break;
         if (!ck(cudaMalloc((void**)&d.bf_x, sizeof(__half) * (size_t)npad * dp), "bf tiles")) break;
         if (!ck(cudaMalloc((void**)&d.bf_px, sizeof(float) * npad), "bf px")) break;
-        if (!ck(cudaMalloc((void**)&d.bf_tbox, sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a)), "bf tile bounds"))
-            break;
-        if (!ck(cudaMalloc((void**)&d.bf_attrs, sizeof(float) * (size_t)npad * d.a), "bf attributes")) break;
-        if (!ck(cudaMalloc((void**)&d.bf_rowpos, sizeof(uint32_t) * (size_t)npad), "bf positions")) break;
-        if (!ck(cudaMalloc((void**)&d.bf_arange, sizeof(float) * 2 * d.a), "bf attribute range")) break;
-        {
-            std::vector<float> ar = attr_range(d);
-            if (!ck(cudaMemcpy(d.bf_arange, ar.data(), sizeof(float) * 2 * d.a, cudaMemcpyHostToDevice), "bf range"))
-                break;
-        }
-        // row order of the copy: Morton order of the points' attributes
-        {
-            unsigned long long *k0 = nullptr, *k1 = nullptr;
-            uint32_t* v0 = nullptr;
-            void* tmp = nullptr;
-            size_t tb = 0;
-            cub::DeviceRadixSort::SortPairs(nullptr, tb, k0, k1, v0, v0, (int)d.n);
-            bool good = ck(cudaMalloc((void**)&k0, 8 * (size_t)d.n), "bf sort") &&
-                        ck(cudaMalloc((void**)&k1, 8 * (size_t)d.n), "bf sort") &&
-                        ck(cudaMalloc((void**)&v0, 4 * (size_t)d.n), "bf sort") &&
-                        ck(cudaMalloc(&tmp, std::max<size_t>(tb, 16)), "bf sort");
-            if (good) {
-                bf_point_keys_kernel<<<(d.n + 255) / 256, 256>>>(d.attrs, d.n, d.a, d.bf_arange, d.bf_arange + d.a,
-                                                                 k0, v0);
-                ck(cub::DeviceRadixSort::SortPairs(tmp, tb, k0, k1, v0, d.bf_rowpos, (int)d.n), "bf sort");
-                ck(cudaDeviceSynchronize(), "bf sort");
-            }
-            for (void* pp : {(void*)k0, (void*)k1, (void*)v0, tmp})
-                if (pp) cudaFree(pp);
-            if (st != GF_OK) break;
-        }
         ck(cudaMemset(sum, 0, sizeof(double) * d.dim), "bf mean");
         ck(cudaMemset(words, 0, 16), "bf words");
         const uint32_t blocks = std::min<uint32_t>(1024, (d.n + 255) / 256);
@@ -1255,26 +1295,91 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
         std::frexp(maxabs > 0.0f ? maxabs : 1.0f, &e);  // maxabs < 2^e
         const int ex = std::min(100, std::max(-100, 14 - e));
         const float s = std::ldexp(1.0f, ex);
-        // order[row] (sorted positions) is read before rowpos[row] is rewritten with padding marks
+        // rows in the attribute tiles' order (rowpos: the sorted positions; padding rows past n)
         bf_convert_kernel<<<148 * 16, 256>>>(x, d.n, d.d4, d.dim, dp, d.bf_mean, s, 1.0 - kappa_of(dp), npad,
                                              d.bf_rowpos, reinterpret_cast<__half*>(d.bf_x), d.bf_px, words + 2);
-        bf_tilebox_kernel<<<(tiles + 7) / 8, 256>>>(d.attrs, d.n, d.a, tbox_stride(d.a), tiles, d.bf_rowpos,
-                                                    d.bf_tbox, d.bf_attrs, d.bf_rowpos);
         if (!ck(cudaMemcpy(wh, words + 2, 4, cudaMemcpyDeviceToHost), "bf residuals")) break;
         if (!ck(cudaGetLastError(), "bf prepare")) break;
         std::memcpy(&d.bf_dmax, &wh[0], 4);
         d.bf_scale = s;
         d.bf_dp = dp;
-        d.bf_tiles = tiles;
-        d.bytes += sizeof(float) * d.dim + sizeof(__half) * (size_t)npad * dp + sizeof(float) * npad +
-                   sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a) + sizeof(float) * (size_t)npad * d.a +
-                   sizeof(uint32_t) * (size_t)npad + sizeof(float) * 2 * d.a;
+        d.bytes += sizeof(float) * d.dim + sizeof(__half) * (size_t)npad * dp + sizeof(float) * npad;
         d.bf_ok = std::isfinite(d.bf_dmax);
     } while (0);
     if (sum) cudaFree(sum);
     if (words) cudaFree(words);
-    if (st != GF_OK || !d.bf_ok) free_bf_tc(d);
+    if (st != GF_OK || !d.bf_ok) {  // the attribute tiles stay; only the fp16 copy goes
+        void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean};
+        for (void* p : ptrs)
+            if (p) cudaFree(p);
+        d.bf_x = nullptr;
+        d.bf_px = d.bf_mean = nullptr;
+        d.bf_ok = false;
+    }
     return st;
+}
+
+namespace {
+// Points inside each query box (prefiltering_tag_elements, real_dataset_adapter.cuh:347-387)
+// from the attribute tiles, one warp per query: every tile's bounds are tested; a tile that
+// lies inside the box adds its count of points with numeric attributes, a tile that meets the
+// box without lying inside it has its 128 rows tested one by one (4 per lane), and the
+// others add nothing.  The counts equal those of testing every point (closed intervals; a
+// NaN is inside no box), at a fraction of the reads: a box meets few tiles partially.
+__global__ void box_count_tiles_kernel(const float* __restrict__ tbox, const float* __restrict__ pattrs,
+                                       const uint32_t* __restrict__ tcnt, uint32_t tiles, uint32_t a, uint32_t a8,
+                                       const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum,
+                                       uint32_t* __restrict__ box) {
+    const uint32_t lane = lane_id();
+    const uint32_t q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (q >= qnum) return;
+    float lo[kMaxAttr], hi[kMaxAttr];
+#pragma unroll
+    for (uint32_t j = 0; j < kMaxAttr; ++j) {
+        lo[j] = j < a ? lb[(size_t)q * a + j] : 0.0f;
+        hi[j] = j < a ? rb[(size_t)q * a + j] : 0.0f;
+    }
+    uint32_t cnt = 0;
+    for (uint32_t t0 = 0; t0 < tiles; t0 += 32) {
+        const uint32_t t = t0 + lane;
+        bool meet = false, inside = false;
+        if (t < tiles) {
+            meet = inside = true;
+            const float* tb = tbox + (size_t)t * 2 * a8;
+#pragma unroll
+            for (uint32_t j = 0; j < kMaxAttr; ++j) {
+                if (j < a) {
+                    const float tl = tb[j], th = tb[a8 + j];
+                    meet = meet & (tl <= hi[j]) & (lo[j] <= th);
+                    inside = inside & (lo[j] <= tl) & (th <= hi[j]);
+                }
+            }
+            inside = inside & meet;
+        }
+        if (inside) cnt += tcnt[t];
+        uint32_t pm = __ballot_sync(kFull, meet && !inside);
+        while (pm) {
+            const uint32_t tt = t0 + __ffs(pm) - 1;
+            pm &= pm - 1;
+            for (uint32_t r = lane; r < kBN; r += 32) {
+                const float* pa = pattrs + ((size_t)tt * kBN + r) * a;
+                bool ok = true;
+#pragma unroll
+                for (uint32_t j = 0; j < kMaxAttr; ++j)
+                    if (j < a) ok = ok & (pa[j] >= lo[j]) & (pa[j] <= hi[j]);
+                cnt += ok;
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(kFull, cnt, o);
+    if (lane == 0) box[q] = cnt;
+}
+}  // namespace
+
+void box_count_tiles(const DeviceIndex& d, const float* lb, const float* rb, uint32_t qnum, uint32_t* box,
+                     cudaStream_t s) {
+    box_count_tiles_kernel<<<(qnum + 7) / 8, 256, 0, s>>>(d.bf_tbox, d.bf_attrs, d.bf_tcnt, d.bf_tiles, d.a,
+                                                          tbox_stride(d.a), lb, rb, qnum, box);
 }
 
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k) { return d.bf_ok && k >= 1 && k <= kMaxK; }

@@ -527,6 +527,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             }
         }
         if (st != GF_OK) break;
+        if ((st = attr_tiles_prepare(d)) != GF_OK) break;        // attribute tiles (box counts, brute force)
         if (d.vec32 && (st = bf_tc_prepare(d)) != GF_OK) break;  // fp16 tiles of the tensor-core brute force
         cudaError_t e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaGetLastError();

@@ -91,6 +91,8 @@ struct DeviceIndex {
     // tensor-core brute force (gf_bf_tc.cu): centred, scaled fp16 copy of the fp32 rows in
     // 128-point tcgen05 tiles, per point (1 - kappa)|x~|^2, per tile attribute bounds
     bool bf_ok = false;
+    bool at_ok = false;          // attribute tiles (bf_tbox, bf_attrs, bf_rowpos, bf_tcnt) built
+    uint32_t* bf_tcnt = nullptr; // bf_tiles: points of each tile whose attributes are all numbers
     uint32_t bf_dp = 0, bf_tiles = 0;   // padded row length (multiple of 16), point tiles
     float bf_scale = 1.0f, bf_dmax = 0.0f;  // power-of-two scale s, largest residual |x - x^|
     void* bf_x = nullptr;        // bf_tiles x 128 x bf_dp halves
@@ -199,7 +201,11 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
                      uint32_t k, uint32_t* ids, float* dist, cudaStream_t s, const gf_bf_params* prm = nullptr,
                      const uint32_t* qmask = nullptr);
 // gf_bf_tc.cu
-gf_status bf_tc_prepare(DeviceIndex& d);  // at index creation, after vec32 and attrs
+gf_status attr_tiles_prepare(DeviceIndex& d);  // at index creation, after attrs
+gf_status bf_tc_prepare(DeviceIndex& d);  // at index creation, after vec32 and attr_tiles_prepare
+// plan box counts from the attribute tiles (d.at_ok); same counts as testing every point
+void box_count_tiles(const DeviceIndex& d, const float* lb, const float* rb, uint32_t qnum, uint32_t* box,
+                     cudaStream_t s);
 void free_bf_tc(DeviceIndex& d);
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
 // Tensor-core pass: writes the proven queries' results and appends the others to

@@ -391,9 +391,13 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
         GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
     }
     if (prefilter > 0.0f) {
-        GF_CUDA(cudaMemsetAsync(p.box, 0, sizeof(uint32_t) * qnum, s));
-        dim3 grid(std::min<uint32_t>((d.n + 256 * 64 - 1) / (256 * 64), 1024), (qnum + kBoxQ - 1) / kBoxQ);
-        box_count_kernel<<<grid, 256, 0, s>>>(d.attrs, d.n, a, p.lb, p.rb, qnum, p.box);
+        if (d.at_ok) {
+            box_count_tiles(d, p.lb, p.rb, qnum, p.box, s);
+        } else {
+            GF_CUDA(cudaMemsetAsync(p.box, 0, sizeof(uint32_t) * qnum, s));
+            dim3 grid(std::min<uint32_t>((d.n + 256 * 64 - 1) / (256 * 64), 1024), (qnum + kBoxQ - 1) / kBoxQ);
+            box_count_kernel<<<grid, 256, 0, s>>>(d.attrs, d.n, a, p.lb, p.rb, qnum, p.box);
+        }
     }
     // processing order: most cells first
     iota_kernel<<<nb, tb, 0, s>>>(p.task + p.max_q, qnum);

@@ -213,3 +213,32 @@ def test_graph_rows_not_a_multiple_of_16_bytes():
         assert np.array_equal(as_u32(ids), ref_ids)
         assert np.array_equal(dist.cpu().numpy(), ref_d)
         assert st["n_exp"] == ref_st[1] and st["n_cross"] == ref_st[2] and st["n_hops"] == ref_st[3]
+
+
+@pytest.mark.parametrize("which", ["small", "odd"])
+def test_box_counts_from_attribute_tiles(which, request):
+    """The plan's box counts (prefilter) come from the attribute tiles: tiles inside a box
+    add their counts, tiles that meet it are tested row by row.  Against the oracle's scan
+    of every point, on the queries' boxes and on edge boxes: the whole domain, empty boxes,
+    boxes that are one point, boxes whose bounds are attribute values of the data."""
+    c = request.getfixturevalue(which)
+    g = gf.Index.create(vectors=c.ds.vectors, attrs=c.ds.attrs.astype(np.float32), grid=c.ix.grid,
+                        l_quant=c.ix.l_quant, r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs,
+                        degree=c.ix.degree, cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels,
+                        keep_fp32=False)
+    rng = np.random.default_rng(3)
+    a = c.ds.attrs.shape[1]
+    at = c.ds.attrs
+    pts = at[rng.integers(0, at.shape[0], 40)]
+    lo = np.concatenate([c.ds.lo, np.full((1, a), -1), np.full((1, a), 5), pts, np.minimum(pts, at[:40]),
+                         at[rng.integers(0, at.shape[0], 40)] - 1]).astype(np.int32)
+    hi = np.concatenate([c.ds.hi, np.full((1, a), 20000), np.full((1, a), 4), pts, np.maximum(pts, at[:40]),
+                         at[rng.integers(0, at.shape[0], 40)] + 300]).astype(np.int32)
+    q = np.repeat(c.ds.queries[:1], lo.shape[0], 0)
+    plan = g.plan(lo.shape[0])
+    plan.build(dev(q), dev(lo), dev(hi), prefilter=0.5)
+    box = plan.read()[4]
+    assert np.array_equal(box, oracle.count_in_box(c.ds.attrs, lo, hi))
+    assert box[c.ds.lo.shape[0]] == at.shape[0] and box[c.ds.lo.shape[0] + 1] == 0
+    plan.close()
+    g.close()
