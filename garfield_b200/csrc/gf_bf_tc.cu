@@ -1191,15 +1191,21 @@ void free_bf_tc(DeviceIndex& d) {
     if (d.bf_ws) cudaFree(d.bf_ws);
     d.bf_ws = nullptr;
     d.bf_ws_bytes = 0;
-    void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean, d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_arange, d.bf_tcnt};
+    void* ptrs[] = {d.bf_x, d.bf_px, d.bf_mean, d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_arange, d.bf_tcnt,
+                    d.bf_sbox, d.bf_scnt};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     d.bf_x = nullptr;
-    d.bf_px = d.bf_mean = d.bf_tbox = d.bf_attrs = d.bf_arange = nullptr;
-    d.bf_rowpos = d.bf_tcnt = nullptr;
+    d.bf_px = d.bf_mean = d.bf_tbox = d.bf_attrs = d.bf_arange = d.bf_sbox = nullptr;
+    d.bf_rowpos = d.bf_tcnt = d.bf_scnt = nullptr;
     d.bf_ok = false;
     d.at_ok = false;
 }
+
+namespace {
+__global__ void super_tile_kernel(const float* __restrict__ tbox, const uint32_t* __restrict__ tcnt, uint32_t tiles,
+                                  uint32_t a8, uint32_t stiles, float* __restrict__ sbox, uint32_t* __restrict__ scnt);
+}  // namespace
 
 // Attribute tiles (every index): rows in the Morton order of their attributes, 128 per
 // tile, each tile's attribute bounds and the tile-padded attribute copy.  Used by the
@@ -1220,6 +1226,10 @@ gf_status attr_tiles_prepare(DeviceIndex& d) {
         if (!ck(cudaMalloc((void**)&d.bf_rowpos, sizeof(uint32_t) * (size_t)npad), "tile positions")) break;
         if (!ck(cudaMalloc((void**)&d.bf_arange, sizeof(float) * 2 * d.a), "attribute range")) break;
         if (!ck(cudaMalloc((void**)&d.bf_tcnt, sizeof(uint32_t) * tiles), "tile counts")) break;
+        const uint32_t stiles = (tiles + 31) / 32;  // super-tiles of 32 tiles (box counts)
+        if (!ck(cudaMalloc((void**)&d.bf_sbox, sizeof(float) * (size_t)stiles * 2 * tbox_stride(d.a)), "super-tiles"))
+            break;
+        if (!ck(cudaMalloc((void**)&d.bf_scnt, sizeof(uint32_t) * stiles), "super-tiles")) break;
         {
             std::vector<float> ar = attr_range(d);
             if (!ck(cudaMemcpy(d.bf_arange, ar.data(), sizeof(float) * 2 * d.a, cudaMemcpyHostToDevice), "range"))
@@ -1241,6 +1251,8 @@ gf_status attr_tiles_prepare(DeviceIndex& d) {
             // rowpos: sorted positions, then padding marks past n
             bf_tilebox_kernel<<<(tiles + 7) / 8, 256>>>(d.attrs, d.n, d.a, tbox_stride(d.a), tiles, d.bf_rowpos,
                                                         d.bf_tbox, d.bf_attrs, d.bf_rowpos, d.bf_tcnt);
+            super_tile_kernel<<<(stiles + 7) / 8, 256>>>(d.bf_tbox, d.bf_tcnt, tiles, tbox_stride(d.a), stiles,
+                                                         d.bf_sbox, d.bf_scnt);
             ck(cudaGetLastError(), "tile bounds");
             ck(cudaDeviceSynchronize(), "tile sort");
         }
@@ -1248,7 +1260,8 @@ gf_status attr_tiles_prepare(DeviceIndex& d) {
             if (pp) cudaFree(pp);
         if (st != GF_OK) break;
         d.bf_tiles = tiles;
-        d.bytes += sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a) + sizeof(float) * (size_t)npad * d.a +
+        d.bf_stiles = stiles;
+        d.bytes += sizeof(float) * (size_t)stiles * 2 * tbox_stride(d.a) + sizeof(uint32_t) * stiles + sizeof(float) * (size_t)tiles * 2 * tbox_stride(d.a) + sizeof(float) * (size_t)npad * d.a +
                    sizeof(uint32_t) * (size_t)npad + sizeof(float) * 2 * d.a + sizeof(uint32_t) * tiles;
         d.at_ok = true;
     } while (0);
@@ -1320,16 +1333,58 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
 }
 
 namespace {
+constexpr uint32_t kSuper = 32;  // tiles per super-tile of the box counts
+
+// Bounds and counts of each super-tile (kSuper consecutive tiles, one warp each).
+__global__ void super_tile_kernel(const float* __restrict__ tbox, const uint32_t* __restrict__ tcnt, uint32_t tiles,
+                                  uint32_t a8, uint32_t stiles, float* __restrict__ sbox, uint32_t* __restrict__ scnt) {
+    const uint32_t lane = lane_id();
+    const uint32_t st = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (st >= stiles) return;
+    const uint32_t t = st * kSuper + lane;
+    uint32_t c = t < tiles ? tcnt[t] : 0u;
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(kFull, c, o);
+    if (lane == 0) scnt[st] = c;
+    for (uint32_t j = 0; j < a8; ++j) {
+        float lo = t < tiles ? tbox[(size_t)t * 2 * a8 + j] : __int_as_float(0x7f800000);
+        float hi = t < tiles ? tbox[(size_t)t * 2 * a8 + a8 + j] : -__int_as_float(0x7f800000);
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = fminf(lo, __shfl_xor_sync(kFull, lo, o));
+            hi = fmaxf(hi, __shfl_xor_sync(kFull, hi, o));
+        }
+        if (lane == 0) {
+            sbox[(size_t)st * 2 * a8 + j] = lo;
+            sbox[(size_t)st * 2 * a8 + a8 + j] = hi;
+        }
+    }
+}
+
+// Whether bounds [b, b + a8) .. [b + a8, b + 2 a8) meet / lie inside the box (a attributes).
+__device__ __forceinline__ void meet_inside(const float* b, uint32_t a, uint32_t a8, const float* lo, const float* hi,
+                                            bool& meet, bool& inside) {
+    meet = inside = true;
+#pragma unroll
+    for (uint32_t j = 0; j < kMaxAttr; ++j) {
+        if (j < a) {
+            const float tl = b[j], th = b[a8 + j];
+            meet = meet & (tl <= hi[j]) & (lo[j] <= th);
+            inside = inside & (lo[j] <= tl) & (th <= hi[j]);
+        }
+    }
+    inside = inside & meet;
+}
+
 // Points inside each query box (prefiltering_tag_elements, real_dataset_adapter.cuh:347-387)
-// from the attribute tiles, one warp per query: every tile's bounds are tested; a tile that
-// lies inside the box adds its count of points with numeric attributes, a tile that meets the
-// box without lying inside it has its 128 rows tested one by one (4 per lane), and the
-// others add nothing.  The counts equal those of testing every point (closed intervals; a
-// NaN is inside no box), at a fraction of the reads: a box meets few tiles partially.
-__global__ void box_count_tiles_kernel(const float* __restrict__ tbox, const float* __restrict__ pattrs,
-                                       const uint32_t* __restrict__ tcnt, uint32_t tiles, uint32_t a, uint32_t a8,
-                                       const float* __restrict__ lb, const float* __restrict__ rb, uint32_t qnum,
-                                       uint32_t* __restrict__ box) {
+// from the attribute tiles, one warp per query, two levels: super-tiles (32 consecutive
+// tiles of the attribute-Morton order) then tiles.  A (super-)tile that lies inside the box
+// adds its count of points with numeric attributes; one that meets the box without lying
+// inside it is opened (its tiles, or its 128 rows, 4 per lane); the others add nothing.  The
+// counts equal those of testing every point (closed intervals; a NaN is inside no box).
+__global__ void box_count_tiles_kernel(const float* __restrict__ sbox, const uint32_t* __restrict__ scnt,
+                                       uint32_t stiles, const float* __restrict__ tbox,
+                                       const float* __restrict__ pattrs, const uint32_t* __restrict__ tcnt,
+                                       uint32_t tiles, uint32_t a, uint32_t a8, const float* __restrict__ lb,
+                                       const float* __restrict__ rb, uint32_t qnum, uint32_t* __restrict__ box) {
     const uint32_t lane = lane_id();
     const uint32_t q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (q >= qnum) return;
@@ -1340,34 +1395,31 @@ __global__ void box_count_tiles_kernel(const float* __restrict__ tbox, const flo
         hi[j] = j < a ? rb[(size_t)q * a + j] : 0.0f;
     }
     uint32_t cnt = 0;
-    for (uint32_t t0 = 0; t0 < tiles; t0 += 32) {
-        const uint32_t t = t0 + lane;
+    for (uint32_t s0 = 0; s0 < stiles; s0 += 32) {
+        const uint32_t st = s0 + lane;
         bool meet = false, inside = false;
-        if (t < tiles) {
-            meet = inside = true;
-            const float* tb = tbox + (size_t)t * 2 * a8;
+        if (st < stiles) meet_inside(sbox + (size_t)st * 2 * a8, a, a8, lo, hi, meet, inside);
+        if (inside) cnt += scnt[st];
+        uint32_t ps = __ballot_sync(kFull, meet && !inside);
+        while (ps) {
+            const uint32_t ss = s0 + __ffs(ps) - 1;
+            ps &= ps - 1;
+            const uint32_t t = ss * kSuper + lane;
+            bool tm = false, ti = false;
+            if (t < tiles) meet_inside(tbox + (size_t)t * 2 * a8, a, a8, lo, hi, tm, ti);
+            if (ti) cnt += tcnt[t];
+            uint32_t pt = __ballot_sync(kFull, tm && !ti);
+            while (pt) {
+                const uint32_t tt = ss * kSuper + __ffs(pt) - 1;
+                pt &= pt - 1;
+                for (uint32_t r = lane; r < kBN; r += 32) {
+                    const float* pa = pattrs + ((size_t)tt * kBN + r) * a;
+                    bool ok = true;
 #pragma unroll
-            for (uint32_t j = 0; j < kMaxAttr; ++j) {
-                if (j < a) {
-                    const float tl = tb[j], th = tb[a8 + j];
-                    meet = meet & (tl <= hi[j]) & (lo[j] <= th);
-                    inside = inside & (lo[j] <= tl) & (th <= hi[j]);
+                    for (uint32_t j = 0; j < kMaxAttr; ++j)
+                        if (j < a) ok = ok & (pa[j] >= lo[j]) & (pa[j] <= hi[j]);
+                    cnt += ok;
                 }
-            }
-            inside = inside & meet;
-        }
-        if (inside) cnt += tcnt[t];
-        uint32_t pm = __ballot_sync(kFull, meet && !inside);
-        while (pm) {
-            const uint32_t tt = t0 + __ffs(pm) - 1;
-            pm &= pm - 1;
-            for (uint32_t r = lane; r < kBN; r += 32) {
-                const float* pa = pattrs + ((size_t)tt * kBN + r) * a;
-                bool ok = true;
-#pragma unroll
-                for (uint32_t j = 0; j < kMaxAttr; ++j)
-                    if (j < a) ok = ok & (pa[j] >= lo[j]) & (pa[j] <= hi[j]);
-                cnt += ok;
             }
         }
     }
@@ -1378,8 +1430,9 @@ __global__ void box_count_tiles_kernel(const float* __restrict__ tbox, const flo
 
 void box_count_tiles(const DeviceIndex& d, const float* lb, const float* rb, uint32_t qnum, uint32_t* box,
                      cudaStream_t s) {
-    box_count_tiles_kernel<<<(qnum + 7) / 8, 256, 0, s>>>(d.bf_tbox, d.bf_attrs, d.bf_tcnt, d.bf_tiles, d.a,
-                                                          tbox_stride(d.a), lb, rb, qnum, box);
+    box_count_tiles_kernel<<<(qnum + 7) / 8, 256, 0, s>>>(d.bf_sbox, d.bf_scnt, d.bf_stiles, d.bf_tbox, d.bf_attrs,
+                                                          d.bf_tcnt, d.bf_tiles, d.a, tbox_stride(d.a), lb, rb, qnum,
+                                                          box);
 }
 
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k) { return d.bf_ok && k >= 1 && k <= kMaxK; }

@@ -93,6 +93,9 @@ struct DeviceIndex {
     bool bf_ok = false;
     bool at_ok = false;          // attribute tiles (bf_tbox, bf_attrs, bf_rowpos, bf_tcnt) built
     uint32_t* bf_tcnt = nullptr; // bf_tiles: points of each tile whose attributes are all numbers
+    uint32_t bf_stiles = 0;      // super-tiles: 32 consecutive tiles (box counts)
+    float* bf_sbox = nullptr;    // bf_stiles x 2 x a8: attribute bounds per super-tile
+    uint32_t* bf_scnt = nullptr; // bf_stiles: sum of the super-tile's bf_tcnt
     uint32_t bf_dp = 0, bf_tiles = 0;   // padded row length (multiple of 16), point tiles
     float bf_scale = 1.0f, bf_dmax = 0.0f;  // power-of-two scale s, largest residual |x - x^|
     void* bf_x = nullptr;        // bf_tiles x 128 x bf_dp halves
