@@ -49,6 +49,12 @@ struct SArgs {
     const uint32_t* __restrict__ cells;
     const uint32_t* __restrict__ box;  // box counts (only when prefilter > 0)
     const uint32_t* __restrict__ skip = nullptr;  // queries answered by the tensor-core exact scan
+    // attribute tiles of a whole index (exact route without a cell view; NULL: scan the cells)
+    const float* __restrict__ sbox = nullptr;   // super-tile bounds (32 tiles each)
+    const float* __restrict__ tbox = nullptr;   // tile bounds (128 rows each)
+    const float* __restrict__ tattrs = nullptr; // row attributes (NaN past n)
+    const uint32_t* __restrict__ trow = nullptr; // row -> position
+    uint32_t nstiles = 0, ntiles = 0, a8 = 0;
     const uint32_t* __restrict__ task;
     const uint32_t* __restrict__ entry;
     uint32_t* queue;
@@ -367,7 +373,53 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
     __syncwarp();
     uint32_t nb = 0, ndist = 0;
     const uint32_t flush_at = A.bcap - 32;
-    for (uint32_t ci = next_cell(A, cl, nc, 0); ci < nc;) {
+    if (A.tbox) {
+        // whole index: the in-box points are found through the attribute tiles (super-tiles,
+        // then tiles that meet the box, then their rows) instead of every row of the cells.
+        // The same points are evaluated with the same distances, and the K smallest keys do
+        // not depend on the order, so the result is the cell scan's.
+        const float* lb = w.lb(A);
+        const float* rb = w.rb(A);
+        auto meets = [&](const float* b) {
+            bool m = true;
+            for (uint32_t j = 0; j < A.a; ++j) m = m && (b[j] <= rb[j]) && (lb[j] <= b[A.a8 + j]);
+            return m;
+        };
+        for (uint32_t s0 = 0; s0 < A.nstiles; s0 += 32) {
+            const uint32_t st = s0 + lane;
+            uint32_t ps = __ballot_sync(kFull, st < A.nstiles && meets(A.sbox + (size_t)st * 2 * A.a8));
+            while (ps) {
+                const uint32_t ss = s0 + __ffs(ps) - 1;
+                ps &= ps - 1;
+                const uint32_t t = ss * 32 + lane;
+                uint32_t pt = __ballot_sync(kFull, t < A.ntiles && meets(A.tbox + (size_t)t * 2 * A.a8));
+                while (pt) {
+                    const uint32_t tt = ss * 32 + __ffs(pt) - 1;
+                    pt &= pt - 1;
+                    for (uint32_t g = 0; g < 4; ++g) {
+                        const uint32_t r = tt * 128 + g * 32 + lane;
+                        const bool ok = in_box(A.tattrs, r, A.a, lb, rb);  // NaN rows (padding) never
+                        append(w.P(A), nb, ok, ok ? __ldg(A.trow + r) : 0u);
+                        if (nb > flush_at) {
+                            __syncwarp();
+                            const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, w.T(A)[A.K - 1], 0ll);
+                            ndist += nb;
+                            merge_step(A, w, A.K, 0, ns, false);
+                            nb = 0;
+                        }
+                    }
+                }
+            }
+        }
+        if (nb) {
+            __syncwarp();
+            const uint32_t ns = eval_sort<NCH, BYTES>(A, w.base, nb, w.T(A)[A.K - 1], 0ll);
+            ndist += nb;
+            merge_step(A, w, A.K, 0, ns, false);
+            nb = 0;
+        }
+    }
+    for (uint32_t ci = A.tbox ? nc : next_cell(A, cl, nc, 0); ci < nc;) {
         const uint32_t cell = cl[ci], lo = A.seg[cell], hi = A.seg[cell + 1];
         const uint32_t cn = next_cell(A, cl, nc, ci + 1);
         const long long vsh = cell_vsh(A, cell);
@@ -1126,6 +1178,15 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     blocks = std::min(blocks, need_blocks);
     GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
     if (!(view && view->accumulate_stats)) GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
+    if (!view && !fullgraph && d.at_ok) {  // exact route through the attribute tiles
+        A.sbox = d.bf_sbox;
+        A.tbox = d.bf_tbox;
+        A.tattrs = d.bf_attrs;
+        A.trow = d.bf_rowpos;
+        A.nstiles = d.bf_stiles;
+        A.ntiles = d.bf_tiles;
+        A.a8 = (d.a + 3) & ~3u;
+    }
     if (P.exact_tc) {
         // exact-route queries: the tensor-core exact scan writes their rows, the search kernel
         // skips them
