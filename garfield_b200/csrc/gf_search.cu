@@ -1153,11 +1153,15 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t lg = 0;
     while ((1u << lg) < hs) ++lg;
     A.hshift = 32 - lg;
-    // staging: up to 16 rows of an odd number of 16-byte chunks, at most 4.5 KB per warp
+    // staging: up to 16 rows of an odd number of 16-byte chunks, at most 4.5 KB per warp; rows
+    // of 1 KB and more get up to 12.5 KB, so that a copy round still brings 8 rows (with 4.5 KB
+    // a 768-dim fp16 row allowed 2, leaving 28 of 32 lanes idle and the copy latency exposed
+    // once per 2 rows)
     const uint32_t nch16 = (A.nch + 15) / 16 * 16;
     A.stage_stride = A.nch | 1u;
+    const uint32_t stage_budget = A.nch >= 64 ? 12800u : 4608u;
     uint32_t sr = 16;
-    while (sr > 1 && sr * A.stage_stride * 16 > 4608) sr >>= 1;
+    while (sr > 1 && sr * A.stage_stride * 16 > stage_budget) sr >>= 1;
     A.stage_rows = sr;
     make_layout(A, nch16, bytes);
 
