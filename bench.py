@@ -19,9 +19,9 @@ length in a fixed sweep whose recall on the ground-truth sample reaches the targ
                                                             all-gathered over NCCL and merged (row e)
   python bench.py --mode bruteforce                        exact filtered k-NN of all queries: tensor-core
                                                             pass vs the CUDA-core kernel
-  python bench.py --impl reference-cuda                     the reference's own CUDA binary: prints
-                                                            "unavailable" (it faults on B200, see
-                                                            REF_CUDA_FAULT)
+  python bench.py --impl reference-cuda                     the reference's own CUDA search
+                                                            (oracle/_ref/realdataset_search) and our
+                                                            CLI on the same reference-format files
 Multi-GPU (torchrun): every rank holds a replica of the index and runs the full query
 batch (weak scaling); the only collective is the max-over-ranks of the timings.
 """
@@ -102,15 +102,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
-def ncu_traffic() -> float | None:
-    """DRAM bytes of one search launch from the committed ncu summary (None if absent)."""
+def ncu_traffic() -> tuple[float | None, str]:
+    """DRAM bytes (read + write) of one search launch and where the figure comes from: the
+    committed ncu summary of the search kernel (profiles/gmg_search_kernel_config2.md, line
+    "traffic_bytes_per_launch: N", with the capture it was read from), not this run."""
     import re
     p = ROOT / "profiles" / "gmg_search_kernel_config2.md"
     if p.exists():
-        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
+        txt = p.read_text()
+        m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", txt)
         if m:
-            return float(m.group(1))
-    return None
+            cap = re.search(r"traffic_capture:\s*(.+)", txt)
+            return float(m.group(1)), ("ncu capture recorded in profiles/gmg_search_kernel_config2.md"
+                                       + (f" ({cap.group(1).strip()})" if cap else "") + ", not measured by this run")
+    return None, "no ncu capture"
 
 
 def peak_hbm() -> tuple[float, str]:
@@ -166,7 +171,10 @@ def dataset_and_index(args, device):
 
 
 def cpu_baseline(ds, sample: int, threads: int, k: int = 10) -> dict:
-    """The oracle's exact filtered scan (naive_brute_force_with_filter restated) on host cores."""
+    """The CPU exact filtered scan on host cores over `sample` queries: the reference's own
+    naive_brute_force_with_filter (compiled from its sources, oracle/_ref/ref_golden) under
+    omp parallel for when that binary is built (kind "reference"), with the oracle's
+    restatement timed beside it; the restatement alone otherwise (kind "port")."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
     q = ds.queries[:sample]
@@ -174,17 +182,34 @@ def cpu_baseline(ds, sample: int, threads: int, k: int = 10) -> dict:
     t0 = time.perf_counter()
     oracle.bruteforce(ds.vectors, ds.attrs, q, ds.lo[:sample], ds.hi[:sample], k, threads)
     dt = time.perf_counter() - t0
-    return {"value": sample / dt, "unit": "queries/s", "cores": threads, "kind": "port",
-            "sample": f"{sample} queries, exact filtered scan over all {ds.vectors.shape[0]} points "
-                      f"({dt:.1f}s)"}
+    port = sample / dt
+    binary = _ref_binary("ref_golden")
+    if binary is None:
+        return {"value": port, "unit": "queries/s", "cores": threads, "kind": "port",
+                "sample": f"{sample} queries, exact filtered scan over all {ds.vectors.shape[0]} points "
+                          f"({dt:.1f}s)"}
+    sec = _time_reference_scan(binary, ds, np.arange(sample), sample, threads)[0]
+    return {"value": sample / sec, "unit": "queries/s", "cores": threads, "kind": "reference",
+            "sample": f"{sample} queries, exact filtered scan over all {ds.vectors.shape[0]} points ({sec:.1f}s): "
+                      f"the reference's naive_brute_force_with_filter under omp parallel for",
+            "port_value": round(port, 2)}
 
 
 # --------------------------------------------------------------------------- arms
 
 def run_ours(args):
+    """Default mode.  One GPU: plan + search of config 2's 10k queries per step.  N GPUs
+    (torchrun, one rank per GPU): every rank holds a replica of the index (config 2 fits
+    one GPU) and searches its own batch of 10k queries per step, drawn from the same
+    distribution (rank r: query stream r, synth.query_stream; rank 0's batch is the
+    one-GPU batch), with no data-path collective: weak scaling, value = N x 10k queries /
+    (max over ranks of the step time).  Beside it, "strong" times the one-GPU batch split
+    over the ranks (dist.shard_range; total work fixed)."""
     import torch
     import torch.distributed as dist
     import garfield_b200 as gf
+    from garfield_b200 import synth
+    from garfield_b200.dist import shard_range
 
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -194,7 +219,23 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
-    ds, ix = dataset_and_index(args, device)
+
+    def reduce_max(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def reduce_sum(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    ds0, ix = dataset_and_index(args, device)
+    ds = synth.query_stream(ds0, rank) if world > 1 else ds0
     t0 = time.time()
     index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
                             r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
@@ -226,13 +267,14 @@ def run_ours(args):
         plan.search(sp(L, width), stream, ids=ids, dist=dist_t)
 
     def find_L(width):
-        """Smallest L of the sweep whose recall reaches the target at this width."""
+        """Smallest L of the sweep whose recall (mean over the ranks' samples) reaches the
+        target at this width; every rank takes the same steps."""
         sweep = []
         for L in ([args.L] if args.L else [x for x in L_SWEEP if x >= K]):
             with torch.cuda.stream(stream):
                 step(L, width)
             stream.synchronize()
-            r = gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)
+            r = reduce_sum(gf.recall(ids[:S].cpu().numpy().view(np.uint32), gt)) / world
             sweep.append((L, round(r, 4)))
             log(f"width={width} L={L} recall@{K}={r:.4f}")
             if r >= args.target:
@@ -249,7 +291,7 @@ def run_ours(args):
                 step(L, width)
             b.record(stream)
         b.synchronize()
-        return a.elapsed_time(b) / n
+        return reduce_max(a.elapsed_time(b) / n)
 
     widths = [args.width] if args.width else [1, 2, 4, 8]
     best = None
@@ -262,35 +304,37 @@ def run_ours(args):
     args.width, L, recall, _, sweep = best
     # L2 flush buffer (> 126 MB L2)
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def timed(build, search, steps):
+        """Device time of `steps` steps (build + search per step), L2 flushed between
+        steps; returns (total ms max over ranks, plan ms list, search ms list, clocks)."""
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            for i in range(steps):
+                with torch.cuda.stream(stream):
+                    flush.fill_(float(i))
+                    ev[i][0].record(stream)
+                    build()
+                    ev[i][1].record(stream)
+                    search()
+                    ev[i][2].record(stream)
+            stream.synchronize()
+        torch.cuda.synchronize()
+        total = reduce_max(float(sum(a.elapsed_time(c) for a, b, c in ev)))
+        return total, [a.elapsed_time(b) for a, b, c in ev], [b.elapsed_time(c) for a, b, c in ev], clocks
+
     for _ in range(args.warmup):
         with torch.cuda.stream(stream):
             step(L, args.width)
-    stream.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        for i in range(args.steps):
-            with torch.cuda.stream(stream):
-                flush.fill_(float(i))
-                ev[i][0].record(stream)
-                plan.build(qd, lod, hid, args.prefilter, stream)
-                ev[i][1].record(stream)
-                plan.search(sp(L, args.width), stream, ids=ids, dist=dist_t)
-                ev[i][2].record(stream)
-        stream.synchronize()
-    torch.cuda.synchronize()
-    step_ms = [a.elapsed_time(c) for a, b, c in ev]
-    plan_ms = [a.elapsed_time(b) for a, b, c in ev]
-    search_ms = [b.elapsed_time(c) for a, b, c in ev]
+    total_ms, plan_ms, search_ms, clocks = timed(lambda: plan.build(qd, lod, hid, args.prefilter, stream),
+                                                 lambda: plan.search(sp(L, args.width), stream, ids=ids, dist=dist_t),
+                                                 args.steps)
     st = plan.stats()
-    total_ms = float(sum(step_ms))
-    if world > 1:
-        t = torch.tensor([total_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     value = world * qnum / (ms_per_step / 1e3)
     # end to end through the C ABI from pinned host buffers
@@ -301,6 +345,8 @@ def run_ours(args):
     params = sp(L, args.width)
     for _ in range(args.warmup):
         index.search_host(qh, lh, hh, e2e_plan, params, prefilter=args.prefilter, stream=stream)
+    if world > 1:
+        dist.barrier()
     e_ms = []
     for i in range(args.steps):
         with torch.cuda.stream(stream):
@@ -311,13 +357,33 @@ def run_ours(args):
         b.record(stream)
         b.synchronize()
         e_ms.append(a.elapsed_time(b))
-    e2e_total = float(sum(e_ms))
-    if world > 1:
-        t = torch.tensor([e2e_total], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_total = float(t.item())
+    e2e_total = reduce_max(float(sum(e_ms)))
     e2e_value = world * qnum / (e2e_total / args.steps / 1e3)
     assert np.array_equal(res_ids, ids.cpu().numpy().view(np.uint32))
+    strong = None
+    if world > 1:
+        # strong scaling: the one-GPU batch (query stream 0) split over the ranks
+        s0, s1 = shard_range(ds0.queries.shape[0], rank, world)
+        sq = torch.from_numpy(ds0.queries[s0:s1]).to(device)
+        sl = torch.from_numpy(ds0.lo[s0:s1].astype(np.float32)).to(device)
+        sh = torch.from_numpy(ds0.hi[s0:s1].astype(np.float32)).to(device)
+        splan = index.plan(max(1, s1 - s0))
+        sids = torch.empty((max(1, s1 - s0), K), dtype=torch.int32, device=device)
+        sdist = torch.empty((max(1, s1 - s0), K), dtype=torch.float32, device=device)
+        for _ in range(args.warmup):
+            with torch.cuda.stream(stream):
+                splan.build(sq, sl, sh, args.prefilter, stream)
+                splan.search(sp(L, args.width), stream, ids=sids, dist=sdist)
+        s_total, s_plan, s_search, _ = timed(lambda: splan.build(sq, sl, sh, args.prefilter, stream),
+                                             lambda: splan.search(sp(L, args.width), stream, ids=sids, dist=sdist),
+                                             args.steps)
+        s_ms = s_total / args.steps
+        strong = {"value": round(ds0.queries.shape[0] / (s_ms / 1e3), 1), "unit": "queries/s",
+                  "ms_per_step": round(s_ms, 4), "queries_per_rank": s1 - s0,
+                  "plan_ms": round(reduce_max(float(np.mean(s_plan))), 4),
+                  "search_ms": round(reduce_max(float(np.mean(s_search))), 4),
+                  "workload": f"the one-GPU batch of {ds0.queries.shape[0]} queries split over {world} ranks, same L"}
+        splan.close()
     # roofline of the search kernel: algorithmic bytes from the device counters
     D, a_attr = ds.vectors.shape[1], ds.attrs.shape[1]
     bytes_step = (st["n_dist"] * (((D + 7) // 8 * 8) * 2 + a_attr * 4) + st["n_exp"] * ix.degree * 4 +
@@ -325,6 +391,7 @@ def run_ours(args):
     kern_s = float(np.mean(search_ms)) / 1e3
     achieved = bytes_step / kern_s / 1e9
     peak, peak_kind = peak_hbm()
+    traffic, traffic_src = ncu_traffic()
     out = {
         "metric": f"QPS at recall@{K}>={args.target} ({SHAPES[args.config].format(sel=args.sel)})",
         "value": round(value, 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
@@ -333,9 +400,11 @@ def run_ours(args):
         "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
         "config": {"workload": (f"config{args.config}: {ds.vectors.shape[0]} x {D} fp32, grid "
                                 f"{'x'.join(str(int(g)) for g in ix.grid)}, R={ix.degree}, E={ix.cross_e}, C={args.C}, "
-                                f"{qnum} queries, sel {args.sel:.0%}, k={K}"),
+                                f"{qnum} queries per GPU, sel {args.sel:.0%}, k={K}"),
                    "L": L, "width": args.width, f"recall_at_{K}": round(recall, 4), "recall_sample": S,
-                   "l2": "flushed (256 MiB write) between timed steps", "parallelism": f"replicas x{world}",
+                   "l2": "flushed (256 MiB write) between timed steps",
+                   "parallelism": (f"replicas x{world}, a distinct batch of {qnum} queries per rank" if world > 1
+                                   else "1 GPU"),
                    "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
                    "prefilter": args.prefilter, "exact_route": ("tensor-core exact scan" if args.exact_tc
                                                                 else "fp16 warp scan"), "n_exact": int(st["n_exact"]),
@@ -345,7 +414,7 @@ def run_ours(args):
         "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                 "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(qnum * K * 4)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": ncu_traffic(),
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
                      "kernel": "gmg_search_kernel", "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": int(bytes_step),
                      "counters": {k: int(v) for k, v in st.items()}},
@@ -354,8 +423,12 @@ def run_ours(args):
         # search (the CUB scan and radix-sort kernels of the planner are library launches)
         "gpu_launches": 8 * args.steps,
     }
+    if strong is not None:
+        out["strong"] = strong
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1, K)
+    plan.close()
+    e2e_plan.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -731,52 +804,219 @@ def run_sharded(args):
         print(json.dumps(out), flush=True)
 
 
+def _ref_binary(name: str) -> Path | None:
+    p = ROOT / "oracle" / "_ref" / name
+    return p if p.exists() and os.access(p, os.X_OK) else None
+
+
+def _write_query_files(d: Path, ds) -> dict:
+    from garfield_b200 import write_attrs, write_fvecs, write_ranges
+    d.mkdir(parents=True, exist_ok=True)
+    paths = {"data": d / "base.fvecs", "attrs": d / "base.attrs", "queries": d / "query.fvecs",
+             "ranges": d / "query.range"}
+    write_fvecs(paths["data"], ds.vectors)
+    write_attrs(paths["attrs"], ds.attrs)
+    write_fvecs(paths["queries"], ds.queries)
+    write_ranges(paths["ranges"], ds.lo, ds.hi)
+    return {k: str(v) for k, v in paths.items()}
+
+
+def _time_reference_scan(binary: Path, ds, rows: np.ndarray, chunk: int, threads: int) -> list:
+    """Wall seconds of the reference's naive_brute_force_with_filter (oracle/_ref/ref_golden
+    bf_omp) over consecutive chunks of the query rows `rows`, `threads` OpenMP threads."""
+    import shutil
+    import tempfile
+    from garfield_b200 import write_fvecs, write_ranges
+    tmp = Path(tempfile.mkdtemp(prefix="gf_refcpu_"))
+    try:
+        base = _write_query_files(tmp, ds)
+        write_fvecs(tmp / "q.fvecs", ds.queries[rows])
+        write_ranges(tmp / "q.range", ds.lo[rows], ds.hi[rows])
+        r = subprocess.run([str(binary), "bf_omp", base["data"], base["attrs"], str(tmp / "q.fvecs"),
+                            str(tmp / "q.range"), "10", str(threads), str(chunk), str(tmp / "out.u32")],
+                           capture_output=True, text=True, timeout=1200)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ref_golden bf_omp failed: {r.stderr[-500:]}")
+    return [float(line.split()[1]) for line in r.stdout.splitlines() if line.startswith("seconds ")]
+
+
 def run_reference_cpu(args):
-    """Reference arm: the CPU exact filtered scan on the host cores, same metric/config."""
+    """Reference arm: the reference's own CPU exact filtered scan on the host cores.
+
+    naive_brute_force_with_filter (gpu_graph.cu:10782-10812) compiled from the reference's
+    sources (oracle/_ref/ref_golden, mode bf_omp) and called per query under omp parallel
+    for, as realdataset_search.cu:2330-2335 does, with all host threads; each step is a
+    bounded sample of the 10k queries.  Without that binary the oracle's restatement of
+    the same scan (oracle/gf_oracle.c) is timed instead (kind "port")."""
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return
     from garfield_b200 import synth
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle
     ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
     threads = os.cpu_count() or 1
     S = args.ref_sample
-    oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[:2], ds.lo[:2], ds.hi[:2], 10, threads)
-    times = []
-    for i in range(args.warmup + args.steps):
-        s0 = (i * S) % max(1, ds.queries.shape[0] - S)
-        t0 = time.perf_counter()
-        oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[s0:s0 + S], ds.lo[s0:s0 + S], ds.hi[s0:s0 + S], 10,
-                          threads)
-        if i >= args.warmup:
-            times.append(time.perf_counter() - t0)
+    binary = _ref_binary("ref_golden")
+    kind = "reference" if binary else "port"
+    steps = args.warmup + args.steps
+    starts = [(i * S) % max(1, ds.queries.shape[0] - S) for i in range(steps)]
+    rows = np.concatenate([np.arange(s0, s0 + S) for s0 in starts])
+    if binary:
+        times = _time_reference_scan(binary, ds, rows, S, threads)[args.warmup:]
+    else:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle
+        times = []
+        for i, s0 in enumerate(starts):
+            sl = slice(s0, s0 + S)
+            t0 = time.perf_counter()
+            oracle.bruteforce(ds.vectors, ds.attrs, ds.queries[sl], ds.lo[sl], ds.hi[sl], 10, threads)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
     value = S / float(np.mean(times))
+    what = ("naive_brute_force_with_filter compiled from the reference's sources, one call per query under "
+            "omp parallel for" if binary else "the oracle's restatement of naive_brute_force_with_filter")
     out = {
         "impl": "reference", "metric": "QPS at recall@10>=0.95 (1M x 128, 2 attrs, 10% sel.)",
         "value": round(value, 2), "unit": "queries/s", "n_gpus": int(os.environ.get("WORLD_SIZE", 1)),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(float(np.mean(times)) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
-        "config": {"workload": "config2: 1M x 128 fp32, 2 attrs, 10k queries, sel 10%, k=10",
-                   "step": f"{S} queries (bounded sample), exact scan (recall 1.0)"},
-        "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": f"{S} queries per step, exact filtered scan over {ds.vectors.shape[0]} points"},
+        "config": {"workload": (f"config2: {ds.vectors.shape[0]} x 128 fp32, 2 attrs, {ds.queries.shape[0]} queries, "
+                                f"sel {args.sel:.0%}, k=10"),
+                   "step": f"{S} queries (bounded sample), exact scan (recall 1.0): {what}"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "queries/s", "cores": threads, "kind": kind,
+                         "sample": f"{S} queries per step, exact filtered scan over {ds.vectors.shape[0]} points "
+                                   f"({what}; file loading not timed)"},
         "e2e": {"value": round(value, 2), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
 
 
-REF_CUDA_FAULT = (
-    "the reference's realdataset_search (built from source for sm_100a) raised an illegal memory access on "
-    "B200: prefiltering_tag_elements is launched <<<qnum, 32>>> without dynamic shared memory "
-    "(real_dataset_adapter.cuh:501) but writes the query box into extern __shared__ memory (:348-353); "
-    "not run again")
+def _cell_major(ds, ix, gt):
+    """The same dataset and index with point ids renumbered cell-major (ids of cell 0
+    first, increasing old id inside a cell).  The reference's load_clustering histograms
+    cells as id / 62500 (tools.cuh:590), which is only the grid's cell when ids are
+    cell-major; positions, graphs (local ids) and cross edges (local ids) are unchanged
+    by the renumbering, so both arms search the same index."""
+    from types import SimpleNamespace
+    from garfield_b200 import indexbuild
+    order = np.argsort(ix.cell_of, kind="stable")
+    inv = np.empty_like(order)
+    inv[order] = np.arange(order.size)
+    ds2 = SimpleNamespace(vectors=ds.vectors[order], attrs=ds.attrs[order], queries=ds.queries, lo=ds.lo, hi=ds.hi)
+    ix2 = indexbuild.GmgArrays(ix.grid, ix.l_quant, ix.r_quant, ix.slices[order], ix.cell_of[order], ix.graphs,
+                               ix.cross[order], ix.labels[order], ix.degree, ix.cross_e)
+    gt2 = np.where(gt == 0xFFFFFFFF, gt, inv[np.minimum(gt, order.size - 1)]).astype(np.uint32)
+    return ds2, ix2, gt2
+
+
+def _read_csv(path: Path) -> list:
+    rows = []
+    for line in path.read_text().strip().splitlines()[1:]:
+        f = line.split(",")
+        rows.append({"ef": int(f[0]), "recall": float(f[1]), "qps": float(f[2]), "cost1": float(f[4]),
+                     "cost2": float(f[5]), "cost3": float(f[6])})
+    return rows
+
+
+def _best(rows: list, target: float):
+    ok = [r for r in rows if r["recall"] >= target]
+    return max(ok, key=lambda r: r["qps"]) if ok else None
 
 
 def run_reference_cuda(args):
-    """The reference's own CUDA search: not run (it faults on this GPU, see REF_CUDA_FAULT)."""
-    print(json.dumps({"impl": "reference-cuda", "unavailable": REF_CUDA_FAULT}), flush=True)
+    """The reference's own CUDA search beside ours on the same files (row N4 of the plan).
+
+    oracle/_ref/realdataset_search is the reference's realdataset_search built from its
+    sources by oracle/build_ref.sh (2 attributes on a 4x4 grid, no range override, and
+    two memory-safety fixes of its planner launches).  Both binaries read the same
+    reference-format files (config 2, ids renumbered cell-major, ground truth from the
+    GPU exact scan) with the reference's flags --prefilter 0.0 --postfilter 17 --degree 32;
+    the reference runs once per --alphas value (its fp16 scale factor; fp16 accumulation
+    overflows without one), ours (garfield_b200/bin/realdataset_search) once.  Each writes
+    the reference's CSV (ef, recall, qps = qnum / (cost1 + cost2 + cost3), ...).  Reported:
+    both sweeps, each side's best QPS at recall >= --target, and the same with the
+    search alone (qnum / cost3)."""
+    import torch
+    import garfield_b200 as gf
+    from garfield_b200 import indexbuild
+    ref = _ref_binary("realdataset_search")
+    ours = ROOT / "garfield_b200" / "bin" / "realdataset_search"
+    if ref is None:
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/realdataset_search is not built "
+                          "(oracle/build_ref.sh needs the reference checkout)"}), flush=True)
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ds, ix = dataset_and_index(args, device)
+    index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
+                            r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=True)
+    gt, _ = index.bruteforce(torch.from_numpy(ds.queries).cuda(), torch.from_numpy(ds.lo.astype(np.float32)).cuda(),
+                             torch.from_numpy(ds.hi.astype(np.float32)).cuda(), 10)
+    gt = gt.cpu().numpy().view(np.uint32)
+    index.close()
+    del index
+    torch.cuda.empty_cache()
+    ds2, ix2, gt2 = _cell_major(ds, ix, gt)
+    out_dir = Path(args.out_dir)
+    d = Path(args.cache) / "ref_files"
+    paths = indexbuild.write_files(d, "cfg2", ds2, ix2, gt=gt2)
+    flags = ["--data_path", paths["data_path"], "--query_path", paths["query_path"], "--range", paths["range"],
+             "--gt", paths["gt"], "--cagra_prefix", paths["cagra_prefix"], "--cagra_suffix", paths["cagra_suffix"],
+             "--global_graph", paths["global_graph"], "--grid", paths["grid"], "--attrs", paths["attrs"],
+             "--cluster", paths["cluster"], "--prefilter", "0.0", "--postfilter", "17", "--degree", str(ix.degree)]
+    out_dir.mkdir(parents=True, exist_ok=True)
+    runs = []
+    for alpha in args.alphas:
+        csv = d / f"reference_{alpha}.csv"
+        csv.unlink(missing_ok=True)
+        t0 = time.time()
+        r = subprocess.run([str(ref)] + flags + ["--result", str(csv), "--f2h_factor", str(alpha)],
+                           capture_output=True, text=True, timeout=args.ref_timeout)
+        log(f"reference alpha={alpha} rc={r.returncode} in {time.time() - t0:.0f}s")
+        (out_dir / f"reference_cuda_alpha{alpha}.log").write_text(
+            r.stdout[-100000:] + "\n---stderr---\n" + r.stderr[-20000:])
+        runs.append({"alpha": alpha, "rc": r.returncode, "rows": _read_csv(csv) if csv.exists() else []})
+        if r.returncode != 0 or "illegal" in (r.stdout + r.stderr):
+            log("reference run failed; not running it again")
+            break
+    csv = d / "ours.csv"
+    csv.unlink(missing_ok=True)
+    r = subprocess.run([str(ours)] + flags + ["--result", str(csv), "--f2h_factor", "1.0", "--width",
+                                              str(args.width or 4)], capture_output=True, text=True, timeout=600)
+    (out_dir / "ours_cli.log").write_text(r.stdout[-50000:] + "\n---stderr---\n" + r.stderr[-20000:])
+    mine = _read_csv(csv) if csv.exists() else []
+    ref_rows = [dict(row, alpha=run["alpha"]) for run in runs for row in run["rows"]]
+    for rows in (ref_rows, mine):
+        for row in rows:
+            row["search_qps"] = round(args.qnum / row["cost3"], 1) if row["cost3"] > 0 else None
+    best_ref, best_ours = _best(ref_rows, args.target), _best(mine, args.target)
+    best_ref_s = max((r for r in ref_rows if r["recall"] >= args.target), key=lambda r: r["search_qps"] or 0,
+                     default=None)
+    best_ours_s = max((r for r in mine if r["recall"] >= args.target), key=lambda r: r["search_qps"] or 0,
+                      default=None)
+    by_ef = {}
+    for row in ref_rows:
+        if row["ef"] not in by_ef or row["recall"] > by_ef[row["ef"]]:
+            by_ef[row["ef"]] = row["recall"]
+    recall_gap = {row["ef"]: round(row["recall"] - by_ef[row["ef"]], 4) for row in mine if row["ef"] in by_ef}
+    print(json.dumps({
+        "impl": "reference-cuda", "metric": f"QPS at recall@10>={args.target} (1M x 128, 2 attrs, {args.sel:.0%} sel.)",
+        "value": None if best_ref is None else best_ref["qps"], "unit": "queries/s",
+        "ours_value": None if best_ours is None else best_ours["qps"],
+        "qps_ratio": (None if not (best_ref and best_ours) else round(best_ours["qps"] / best_ref["qps"], 2)),
+        "search_only_ratio": (None if not (best_ref_s and best_ours_s) else
+                              round(best_ours_s["search_qps"] / best_ref_s["search_qps"], 2)),
+        "best_reference": best_ref, "best_ours": best_ours, "best_reference_search_only": best_ref_s,
+        "best_ours_search_only": best_ours_s, "recall_ours_minus_reference_by_ef": recall_gap,
+        # north star: graph-search recall within 0.5 points of the reference's at matched L
+        "recall_within_half_point": bool(recall_gap) and min(recall_gap.values()) >= -0.005,
+        "reference_runs": runs, "ours_rows": mine, "qnum": int(args.qnum),
+        "files": "config2, ids renumbered cell-major, ground truth = GPU exact scan",
+        "flags": "--prefilter 0.0 --postfilter 17 --degree 32 (ours adds --width and --f2h_factor 1.0)"}), flush=True)
 
 
 def main():
@@ -802,8 +1042,9 @@ def main():
     ap.add_argument("--cpu-sample", dest="cpu_sample", type=int, default=200)
     ap.add_argument("--ref-sample", dest="ref_sample", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", dest="no_cpu_baseline", action="store_true")
-    ap.add_argument("--cache", default="/tmp/gf_cache")
-    ap.add_argument("--alphas", type=float, nargs="+", default=[0.01])
+    ap.add_argument("--cache", default=str(ROOT / ".gf_cache"))  # synthetic indexes, git- and gpurun-ignored
+    ap.add_argument("--out-dir", dest="out_dir", default=str(ROOT / "gpurun_out"))  # logs of --impl reference-cuda
+    ap.add_argument("--alphas", type=float, nargs="+", default=[0.01, 0.005, 0.02])
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
     ap.add_argument("--mode", default="in-memory",
                     choices=["in-memory", "out-of-core", "sharded", "bruteforce", "fullgraph"])

@@ -55,7 +55,7 @@ namespace {
 using namespace dev;
 
 constexpr uint32_t kBM = 128;          // queries per tile (TMEM lanes)
-constexpr uint32_t kBN = 128;          // points per tile (accumulator columns)
+constexpr uint32_t kBN = kTileRows;    // points per tile (accumulator columns)
 constexpr uint32_t kKC = 64;           // elements per K chunk (8 core-matrix columns)
 constexpr uint32_t kChunkBytes = kBN * kKC * 2;  // 16 KB
 constexpr uint32_t kColBytes = kBN * 16;         // one 16-byte core-matrix column of 128 rows
@@ -1226,7 +1226,7 @@ gf_status attr_tiles_prepare(DeviceIndex& d) {
         if (!ck(cudaMalloc((void**)&d.bf_rowpos, sizeof(uint32_t) * (size_t)npad), "tile positions")) break;
         if (!ck(cudaMalloc((void**)&d.bf_arange, sizeof(float) * 2 * d.a), "attribute range")) break;
         if (!ck(cudaMalloc((void**)&d.bf_tcnt, sizeof(uint32_t) * tiles), "tile counts")) break;
-        const uint32_t stiles = (tiles + 31) / 32;  // super-tiles of 32 tiles (box counts)
+        const uint32_t stiles = (tiles + kSuperTiles - 1) / kSuperTiles;  // super-tiles (box counts)
         if (!ck(cudaMalloc((void**)&d.bf_sbox, sizeof(float) * (size_t)stiles * 2 * tbox_stride(d.a)), "super-tiles"))
             break;
         if (!ck(cudaMalloc((void**)&d.bf_scnt, sizeof(uint32_t) * stiles), "super-tiles")) break;
@@ -1333,7 +1333,7 @@ gf_status bf_tc_prepare(DeviceIndex& d) {
 }
 
 namespace {
-constexpr uint32_t kSuper = 32;  // tiles per super-tile of the box counts
+constexpr uint32_t kSuper = kSuperTiles;  // tiles per super-tile of the box counts
 
 // Bounds and counts of each super-tile (kSuper consecutive tiles, one warp each).
 __global__ void super_tile_kernel(const float* __restrict__ tbox, const uint32_t* __restrict__ tcnt, uint32_t tiles,

@@ -102,7 +102,7 @@ int main(int argc, char** argv) {
     fs.cagra_prefix = cprefix.c_str();
     fs.cagra_suffix = csuffix.c_str();
     fs.global_graph = global.c_str();
-    fs.grid = (normal && grid.empty()) ? nullptr : grid.c_str();
+    fs.grid = normal ? nullptr : grid.c_str();  // normaldataset_search ignores --grid
     fs.uniform_dims = (uint32_t)shape.size();
     fs.uniform_shape = shape.data();
     fs.uniform_lo = domain_lo;

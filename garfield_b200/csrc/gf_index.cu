@@ -350,6 +350,36 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     std::vector<float> attrs((size_t)n * d.a);
     for (uint32_t p = 0; p < n; ++p)
         std::memcpy(&attrs[(size_t)p * d.a], ds->attrs + (size_t)i2g[p] * d.a, sizeof(float) * d.a);
+    // Do the cells hold their rows?  Every (numeric) attribute of a row must lie in the
+    // closed range [l_quant, r_quant] of its cell's slice in that dimension; cell ids are
+    // mixed radix over the slices, last dimension fastest (indexbuild/tools.py:112-120).
+    // Only then is "every in-box row of the index" the same set as "every in-box row of
+    // the cells the box meets" (the reference's exact route scans the query's cells,
+    // gpu_graph.cu:3788-4022), which lets the search find exact-route rows through the
+    // attribute tiles.  cell_of comes from the caller, and the reference's quantiles are
+    // integers (real_dataset_adapter.cuh:578), so fractional attributes can fall between
+    // two slices; such an index keeps the cell scan.
+    d.cells_hold_rows = true;
+    {
+        std::vector<uint32_t> goff(d.a, 0);
+        for (uint32_t j = 1; j < d.a; ++j) goff[j] = goff[j - 1] + d.grid[j - 1];
+        std::vector<uint32_t> sl(d.a);
+        for (uint32_t c = 0; c < P && d.cells_hold_rows; ++c) {
+            uint32_t rest = c;
+            for (uint32_t j = d.a; j-- > 0;) {
+                sl[j] = goff[j] + rest % d.grid[j];
+                rest /= d.grid[j];
+            }
+            for (uint32_t p = d.seg_h[c]; p < d.seg_h[c + 1] && d.cells_hold_rows; ++p)
+                for (uint32_t j = 0; j < d.a; ++j) {
+                    const float v = attrs[(size_t)p * d.a + j];
+                    if (v < d.lq[sl[j]] || v > d.rq[sl[j]]) {  // NaN rows are in no box: they pass
+                        d.cells_hold_rows = false;
+                        break;
+                    }
+                }
+        }
+    }
 
     // clusters (load_clustering, tools.cuh:569-602): centroid = float mean accumulated in
     // global point order; hist[cell][label]

@@ -34,6 +34,15 @@ gf_status cuda_fail(cudaError_t e, const char* what);
 // Device-resident index in cell-major order: point positions seg[c] .. seg[c+1]-1
 // belong to cell c, in increasing global id (the reference's "logical position",
 // offset[pid] + local_idx, tools.cuh:862-889).
+// Geometry of the attribute tiles (gf_bf_tc.cu attr_tiles_prepare): rows of the index in
+// the Morton order of their attributes, kTileRows per tile, kSuperTiles tiles per
+// super-tile.  The box counts and the search's exact route walk them one warp per query,
+// one lane per tile of a super-tile and 32 rows of a tile per step.
+constexpr uint32_t kTileRows = 128;
+constexpr uint32_t kSuperTiles = 32;
+static_assert(kSuperTiles == 32, "one lane per tile of a super-tile");
+static_assert(kTileRows % 32 == 0, "tiles are walked 32 rows at a time");
+
 struct DeviceIndex {
     int device = 0;
     uint32_t n = 0, dim = 0, d8 = 0, d4 = 0, a = 0, ncells = 0, degree = 0, E = 0, C = 0;
@@ -92,6 +101,7 @@ struct DeviceIndex {
     // 128-point tcgen05 tiles, per point (1 - kappa)|x~|^2, per tile attribute bounds
     bool bf_ok = false;
     bool at_ok = false;          // attribute tiles (bf_tbox, bf_attrs, bf_rowpos, bf_tcnt) built
+    bool cells_hold_rows = false; // every row's attributes lie in its cell's slice ranges
     uint32_t* bf_tcnt = nullptr; // bf_tiles: points of each tile whose attributes are all numbers
     uint32_t bf_stiles = 0;      // super-tiles: 32 consecutive tiles (box counts)
     float* bf_sbox = nullptr;    // bf_stiles x 2 x a8: attribute bounds per super-tile

@@ -391,13 +391,13 @@ __device__ __noinline__ uint32_t exact_route(const SArgs& A, uint32_t* base, uin
             while (ps) {
                 const uint32_t ss = s0 + __ffs(ps) - 1;
                 ps &= ps - 1;
-                const uint32_t t = ss * 32 + lane;
+                const uint32_t t = ss * kSuperTiles + lane;
                 uint32_t pt = __ballot_sync(kFull, t < A.ntiles && meets(A.tbox + (size_t)t * 2 * A.a8));
                 while (pt) {
-                    const uint32_t tt = ss * 32 + __ffs(pt) - 1;
+                    const uint32_t tt = ss * kSuperTiles + __ffs(pt) - 1;
                     pt &= pt - 1;
-                    for (uint32_t g = 0; g < 4; ++g) {
-                        const uint32_t r = tt * 128 + g * 32 + lane;
+                    for (uint32_t g = 0; g < kTileRows / 32; ++g) {
+                        const uint32_t r = tt * kTileRows + g * 32 + lane;
                         const bool ok = in_box(A.tattrs, r, A.a, lb, rb);  // NaN rows (padding) never
                         append(w.P(A), nb, ok, ok ? __ldg(A.trow + r) : 0u);
                         if (nb > flush_at) {
@@ -1182,7 +1182,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     blocks = std::min(blocks, need_blocks);
     GF_CUDA(cudaMemsetAsync(p.scratch, 0, sizeof(uint32_t), s));
     if (!(view && view->accumulate_stats)) GF_CUDA(cudaMemsetAsync(p.stats, 0, 8 * sizeof(unsigned long long), s));
-    if (!view && !fullgraph && d.at_ok) {  // exact route through the attribute tiles
+    if (!view && !fullgraph && d.at_ok && d.cells_hold_rows) {  // exact route through the attribute tiles
         A.sbox = d.bf_sbox;
         A.tbox = d.bf_tbox;
         A.tattrs = d.bf_attrs;

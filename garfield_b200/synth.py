@@ -115,7 +115,7 @@ def make(n: int, dim: int, n_centers: int, qnum: int, grid: tuple[int, ...], sel
     lo, hi = boxes(qnum, len(grid), domain, selectivity, rb)
     return Dataset(vectors, attrs, queries, lo, hi, tuple(grid), cell_of,
                    dict(n=n, dim=dim, n_centers=n_centers, qnum=qnum, selectivity=selectivity, domain=domain,
-                        sigma=sigma, seed=seed))
+                        sigma=sigma, seed=seed, normalize=normalize, sphere=sphere, center_hi=center_hi))
 
 
 def sphere_mixture(n: int, dim: int, n_centers: int, sigma: float, rng: np.random.Generator,
@@ -213,3 +213,33 @@ def config5(seed: int = DEFAULT_SEED, n: int = 1_000_000_000, qnum: int = 100_00
     ds.vectors = codes.astype(np.float32)
     ds.meta.update(k=10, R=32, E=2)
     return ds, codes
+
+
+def query_stream(ds: Dataset, stream: int, selectivity: float | None = None) -> Dataset:
+    """Another batch of queries from `ds`'s distribution (same mixture centers, same box
+    rule, the same number of queries) for the query stream `stream` >= 1 of a multi-GPU
+    run; stream 0 is ds itself.  The centers are redrawn from the vector seed (they are
+    the first draw of its generator); queries and boxes use seeds seed + 2 + 1000 * stream
+    and seed + 3 + 1000 * stream.  Only for make()-style datasets (configs 1, 2, 4, 5)."""
+    if stream == 0:
+        return ds
+    m = ds.meta
+    seed, dim, n_centers, qnum = m["seed"], m["dim"], m["n_centers"], m["qnum"]
+    sel = m["selectivity"] if selectivity is None else selectivity
+    normalize = bool(m.get("normalize", False))
+    sphere = bool(m.get("sphere", False))
+    rv = np.random.default_rng(seed)
+    if sphere:
+        centers = rv.standard_normal((n_centers, dim), dtype=np.float32)
+        centers /= np.maximum(np.linalg.norm(centers, axis=1, keepdims=True), 1e-12)
+    else:
+        centers = rv.uniform(0.0, m.get("center_hi", 255.0), size=(n_centers, dim)).astype(np.float32)
+    rq = np.random.default_rng(seed + 2 + 1000 * stream)
+    if sphere:
+        queries, _, _ = sphere_mixture(qnum, dim, n_centers, m["sigma"], rq, centers=centers)
+    else:
+        queries, _, _ = gaussian_mixture(qnum, dim, n_centers, m["sigma"], rq, centers=centers,
+                                         clip_min=None if normalize else 0.0, normalize=normalize)
+    rb = np.random.default_rng(seed + 3 + 1000 * stream)
+    lo, hi = boxes(qnum, len(ds.grid), m["domain"], sel, rb)
+    return Dataset(ds.vectors, ds.attrs, queries, lo, hi, ds.grid, ds.cell_of, dict(m, stream=stream))

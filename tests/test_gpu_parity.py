@@ -242,3 +242,45 @@ def test_box_counts_from_attribute_tiles(which, request):
     assert box[c.ds.lo.shape[0]] == at.shape[0] and box[c.ds.lo.shape[0] + 1] == 0
     plan.close()
     g.close()
+
+
+def test_exact_route_rows_outside_their_cells(small):
+    """The exact route scans the in-box rows of the query's cells.  When a row's attributes
+    fall outside its cell's slice ranges (fractional attributes between integer quantiles,
+    or a cell_of that disagrees with the ranges), that set differs from "every in-box row of
+    the index", so the search must keep the cell scan: boxes inside the gap between two
+    slices meet no cell and return nothing, like the oracle's."""
+    c = small
+    attrs = c.ds.attrs.astype(np.float32).copy()
+    g0 = int(c.ix.grid[0])
+    lq, rq = c.ix.l_quant[:g0].astype(np.float32), c.ix.r_quant[:g0].astype(np.float32)
+    slice0 = c.ix.slices[:, 0]
+    edge = attrs[:, 0] == rq[slice0]               # rows on the upper edge of their slice
+    edge &= slice0 < g0 - 1
+    attrs[edge, 0] += 0.5                          # now strictly between two slices
+    assert edge.sum() > 0
+    idx = gf.Index.create(vectors=c.ds.vectors, attrs=attrs, grid=c.ix.grid, l_quant=c.ix.l_quant,
+                          r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs, degree=c.ix.degree,
+                          cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels, keep_fp32=True)
+    q = c.ds.queries.shape[0]
+    lo = c.ds.lo.astype(np.float32).copy()
+    hi = c.ds.hi.astype(np.float32).copy()
+    # half of the boxes sit in the gap above slice 0 on dimension 0
+    gap = np.arange(q) % 2 == 0
+    lo[gap, 0], hi[gap, 0] = rq[0] + 0.25, rq[0] + 0.75
+    lo[gap, 1], hi[gap, 1] = -1e9, 1e9
+    counts, offsets, cells_u = oracle.plan_cells(lo, hi, c.ix.grid, c.ix.l_quant, c.ix.r_quant)
+    assert (counts[gap] == 0).all()
+    cells, _ = oracle.order_cells(c.ds.queries, c.centroids, c.hist, counts, offsets, cells_u)
+    box = oracle.count_in_box(attrs, lo, hi)
+    assert (box[gap] > 0).sum() > 0                 # rows of the index do lie in those boxes
+    plan = idx.plan(q)
+    plan.build(dev(c.ds.queries), dev(lo), dev(hi), prefilter=1.0)
+    ids, dist = plan.search(gf.SearchParams(L=32, k=10))
+    ent = c.entry(c.ix.degree)
+    ref_ids, ref_d, _ = oracle.search(c.ix, c.ds.vectors, attrs, c.ds.queries, lo, hi, counts, offsets, cells, ent,
+                                      L=32, K=10, prefilter=1.0, box_counts=box)
+    assert np.array_equal(as_u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+    assert (as_u32(ids)[gap] == gf.NO_ID).all()
+    plan.close()
+    idx.close()
