@@ -144,12 +144,23 @@ def dataset_and_index(args, device):
     else:
         ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
     log(f"dataset {ds.vectors.shape} in {time.time() - t0:.1f}s")
-    key = f"cfg{args.config}_n{args.n}_s{args.seed}_R{args.R}_E{args.E}_C{args.C}.npz"
+    key = f"cfg{args.config}_n{args.n}_s{args.seed}_R{args.R}_E{args.E}_C{args.C}"
     cache = Path(args.cache) / key if args.cache else None
-    if cache is not None and cache.exists():
-        z = np.load(cache)
+    names = ("grid", "l_quant", "r_quant", "slices", "cell_of", "graphs", "cross", "labels", "meta")
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if cache is not None and rank != 0 and world > 1:
+        # rank 0 builds (or loads) the index; the others wait for its cache directory
+        t0 = time.time()
+        while not (cache / "meta.npy").exists():
+            if time.time() - t0 > 3600:
+                raise RuntimeError(f"no index cache at {cache} after an hour")
+            time.sleep(2)
+    if cache is not None and (cache / "meta.npy").exists():
+        # arrays memory-mapped: the ranks of one box share the page cache
+        z = {k: np.load(cache / f"{k}.npy", mmap_mode="r") for k in names}
         ix = indexbuild.GmgArrays(z["grid"], z["l_quant"], z["r_quant"], z["slices"], z["cell_of"], z["graphs"],
-                                  z["cross"], z["labels"], int(z["degree"]), int(z["cross_e"]))
+                                  z["cross"], z["labels"], int(z["meta"][0]), int(z["meta"][1]))
         log(f"index loaded from {cache}")
     else:
         t0 = time.time()
@@ -158,15 +169,21 @@ def dataset_and_index(args, device):
         torch.cuda.synchronize()
         log(f"index built in {time.time() - t0:.1f}s")
         if cache is not None:
+            import shutil
+            tmp = cache.with_name(f"{cache.name}.{os.getpid()}.tmp")
             try:
-                cache.parent.mkdir(parents=True, exist_ok=True)
-                tmp = cache.with_suffix(f".{os.getpid()}.tmp.npz")
-                np.savez(tmp, grid=ix.grid, l_quant=ix.l_quant, r_quant=ix.r_quant, slices=ix.slices,
-                         cell_of=ix.cell_of, graphs=ix.graphs, cross=ix.cross, labels=ix.labels,
-                         degree=ix.degree, cross_e=ix.cross_e)
-                os.replace(tmp, cache)
+                tmp.mkdir(parents=True, exist_ok=True)
+                arrs = {"grid": ix.grid, "l_quant": ix.l_quant, "r_quant": ix.r_quant, "slices": ix.slices,
+                        "cell_of": ix.cell_of, "graphs": ix.graphs, "cross": ix.cross, "labels": ix.labels}
+                for k, v in arrs.items():
+                    np.save(tmp / f"{k}.npy", np.ascontiguousarray(v))
+                np.save(tmp / "meta.npy", np.array([ix.degree, ix.cross_e], np.int64))  # written last
+                if cache.exists():
+                    shutil.rmtree(tmp, ignore_errors=True)
+                else:
+                    os.replace(tmp, cache)
             except OSError:
-                pass
+                shutil.rmtree(tmp, ignore_errors=True)
     return ds, ix
 
 
@@ -260,7 +277,7 @@ def run_ours(args):
     dist_t = torch.empty((qnum, K), dtype=torch.float32, device=device)
 
     def sp(L, width):
-        return gf.SearchParams(L=L, k=K, width=width, exact_tc=args.exact_tc)
+        return gf.SearchParams(L=L, k=K, width=width, exact_tc=args.exact_tc, route=args.route)
 
     def step(L, width):
         plan.build(qd, lod, hid, args.prefilter, stream)
@@ -293,7 +310,7 @@ def run_ours(args):
         b.synchronize()
         return reduce_max(a.elapsed_time(b) / n)
 
-    widths = [args.width] if args.width else [1, 2, 4, 8]
+    widths = [args.width] if args.width else [4, 8]  # widths 1 and 2 were slower at every L on B200
     best = None
     for wd in widths:
         L_w, r_w, sw = find_L(wd)
@@ -408,6 +425,8 @@ def run_ours(args):
                    "plan_ms": round(float(np.mean(plan_ms)), 4), "search_ms": round(float(np.mean(search_ms)), 4),
                    "prefilter": args.prefilter, "exact_route": ("tensor-core exact scan" if args.exact_tc
                                                                 else "fp16 warp scan"), "n_exact": int(st["n_exact"]),
+                   "route": ("by cost: tensor-core exact scan when box count < 150 x cells x (L + 64)"
+                             if args.route else "the reference's (postfilter / prefilter thresholds)"),
                    "sweep": sweep,
                    "cross_edges": (f"spokesman rows only: {index.cross_rows} of {index.n} (compress_global_graph_extreme)"
                                    if args.cross_spokesman else "full")},
@@ -530,37 +549,56 @@ def peak_tensor() -> tuple[float, str]:
 
 
 def run_bruteforce(args):
-    """Exact filtered k-NN mode (gf_bruteforce, the GPU ground truth): config-2 data, all 10k
-    queries, k = 10.  Times the tensor-core pass (query x point products on tcgen05 with a
-    proven error bound, exact re-rank, CUDA-core answer for unproven queries) beside the
-    CUDA-core kernel on the same inputs, and checks that both return the same ids and
-    distances.  The roofline is the tensor pipe: executed MMA FLOPs per second."""
+    """Exact filtered k-NN mode (gf_bruteforce, the GPU ground truth): --config's data, all
+    queries, k = 10 (100 for config 3).  Times the tensor-core pass (query x point products on
+    tcgen05 with a proven error bound, exact re-rank, CUDA-core answer for unproven queries)
+    and, while points x queries stays below 1e10, the CUDA-core kernel on the same inputs,
+    checking that both return the same ids and distances.  The roofline is the tensor pipe:
+    executed MMA FLOPs per second.  Under torchrun every rank holds the index and takes its
+    slice of the query batch (dist.shard_range; strong scaling, the batch is fixed)."""
     import torch
+    import torch.distributed as dist
     import garfield_b200 as gf
     from garfield_b200 import indexbuild, synth
+    from garfield_b200.dist import shard_range
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+
+    def reduce_max(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     K = args.k
     if args.config == 3:
         ds = synth.config3(seed=args.seed, n=args.n, qnum=args.qnum, n_centers=max(10, args.n // 1000),
                            selectivity=args.sel)
-        shape = f"{args.n // 10**6}M x 96 unit-norm, 3 attrs on 4x4x4, {args.sel:.0%} sel., k=100"
+        shape = f"{args.n / 1e6:g}M x 96 unit-norm, 3 attrs on 4x4x4, {args.sel:.0%} sel., k=100"
     elif args.config == 4:
         ds = synth.config4(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
-        shape = f"{args.n // 10**6}M x 768 unit-norm, 2 attrs on 8x8, {args.sel:.0%} sel., k=10"
+        shape = f"{args.n / 1e6:g}M x 768 unit-norm, 2 attrs on 8x8, {args.sel:.0%} sel., k=10"
     else:
         ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
-        shape = f"{args.n // 10**6}M x 128, 2 attrs, {args.sel:.0%} sel., k=10"
+        shape = f"{args.n / 1e6:g}M x 128, 2 attrs, {args.sel:.0%} sel., k=10"
     lq, rq, _, cell_of = indexbuild.quantile_grid(ds.attrs, ds.grid)
     n, D = ds.vectors.shape
     index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=np.asarray(ds.grid, np.uint32),
                             l_quant=lq, r_quant=rq, cell_of=cell_of, graphs=np.zeros((n, 1), np.uint32), degree=1,
                             keep_fp32=True, device=local)
-    qnum = ds.queries.shape[0]
-    qd = torch.from_numpy(ds.queries).to(device)
-    lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
-    hid = torch.from_numpy(ds.hi.astype(np.float32)).to(device)
+    qtot = ds.queries.shape[0]
+    s0, s1 = shard_range(qtot, rank, world) if world > 1 else (0, qtot)
+    qnum = s1 - s0
+    qd = torch.from_numpy(ds.queries[s0:s1]).to(device)
+    lod = torch.from_numpy(ds.lo[s0:s1].astype(np.float32)).to(device)
+    hid = torch.from_numpy(ds.hi[s0:s1].astype(np.float32)).to(device)
     stream = torch.cuda.Stream(device)
     flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
     stats = torch.zeros(3, dtype=torch.int32, device=device)
@@ -569,6 +607,8 @@ def run_bruteforce(args):
         for _ in range(warmup):
             index.bruteforce(qd, lod, hid, K, stream=stream, path=path, stats=stats)
         stream.synchronize()
+        if world > 1:
+            dist.barrier()
         ms = []
         with ClockSampler(local) as clocks:
             for i in range(steps):
@@ -576,21 +616,27 @@ def run_bruteforce(args):
                     flush.fill_(float(i))
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                ids, dist = index.bruteforce(qd, lod, hid, K, stream=stream, path=path, stats=stats)
+                ids, dist_t = index.bruteforce(qd, lod, hid, K, stream=stream, path=path, stats=stats)
                 b.record(stream)
                 b.synchronize()
                 ms.append(a.elapsed_time(b))
-        return ids, dist, float(np.mean(ms)), stats.cpu().numpy().copy(), clocks.summary()
+        return ids, dist_t, float(np.mean(ms)), stats.cpu().numpy().copy(), clocks.summary()
 
     t_ids, t_d, t_ms, st, clocks = timed(2, args.steps, args.warmup)
-    c_ids, c_d, c_ms, _, _ = timed(1, 1, 1)
-    same = bool(torch.equal(t_ids, c_ids) and torch.equal(t_d, c_d))
+    total_ms = reduce_max(t_ms * args.steps)
+    ms_step = total_ms / args.steps
+    cuda_core = float(n) * float(qtot) < 1e10  # the CUDA-core kernel scans every point per query
+    if cuda_core:
+        c_ids, c_d, c_ms, _, _ = timed(1, 1, 1)
+        same = bool(torch.equal(t_ids, c_ids) and torch.equal(t_d, c_d))
     # end to end: host queries and boxes in pinned memory, ids back to the host
-    qh, lh, hh = (torch.from_numpy(x).pin_memory() for x in (ds.queries, ds.lo.astype(np.float32),
-                                                              ds.hi.astype(np.float32)))
+    qh, lh, hh = (torch.from_numpy(np.ascontiguousarray(x)).pin_memory()
+                  for x in (ds.queries[s0:s1], ds.lo[s0:s1].astype(np.float32), ds.hi[s0:s1].astype(np.float32)))
     qg, lg, hg = torch.empty_like(qd), torch.empty_like(lod), torch.empty_like(hid)
     ih = torch.empty((qnum, K), dtype=torch.int32).pin_memory()
     e_ms = []
+    if world > 1:
+        dist.barrier()
     for i in range(max(args.warmup, 1) + args.steps):
         with torch.cuda.stream(stream):
             flush.fill_(float(i))
@@ -606,33 +652,45 @@ def run_bruteforce(args):
         if i >= max(args.warmup, 1):
             e_ms.append(a.elapsed_time(b))
     assert torch.equal(ih, t_ids.cpu())
+    e2e_ms = reduce_max(float(np.sum(e_ms))) / args.steps
     products = int(st[2])
     dp = (D + 15) // 16 * 16
     flops = 2.0 * products * 128 * 128 * dp
     achieved = flops / (t_ms / 1e3) / 1e12
     peak, peak_kind = peak_tensor()
     out = {"metric": f"exact filtered k-NN queries/s ({shape})",
-           "value": round(qnum / (t_ms / 1e3), 1), "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True, "scaling": "weak",
+           "value": round(qtot / (ms_step / 1e3), 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+           "scaling": "strong" if world > 1 else "weak",
            "vs_baseline": None, "dtype": "f16 products, f32 accumulate, f32 exact re-rank",
            "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
-           "config": {"workload": f"config{args.config} brute force: {n} x {D} fp32, {qnum} queries, "
-                                  f"sel {args.sel:.0%}, k={K}",
-                      "l2": "flushed (256 MiB write) between timed steps",
-                      "cuda_core_ms_per_step": round(c_ms, 3), "speedup_vs_cuda_cores": round(c_ms / t_ms, 2),
-                      "identical_to_cuda_cores": same, "fallback_queries": int(st[0]), "timeouts": int(st[1]),
-                      "tile_products": products, "dense_products": ((qnum + 127) // 128) * ((n + 127) // 128)},
-           "e2e": {"value": round(qnum / (float(np.mean(e_ms)) / 1e3), 1), "unit": "queries/s",
-                   "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes), "d2h_bytes_per_step": int(ih.nbytes)},
+           "config": {"workload": f"config{args.config} brute force: {n} x {D} fp32, {qtot} queries"
+                                  f"{f' split over {world} ranks' if world > 1 else ''}, sel {args.sel:.0%}, k={K}",
+                      "recall": "1.0 (exact)", "l2": "flushed (256 MiB write) between timed steps",
+                      "fallback_queries_rank0": int(st[0]), "timeouts_rank0": int(st[1]),
+                      "tile_products_rank0": products,
+                      "dense_products_rank0": ((qnum + 127) // 128) * ((n + 127) // 128)},
+           "e2e": {"value": round(qtot / (e2e_ms / 1e3), 1), "unit": "queries/s",
+                   "h2d_bytes_per_step": int(qh.nbytes + lh.nbytes + hh.nbytes) * world,
+                   "d2h_bytes_per_step": int(ih.nbytes) * world},
            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                        "frac": round(achieved / peak, 4), "traffic": None, "kernel": "bf_tc_kernel (whole call timed)",
-                        "peak_kind": peak_kind, "flops_per_step": flops},
+                        "frac": round(achieved / peak, 4), "traffic": None,
+                        "kernel": "bf_tc_kernel (whole call timed, rank 0)",
+                        "peak_kind": peak_kind, "flops_per_step_rank0": flops},
            "clocks": clocks,
            # morton, 3 radix-sort passes are CUB's; prep, boxes, tiles, tc, merge, CUDA-core list
            "gpu_launches": 6 * args.steps}
-    if not args.no_cpu_baseline:
+    if cuda_core:
+        out["config"].update({"cuda_core_ms_per_step": round(c_ms, 3), "speedup_vs_cuda_cores": round(c_ms / t_ms, 2),
+                              "identical_to_cuda_cores": same})
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(ds, args.cpu_sample, os.cpu_count() or 1, K)
-    print(json.dumps(out), flush=True)
+    index.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
 
 
 def run_fullgraph(args):
@@ -1029,9 +1087,10 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])  # data shape (in-memory, bruteforce)
     ap.add_argument("--prefilter", type=float, default=0.0)  # --prefilter: box share at or below -> exact route
     ap.add_argument("--exact-tc", dest="exact_tc", type=int, default=0)  # exact route on the tensor cores
+    ap.add_argument("--route", type=int, default=0)  # 1: route each query by cost (graph or tensor-core scan)
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
-    ap.add_argument("--width", type=int, default=0)  # 0 = pick the fastest of 1, 2, 4, 8
+    ap.add_argument("--width", type=int, default=0)  # 0 = pick the faster of 4 and 8
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--qnum", type=int, default=10_000)
     ap.add_argument("--R", type=int, default=None)  # default: 32, 64 for config 4
@@ -1055,6 +1114,9 @@ def main():
     if args.sel is None:
         args.sel = {2: 0.10, 3: 0.05, 4: 0.02}[args.config]
     args.k = 100 if args.config == 3 else 10
+    if args.route:  # routing by cost needs the box counts and the tensor-core exact scan
+        args.exact_tc = 1
+        args.prefilter = max(args.prefilter, 1e-9)
     if args.R is None:
         args.R = 64 if args.config == 4 else 32
     if args.config != 2 and args.mode not in ("in-memory", "bruteforce"):

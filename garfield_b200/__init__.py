@@ -69,7 +69,8 @@ class _IndexFiles(C.Structure):
 
 class _SearchParams(C.Structure):
     _fields_ = [(n, C.c_uint32) for n in
-                ("L", "k", "width", "max_iter", "n_entry", "postfilter", "hash_slots", "test_wait", "exact_tc")]
+                ("L", "k", "width", "max_iter", "n_entry", "postfilter", "hash_slots", "test_wait", "exact_tc",
+                 "route")]
 
 
 class _BfParams(C.Structure):
@@ -200,10 +201,11 @@ class SearchParams:
     hash_slots: int = 0       # 0 = automatic
     test_wait: int = 0        # test hook: staging waits give up after this many polls and never complete
     exact_tc: int = 0         # 1: exact-route queries go to the tensor-core exact scan (fp32 rows)
+    route: int = 0            # 1: also route by cost (box count vs cells x (L + 64)); needs exact_tc
 
     def _c(self) -> _SearchParams:
         return _SearchParams(self.L, self.k, self.width, self.max_iter, self.n_entry, self.postfilter,
-                             self.hash_slots, self.test_wait, self.exact_tc)
+                             self.hash_slots, self.test_wait, self.exact_tc, self.route)
 
 
 # ------------------------------------------------------------------ index

@@ -6,7 +6,8 @@
 // cost1), cost3 = search kernel; all in seconds, measured with CUDA events.
 // qps = qnum / (cost1 + cost2 + cost3) as in realdataset_search.cu:2506-2508.
 // Extra flags: --ef "10,20,..." (default: the reference's 33-value sweep), --k,
-// --width, --device, --max_iter.
+// --width, --device, --max_iter, --exact_tc (exact route on the tensor cores), --route 1
+// (route each query by cost: graph walk or tensor-core exact scan).
 // Invoked as normaldataset_search (normaldataset_search.cu:1748-2104) the grid is
 // uniform instead of read from --grid: --shape "16" (slices per attribute, the
 // reference's compiled-in default) over [--domain_lo, --domain_hi) = [0, 1e6), and the
@@ -47,7 +48,7 @@ std::vector<uint32_t> parse_list(const std::string& s) {
 int main(int argc, char** argv) {
     std::string data, query, range, gt, cprefix, csuffix = ".cagra32", global, grid, attrs, cluster, result = "result.csv";
     float prefilter = 0.0f, f2h = 1.0f;
-    uint32_t postfilter = 0xFFFFFFFFu, degree = 32, k = 10, width = 1, max_iter = 10000, exact_tc = 0;
+    uint32_t postfilter = 0xFFFFFFFFu, degree = 32, k = 10, width = 1, max_iter = 10000, exact_tc = 0, route = 0;
     int device = 0;
     std::string prog = argv[0];
     const bool normal = prog.size() >= 20 && prog.compare(prog.size() - 20, 20, "normaldataset_search") == 0;
@@ -79,6 +80,7 @@ int main(int argc, char** argv) {
         else if (a == "--width") width = (uint32_t)std::stoul(v);
         else if (a == "--max_iter") max_iter = (uint32_t)std::stoul(v);
         else if (a == "--exact_tc") exact_tc = (uint32_t)std::stoul(v);
+        else if (a == "--route") route = (uint32_t)std::stoul(v);
         else if (a == "--device") device = std::stoi(v);
         else if (a == "--shape") shape = parse_list(v);
         else if (a == "--domain_lo") domain_lo = std::stof(v);
@@ -91,13 +93,16 @@ int main(int argc, char** argv) {
         fprintf(stderr,
                 "usage: %s --data_path F --query_path F --range F --gt F --cagra_prefix P --cagra_suffix S "
                 "--global_graph F --grid F --attrs F [--cluster F] [--result F] [--prefilter x] [--postfilter n] "
-                "[--f2h_factor a] [--degree R] [--ef l1,l2,..] [--k K] [--width W] [--device d] [--exact_tc 0|1]\n",
+                "[--f2h_factor a] [--degree R] [--ef l1,l2,..] [--k K] [--width W] [--device d] [--exact_tc 0|1] "
+                "[--route 0|1]\n",
                 argv[0]);
         return 2;
     }
     gf_index_files fs;
     memset(&fs, 0, sizeof(fs));
     fs.data_path = data.c_str();
+    if (route) exact_tc = 1;            // routing by cost sends queries to the tensor-core exact scan
+    if (route && !(prefilter > 0.0f)) prefilter = 1e-9f;  // box counts without the prefilter rule
     fs.keep_fp32 = exact_tc ? 1u : 0u;  // the tensor-core exact route reads the fp32 rows
     fs.cagra_prefix = cprefix.c_str();
     fs.cagra_suffix = csuffix.c_str();
@@ -166,6 +171,7 @@ int main(int argc, char** argv) {
         p.max_iter = max_iter;
         p.postfilter = postfilter;
         p.exact_tc = exact_tc;
+        p.route = route;
         cudaEventRecord(e0, 0);
         if ((st = gf_plan_queries(idx, plan, dq, dl, dr, qnum, prefilter, nullptr)) != GF_OK) return die("plan", st);
         cudaEventRecord(e1, 0);

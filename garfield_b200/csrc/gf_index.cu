@@ -608,6 +608,7 @@ void gf_search_defaults(gf_search_params* p) {
     p->hash_slots = 0;
     p->test_wait = 0;
     p->exact_tc = 0;
+    p->route = 0;
 }
 
 gf_status gf_index_create(const gf_index_desc* desc, int device, gf_index** out) {

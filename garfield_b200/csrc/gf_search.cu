@@ -1014,17 +1014,19 @@ CellView shard_view(const DeviceIndex& d) {
 
 namespace {
 // Queries of a whole-index search that take the exact route (the search kernel's rule:
-// a non-empty cell list and >= postfilter cells or a box share <= prefilter) are marked for
-// the tensor-core exact scan (gf_search_params.exact_tc); their number goes to n_exact and
-// n_queries.
+// a non-empty cell list and >= postfilter cells or a box share <= prefilter; with route_slots
+// > 0 also a box count below route_slots x cells, the cost rule of gf_search_params.route)
+// are marked for the tensor-core exact scan (gf_search_params.exact_tc); their number goes
+// to n_exact and n_queries.
 __global__ void mark_exact_kernel(const uint32_t* __restrict__ counts, const uint32_t* __restrict__ box, uint32_t n,
-                                  uint32_t qnum, uint32_t postfilter, float prefilter, uint32_t* __restrict__ mark,
-                                  unsigned long long* stats) {
+                                  uint32_t qnum, uint32_t postfilter, float prefilter, unsigned long long route_slots,
+                                  uint32_t* __restrict__ mark, unsigned long long* stats) {
     const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
     bool ex = false;
     if (q < qnum) {
         const uint32_t nc = counts[q];
-        ex = nc > 0 && (nc >= postfilter || (box && (float)((double)box[q] / (double)n) <= prefilter));
+        ex = nc > 0 && (nc >= postfilter || (box && (float)((double)box[q] / (double)n) <= prefilter) ||
+                        (box && route_slots && (unsigned long long)box[q] < route_slots * nc));
         mark[q] = ex ? 1u : 0u;
     }
     const uint32_t b = __ballot_sync(kFull, ex);
@@ -1048,6 +1050,10 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (P.k == 0 || P.k > 1024) return fail(GF_ERR_ARG, "k must be 1..1024");
     if (P.L < P.k || P.L > 4096) return fail(GF_ERR_ARG, "L must be k..4096");
     if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
+    if (P.route > 1) return fail(GF_ERR_ARG, "route must be 0 or 1");
+    if (P.route && !P.exact_tc) return fail(GF_ERR_ARG, "route = 1 sends queries to the tensor-core exact scan: set exact_tc");
+    if (P.route && !(p.prefilter > 0.0f))
+        return fail(GF_ERR_STATE, "route = 1 needs box counts: build the plan with prefilter > 0");
     if (P.exact_tc) {
         if (view || fullgraph || d.sharded || d.host_graph)
             return fail(GF_ERR_ARG, "exact_tc applies to gf_search / gf_search_host on a whole device-resident index");
@@ -1195,8 +1201,10 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
         // exact-route queries: the tensor-core exact scan writes their rows, the search kernel
         // skips them
         if (!p.xmark) GF_CUDA(cudaMalloc((void**)&p.xmark, sizeof(uint32_t) * std::max<uint32_t>(p.max_q, 1)));
+        const unsigned long long route_slots =
+            P.route ? (unsigned long long)GF_ROUTE_ROWS_PER_SLOT * (P.L + kHopSlots) : 0ull;
         mark_exact_kernel<<<(p.qnum + 255) / 256, 256, 0, s>>>(p.counts, A.box, d.n, p.qnum, P.postfilter,
-                                                                p.prefilter, p.xmark, p.stats);
+                                                                p.prefilter, route_slots, p.xmark, p.stats);
         GF_CUDA(cudaGetLastError());
         gf_status st = bruteforce(idx, p.q32, p.lb, p.rb, p.qnum, P.k, ids, dist, s, nullptr, p.xmark);
         if (st != GF_OK) return st;

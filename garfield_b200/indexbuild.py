@@ -10,7 +10,9 @@ this module builds the same files with torch (GPU when present, else CPU):
                   nearest points of other k-means clusters (links to neighbouring clusters),
                   each robust-pruned with alpha = 1.2 (the DiskANN/Vamana rule)
   cross_edges     indexbuild/global_graph_build.py:116-157: for every point and every cell, the
-                  E nearest points of that cell (local ids), here exact
+                  E nearest points of that cell (local ids), here exact up to 2M points, and
+                  above found by this library's own beam search of each cell's graph
+                  (cross_edges_by_search), as the reference does with cagra.search
   kmeans          indexbuild/clustering.py:68-88 (cuVS k-means); here Lloyd iterations
 
 Outputs use the reference's on-disk layout (global point order): graphs of all cells
@@ -209,6 +211,67 @@ def cross_edges(x, cell_of_t, seg, E: int = 2, chunk: int = 8192):
     return out
 
 
+def cross_edges_by_search(vectors: np.ndarray, attrs: np.ndarray, grid, l_quant, r_quant, cell_of: np.ndarray,
+                          graphs: np.ndarray, R: int, E: int = 2, L: int = 32, width: int = 4,
+                          chunk: int = 1 << 20, device=None) -> np.ndarray:
+    """Cross-cell edges found by searching: for every point and every other cell, the E
+    nearest points of that cell that a beam search of the cell's own graph finds (L, width),
+    as local ids of that cell.  The reference builds its cross edges the same way, with
+    cagra.search over each cell's index for all points (indexbuild/global_graph_build.py:
+    116-157); the exact version (cross_edges) costs n^2 distances, which 10M points cannot
+    afford.  The searches run on this library's own kernels: an index over the per-cell
+    graphs without cross edges, every point as a query whose box is the target cell's
+    slice box, searched inside that one cell (Plan.search_batched with the single batch
+    [cell]).  A point's slots of its own cell hold its own local id (never read: a hop
+    leaves a visited cell for an unvisited one).  Returns n x (cells * E) uint32."""
+    import garfield_b200 as gf
+    dev = _device(device)
+    dev_index = dev.index if dev.type == "cuda" and dev.index is not None else 0
+    n, a = attrs.shape
+    grid = np.asarray(grid, np.int64)
+    P = int(np.prod(grid))
+    goff = np.concatenate([[0], np.cumsum(grid)[:-1]])
+    lqf, rqf = np.asarray(l_quant, np.float32), np.asarray(r_quant, np.float32)
+    sizes = np.bincount(cell_of, minlength=P)
+    seg = np.concatenate([[0], np.cumsum(sizes)])
+    order = np.argsort(cell_of, kind="stable")
+    local = np.empty(n, np.uint32)
+    local[order] = (np.arange(n) - seg[cell_of[order]]).astype(np.uint32)
+    index = gf.Index.create(vectors=vectors, attrs=attrs.astype(np.float32), grid=grid.astype(np.uint32),
+                            l_quant=l_quant, r_quant=r_quant, cell_of=cell_of, graphs=graphs, degree=R,
+                            keep_fp32=False, device=dev_index)
+    out = np.empty((n, P * E), np.uint32)
+    xs = torch.from_numpy(np.ascontiguousarray(vectors, np.float32)).to(dev)
+    plan = index.plan(min(chunk, n))
+    params = gf.SearchParams(L=max(L, E), k=E, width=width)
+    for c in range(P):
+        rest, sl = c, np.zeros(a, np.int64)
+        for j in range(a - 1, -1, -1):
+            sl[j] = rest % grid[j]
+            rest //= grid[j]
+        lo = torch.from_numpy(np.array([lqf[goff[j] + sl[j]] for j in range(a)], np.float32)).to(dev)
+        hi = torch.from_numpy(np.array([rqf[goff[j] + sl[j]] for j in range(a)], np.float32)).to(dev)
+        for s in range(0, n, chunk):
+            e = min(n, s + chunk)
+            lb = lo[None, :].expand(e - s, a).contiguous()
+            rb = hi[None, :].expand(e - s, a).contiguous()
+            plan.build(xs[s:e], lb, rb)
+            ids, _ = plan.search_batched([[c]], params)
+            g = ids.cpu().numpy().view(np.uint32)
+            found = g != gf.NO_ID
+            loc = np.where(found, local[np.minimum(g, n - 1)], 0).astype(np.uint32)
+            # fewer than E found (a cell smaller than E): repeat the first
+            loc = np.where(found, loc, loc[:, :1])
+            out[s:e, c * E:(c + 1) * E] = loc
+    own = cell_of.astype(np.int64)
+    for j in range(E):
+        out[np.arange(n), own * E + j] = local
+    plan.close()
+    index.close()
+    del xs
+    return out
+
+
 def kmeans(x, C: int, iters: int = 10, seed: int = 0, chunk: int = 65536):
     """Lloyd k-means; returns int32 labels."""
     n = x.shape[0]
@@ -245,8 +308,14 @@ class GmgArrays:
 
 
 def build(vectors: np.ndarray, attrs: np.ndarray, grid, R: int = 32, E: int = 2, C: int = 1000,
-          kmeans_iters: int = 10, seed: int = 0, device=None, cluster_links: bool = True) -> GmgArrays:
+          kmeans_iters: int = 10, seed: int = 0, device=None, cluster_links: bool = True,
+          cross: str = "auto") -> GmgArrays:
+    """The whole index.  cross: "exact" (every point against every cell, n^2 distances),
+    "search" (cross_edges_by_search, needs a CUDA device and the built library) or "auto"
+    (exact up to 2M points, search above)."""
     dev = _device(device)
+    if cross == "auto":
+        cross = "search" if vectors.shape[0] > 2_000_000 and dev.type == "cuda" else "exact"
     old_tf32 = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
@@ -268,11 +337,16 @@ def build(vectors: np.ndarray, attrs: np.ndarray, grid, R: int = 32, E: int = 2,
                 continue
             gcell = cell_graph(xo[lo:hi], R, labels=lo_lab[lo:hi] if cluster_links else None)
             graphs[lo:hi] = gcell.cpu().numpy().astype(np.uint32)
-        cr = cross_edges(xo, None, seg, E)
-        cross = np.empty((n, P * E), np.uint32)
-        cross[order] = cr.cpu().numpy().astype(np.uint32)
         labels = labels.cpu().numpy().astype(np.int32)
-        return GmgArrays(np.asarray(grid, np.uint32), lq, rq, slices, cell_of, graphs, cross, labels, R, E)
+        if cross == "search":
+            del xo
+            cross_arr = cross_edges_by_search(vectors, attrs, grid, lq, rq, cell_of, graphs, R, E, device=dev)
+        else:
+            cr = cross_edges(xo, None, seg, E)
+            cross_arr = np.empty((n, P * E), np.uint32)
+            cross_arr[order] = cr.cpu().numpy().astype(np.uint32)
+            del cr
+        return GmgArrays(np.asarray(grid, np.uint32), lq, rq, slices, cell_of, graphs, cross_arr, labels, R, E)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old_tf32
 

@@ -141,7 +141,21 @@ typedef struct {
                             Needs keep_fp32, dim <= 1024 and k <= 128; gf_search and
                             gf_search_host only (GF_ERR_ARG for batched, sharded, full-graph and
                             no-allocation searches). */
+    uint32_t route;      /* 0 = the reference's routing (postfilter, plan prefilter).  1 = also
+                            by cost (no counterpart in the reference, which has only the two
+                            thresholds): a query with nc planned cells and b in-box points goes
+                            to the tensor-core exact scan when b < GF_ROUTE_ROWS_PER_SLOT * nc *
+                            (L + 64), an estimate that the scan of its in-box rows costs less
+                            than walking L list slots (plus a hop's 64) in each of its cells.
+                            Needs exact_tc = 1 and box counts (a plan built with prefilter > 0,
+                            e.g. 1e-9 to route by cost only). */
 } gf_search_params;
+
+/* Tensor-core exact-scan rows that cost about as much as one list slot of one cell of the
+ * graph route (gf_search_params.route = 1), from B200 measurements of both routes at
+ * 96- and 128-dim rows, k = 10 and 100 (1M points: config 2 at 1% and 10% boxes, the
+ * configuration-3 shape at 5% boxes). */
+#define GF_ROUTE_ROWS_PER_SLOT 150u
 
 /* Per-search counters (device-side, summed over queries). */
 typedef struct {

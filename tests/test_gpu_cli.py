@@ -69,8 +69,9 @@ def test_realdataset_search_csv(small, files, tmp_path, width):
     qnum = small.ds.queries.shape[0]
     for ef, recall, qps, total, c1, c2, c3, kern in rows:
         assert abs(recall - _library_recall(small, int(ef), width)) < 2e-6
-        assert abs(total - (c1 + c2 + c3)) < 2e-6 and c3 > 0 and kern == c3
-        assert abs(qps - qnum / total) <= 1e-3 * qps + 1e-3
+        assert abs(total - (c1 + c2 + c3)) < 3e-6 and c3 > 0 and kern == c3
+        # the CSV rounds total to 1 us (%.6f seconds) and qps to 1e-3
+        assert abs(qps * total - qnum) <= qps * 1e-6 + 1e-2
     assert rows[-1][1] >= 0.9
 
 

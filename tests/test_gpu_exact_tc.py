@@ -120,3 +120,34 @@ def test_exact_tc_refusals(small):
     assert np.array_equal(ids.cpu().numpy().view(np.uint32), ref)
     plan.close()
     g.close()
+
+
+def test_route_by_cost(small):
+    """gf_search_params.route = 1: a query also goes to the tensor-core exact scan when its
+    box count is below GF_ROUTE_ROWS_PER_SLOT (150) x cells x (L + 64).  The rule on the
+    host must mark the same queries (n_exact), and their rows must be the exact scan's."""
+    c = small
+    g = make(c, keep_fp32=True)
+    q = c.ds.queries.shape[0]
+    L, k = 48, 10
+    lo, hi = c.ds.lo.copy(), c.ds.hi.copy()
+    lo[::3] = -1, -1          # a third of the boxes cover the whole domain
+    hi[::3] = 20000, 20000
+    counts, _, _ = oracle.plan_cells(lo, hi, c.ix.grid, c.ix.l_quant, c.ix.r_quant)
+    box = oracle.count_in_box(c.ds.attrs, lo, hi)
+    ex = (counts > 0) & (box.astype(np.int64) < 150 * counts.astype(np.int64) * (L + 64))
+    plan = g.plan(q)
+    plan.build(dev(c.ds.queries), dev(lo), dev(hi), prefilter=1e-9)
+    ids, dist = plan.search(gf.SearchParams(L=L, k=k, exact_tc=1, route=1))
+    assert plan.stats()["n_exact"] == int(ex.sum()) > 0
+    bf_ids, bf_d = oracle.bruteforce(c.ds.vectors, c.ds.attrs, c.ds.queries, lo, hi, k)
+    ids, dist = ids.cpu().numpy().view(np.uint32), dist.cpu().numpy()
+    assert np.array_equal(ids[ex], bf_ids[ex]) and np.array_equal(dist[ex], bf_d[ex])
+    # without the tensor-core scan, or without box counts, the option is refused
+    with pytest.raises(gf.GarfieldError):
+        plan.search(gf.SearchParams(L=L, k=k, route=1))
+    plan.build(dev(c.ds.queries), dev(lo), dev(hi))
+    with pytest.raises(gf.GarfieldError):
+        plan.search(gf.SearchParams(L=L, k=k, exact_tc=1, route=1))
+    plan.close()
+    g.close()

@@ -50,3 +50,23 @@ def test_quantile_boxes_on_ties():
     lo, hi = synth.quantile_boxes(attrs, 50, 0.25, np.random.default_rng(4))
     assert (lo[:, 0] == 0).all() and (hi[:, 0] == 0).all()  # a constant attribute: every box holds it
     assert (hi[:, 1] >= lo[:, 1]).all()
+
+
+def test_query_stream_draws_new_queries_from_the_same_distribution():
+    """Multi-GPU weak scaling: rank r searches query stream r (stream 0 = the dataset's own
+    batch).  Other streams are reproducible, differ from stream 0 and come from the same
+    mixture centers and box rule."""
+    from garfield_b200 import synth
+    ds = synth.make(4000, 16, 8, 200, (2, 2), 0.10, seed=5)
+    assert synth.query_stream(ds, 0) is ds
+    s1, s1b, s2 = synth.query_stream(ds, 1), synth.query_stream(ds, 1), synth.query_stream(ds, 2)
+    assert np.array_equal(s1.queries, s1b.queries) and np.array_equal(s1.lo, s1b.lo)
+    assert not np.array_equal(s1.queries, ds.queries) and not np.array_equal(s1.queries, s2.queries)
+    assert s1.queries.shape == ds.queries.shape and s1.queries.dtype == ds.queries.dtype
+    assert s1.vectors is ds.vectors and s1.attrs is ds.attrs
+    assert np.array_equal(s1.hi - s1.lo, ds.hi - ds.lo)  # same box side
+    centers = np.random.default_rng(5).uniform(0.0, 255.0, size=(8, 16)).astype(np.float32)
+
+    def nearest(q):
+        return ((q[:, None, :] - centers[None]) ** 2).sum(-1).min(1).mean()
+    assert abs(nearest(s1.queries) / nearest(ds.queries) - 1) < 0.1
