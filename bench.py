@@ -141,6 +141,11 @@ def dataset_and_index(args, device):
                            selectivity=args.sel)
     elif args.config == 4:
         ds = synth.config4(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
+    elif args.config == 5:
+        # uint8 rows; one mixture component per 10k points, as 100k centres for 1B points
+        ds, codes = synth.config5(seed=args.seed, n=args.n, qnum=args.qnum, n_centers=max(10, args.n // 10000),
+                                  selectivity=args.sel)
+        ds.codes = codes
     else:
         ds = synth.config2(seed=args.seed, selectivity=args.sel, n=args.n, qnum=args.qnum)
     log(f"dataset {ds.vectors.shape} in {time.time() - t0:.1f}s")
@@ -314,7 +319,10 @@ def run_ours(args):
     best = None
     for wd in widths:
         L_w, r_w, sw = find_L(wd)
-        ms = quick_ms(L_w, wd) if r_w >= args.target or len(widths) == 1 else float("inf")
+        if len(widths) == 1:
+            ms = 0.0  # nothing to choose between
+        else:
+            ms = quick_ms(L_w, wd) if r_w >= args.target else float("inf")
         log(f"width={wd}: L={L_w} recall={r_w:.4f} {ms:.3f} ms/step")
         if best is None or ms < best[3]:
             best = (wd, L_w, r_w, ms, sw)
@@ -469,6 +477,9 @@ def run_out_of_core(args):
     common = dict(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
                   r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree, cross=ix.cross,
                   cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, device=local)
+    if args.config == 5:
+        # uint8 rows decoded as code / 100 (the reference's u8 path), queries scaled by 0.01
+        common.update(codec=2, codes=ds.codes, f2h_factor=0.01)
     streamed = gf.Index.create(**common, keep_fp32=True, host_graph=True)
     resident = gf.Index.create(**common, keep_fp32=False, host_graph=False)
     qnum = ds.queries.shape[0]
@@ -526,12 +537,16 @@ def run_out_of_core(args):
                      "h2d_graph_bytes_per_step": h2d if name == "streamed" else 0}
         res["batches"], res["splits"], res["schedule_ms"] = batches, splits, round(sched_ms, 3)
         plan.close()
-    out = {"metric": "QPS at recall@10>=0.95, graphs streamed per batch of cells (1M x 128, 2 attrs, 10% sel.)",
+    shape = (f"{ds.vectors.shape[0] / 1e6:g}M x 128 uint8, 2 attrs on 16x16, {args.sel:.0%} sel." if args.config == 5
+             else "1M x 128, 2 attrs, 10% sel.")
+    out = {"metric": f"QPS at recall@10>=0.95, graphs streamed per batch of cells ({shape})",
            "value": res["streamed"]["qps"], "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": res["streamed"]["ms_per_step"], "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
-           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
-           "config": {"workload": "config2, out-of-core batches", "batch_cells": args.batch_cells, "width": width,
+           "scaling": "weak", "vs_baseline": None,
+           "dtype": "u8 storage, f32 accumulate" if args.config == 5 else "f16 storage, f32 accumulate",
+           "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
+           "config": {"workload": f"config{args.config}: {ds.vectors.shape[0]} points, {qnum} queries, out-of-core batches",
+                      "batch_cells": args.batch_cells, "width": width,
                       "n_batches": len(res["batches"]), "splits": res["splits"], "schedule_ms": res["schedule_ms"],
                       "batches": res["batches"], "streamed": res["streamed"], "resident_same_batches": res["resident"],
                       "l2": "flushed (256 MiB write) between timed steps"}}
@@ -777,10 +792,11 @@ def run_sharded(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     ds, ix = dataset_and_index(args, device)
     mine = shard_cells(ix.grid, world)[rank]
+    codec = dict(codec=2, codes=ds.codes, f2h_factor=0.01) if args.config == 5 else dict(f2h_factor=1.0)
     index = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
                             r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
-                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, f2h_factor=1.0, keep_fp32=False,
-                            shard_cells=mine if world > 1 else None, device=local)
+                            cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=False,
+                            shard_cells=mine if world > 1 else None, device=local, **codec)
     qnum = ds.queries.shape[0]
     qd = torch.from_numpy(ds.queries).to(device)
     lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
@@ -801,10 +817,10 @@ def run_sharded(args):
     # ground truth: exact scan on a whole index on rank 0, broadcast
     gt = torch.zeros((S, 10), dtype=torch.int32, device=device)
     if rank == 0:
-        whole = gf.Index.create(vectors=ds.vectors,
-                                attrs=ds.attrs.astype(np.float32), grid=ix.grid, l_quant=ix.l_quant,
-                                r_quant=ix.r_quant, cell_of=ix.cell_of, graphs=ix.graphs, degree=ix.degree,
-                                cross=ix.cross, cross_e=ix.cross_e, labels=ix.labels, keep_fp32=True, device=local)
+        whole = gf.Index.create(vectors=ds.vectors, attrs=ds.attrs.astype(np.float32), grid=ix.grid,
+                                l_quant=ix.l_quant, r_quant=ix.r_quant, cell_of=ix.cell_of,
+                                graphs=np.zeros((ds.vectors.shape[0], 1), np.uint32), degree=1, keep_fp32=True,
+                                device=local)
         gt.copy_(whole.bruteforce(qd[:S].contiguous(), lod[:S].contiguous(), hid[:S].contiguous(), 10)[0])
         whole.close()
         del whole
@@ -843,12 +859,16 @@ def run_sharded(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     ms = total_ms / args.steps
-    out = {"metric": "QPS at recall@10>=0.95, cell-sharded index (1M x 128, 2 attrs, 10% sel.)",
+    shape = (f"{ds.vectors.shape[0] / 1e6:g}M x 128 uint8, 2 attrs on 16x16, {args.sel:.0%} sel." if args.config == 5
+             else "1M x 128, 2 attrs, 10% sel.")
+    out = {"metric": f"QPS at recall@10>=0.95, cell-sharded index ({shape})",
            "value": round(qnum / (ms / 1e3), 1), "unit": "queries/s", "n_gpus": world, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-           "vs_baseline": None, "dtype": "f16 storage, f32 accumulate",
-           "data": "synthetic (seeded Gaussian mixture; BASELINE config 2 shapes)",
-           "config": {"workload": "config2, cell-sharded", "parallelism": f"cell shards x{world}", "L": L,
+           "vs_baseline": None,
+           "dtype": "u8 storage, f32 accumulate" if args.config == 5 else "f16 storage, f32 accumulate",
+           "data": f"synthetic (seeded Gaussian mixture; BASELINE config {args.config} shapes)",
+           "config": {"workload": f"config{args.config}: {ds.vectors.shape[0]} points, {qnum} queries, cell-sharded",
+                      "parallelism": f"cell shards x{world}", "L": L,
                       "width": width, "recall_at_10": round(recall, 4), "recall_sample": S, "sweep": sweep,
                       "shard_cells": mine, "device_bytes_rank0": index.device_bytes,
                       "exchange_bytes_per_rank": qnum * 10 * 8,
@@ -1084,7 +1104,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-cuda"])
     ap.add_argument("--sel", type=float, default=None)  # default: 0.10 (config 2), 0.02 (config 4)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4])  # data shape (in-memory, bruteforce)
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])  # data shape
     ap.add_argument("--prefilter", type=float, default=0.0)  # --prefilter: box share at or below -> exact route
     ap.add_argument("--exact-tc", dest="exact_tc", type=int, default=0)  # exact route on the tensor cores
     ap.add_argument("--route", type=int, default=0)  # 1: route each query by cost (graph or tensor-core scan)
@@ -1112,15 +1132,17 @@ def main():
                     help="keep the cross-cell edges of spokesmen only (row f2 of the scope table)")
     args = ap.parse_args()
     if args.sel is None:
-        args.sel = {2: 0.10, 3: 0.05, 4: 0.02}[args.config]
+        args.sel = {2: 0.10, 3: 0.05, 4: 0.02, 5: 0.01}[args.config]
     args.k = 100 if args.config == 3 else 10
     if args.route:  # routing by cost needs the box counts and the tensor-core exact scan
         args.exact_tc = 1
         args.prefilter = max(args.prefilter, 1e-9)
     if args.R is None:
         args.R = 64 if args.config == 4 else 32
-    if args.config != 2 and args.mode not in ("in-memory", "bruteforce"):
+    if args.config in (3, 4) and args.mode not in ("in-memory", "bruteforce"):
         ap.error("--config 3 and 4 apply to the in-memory and bruteforce modes")
+    if args.config == 5 and args.mode not in ("out-of-core", "sharded"):
+        ap.error("--config 5 applies to the out-of-core and sharded modes")
     if args.impl == "ours" and args.mode == "out-of-core":
         run_out_of_core(args)
     elif args.impl == "ours" and args.mode == "sharded":
