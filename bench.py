@@ -10,9 +10,9 @@ qnum / (cost1 + cost2 + cost3) (realdataset_search.cu:2506-2508).  L is the smal
 length in a fixed sweep whose recall on the ground-truth sample reaches the target.
 
   python bench.py [--gpus N --steps K --warmup W]           this implementation
-  python bench.py --impl reference                          CPU exact filtered scan (the
-                                                            oracle's restatement of the
-                                                            reference's CPU path) on host cores
+  python bench.py --impl reference                          the reference's CPU exact filtered scan
+                                                            (naive_brute_force_with_filter, built
+                                                            from its sources) on the host cores
   python bench.py --mode out-of-core [--batch-cells B]     graphs in pinned host memory, streamed
                                                             per scheduled batch of B cells (row a17)
   torchrun ... bench.py --mode sharded                     cell-sharded index over the ranks, keys
@@ -22,8 +22,12 @@ length in a fixed sweep whose recall on the ground-truth sample reaches the targ
   python bench.py --impl reference-cuda                     the reference's own CUDA search
                                                             (oracle/_ref/realdataset_search) and our
                                                             CLI on the same reference-format files
-Multi-GPU (torchrun): every rank holds a replica of the index and runs the full query
-batch (weak scaling); the only collective is the max-over-ranks of the timings.
+  --config 3 / 4 (in-memory, bruteforce), --config 5 (out-of-core, sharded), --route 1
+  (per-query choice of graph walk or tensor-core exact scan).
+Multi-GPU (torchrun): every rank holds a replica of the index and searches its own batch
+of queries from the same distribution (weak scaling, `value`); the one-GPU batch split over
+the ranks is timed beside it (`strong`).  The collectives are the max-over-ranks of the
+timings and the recall averages.
 """
 from __future__ import annotations
 
