@@ -1138,9 +1138,8 @@ def main():
     if args.sel is None:
         args.sel = {2: 0.10, 3: 0.05, 4: 0.02, 5: 0.01}[args.config]
     args.k = 100 if args.config == 3 else 10
-    if args.route:  # routing by cost needs the box counts and the tensor-core exact scan
+    if args.route:  # routing by cost sends queries to the tensor-core exact scan
         args.exact_tc = 1
-        args.prefilter = max(args.prefilter, 1e-9)
     if args.R is None:
         args.R = 64 if args.config == 4 else 32
     if args.config in (3, 4) and args.mode not in ("in-memory", "bruteforce"):

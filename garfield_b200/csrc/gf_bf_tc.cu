@@ -56,8 +56,12 @@ using namespace dev;
 
 constexpr uint32_t kBM = 128;          // queries per tile (TMEM lanes)
 constexpr uint32_t kBN = kTileRows;    // points per tile (accumulator columns)
-constexpr uint32_t kKC = 64;           // elements per K chunk (8 core-matrix columns)
+constexpr uint32_t kKC = 64;           // elements per K chunk of the index layout (8 core-matrix columns)
 constexpr uint32_t kChunkBytes = kBN * kKC * 2;  // 16 KB
+// The tiled layouts are column-major over 8-element core-matrix columns, so elements
+// [e, e + m) of a 128-row tile (e, m multiples of 16) are one contiguous run of m * 256 bytes
+// starting at half e * 128: a pipeline stage can carry any multiple of 16 elements.  A call
+// stages kc = 64 or 32 elements at a time (TcArgs::kc), whichever keeps more bytes in flight.
 constexpr uint32_t kColBytes = kBN * 16;         // one 16-byte core-matrix column of 128 rows
 constexpr uint32_t kAcc = 4;           // TMEM accumulators of kBN columns
 constexpr uint32_t kMeta = 8;          // tile metadata slots (copies run up to kMeta tiles ahead)
@@ -528,7 +532,7 @@ struct TcArgs {
     uint2* cand;             // rows x LISTS x KM (a bits, position)
     uint32_t* cand_n;        // rows x LISTS (0 = empty, kEmpty = list not valid)
     uint32_t* timeouts;
-    uint32_t qtiles, tiles, a, a8, dp, nck, stages;
+    uint32_t qtiles, tiles, a, a8, dp, nck, stages, kc;  // kc: elements per stage (64 or 32)
     uint32_t stream_a;  // 1: the query tile's chunks are copied into every stage beside the point chunk
     uint32_t polls;     // bound of every barrier wait
     uint32_t extra_tx;  // test hook: bytes the query-tile load expects but never receives
@@ -574,12 +578,12 @@ __host__ __device__ inline uint32_t tbox_stride(uint32_t a) { return (a + 3) / 4
 // holds a tile's px (128 floats), its rows' positions (128), its points' attributes (128 x a
 // floats) and the tile's attribute bounds (2 x a8 floats).
 // With stream_a (rows wider than kResidentDp) there is no resident query tile: a stage holds
-// the query tile's chunk (first kChunkBytes) and the point tile's chunk of the same K range.
+// the query tile's chunk (first half) and the point tile's chunk of the same K range.
 struct TcLayout {
     uint32_t a_off, b_off, stage_bytes, meta_off, meta_bytes, la_off, lp_off, box_off, bar_off, total;
 };
 __host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint32_t a, uint32_t stream_a, uint32_t km,
-                                              uint32_t own) {
+                                              uint32_t own, uint32_t kc) {
     TcLayout L;
     uint32_t o = 0;
     L.a_off = o;
@@ -588,7 +592,7 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t dp, uint32_t stages, uint
         o = (o + 1023u) & ~1023u;
     }
     L.b_off = o;
-    L.stage_bytes = stream_a ? 2 * kChunkBytes : kChunkBytes;
+    L.stage_bytes = (stream_a ? 2u : 1u) * kBN * kc * 2;
     o += stages * L.stage_bytes;
     L.meta_off = o;
     L.meta_bytes = kBN * 4 * (2 + a) + 8 * tbox_stride(a);
@@ -643,7 +647,7 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
     using C = Lists<DEEP>;
     extern __shared__ unsigned char bf_smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(bf_smem_raw) + 1023) & ~uintptr_t(1023));
-    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a, A.stream_a, C::KM, C::OWN);
+    const TcLayout Lo = tc_layout(A.dp, A.stages, A.a, A.stream_a, C::KM, C::OWN, A.kc);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lo.bar_off);
     uint64_t* full = bars;
     uint64_t* empty = full + A.stages;
@@ -711,7 +715,8 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
     const uint32_t tmem = *tmem_slot;
     const uint32_t T = hi - lo;
 
-    auto chunk_bytes = [&](uint32_t ch) { return kBN * min(kKC, A.dp - ch * kKC) * 2; };
+    const uint32_t kc = A.kc;
+    auto chunk_bytes = [&](uint32_t ch) { return kBN * min(kc, A.dp - ch * kc) * 2; };
     if (warp == 0) {
         // -------------------------------------------------------------- producer warp
         // Bulk copies: the query tile's rows (A), then per point tile its metadata slot and its
@@ -733,7 +738,7 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
         auto load_a = [&](uint32_t qt) {
             mbar_arrive_expect_tx(aload, kBM * A.dp * 2 + A.extra_tx);
             for (uint32_t ch = 0; ch < A.nck; ++ch)
-                bulk_g2s(sm + Lo.a_off + ch * kChunkBytes, A.at + (size_t)qt * kBM * A.dp + (size_t)ch * (kBM * kKC),
+                bulk_g2s(sm + Lo.a_off + ch * (kBM * kc * 2), A.at + (size_t)qt * kBM * A.dp + (size_t)ch * (kBM * kc),
                          chunk_bytes(ch), aload);
         };
         bool ok = true;
@@ -771,12 +776,12 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
                     unsigned char* stg = sm + Lo.b_off + st * Lo.stage_bytes;
                     if (A.stream_a) {
                         mbar_arrive_expect_tx(&full[st], 2 * bytes + A.extra_tx);
-                        bulk_g2s(stg, A.at + (size_t)cq * kBM * A.dp + (size_t)ch * (kBM * kKC), bytes, &full[st]);
-                        stg += kChunkBytes;
+                        bulk_g2s(stg, A.at + (size_t)cq * kBM * A.dp + (size_t)ch * (kBM * kc), bytes, &full[st]);
+                        stg += kBN * kc * 2;
                     } else {
                         mbar_arrive_expect_tx(&full[st], bytes);
                     }
-                    bulk_g2s(stg, A.xt + tile * tile_halves + (size_t)ch * (kBN * kKC), bytes, &full[st]);
+                    bulk_g2s(stg, A.xt + tile * tile_halves + (size_t)ch * (kBN * kc), bytes, &full[st]);
                 }
             }
         }
@@ -822,10 +827,10 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
                     const uint32_t st = i % A.stages;
                     if (!(ok = bwait(&full[st], (i / A.stages) & 1u, stop, A.polls))) break;
                     tc_fence_after();
-                    const uint32_t ksteps = min(kKC, A.dp - ch * kKC) / 16;
+                    const uint32_t ksteps = min(kc, A.dp - ch * kc) / 16;
                     const uint32_t sst = smem_u32(sB + st * Lo.stage_bytes);
-                    const uint32_t a0 = A.stream_a ? sst : smem_u32(sA + ch * kChunkBytes);
-                    const uint32_t b0 = A.stream_a ? sst + kChunkBytes : sst;
+                    const uint32_t a0 = A.stream_a ? sst : smem_u32(sA + ch * (kBM * kc * 2));
+                    const uint32_t b0 = A.stream_a ? sst + kBN * kc * 2 : sst;
                     for (uint32_t s = 0; s < ksteps; ++s)
                         mma_f16(tmem + b * kBN, kmajor_desc(a0 + s * 2 * kColBytes, kColBytes, 128),
                                 kmajor_desc(b0 + s * 2 * kColBytes, kColBytes, 128), (ch | s) ? 1u : 0u);
@@ -1384,7 +1389,8 @@ __global__ void box_count_tiles_kernel(const float* __restrict__ sbox, const uin
                                        uint32_t stiles, const float* __restrict__ tbox,
                                        const float* __restrict__ pattrs, const uint32_t* __restrict__ tcnt,
                                        uint32_t tiles, uint32_t a, uint32_t a8, const float* __restrict__ lb,
-                                       const float* __restrict__ rb, uint32_t qnum, uint32_t* __restrict__ box) {
+                                       const float* __restrict__ rb, uint32_t qnum, uint32_t* __restrict__ box,
+                                       uint32_t coarse) {
     const uint32_t lane = lane_id();
     const uint32_t q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (q >= qnum) return;
@@ -1408,6 +1414,10 @@ __global__ void box_count_tiles_kernel(const float* __restrict__ sbox, const uin
             bool tm = false, ti = false;
             if (t < tiles) meet_inside(tbox + (size_t)t * 2 * a8, a, a8, lo, hi, tm, ti);
             if (ti) cnt += tcnt[t];
+            if (coarse) {  // estimate: half of each tile that meets the box without lying inside it
+                if (tm && !ti) cnt += tcnt[t] >> 1;
+                continue;
+            }
             uint32_t pt = __ballot_sync(kFull, tm && !ti);
             while (pt) {
                 const uint32_t tt = ss * kSuper + __ffs(pt) - 1;
@@ -1429,10 +1439,10 @@ __global__ void box_count_tiles_kernel(const float* __restrict__ sbox, const uin
 }  // namespace
 
 void box_count_tiles(const DeviceIndex& d, const float* lb, const float* rb, uint32_t qnum, uint32_t* box,
-                     cudaStream_t s) {
+                     cudaStream_t s, bool coarse) {
     box_count_tiles_kernel<<<(qnum + 7) / 8, 256, 0, s>>>(d.bf_sbox, d.bf_scnt, d.bf_stiles, d.bf_tbox, d.bf_attrs,
                                                           d.bf_tcnt, d.bf_tiles, d.a, tbox_stride(d.a), lb, rb, qnum,
-                                                          box);
+                                                          box, coarse ? 1u : 0u);
 }
 
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k) { return d.bf_ok && k >= 1 && k <= kMaxK; }
@@ -1491,7 +1501,7 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
                     const uint32_t* qmask) {
     DeviceIndex& d = idx->d;
     const uint32_t qtiles = (qnum + kBM - 1) / kBM, qpad = qtiles * kBM;
-    const uint32_t dp = d.bf_dp, nck = (dp + kKC - 1) / kKC, a = d.a;
+    const uint32_t dp = d.bf_dp, a = d.a;
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, d.device);
     const uint32_t grid = (uint32_t)std::max(1, nsm);  // persistent: one CTA per SM
@@ -1501,10 +1511,29 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     const bool deep = k > kMaxKShallow;
     const uint32_t km = deep ? Lists<true>::KM : Lists<false>::KM, own = deep ? Lists<true>::OWN : Lists<false>::OWN;
     const uint32_t nlists = deep ? Lists<true>::LISTS : Lists<false>::LISTS;
-    const uint32_t stream = (dp > kResidentDp || tc_layout(dp, 2, a, 0, km, own).total > kSmemLimit) ? 1u : 0u;
-    uint32_t stages = 8;
-    while (stages > 2 && tc_layout(dp, stages, a, stream, km, own).total > kSmemLimit) --stages;
-    const TcLayout Lo = tc_layout(dp, stages, a, stream, km, own);
+    const uint32_t stream = (dp > kResidentDp || tc_layout(dp, 2, a, 0, km, own, kKC).total > kSmemLimit) ? 1u : 0u;
+    // stage width: 64 elements, or 32 when the ring then holds a fifth more useful bytes
+    // (rows whose width is not a multiple of 64 waste part of a 64-element stage; the deep
+    // lists leave room for few stages)
+    auto fit = [&](uint32_t kc, uint32_t max_stages) {
+        uint32_t st = max_stages;
+        while (st > 2 && tc_layout(dp, st, a, stream, km, own, kc).total > kSmemLimit) --st;
+        return st;
+    };
+    auto in_flight = [&](uint32_t kc, uint32_t st) {  // useful bytes of st stages, averaged over a tile
+        const uint32_t n = (dp + kc - 1) / kc;
+        return (double)st * (double)dp * kBN * 2 / n;
+    };
+    uint32_t kc = kKC, stages = fit(kKC, 8);
+    {
+        const uint32_t st32 = fit(32, 16);
+        if (in_flight(32, st32) > 1.2 * in_flight(kKC, stages)) {
+            kc = 32;
+            stages = st32;
+        }
+    }
+    const uint32_t nck = (dp + kc - 1) / kc;
+    const TcLayout Lo = tc_layout(dp, stages, a, stream, km, own, kc);
     if (Lo.total > kSmemLimit) return fail(GF_ERR_ARG, "tensor-core brute force: shared memory");
 
     size_t tmp_sort = sort_tmp_bytes(qnum);
@@ -1568,6 +1597,7 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     T.a = a;
     T.dp = dp;
     T.nck = nck;
+    T.kc = kc;
     T.stages = stages;
     T.stream_a = stream;
     void (*kern)(TcArgs) =

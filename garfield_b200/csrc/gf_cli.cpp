@@ -102,7 +102,6 @@ int main(int argc, char** argv) {
     memset(&fs, 0, sizeof(fs));
     fs.data_path = data.c_str();
     if (route) exact_tc = 1;            // routing by cost sends queries to the tensor-core exact scan
-    if (route && !(prefilter > 0.0f)) prefilter = 1e-9f;  // box counts without the prefilter rule
     fs.keep_fp32 = exact_tc ? 1u : 0u;  // the tensor-core exact route reads the fp32 rows
     fs.cagra_prefix = cprefix.c_str();
     fs.cagra_suffix = csuffix.c_str();

@@ -216,9 +216,11 @@ gf_status bruteforce(gf_index* idx, const float* queries, const float* lb, const
 // gf_bf_tc.cu
 gf_status attr_tiles_prepare(DeviceIndex& d);  // at index creation, after attrs
 gf_status bf_tc_prepare(DeviceIndex& d);  // at index creation, after vec32 and attr_tiles_prepare
-// plan box counts from the attribute tiles (d.at_ok); same counts as testing every point
+// plan box counts from the attribute tiles (d.at_ok); same counts as testing every point.
+// coarse: an estimate without the row scan (points of tiles inside the box, plus half of the
+// points of each tile that meets it only in part), for the search's cost rule
 void box_count_tiles(const DeviceIndex& d, const float* lb, const float* rb, uint32_t qnum, uint32_t* box,
-                     cudaStream_t s);
+                     cudaStream_t s, bool coarse = false);
 void free_bf_tc(DeviceIndex& d);
 bool bf_tc_usable(const DeviceIndex& d, uint32_t k);
 // Tensor-core pass: writes the proven queries' results and appends the others to

@@ -1052,8 +1052,9 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     if (P.width == 0 || P.width > 32) return fail(GF_ERR_ARG, "width must be 1..32");
     if (P.route > 1) return fail(GF_ERR_ARG, "route must be 0 or 1");
     if (P.route && !P.exact_tc) return fail(GF_ERR_ARG, "route = 1 sends queries to the tensor-core exact scan: set exact_tc");
-    if (P.route && !(p.prefilter > 0.0f))
-        return fail(GF_ERR_STATE, "route = 1 needs box counts: build the plan with prefilter > 0");
+    if (P.route && !(p.prefilter > 0.0f) && !d.at_ok)
+        return fail(GF_ERR_STATE, "route = 1 needs box counts: an index with attribute tiles, or a plan built with "
+                                  "prefilter > 0");
     if (P.exact_tc) {
         if (view || fullgraph || d.sharded || d.host_graph)
             return fail(GF_ERR_ARG, "exact_tc applies to gf_search / gf_search_host on a whole device-resident index");
@@ -1203,8 +1204,15 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
         if (!p.xmark) GF_CUDA(cudaMalloc((void**)&p.xmark, sizeof(uint32_t) * std::max<uint32_t>(p.max_q, 1)));
         const unsigned long long route_slots =
             P.route ? (unsigned long long)GF_ROUTE_ROWS_PER_SLOT * (P.L + kHopSlots) : 0ull;
-        mark_exact_kernel<<<(p.qnum + 255) / 256, 256, 0, s>>>(p.counts, A.box, d.n, p.qnum, P.postfilter,
-                                                                p.prefilter, route_slots, p.xmark, p.stats);
+        const uint32_t* box = A.box;
+        if (P.route && !box) {
+            // no exact counts in the plan: the cost rule takes the tile-level estimate
+            box_count_tiles(d, p.lb, p.rb, p.qnum, p.box, s, true);
+            box = p.box;
+        }
+        mark_exact_kernel<<<(p.qnum + 255) / 256, 256, 0, s>>>(p.counts, box, d.n, p.qnum, P.postfilter,
+                                                                A.box ? p.prefilter : 0.0f, route_slots, p.xmark,
+                                                                p.stats);
         GF_CUDA(cudaGetLastError());
         gf_status st = bruteforce(idx, p.q32, p.lb, p.rb, p.qnum, P.k, ids, dist, s, nullptr, p.xmark);
         if (st != GF_OK) return st;

@@ -147,8 +147,10 @@ typedef struct {
                             to the tensor-core exact scan when b < GF_ROUTE_ROWS_PER_SLOT * nc *
                             (L + 64), an estimate that the scan of its in-box rows costs less
                             than walking L list slots (plus a hop's 64) in each of its cells.
-                            Needs exact_tc = 1 and box counts (a plan built with prefilter > 0,
-                            e.g. 1e-9 to route by cost only). */
+                            Needs exact_tc = 1.  b is the plan's exact box count when the plan
+                            was built with prefilter > 0, else an estimate the search makes from
+                            the index's attribute tiles (the points of tiles inside the box plus
+                            half of those of tiles that meet it in part). */
 } gf_search_params;
 
 /* Tensor-core exact-scan rows that cost about as much as one list slot of one cell of the

@@ -143,11 +143,19 @@ def test_route_by_cost(small):
     bf_ids, bf_d = oracle.bruteforce(c.ds.vectors, c.ds.attrs, c.ds.queries, lo, hi, k)
     ids, dist = ids.cpu().numpy().view(np.uint32), dist.cpu().numpy()
     assert np.array_equal(ids[ex], bf_ids[ex]) and np.array_equal(dist[ex], bf_d[ex])
-    # without the tensor-core scan, or without box counts, the option is refused
+    # without the tensor-core scan the option is refused
     with pytest.raises(gf.GarfieldError):
         plan.search(gf.SearchParams(L=L, k=k, route=1))
+    # a plan without box counts: the search estimates them from the attribute tiles; every
+    # row is the exact scan's or the graph search's
     plan.build(dev(c.ds.queries), dev(lo), dev(hi))
-    with pytest.raises(gf.GarfieldError):
-        plan.search(gf.SearchParams(L=L, k=k, exact_tc=1, route=1))
+    ids2, dist2 = plan.search(gf.SearchParams(L=L, k=k, exact_tc=1, route=1))
+    n2 = plan.stats()["n_exact"]
+    ids2, dist2 = ids2.cpu().numpy().view(np.uint32), dist2.cpu().numpy()
+    g_ids, g_d = plan.search(gf.SearchParams(L=L, k=k))
+    g_ids, g_d = g_ids.cpu().numpy().view(np.uint32), g_d.cpu().numpy()
+    exact_rows = np.all(ids2 == bf_ids, 1) & np.all(dist2 == bf_d, 1)
+    graph_rows = np.all(ids2 == g_ids, 1) & np.all(dist2 == g_d, 1)
+    assert (exact_rows | graph_rows).all() and n2 >= int(ex.sum()) * 0.5
     plan.close()
     g.close()
