@@ -484,8 +484,15 @@ def run_out_of_core(args):
     if args.config == 5:
         # uint8 rows decoded as code / 100 (the reference's u8 path), queries scaled by 0.01
         common.update(codec=2, codes=ds.codes, f2h_factor=0.01)
-    streamed = gf.Index.create(**common, keep_fp32=True, host_graph=True)
-    resident = gf.Index.create(**common, keep_fp32=False, host_graph=False)
+    streamed = gf.Index.create(**common, keep_fp32=True, host_graph=True, cross_spokesman=args.cross_spokesman)
+    resident = gf.Index.create(**common, keep_fp32=False, host_graph=False, cross_spokesman=args.cross_spokesman)
+    P = int(np.prod(ix.grid))
+    seg = np.bincount(ix.cell_of, minlength=P)
+    xrows = seg  # cross rows of each cell: its points, or its spokesmen
+    if args.cross_spokesman:
+        spk, _, _ = gf.spokesman(seg, ix.graphs)
+        pos = np.arange(len(spk))
+        xrows = np.bincount(np.repeat(np.arange(P), seg)[spk == pos], minlength=P)
     qnum = ds.queries.shape[0]
     qd = torch.from_numpy(ds.queries).to(device)
     lod = torch.from_numpy(ds.lo.astype(np.float32)).to(device)
@@ -534,8 +541,7 @@ def run_out_of_core(args):
                 b.record(stream)
             b.synchronize()
             ms.append(a.elapsed_time(b))
-        seg = np.bincount(ix.cell_of, minlength=int(np.prod(ix.grid)))
-        h2d = sum(int(seg[c]) * ix.degree * 4 + len(bt) * int(seg[c]) * ix.cross_e * 4 for bt in batches for c in bt)
+        h2d = sum(int(seg[c]) * ix.degree * 4 + len(bt) * int(xrows[c]) * ix.cross_e * 4 for bt in batches for c in bt)
         res[name] = {"qps": round(qnum / (float(np.mean(ms)) / 1e3), 1), "ms_per_step": round(float(np.mean(ms)), 4),
                      "L": L, "recall_at_10": round(recall, 4), "sweep": sweep,
                      "h2d_graph_bytes_per_step": h2d if name == "streamed" else 0}
@@ -553,6 +559,8 @@ def run_out_of_core(args):
                       "batch_cells": args.batch_cells, "width": width,
                       "n_batches": len(res["batches"]), "splits": res["splits"], "schedule_ms": res["schedule_ms"],
                       "batches": res["batches"], "streamed": res["streamed"], "resident_same_batches": res["resident"],
+                      "cross_edges": (f"spokesman rows only: {streamed.cross_rows} of {streamed.n}"
+                                      if args.cross_spokesman else "full"),
                       "l2": "flushed (256 MiB write) between timed steps"}}
     print(json.dumps(out), flush=True)
 

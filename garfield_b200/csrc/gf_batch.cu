@@ -86,7 +86,6 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
     Plan& p = plan->p;
     if (!p.planned) return fail(GF_ERR_STATE, "gf_search_batched before gf_plan_queries");
     if (d.sharded) return fail(GF_ERR_STATE, "gf_search_batched on a shard: search it with gf_search_keys");
-    if (d.spk_rank) return fail(GF_ERR_STATE, "gf_search_batched on spokesman-compressed cross edges: use gf_search");
     gf_search_params P;
     if (prm && prm->exact_tc) return fail(GF_ERR_ARG, "exact_tc applies to gf_search and gf_search_host");
     gf_search_defaults(&P);
@@ -167,11 +166,19 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
         CellView v;
         size_t pts = 0;  // points in the batch
         for (uint32_t i = 0; i < B; ++i) pts += d.seg_h[cb[i] + 1] - d.seg_h[cb[i]];
+        // cross rows of a cell: its positions, or its spokesmen's ranks (compressed edges);
+        // xofs entries are a block's start less its first row times the row stride
+        const bool spkr = !d.spk_start_h.empty();
+        auto row0 = [&](uint32_t c) -> size_t { return spkr ? d.spk_start_h[c] : d.seg_h[c]; };
+        auto nrows = [&](uint32_t c) -> size_t {
+            return spkr ? d.spk_start_h[c + 1] - d.spk_start_h[c] : d.seg_h[c + 1] - d.seg_h[c];
+        };
+        size_t xrows = 0;  // cross rows of the batch's cells
+        for (uint32_t i = 0; i < B; ++i) xrows += nrows(cb[i]);
         if (!d.host_graph) {
             for (uint32_t i = 0; i < B; ++i) gofs[i] = (long long)d.seg_h[cb[i]] * R;
             for (uint32_t it = 0; it < B; ++it)
-                for (uint32_t is = 0; is < B; ++is)
-                    xofs[(size_t)it * B + is] = (long long)d.seg_h[cb[is]] * NC * E + (long long)cb[it] * E;
+                for (uint32_t is = 0; is < B; ++is) xofs[(size_t)it * B + is] = (long long)cb[it] * E;
             v.graph = d.graph;
             v.cross = d.cross;
             v.xstride = NC * E;
@@ -184,12 +191,12 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
             long long x = 0;
             for (uint32_t it = 0; it < B; ++it)
                 for (uint32_t is = 0; is < B; ++is) {
-                    xofs[(size_t)it * B + is] = x;
-                    x += (long long)(d.seg_h[cb[is] + 1] - d.seg_h[cb[is]]) * E;
+                    xofs[(size_t)it * B + is] = x - (long long)row0(cb[is]) * E;
+                    x += (long long)nrows(cb[is]) * E;
                 }
             GF_TRY_STATUS(grow(&bs.gbuf[t], &bs.gcap[t], std::max<size_t>(pts * R, 1), bs.searched[t], bs.used[t]));
             GF_TRY_STATUS(
-                grow(&bs.xbuf[t], &bs.xcap[t], std::max<size_t>(pts * B * E, 1), bs.searched[t], bs.used[t]));
+                grow(&bs.xbuf[t], &bs.xcap[t], std::max<size_t>(xrows * B * E, 1), bs.searched[t], bs.used[t]));
             v.graph = bs.gbuf[t];
             v.cross = bs.xbuf[t];
             v.xstride = E;
@@ -210,11 +217,11 @@ gf_status search_batched(gf_index* idx, gf_plan* plan, const gf_search_params* p
                 for (uint32_t it = 0; it < B; ++it)
                     for (uint32_t is = 0; is < B; ++is) {
                         const uint32_t ct = cb[it], cs = cb[is];
-                        const size_t rows = d.seg_h[cs + 1] - d.seg_h[cs];
+                        const size_t rows = nrows(cs);
                         if (rows)
-                            GF_CUDA(cudaMemcpyAsync(bs.xbuf[t] + xofs[(size_t)it * B + is],
-                                                    d.cross_h + ((size_t)ct * d.n + d.seg_h[cs]) * E, rows * E * 4,
-                                                    cudaMemcpyHostToDevice, bs.copy));
+                            GF_CUDA(cudaMemcpyAsync(bs.xbuf[t] + xofs[(size_t)it * B + is] + (long long)row0(cs) * E,
+                                                    d.cross_h + ((size_t)ct * d.cross_rows + row0(cs)) * E,
+                                                    rows * E * 4, cudaMemcpyHostToDevice, bs.copy));
                     }
         }
         GF_CUDA(cudaEventRecord(bs.copied[t], bs.copy));

@@ -1512,9 +1512,10 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     const uint32_t km = deep ? Lists<true>::KM : Lists<false>::KM, own = deep ? Lists<true>::OWN : Lists<false>::OWN;
     const uint32_t nlists = deep ? Lists<true>::LISTS : Lists<false>::LISTS;
     const uint32_t stream = (dp > kResidentDp || tc_layout(dp, 2, a, 0, km, own, kKC).total > kSmemLimit) ? 1u : 0u;
-    // stage width: 64 elements, or 32 when the ring then holds a fifth more useful bytes
-    // (rows whose width is not a multiple of 64 waste part of a 64-element stage; the deep
-    // lists leave room for few stages)
+    // stage width: 64 elements, or 32 when 64-element stages would leave only two in the ring
+    // and 32-element ones hold a fifth more useful bytes (measured on configuration 3, deep
+    // lists at 96 dims: 3 stages of 64 against 6 of 32 made no difference, so 64 stays the
+    // default; per-stage barrier work grows as the stages shrink)
     auto fit = [&](uint32_t kc, uint32_t max_stages) {
         uint32_t st = max_stages;
         while (st > 2 && tc_layout(dp, st, a, stream, km, own, kc).total > kSmemLimit) --st;
@@ -1527,7 +1528,7 @@ gf_status bf_tc_run(gf_index* idx, const float* queries, const float* lb, const 
     uint32_t kc = kKC, stages = fit(kKC, 8);
     {
         const uint32_t st32 = fit(32, 16);
-        if (in_flight(32, st32) > 1.2 * in_flight(kKC, stages)) {
+        if (stages <= 2 && in_flight(32, st32) > 1.2 * in_flight(kKC, stages)) {
             kc = 32;
             stages = st32;
         }

@@ -155,8 +155,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         return fail(GF_ERR_ARG, "int8 codes need their scales and zero points");
     if (sharded && (ds->host_graph || ds->keep_fp32))
         return fail(GF_ERR_ARG, "a shard cannot keep host graphs or fp32 vectors");
-    if (ds->cross_spokesman && (sharded || ds->host_graph))
-        return fail(GF_ERR_ARG, "spokesman-compressed cross edges need a whole device-resident index");
+    if (ds->cross_spokesman && sharded)
+        return fail(GF_ERR_ARG, "spokesman-compressed cross edges need a whole index (not a shard)");
     uint64_t ncells = 1, nq = 0;
     for (uint32_t j = 0; j < ds->n_attr; ++j) {
         if (ds->grid[j] == 0) return fail(GF_ERR_ARG, "zero grid size");
@@ -235,6 +235,23 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     std::vector<uint32_t> graph, cross;
     uint32_t* gdst = nullptr;
     uint32_t* xdst = nullptr;
+    // spokesman compression (compress_global_graph_extreme, tools.cuh:917-1010): a position
+    // reads the cross row of its spokesman's rank; ranks are in position order and a
+    // spokesman lies in its points' cell, so the ranks of cell c are spk_start_h[c] ..
+    std::vector<uint32_t> spk, spk_rank;
+    uint32_t n_spk = n;
+    const bool use_spk = ds->cross_spokesman && E;
+    if (use_spk) {
+        std::vector<uint32_t> sizes(P);
+        for (uint32_t c = 0; c < P; ++c) sizes[c] = d.seg_h[c + 1] - d.seg_h[c];
+        spk.resize(n);
+        spk_rank.resize(n);
+        spokesman_assign(n, P, sizes.data(), R, ds->graphs, spk.data(), spk_rank.data(), &n_spk);
+        d.spk_start_h.assign(P + 1, 0);
+        for (uint32_t p = 0; p < n; ++p)
+            if (spk[p] == p) d.spk_start_h[ds->cell_of[i2g[p]] + 1]++;
+        for (uint32_t c = 0; c < P; ++c) d.spk_start_h[c + 1] += d.spk_start_h[c];
+    }
     // stored rows: every position, or the shard's cells back to back in shard order
     std::vector<uint32_t> row_pos;  // stored row -> position (shard only)
     std::vector<int32_t> sh_slot;
@@ -271,9 +288,13 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         // cross blocks [target slot][source slot]: source rows of the source cell, E each
         sh_xofs.assign((size_t)S * S, 0);
         long long x = 0;
+        // cross_row reads xofs[target][source] + source position * E: each entry is the
+        // block's start less the source cell's first position times E
+        std::vector<long long> xstart((size_t)S * S);
         for (uint32_t bt = 0; bt < S; ++bt)
             for (uint32_t bs = 0; bs < S; ++bs) {
-                sh_xofs[(size_t)bt * S + bs] = x;
+                xstart[(size_t)bt * S + bs] = x;
+                sh_xofs[(size_t)bt * S + bs] = x - (long long)d.seg_h[d.shard_cells[bs]] * E;
                 x += (long long)(d.seg_h[d.shard_cells[bs] + 1] - d.seg_h[d.shard_cells[bs]]) * E;
             }
         cross.assign(std::max<long long>(x, 1), kEmpty);
@@ -281,7 +302,7 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
             const uint32_t ct = d.shard_cells[bt], tbase = d.seg_h[ct], tsz = d.seg_h[ct + 1] - tbase;
             for (uint32_t bs = 0; bs < S; ++bs) {
                 const uint32_t cs = d.shard_cells[bs];
-                uint32_t* dst = cross.data() + sh_xofs[(size_t)bt * S + bs];
+                uint32_t* dst = cross.data() + xstart[(size_t)bt * S + bs];
                 for (uint32_t p = d.seg_h[cs]; p < d.seg_h[cs + 1]; ++p)
                     for (uint32_t j = 0; j < E; ++j) {
                         const uint32_t loc = ds->cross[(size_t)i2g[p] * P * E + (size_t)ct * E + j];
@@ -292,7 +313,8 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
     } else if (d.host_graph) {
         DeviceGuard g0(device);
         cudaError_t e = cudaMallocHost((void**)&d.graph_h, std::max<size_t>((size_t)n * R, 1) * 4);
-        if (e == cudaSuccess && E) e = cudaMallocHost((void**)&d.cross_h, std::max<size_t>((size_t)n * P * E, 1) * 4);
+        if (e == cudaSuccess && E)
+            e = cudaMallocHost((void**)&d.cross_h, std::max<size_t>((size_t)n_spk * P * E, 1) * 4);
         if (e != cudaSuccess) {
             free_index(d);
             delete ix;
@@ -321,9 +343,11 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         for (uint32_t g = 0; g < n; ++g) {
             const uint32_t* src = ds->cross + (size_t)g * rowlen;
             const size_t pos = pos_of[g];
+            if (d.host_graph && use_spk && spk[pos] != pos) continue;  // only spokesmen keep a row
+            const size_t hrow = d.host_graph && use_spk ? spk_rank[pos] : pos;
             for (uint32_t c = 0; c < P; ++c) {
                 uint32_t base = d.seg_h[c], sz = d.seg_h[c + 1] - base;
-                uint32_t* dst = d.host_graph ? xdst + ((size_t)c * n + pos) * E : xdst + pos * rowlen + (size_t)c * E;
+                uint32_t* dst = d.host_graph ? xdst + ((size_t)c * n_spk + hrow) * E : xdst + pos * rowlen + (size_t)c * E;
                 for (uint32_t j = 0; j < E; ++j) {
                     uint32_t loc = src[c * E + j];
                     dst[j] = loc < sz ? base + loc : kEmpty;
@@ -332,20 +356,17 @@ static gf_status create(const gf_index_desc* ds, int device, gf_index** out) {
         }
     }
     d.cross_rows = n;
-    std::vector<uint32_t> spk_rank;
-    if (ds->cross_spokesman && E) {
-        // keep the rows of spokesmen only; a position reads the row of its spokesman's rank
-        std::vector<uint32_t> spk(n), sizes(P);
-        spk_rank.resize(n);
-        for (uint32_t c = 0; c < P; ++c) sizes[c] = d.seg_h[c + 1] - d.seg_h[c];
-        uint32_t ns = 0;
-        spokesman_assign(n, P, sizes.data(), R, ds->graphs, spk.data(), spk_rank.data(), &ns);
-        const size_t rowlen = (size_t)P * E;
-        std::vector<uint32_t> comp((size_t)ns * rowlen);
-        for (uint32_t p = 0; p < n; ++p)
-            if (spk[p] == p) std::memcpy(&comp[(size_t)spk_rank[p] * rowlen], &cross[(size_t)p * rowlen], rowlen * 4);
-        cross.swap(comp);
-        d.cross_rows = ns;
+    if (use_spk) {
+        d.cross_rows = n_spk;
+        if (!d.host_graph) {
+            // keep the rows of spokesmen only; a position reads the row of its spokesman's rank
+            const size_t rowlen = (size_t)P * E;
+            std::vector<uint32_t> comp((size_t)n_spk * rowlen);
+            for (uint32_t p = 0; p < n; ++p)
+                if (spk[p] == p)
+                    std::memcpy(&comp[(size_t)spk_rank[p] * rowlen], &cross[(size_t)p * rowlen], rowlen * 4);
+            cross.swap(comp);
+        }
     }
     std::vector<float> attrs((size_t)n * d.a);
     for (uint32_t p = 0; p < n; ++p)

@@ -67,6 +67,7 @@ struct DeviceIndex {
     uint32_t* graph = nullptr;   // n x degree positions (NULL when host_graph)
     uint32_t* cross = nullptr;   // cross_rows x (ncells*E) positions (NULL when host_graph)
     uint32_t cross_rows = 0;     // n, or the number of spokesmen (cross_spokesman)
+    std::vector<uint32_t> spk_start_h;  // cross_spokesman: first spokesman rank of each cell (ncells + 1)
     uint32_t* spk_rank = nullptr; // n: row of each position's cross edges (spokesman rank), or NULL
     // full-graph ablation (gf_index_assemble): n x fdeg positions, entry positions
     uint32_t* fgraph = nullptr;
@@ -77,7 +78,8 @@ struct DeviceIndex {
     // device per batch of cells (gf_search_batched)
     bool host_graph = false;
     uint32_t* graph_h = nullptr; // pinned, n x degree positions (position order)
-    uint32_t* cross_h = nullptr; // pinned, ncells x n x E: [target cell][source position][edge]
+    uint32_t* cross_h = nullptr; // pinned, ncells x cross_rows x E: [target cell][source row][edge] (rows:
+                                 // positions, or spokesman ranks with cross_spokesman)
     // shard: the device holds the vectors, graph rows and cross blocks of shard_cells only
     // (compact, in shard order); positions, attributes and ids stay global
     bool sharded = false;

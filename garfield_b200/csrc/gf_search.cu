@@ -344,7 +344,10 @@ __device__ __forceinline__ long long cross_row(const SArgs& A, uint32_t src, uin
         else
             hi = mid;
     }
-    return A.xofs[(long long)A.slot[next] * A.nslots + A.slot[lo]] + (long long)(src - A.seg[lo]) * A.xstride;
+    // xofs[target slot][source slot] is the block's start less its first row times xstride;
+    // a source row is the position, or its spokesman's rank with compressed cross edges
+    const uint32_t row = A.spk ? __ldg(A.spk + src) : src;
+    return A.xofs[(long long)A.slot[next] * A.nslots + A.slot[lo]] + (long long)row * A.xstride;
 }
 
 // Append the positions held by lanes with ok=true to P at nb (warp-uniform counter).
@@ -1107,7 +1110,7 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     A.xstride = view ? view->xstride : 0;
     A.seg = d.seg;
     A.i2g = d.i2g;
-    A.spk = view ? nullptr : d.spk_rank;
+    A.spk = d.spk_rank;
     A.q16 = p.q16;
     A.lb = p.lb;
     A.rb = p.rb;

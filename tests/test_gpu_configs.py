@@ -5,8 +5,9 @@ oracle finishes in seconds (the generators are the full-size ones with fewer poi
   mixture component's band) on a 4x4x4 grid, ~5% boxes in rank space, k = 100;
 - config 4: 768-dim unit-normalised mixture, attributes on [0, 2^20) on an 8x8 grid,
   degree 64, ~2% boxes;
-- config 5: uint8 rows (codec 2), a 16x16 grid, ~1% boxes; plain, spokesman-compressed,
-  scheduled out-of-core batches and four cell shards.
+- config 5: uint8 rows (codec 2), a 16x16 grid, ~1% boxes; plain, spokesman-compressed
+  (also searched by batches, resident and streamed), scheduled out-of-core batches and four
+  cell shards.
 
 Every search compares ids, canonical distances and traversal counters with the oracle bit
 for bit; the brute force compares ids and distances with the oracle's exact scan."""
@@ -162,6 +163,18 @@ def test_config5_shape(c5):
     ix2 = dataclasses.replace(c.ix, cross=oracle.expand_spokesman_cross(c.ix.cell_of, c.ix.graphs, c.ix.cross))
     ps = plan_of(gs, c)
     check_search(c, ps, 64, 2, 10, ix=ix2, **okw)
+    # the same compressed rows searched by batches, device-resident and streamed from pinned
+    # host memory (each batch copies the spokesmen's cross blocks only)
+    ref_ids, ref_d, _ = ref_search(c, ix=ix2, L=48, K=10, batches=batches, **okw)
+    ids, dist = ps.search_batched(batches, gf.SearchParams(L=48, k=10))
+    assert np.array_equal(u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+    ghs = make(c, keep_fp32=False, codec=2, codes=c.codes, f2h_factor=0.01, host_graph=True, cross_spokesman=True)
+    assert ghs.cross_rows == gs.cross_rows
+    phs = plan_of(ghs, c)
+    ids, dist = phs.search_batched(batches, gf.SearchParams(L=48, k=10))
+    assert np.array_equal(u32(ids), ref_ids) and np.array_equal(dist.cpu().numpy(), ref_d)
+    phs.close()
+    ghs.close()
     ps.close()
     gs.close()
     # four cell shards, keys merged
