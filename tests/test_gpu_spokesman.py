@@ -1,7 +1,8 @@
 """Search on a spokesman-compressed index (gf_index_desc.cross_spokesman; the cross-edge
 compression of compress_global_graph_extreme, tools.cuh:917-1010) against the oracle's
 search over the expanded cross edges (each point's row replaced by its spokesman's row):
-ids and canonical distances bit for bit; recall beside the uncompressed index."""
+ids and canonical distances bit for bit, for whole-index and batched searches (rows
+device-resident or streamed from pinned host memory); recall beside the uncompressed index."""
 from __future__ import annotations
 
 import ctypes as C
@@ -69,11 +70,29 @@ def test_spokesman_recall_and_refusals(small):
            C.byref(cp), C.c_void_p(ids.data_ptr()), None, C.c_void_p(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     assert st == 0 and torch.equal(ids, ref_ids)
-    # batched search addresses full cross rows per cell: refused on a compressed index
-    plan = comp.plan(q.shape[0])
-    plan.build(q, lo, hi)
+    # batched search over the compressed rows, device-resident and streamed from pinned host
+    # memory: the oracle's batched search over the expanded table
+    ix2 = dataclasses.replace(c.ix, cross=oracle.expand_spokesman_cross(c.ix.cell_of, c.ix.graphs, c.ix.cross))
+    batches = [[0, 1], [2, 3]]
+    ref, ref_d, _ = oracle.search(ix2, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts,
+                                  c.offsets, c.cells, c.entry(c.ix.degree), L=64, K=10, width=4, batches=batches)
+    host = gf.Index.create(vectors=c.ds.vectors, attrs=c.ds.attrs.astype(np.float32), grid=c.ix.grid,
+                           l_quant=c.ix.l_quant, r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs,
+                           degree=c.ix.degree, cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels,
+                           cross_spokesman=True, host_graph=True, keep_fp32=False)
+    for g in (comp, host):
+        plan = g.plan(q.shape[0])
+        plan.build(q, lo, hi)
+        ids, dist = plan.search_batched(batches, p)
+        assert np.array_equal(ids.cpu().numpy().view(np.uint32), ref)
+        assert np.array_equal(dist.cpu().numpy(), ref_d)
+        plan.close()
+    host.close()
+    # a shard keeps its cells' cross blocks in full: compression is refused there
     with pytest.raises(gf.GarfieldError):
-        plan.search_batched([[0, 1], [2, 3]], p)
-    plan.close()
+        gf.Index.create(vectors=c.ds.vectors, attrs=c.ds.attrs.astype(np.float32), grid=c.ix.grid,
+                        l_quant=c.ix.l_quant, r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs,
+                        degree=c.ix.degree, cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels,
+                        cross_spokesman=True, shard_cells=[0, 1], keep_fp32=False)
     full.close()
     comp.close()
