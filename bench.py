@@ -1123,7 +1123,8 @@ def main():
     ap.add_argument("--target", type=float, default=0.95)
     ap.add_argument("--L", type=int, default=0)
     ap.add_argument("--width", type=int, default=0)  # 0 = pick the faster of 4 and 8
-    ap.add_argument("--n", type=int, default=1_000_000)
+    # --points is the same flag for launchers whose own parser takes "--n" as an abbreviation
+    ap.add_argument("--n", "--points", dest="n", type=int, default=1_000_000)
     ap.add_argument("--qnum", type=int, default=10_000)
     ap.add_argument("--R", type=int, default=None)  # default: 32, 64 for config 4
     ap.add_argument("--E", type=int, default=2)
