@@ -743,11 +743,12 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
         };
         bool ok = true;
         uint32_t cq = qt0, na = 1, i = 0, nm = 0;  // A loads, chunks and metadata slots issued
+        uint32_t pnext = A.pre[cq + 1];  // first product of the next query tile (read once per tile change)
         if (lane == 0 && !A.stream_a) load_a(qt0);
         for (uint32_t t = 0; ok && t < T; ++t) {
             const uint32_t tile = tile_of(t);
             const uint32_t qprev = cq;
-            while (A.pre[cq + 1] <= lo + t) ++cq;
+            while (pnext <= lo + t) pnext = A.pre[++cq + 1];
             if (cq != qprev && !A.stream_a) {
                 // a new query tile: its rows replace A once the MMAs of the previous one are done
                 ok = __all_sync(kFull, bwait(afree, (na - 1) & 1u, stop, A.polls));
@@ -813,10 +814,11 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
             const unsigned char* sB = sm + Lo.b_off;
             bool ok = true;
             uint32_t cq = qt0, na = 0, i = 0;
+            uint32_t pnext = A.pre[cq + 1];  // first product of the next query tile
             for (uint32_t t = 0; t < T; ++t) {
                 const uint32_t b = t % kAcc;
                 const uint32_t qprev = cq;
-                while (A.pre[cq + 1] <= lo + t) ++cq;
+                while (pnext <= lo + t) pnext = A.pre[++cq + 1];
                 if (!A.stream_a && (t == 0 || cq != qprev)) {
                     if (!(ok = bwait(aload, na & 1u, stop, A.polls))) break;
                     ++na;
@@ -838,7 +840,7 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
                 }
                 if (!ok) break;
                 mma_commit(&tfull[b]);
-                if (!A.stream_a && (t + 1 == T || A.pre[cq + 1] <= lo + t + 1))
+                if (!A.stream_a && (t + 1 == T || pnext <= lo + t + 1))
                     mma_commit(afree);  // last tile of this query tile
             }
             if (!ok) *stop = 1u;
