@@ -36,8 +36,11 @@ def test_config2_planner_and_search_match_oracle(config2):
     plan.build(dev(ds.queries), dev(ds.lo), dev(ds.hi))
     counts, offsets, cells, top4, _ = plan.read()
     ncells = int(np.prod(ix.grid))
+    # the cell intersection on its own: the oracle's cell lists from the boxes and quantiles
+    ocounts, ooffsets, ounordered = oracle.plan_cells(ds.lo, ds.hi, ix.grid, ix.l_quant, ix.r_quant)
+    assert np.array_equal(counts, ocounts) and np.array_equal(offsets, ooffsets)
     cent, hist = oracle.cluster_info(ds.vectors, ix.labels, ix.cell_of, ncells)
-    ocells, otop4 = oracle.order_cells(ds.queries, cent, hist, counts, offsets, cells.copy())
+    ocells, otop4 = oracle.order_cells(ds.queries, cent, hist, ocounts, ooffsets, ounordered.copy())
     assert np.array_equal(top4, otop4) and np.array_equal(cells, ocells)
     ids, dist = plan.search(gf.SearchParams(L=40, k=10, width=4))
     st = plan.stats()
