@@ -787,7 +787,8 @@ def run_fullgraph(args):
 
 def run_sharded(args):
     """Cell-sharded mode (row e, strong scaling): rank r of N holds the cells
-    dist.shard_cells(grid, N)[r] only; a step plans all queries on every rank, searches them
+    dist.shard_cells(grid, N)[r] only; a step plans the queries on every rank (cell lists of
+    all of them, centroid order only for those with two or more local cells), searches them
     among the local cells (gf_search_keys), all-gathers the (qnum, k) merge keys over NCCL
     and merges them (gf_merge_keys) on every rank."""
     import torch

@@ -119,7 +119,8 @@ __device__ __forceinline__ void store_split(float* hi, float* lo, uint32_t at, f
 __global__ void __launch_bounds__(128) centroid_dot_tc_kernel(const float* __restrict__ Q, uint32_t qnum, uint32_t dim,
                                                               const float* __restrict__ Cm, uint32_t C,
                                                               const float* __restrict__ mean, float* __restrict__ S,
-                                                              uint32_t s_stride, uint32_t* __restrict__ timeouts) {
+                                                              uint32_t s_stride, uint32_t* __restrict__ timeouts,
+                                                              const uint32_t* __restrict__ live) {
     extern __shared__ __align__(128) unsigned char tc_smem[];
     float* Ah = reinterpret_cast<float*>(tc_smem);  // queries, hi parts
     float* Al = Ah + kTcChunkFloats;                // queries, lo parts
@@ -129,6 +130,8 @@ __global__ void __launch_bounds__(128) centroid_dot_tc_kernel(const float* __res
     __shared__ uint32_t tmem_base;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t q0 = blockIdx.x * kTcM, c0 = blockIdx.y * kTcN;
+    if (live) qnum = min(live[0], qnum);  // rows in use (a shard's listed queries)
+    if (q0 >= qnum) return;               // before the TMEM allocation: the whole block leaves
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
                      "r"(kTcN));
@@ -367,11 +370,13 @@ __global__ void __launch_bounds__(128) centroid_select_kernel(const float* __res
                                                               const float* __restrict__ mean,
                                                               const float2* __restrict__ cnorm,
                                                               uint32_t* __restrict__ top4,
-                                                              uint32_t* __restrict__ counters) {
+                                                              uint32_t* __restrict__ counters,
+                                                              const uint32_t* __restrict__ live) {
     __shared__ uint32_t cand[4][kMaxCand];
     extern __shared__ __align__(16) float rr_smem[];  // kSelectSmem bytes
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t q = blockIdx.x * 4 + warp;
+    if (live) qnum = min(live[0], qnum);  // row q is query live[1 + q]
     if (q >= qnum) return;
     const float kInf = __int_as_float(0x7f800000);
     const float* qv = Q + (size_t)q * dim;
@@ -481,7 +486,8 @@ __global__ void __launch_bounds__(128) centroid_select_kernel(const float* __res
         for (uint32_t r = 1; r < 4; ++r)
             if (lane == r) mine = best[r];
     }
-    if (lane < 4) top4[(size_t)q * 4 + lane] = mine == kEmptyKey ? kEmpty : key_pos(mine);
+    const size_t out = live ? live[1 + q] : q;
+    if (lane < 4) top4[out * 4 + lane] = mine == kEmptyKey ? kEmpty : key_pos(mine);
 }
 
 }  // namespace
@@ -491,7 +497,7 @@ bool centroid_tc_usable(const DeviceIndex& d) { return d.C >= kTcN && d.cnorm !=
 size_t centroid_tc_stride(const DeviceIndex& d) { return ((size_t)d.C + kTcN - 1) / kTcN * kTcN; }
 
 gf_status centroid_top4_tc(const DeviceIndex& d, const float* q32, uint32_t qnum, float* S, uint32_t* top4,
-                           uint32_t* counters, cudaStream_t s) {
+                           uint32_t* counters, cudaStream_t s, const uint32_t* live) {
     static bool attr_set[64] = {false};
     if (d.device >= 0 && d.device < 64 && !attr_set[d.device]) {
         GF_CUDA(cudaFuncSetAttribute(centroid_dot_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -503,10 +509,10 @@ gf_status centroid_top4_tc(const DeviceIndex& d, const float* q32, uint32_t qnum
     const uint32_t stride = (uint32_t)centroid_tc_stride(d);
     dim3 grid((qnum + kTcM - 1) / kTcM, (d.C + kTcN - 1) / kTcN);
     centroid_dot_tc_kernel<<<grid, 128, kTcSmem, s>>>(q32, qnum, d.dim, d.centroids, d.C, d.cmean, S, stride,
-                                                      counters);
+                                                      counters, live);
     GF_CUDA(cudaGetLastError());
     centroid_select_kernel<<<(qnum + 3) / 4, 128, kSelectSmem, s>>>(S, stride, qnum, d.C, q32, d.dim, d.centroids, d.cmean,
-                                                         reinterpret_cast<const float2*>(d.cnorm), top4, counters);
+                                                         reinterpret_cast<const float2*>(d.cnorm), top4, counters, live);
     GF_CUDA(cudaGetLastError());
     return GF_OK;
 }

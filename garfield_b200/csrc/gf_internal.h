@@ -160,6 +160,10 @@ struct Plan {
     BatchState* batch = nullptr;  // created by the first gf_search_batched
     unsigned long long* run = nullptr;  // running keys of searches on a shard index
     uint32_t* xmark = nullptr;          // max_q: queries answered by the tensor-core exact scan (exact_tc)
+    // shard indexes: live[0] = queries with two or more of the shard's cells, live[1..] their
+    // ids; lq32 their fp32 rows, gathered for the centroid planner
+    uint32_t* live = nullptr;
+    float* lq32 = nullptr;
     size_t run_cap = 0;
 };
 
@@ -179,11 +183,19 @@ uint32_t centroid_splits(uint32_t C);  // centroid ranges of the top-4 kernel
 uint32_t centroid_chunk(uint32_t C);   // centroids per range (multiple of 128)
 gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const float* lb, const float* rb,
                        uint32_t qnum, float prefilter, cudaStream_t s);
+// Significant bits of a query's cell count (0..ncells): the task-order radix sort reads only
+// these, one pass per 8 bits instead of four for the whole word; the order is the same.
+inline int count_sort_bits(uint32_t ncells) {
+    int b = 1;
+    while (b < 32 && (ncells >> b)) ++b;
+    return b;
+}
 // gf_centroid_tc.cu
 bool centroid_tc_usable(const DeviceIndex& d);
 size_t centroid_tc_stride(const DeviceIndex& d);  // floats per row of the plan's S
+// live (nullable, device): live[0] rows of q32 in use, row j being query live[1 + j]
 gf_status centroid_top4_tc(const DeviceIndex& d, const float* q32, uint32_t qnum, float* S, uint32_t* top4,
-                           uint32_t* counters, cudaStream_t s);
+                           uint32_t* counters, cudaStream_t s, const uint32_t* live = nullptr);
 // gf_search.cu
 // Restriction of one search launch to a set of cells ("slots"), whose graph rows and
 // cross-edge rows may lie anywhere in device memory (batched and out-of-core search).

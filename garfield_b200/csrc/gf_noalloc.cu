@@ -112,7 +112,8 @@ extern "C" gf_status gf_search_noalloc(gf_index* idx, const float* queries, cons
     p.stats = cv.take<unsigned long long>(8);
     size_t t1 = 0, t2 = 0;
     cub::DeviceScan::ExclusiveSum(nullptr, t1, p.counts, p.offsets, (int)Q);
-    cub::DeviceRadixSort::SortPairsDescending(nullptr, t2, p.counts, p.task, p.task, p.task, (int)Q, 0, 32);
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, t2, p.counts, p.task, p.task, p.task, (int)Q, 0,
+                                              count_sort_bits(d.ncells));
     p.scan_tmp_bytes = std::max(t1, t2);
     p.scan_tmp = cv.take<unsigned char>(p.scan_tmp_bytes);
     if (cv.used > kNoAllocScratchBytes)

@@ -145,13 +145,16 @@ constexpr uint32_t kTileWords = kTD * (kTQ + kTC);
 __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restrict__ queries, uint32_t qnum,
                                                             uint32_t dim, const float* __restrict__ cent,
                                                             uint32_t C, uint32_t c_chunk, float* __restrict__ part_d,
-                                                            uint32_t* __restrict__ part_i) {
+                                                            uint32_t* __restrict__ part_i,
+                                                            const uint32_t* __restrict__ live) {
     // staging tiles (qt: kTD x kTQ, ct: kTD x kTC), then the distance tile (kTQ x kTC)
     __shared__ __align__(16) float sm[kTQ * kTC > kTileWords ? kTQ * kTC : kTileWords];
     float* qt = sm;
     float* ct = sm + kTD * kTQ;
     const uint32_t t = threadIdx.x, qg = t & 7, cg = t >> 3;
     const uint32_t q0 = blockIdx.x * kTQ;
+    const uint32_t qn = live ? min(live[0], qnum) : qnum;  // rows in use (a shard's listed queries)
+    if (q0 >= qn) return;
     const uint32_t cbeg = blockIdx.y * c_chunk, cend = min(C, cbeg + c_chunk);
     f2x acc2[8][2];  // (query i, centroid pair j) partial distances, fp32 pairs
 #pragma unroll
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
             const uint32_t e2 = isq ? e : e - kTQ * (kTD / 4);
             const uint32_t rows = isq ? kTQ : kTC;
             const uint32_t r = e2 % rows, dd = (e2 / rows) * 4;
-            const uint32_t g = (isq ? q0 : cbeg) + r, lim = isq ? qnum : cend;
+            const uint32_t g = (isq ? q0 : cbeg) + r, lim = isq ? qn : cend;
             const float* src = isq ? queries : cent;
             float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             if (g < lim) {
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
         for (int r = 0; r < 4; ++r)
             if (oi[r] != kEmpty) insert(od[r], oi[r]);
     }
-    if (part == 0 && q0 + ql < qnum) {
+    if (part == 0 && q0 + ql < qn) {
         const size_t o = ((size_t)(q0 + ql) * gridDim.y + blockIdx.y) * 4;
         for (int r = 0; r < 4; ++r) {
             part_d[o + r] = bd[r];
@@ -264,11 +267,13 @@ __global__ void __launch_bounds__(256) centroid_top4_kernel(const float* __restr
     }
 }
 
-// Merge the per-range candidates of each query into its 4 nearest centroids.
+// Merge the per-range candidates of each query into its 4 nearest centroids.  With a
+// list `live` (shard planning), row q is query live[1 + q] and rows from live[0] on are unused.
 __global__ void centroid_merge_kernel(uint32_t qnum, uint32_t splits, const float* __restrict__ part_d,
-                                      const uint32_t* __restrict__ part_i, uint32_t* __restrict__ top4) {
+                                      const uint32_t* __restrict__ part_i, uint32_t* __restrict__ top4,
+                                      const uint32_t* __restrict__ live) {
     const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= qnum) return;
+    if (q >= (live ? min(live[0], qnum) : qnum)) return;
     float fd[4];
     uint32_t fi[4];
     for (int r = 0; r < 4; ++r) {
@@ -290,20 +295,28 @@ __global__ void centroid_merge_kernel(uint32_t qnum, uint32_t splits, const floa
             fi[k - 1] = ti;
         }
     }
-    for (int r = 0; r < 4; ++r) top4[(size_t)q * 4 + r] = fi[r];
+    const size_t out = live ? live[1 + q] : q;
+    for (int r = 0; r < 4; ++r) top4[out * 4 + r] = fi[r];
 }
 
 // Score = sum over the 4 nearest centroids of hist[cell][centroid]; cells ordered by
 // decreasing score, ties by increasing cell id (sort_by_clustering_info_weighted,
-// gpu_graph.cu:11344-11396).  One warp per query; rank sort over the query's cells.
+// gpu_graph.cu:11344-11396).  One warp per query; rank sort over the query's cells.  With
+// a list `live` (shard planning) warp j orders query live[1 + j], for j < live[0].
 constexpr uint32_t kMaxSortCells = 1024;
 __global__ void order_cells_kernel(uint32_t qnum, const uint32_t* __restrict__ counts,
                                    const uint32_t* __restrict__ offsets, uint32_t* __restrict__ cells,
-                                   const uint32_t* __restrict__ top4, const uint32_t* __restrict__ hist, uint32_t C) {
+                                   const uint32_t* __restrict__ top4, const uint32_t* __restrict__ hist, uint32_t C,
+                                   const uint32_t* __restrict__ live) {
     __shared__ uint64_t keys[4][kMaxSortCells];
     const uint32_t w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t q = blockIdx.x * 4 + w;
-    if (q >= qnum) return;
+    uint32_t q = blockIdx.x * 4 + w;
+    if (live) {
+        if (q >= min(live[0], qnum)) return;
+        q = live[1 + q];
+    } else if (q >= qnum) {
+        return;
+    }
     const uint32_t m = counts[q];
     if (m <= 1) return;
     uint32_t* cl = cells + offsets[q];
@@ -323,6 +336,35 @@ __global__ void order_cells_kernel(uint32_t qnum, const uint32_t* __restrict__ c
         for (uint32_t j = 0; j < m; ++j) rank += keys[w][j] < k;
         cl[rank] = (uint32_t)k;
     }
+}
+
+// Shard planning: a shard searches only its own cells, so a query's cell order changes its
+// results there only when two or more of its cells are the shard's.  Those queries are
+// listed in live[1..] (live[0] = their number; list order is arbitrary, each query's
+// planning is independent of its row) and their fp32 rows gathered into rows[j * dim].
+// One warp per query.
+__global__ void local_queries_kernel(uint32_t qnum, const uint32_t* __restrict__ counts,
+                                     const uint32_t* __restrict__ offsets, const uint32_t* __restrict__ cells,
+                                     const int32_t* __restrict__ slot, const float* __restrict__ q32, uint32_t dim,
+                                     uint32_t* __restrict__ live, float* __restrict__ rows) {
+    const uint32_t w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t q = blockIdx.x * 4 + w;
+    if (q >= qnum) return;
+    const uint32_t m = counts[q];
+    const uint32_t* cl = cells + offsets[q];
+    uint32_t held = 0;
+    for (uint32_t i0 = 0; i0 < m && held < 2; i0 += 32) {
+        const uint32_t i = i0 + lane;
+        held += __popc(__ballot_sync(0xFFFFFFFFu, i < m && slot[cl[i]] >= 0));
+    }
+    if (held < 2) return;
+    uint32_t j = 0;
+    if (lane == 0) {
+        j = atomicAdd(live, 1u);
+        live[1 + j] = q;
+    }
+    j = __shfl_sync(0xFFFFFFFFu, j, 0);
+    for (uint32_t k = lane; k < dim; k += 32) rows[(size_t)j * dim + k] = q32[(size_t)q * dim + k];
 }
 
 // Task order: queries with more cells first (gpu_graph.cu:12485-12493).
@@ -377,16 +419,31 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     // planner counters, read by gf_plan_stats: scratch[8] tensor-core waits that ran out,
     // [9] queries that fell back to the exact centroid scan, [10] centroids re-ranked exactly
     GF_CUDA(cudaMemsetAsync(p.scratch + 8, 0, 3 * sizeof(uint32_t), s));
+    // a shard plans only the queries with two or more of its cells (the grids stay sized for
+    // qnum; blocks past the device-side count return at once, so the host never waits)
+    const float* rows = p.q32;
+    const uint32_t* live = nullptr;
+    if (d.C && p.live) {
+        GF_CUDA(cudaMemsetAsync(p.live, 0, sizeof(uint32_t), s));
+        GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
+        local_queries_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, d.sh_slot, p.q32,
+                                                            d.dim, p.live, p.lq32);
+        rows = p.lq32;
+        live = p.live;
+    }
     if (d.C && p.S && centroid_tc_usable(d)) {  // tensor-core products + exact re-rank
-        gf_status st = centroid_top4_tc(d, p.q32, qnum, p.S, p.top4, p.scratch + 8, s);
+        gf_status st = centroid_top4_tc(d, rows, qnum, p.S, p.top4, p.scratch + 8, s, live);
         if (st != GF_OK) return st;
-        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
+        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C,
+                                                          live);
     } else if (d.C) {
         const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
         dim3 grid((qnum + kTQ - 1) / kTQ, S);
-        centroid_top4_kernel<<<grid, 256, 0, s>>>(p.q32, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i);
-        centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, s>>>(qnum, S, p.part_d, p.part_i, p.top4);
-        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C);
+        centroid_top4_kernel<<<grid, 256, 0, s>>>(rows, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i,
+                                                  live);
+        centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, s>>>(qnum, S, p.part_d, p.part_i, p.top4, live);
+        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C,
+                                                          live);
     } else {
         GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
     }
@@ -403,7 +460,8 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     iota_kernel<<<nb, tb, 0, s>>>(p.task + p.max_q, qnum);
     size_t tmp2 = p.scan_tmp_bytes;
     GF_CUDA(cub::DeviceRadixSort::SortPairsDescending(p.scan_tmp, tmp2, p.counts, p.task + 2 * p.max_q,
-                                                      p.task + p.max_q, p.task, (int)qnum, 0, 32, s));
+                                                      p.task + p.max_q, p.task, (int)qnum, 0,
+                                                      count_sort_bits(d.ncells), s));
     GF_CUDA(cudaGetLastError());
     p.planned = true;
     return GF_OK;
@@ -427,7 +485,7 @@ struct DeviceGuard2 {
 
 void free_plan(Plan& p) {
     void* ptrs[] = {p.S, p.q16, p.q32, p.lb, p.rb, p.counts, p.offsets, p.cells, p.top4, p.box, p.task, p.scratch,
-                    p.stats, p.scan_tmp, p.part_d, p.part_i};
+                    p.stats, p.scan_tmp, p.part_d, p.part_i, p.live, p.lq32};
     for (void* x : ptrs)
         if (x) cudaFree(x);
     if (p.io) cudaFree(p.io);
@@ -470,11 +528,16 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
     A((void**)&p.box, Q * 4);
     A((void**)&p.task, Q * 3 * 4);
     A((void**)&p.scratch, 64);
+    if (d.sharded) {
+        A((void**)&p.live, (Q + 1) * 4);
+        A((void**)&p.lq32, Q * d.dim * 4);
+    }
     A((void**)&p.stats, 8 * sizeof(unsigned long long));
     if (e == cudaSuccess) {
         size_t t1 = 0, t2 = 0;
         cub::DeviceScan::ExclusiveSum(nullptr, t1, p.counts, p.offsets, (int)Q);
-        cub::DeviceRadixSort::SortPairsDescending(nullptr, t2, p.counts, p.task, p.task, p.task, (int)Q, 0, 32);
+        cub::DeviceRadixSort::SortPairsDescending(nullptr, t2, p.counts, p.task, p.task, p.task, (int)Q, 0,
+                                              count_sort_bits(d.ncells));
         p.scan_tmp_bytes = std::max(t1, t2);
         A(&p.scan_tmp, p.scan_tmp_bytes);
     }

@@ -107,3 +107,22 @@ def small():
 def odd():
     """12k x 100 (row padding), 3 attributes on a 2x2x2 grid, unbalanced quantile cells."""
     return Case(12000, 100, 40, 200, (2, 2, 2), 0.15, R=16, E=2, C=40, seed=23, stratified=False)
+
+
+def check_shard_plan(c, shard, top4, cells):
+    """A shard's plan (gf_plan_read of a shard_cells index) against the whole-index plan
+    c.top4 / c.cells: queries with two or more of the shard's cells get the same top4 and
+    cell order; the others keep top4 empty and their cells in increasing id."""
+    held = set(int(x) for x in shard)
+    n_local = 0
+    for q in range(c.counts.shape[0]):
+        o, m = int(c.offsets[q]), int(c.counts[q])
+        mine = cells[o:o + m]
+        if sum(int(x) in held for x in mine) >= 2:
+            n_local += 1
+            assert np.array_equal(top4[q], c.top4[q]), q
+            assert np.array_equal(mine, c.cells[o:o + m]), q
+        else:
+            assert (top4[q] == 0xFFFFFFFF).all(), q
+            assert np.array_equal(mine, np.sort(c.cells[o:o + m])), q
+    return n_local

@@ -48,6 +48,43 @@ def test_tensor_core_top4_matches_oracle(many_clusters):
         assert np.array_equal(ids.cpu().numpy().view(np.uint32), ref)
 
 
+def test_tensor_core_planner_on_shards(many_clusters):
+    """Shard indexes plan only the queries with two or more of their cells (gathered rows,
+    a device-side count): the same top4 and order for those, and merged shard searches
+    equal the oracle's batched search with the shards as batches.  Every second query's
+    box is shrunk to 1 % so that it holds one or two cells; two shards of two cells plan
+    some queries each, four shards of one cell plan none."""
+    import types
+    from conftest import check_shard_plan
+    from garfield_b200.dist import shard_cells
+    c = many_clusters[0]
+    lo, hi = c.ds.lo.copy(), c.ds.hi.copy()
+    hi[1::2] = lo[1::2] + (hi[1::2] - lo[1::2]) // 100  # integer bounds, as generated
+    counts, offsets, unordered = oracle.plan_cells(lo, hi, c.ix.grid, c.ix.l_quant, c.ix.r_quant)
+    cells, top4 = oracle.order_cells(c.ds.queries, c.centroids, c.hist, counts, offsets, unordered.copy())
+    want = types.SimpleNamespace(counts=counts, offsets=offsets, cells=cells, top4=top4)
+    qnum = c.ds.queries.shape[0]
+    for world, lo_planned, hi_planned in ((2, 1, qnum - 1), (4, 0, 0)):
+        shards = shard_cells(c.ix.grid, world)
+        keys = []
+        for sh in shards:
+            g = gf.Index.create(vectors=c.ds.vectors, attrs=c.ds.attrs.astype(np.float32), grid=c.ix.grid,
+                                l_quant=c.ix.l_quant, r_quant=c.ix.r_quant, cell_of=c.ix.cell_of, graphs=c.ix.graphs,
+                                degree=c.ix.degree, cross=c.ix.cross, cross_e=c.ix.cross_e, labels=c.ix.labels,
+                                keep_fp32=False, shard_cells=sh)
+            plan = g.plan(qnum)
+            plan.build(dev(c.ds.queries), dev(lo), dev(hi))
+            _, _, got_cells, got_top4, _ = plan.read()
+            n = check_shard_plan(want, sh, got_top4, got_cells)
+            assert lo_planned <= n <= hi_planned, (world, sh, n)
+            keys.append(plan.search_keys(gf.SearchParams(L=48, k=10)).clone())
+            assert plan.stats()["n_plan_fallbacks"] == 0
+        ids, _ = g.merge_keys(torch.stack(keys, 0), 10)
+        ref, _, _ = oracle.search(c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, lo, hi, counts, offsets, cells,
+                                  c.entry(c.ix.degree), L=48, K=10, batches=shards)
+        assert np.array_equal(ids.cpu().numpy().view(np.uint32), ref)
+
+
 def _with_empty_cluster(c, gap):
     """c's clustering with label `gap` left empty: its centroid is 0/0 (NaN), as the
     reference's load_clustering computes it, and it must rank after every real centroid."""

@@ -40,12 +40,16 @@ def test_sharded_search_matches_oracle(which, world, request):
     idx = [make(c, keep_fp32=False, shard_cells=s) for s in shards]
     whole = make(c, keep_fp32=False)
     assert all(i.device_bytes < whole.device_bytes for i in idx) or world == 1
+    from conftest import check_shard_plan
     for L, width in ((32, 1), (64, 4)):
         params = gf.SearchParams(L=L, k=10, width=width)
         keys = []
-        for i in idx:
+        for i, sh in zip(idx, shards):
             plan = i.plan(c.ds.queries.shape[0])
             plan.build(dev(c.ds.queries), dev(c.ds.lo), dev(c.ds.hi))
+            if L == 32:  # each shard orders the cells of its multi-cell queries only
+                _, _, cells, top4, _ = plan.read()
+                check_shard_plan(c, sh, top4, cells)
             keys.append(plan.search_keys(params).clone())
         ids, dist = idx[0].merge_keys(torch.stack(keys, 0), 10)
         ref_ids, ref_d, _ = _oracle(c, shards, L=L, K=10, width=width)
