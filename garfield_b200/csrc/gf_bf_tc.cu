@@ -959,9 +959,18 @@ __global__ void __launch_bounds__(Lists<DEEP>::THREADS, 1) bf_tc_kernel(const __
                             if (mask) {
                                 const uint32_t j = __ffs(mask) - 1;
                                 mask &= mask - 1;
-                                float aj = av[0];
+                                // av[j] for the lane's own j: a five-level select tree (31
+                                // selects, five deep, instead of a chain 31 deep)
+                                float s16[16], s8[8], s4[4], s2[2];
 #pragma unroll
-                                for (uint32_t jj = 1; jj < 32; ++jj) aj = j == jj ? av[jj] : aj;
+                                for (uint32_t u = 0; u < 16; ++u) s16[u] = (j & 16u) ? av[u + 16] : av[u];
+#pragma unroll
+                                for (uint32_t u = 0; u < 8; ++u) s8[u] = (j & 8u) ? s16[u + 8] : s16[u];
+#pragma unroll
+                                for (uint32_t u = 0; u < 4; ++u) s4[u] = (j & 4u) ? s8[u + 4] : s8[u];
+#pragma unroll
+                                for (uint32_t u = 0; u < 2; ++u) s2[u] = (j & 2u) ? s4[u + 2] : s4[u];
+                                const float aj = (j & 1u) ? s2[1] : s2[0];
                                 if (aj < thr) {
                                     const uint32_t pos = mpos[col + j];
                                     if (n < C::KM) {
