@@ -454,6 +454,11 @@ def run_ours(args):
         # search (the CUB scan and radix-sort kernels of the planner are library launches)
         "gpu_launches": 8 * args.steps,
     }
+    if args.exact_tc and st["n_exact"]:
+        # the exact scan's time is inside search_ms, its work is not in the algorithmic bytes
+        out["roofline"]["note"] = (f"{int(st['n_exact'])} of {int(st['n_queries'])} queries took the tensor-core "
+                                   "exact scan (bf_tc_kernel): its time is inside search_ms but its bytes are not "
+                                   "counted here; --mode bruteforce gives that kernel's roofline")
     if strong is not None:
         out["strong"] = strong
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
