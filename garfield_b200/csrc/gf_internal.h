@@ -164,6 +164,11 @@ struct Plan {
     // ids; lq32 their fp32 rows, gathered for the centroid planner
     uint32_t* live = nullptr;
     float* lq32 = nullptr;
+    // side stream of the centroid stage (whole indexes; null: everything on the caller's stream)
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    // pinned: the timeout counters of the last gf_search_host, read back with its results
+    unsigned long long* flags_h = nullptr;
     size_t run_cap = 0;
 };
 

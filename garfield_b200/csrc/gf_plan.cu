@@ -409,6 +409,35 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     GF_CUDA(cudaMemcpyAsync(p.lb, lb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
     GF_CUDA(cudaMemcpyAsync(p.rb, rb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
     GF_CUDA(cudaMemcpyAsync(p.q32, queries, sizeof(float) * qnum * d.dim, cudaMemcpyDeviceToDevice, s));
+    // planner counters, read by gf_plan_stats: scratch[8] tensor-core waits that ran out,
+    // [9] queries that fell back to the exact centroid scan, [10] centroids re-ranked exactly
+    GF_CUDA(cudaMemsetAsync(p.scratch + 8, 0, 3 * sizeof(uint32_t), s));
+    // 4 nearest centroids of rows[0 .. qnum) (with `live`: of the listed rows) into top4
+    auto centroids = [&](cudaStream_t cs, const float* rows, const uint32_t* live) -> gf_status {
+        if (p.S && centroid_tc_usable(d)) {  // tensor-core products + exact re-rank
+            return centroid_top4_tc(d, rows, qnum, p.S, p.top4, p.scratch + 8, cs, live);
+        }
+        const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
+        dim3 grid((qnum + kTQ - 1) / kTQ, S);
+        centroid_top4_kernel<<<grid, 256, 0, cs>>>(rows, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i,
+                                                   live);
+        centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, cs>>>(qnum, S, p.part_d, p.part_i, p.top4, live);
+        GF_CUDA(cudaGetLastError());
+        return GF_OK;
+    };
+    // On a whole index the centroid top-4 needs only the query rows: it runs on the plan's
+    // side stream while this stream builds the cell lists and the task order, and the cell
+    // order waits for both.  A shard lists its multi-cell queries from the cell lists first
+    // (the grids stay sized for qnum; blocks past the device-side count return at once, so
+    // the host never waits), so there everything stays on this stream.
+    const bool fork = d.C && p.side && !p.live;
+    if (fork) {
+        GF_CUDA(cudaEventRecord(p.ev_fork, s));
+        GF_CUDA(cudaStreamWaitEvent(p.side, p.ev_fork, 0));
+        gf_status st = centroids(p.side, p.q32, nullptr);
+        if (st != GF_OK) return st;
+        GF_CUDA(cudaEventRecord(p.ev_join, p.side));
+    }
     launch_f2h(p.q32, qnum, d.dim, d.d8, d.alpha, p.q16, s);
     const uint32_t tb = 128, nb = (qnum + tb - 1) / tb;
     plan_count_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts);
@@ -416,36 +445,19 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     GF_CUDA(cub::DeviceScan::ExclusiveSum(p.scan_tmp, tmp, p.counts, p.offsets, (int)qnum, s));
     plan_fill_kernel<<<nb, tb, 0, s>>>(p.lb, p.rb, qnum, a, d.grid_d, d.lq_d, d.rq_d, p.counts, p.offsets,
                                        p.cells);
-    // planner counters, read by gf_plan_stats: scratch[8] tensor-core waits that ran out,
-    // [9] queries that fell back to the exact centroid scan, [10] centroids re-ranked exactly
-    GF_CUDA(cudaMemsetAsync(p.scratch + 8, 0, 3 * sizeof(uint32_t), s));
-    // a shard plans only the queries with two or more of its cells (the grids stay sized for
-    // qnum; blocks past the device-side count return at once, so the host never waits)
-    const float* rows = p.q32;
     const uint32_t* live = nullptr;
-    if (d.C && p.live) {
-        GF_CUDA(cudaMemsetAsync(p.live, 0, sizeof(uint32_t), s));
-        GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
-        local_queries_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, d.sh_slot, p.q32,
-                                                            d.dim, p.live, p.lq32);
-        rows = p.lq32;
-        live = p.live;
-    }
-    if (d.C && p.S && centroid_tc_usable(d)) {  // tensor-core products + exact re-rank
-        gf_status st = centroid_top4_tc(d, rows, qnum, p.S, p.top4, p.scratch + 8, s, live);
+    if (d.C && !fork) {
+        const float* rows = p.q32;
+        if (p.live) {
+            GF_CUDA(cudaMemsetAsync(p.live, 0, sizeof(uint32_t), s));
+            GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
+            local_queries_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, d.sh_slot,
+                                                                p.q32, d.dim, p.live, p.lq32);
+            rows = p.lq32;
+            live = p.live;
+        }
+        gf_status st = centroids(s, rows, live);
         if (st != GF_OK) return st;
-        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C,
-                                                          live);
-    } else if (d.C) {
-        const uint32_t S = centroid_splits(d.C), chunk = centroid_chunk(d.C);
-        dim3 grid((qnum + kTQ - 1) / kTQ, S);
-        centroid_top4_kernel<<<grid, 256, 0, s>>>(rows, qnum, d.dim, d.centroids, d.C, chunk, p.part_d, p.part_i,
-                                                  live);
-        centroid_merge_kernel<<<(qnum + 127) / 128, 128, 0, s>>>(qnum, S, p.part_d, p.part_i, p.top4, live);
-        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C,
-                                                          live);
-    } else {
-        GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
     }
     if (prefilter > 0.0f) {
         if (d.at_ok) {
@@ -462,6 +474,13 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     GF_CUDA(cub::DeviceRadixSort::SortPairsDescending(p.scan_tmp, tmp2, p.counts, p.task + 2 * p.max_q,
                                                       p.task + p.max_q, p.task, (int)qnum, 0,
                                                       count_sort_bits(d.ncells), s));
+    if (d.C) {
+        if (fork) GF_CUDA(cudaStreamWaitEvent(s, p.ev_join, 0));
+        order_cells_kernel<<<(qnum + 3) / 4, 128, 0, s>>>(qnum, p.counts, p.offsets, p.cells, p.top4, d.hist, d.C,
+                                                          live);
+    } else {
+        GF_CUDA(cudaMemsetAsync(p.top4, 0xFF, sizeof(uint32_t) * 4 * qnum, s));
+    }
     GF_CUDA(cudaGetLastError());
     p.planned = true;
     return GF_OK;
@@ -490,6 +509,13 @@ void free_plan(Plan& p) {
         if (x) cudaFree(x);
     if (p.io) cudaFree(p.io);
     if (p.xmark) cudaFree(p.xmark);
+    if (p.ev_fork) cudaEventDestroy(p.ev_fork);
+    if (p.ev_join) cudaEventDestroy(p.ev_join);
+    if (p.side) cudaStreamDestroy(p.side);
+    if (p.flags_h) cudaFreeHost(p.flags_h);
+    p.flags_h = nullptr;
+    p.side = nullptr;
+    p.ev_fork = p.ev_join = nullptr;
     if (p.run) cudaFree(p.run);
     free_batch_state(p.batch);
     p.batch = nullptr;
@@ -528,9 +554,14 @@ gf_status gf_plan_create(gf_index* idx, uint32_t max_queries, gf_plan** out) {
     A((void**)&p.box, Q * 4);
     A((void**)&p.task, Q * 3 * 4);
     A((void**)&p.scratch, 64);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&p.flags_h, 2 * sizeof(unsigned long long));
     if (d.sharded) {
         A((void**)&p.live, (Q + 1) * 4);
         A((void**)&p.lq32, Q * d.dim * 4);
+    } else if (e == cudaSuccess && d.C) {
+        e = cudaStreamCreateWithFlags(&p.side, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.ev_fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p.ev_join, cudaEventDisableTiming);
     }
     A((void**)&p.stats, 8 * sizeof(unsigned long long));
     if (e == cudaSuccess) {
@@ -667,12 +698,12 @@ gf_status gf_search_host(gf_index* idx, gf_plan* plan, const gf_search_params* p
         if (dist_host &&
             (e = cudaMemcpyAsync(dist_host, ddist, 4ull * qnum * P.k, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
             break;
+        // the search's and the planner's timeout counters come back with the results
+        p.flags_h[1] = 0;
+        if ((e = cudaMemcpyAsync(p.flags_h, p.stats + 7, 8, cudaMemcpyDeviceToHost, s)) != cudaSuccess) break;
+        if ((e = cudaMemcpyAsync(p.flags_h + 1, p.scratch + 8, 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess) break;
         e = cudaStreamSynchronize(s);
-        unsigned long long to = 0;
-        uint32_t pto = 0;
-        if (e == cudaSuccess) e = cudaMemcpy(&to, p.stats + 7, sizeof(to), cudaMemcpyDeviceToHost);
-        if (e == cudaSuccess) e = cudaMemcpy(&pto, p.scratch + 8, sizeof(pto), cudaMemcpyDeviceToHost);
-        if (e == cudaSuccess && (to || pto)) st = fail(GF_ERR_TIMEOUT, "a bounded device wait ran out");
+        if (e == cudaSuccess && (p.flags_h[0] || p.flags_h[1])) st = fail(GF_ERR_TIMEOUT, "a bounded device wait ran out");
     } while (0);
     if (st != GF_OK) return st;
     if (e != cudaSuccess) return cuda_fail(e, "gf_search_host");
