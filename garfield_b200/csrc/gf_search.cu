@@ -629,19 +629,19 @@ __global__ void __launch_bounds__(128, 5) gmg_search_kernel(const __grid_constan
                         {
                             key_t* T = w.T(A);
                             uint32_t* picks = w.picks(A);
+                            // the first W unexplored entries in list order: each lane's rank
+                            // among them is a prefix count of the ballot
                             for (uint32_t i0 = 0; i0 < A.L && np < A.W; i0 += 32) {
-                                uint32_t i = i0 + lane;
-                                key_t k = i < A.L ? T[i] : kEmptyKey;
-                                uint32_t msk = __ballot_sync(kFull, (k & kKeyExplored) == 0);
-                                while (msk && np < A.W) {
-                                    uint32_t b = __ffs(msk) - 1;
-                                    msk &= msk - 1;
-                                    if (lane == b) {
-                                        T[i] = k | kKeyExplored;
-                                        picks[np] = key_pos(k);
-                                    }
-                                    ++np;
+                                const uint32_t i = i0 + lane;
+                                const key_t k = i < A.L ? T[i] : kEmptyKey;
+                                const bool fresh = (k & kKeyExplored) == 0;
+                                const uint32_t msk = __ballot_sync(kFull, fresh);
+                                const uint32_t r = np + __popc(msk & lanemask_lt());
+                                if (fresh && r < A.W) {
+                                    T[i] = k | kKeyExplored;
+                                    picks[r] = key_pos(k);
                                 }
+                                np = min(np + __popc(msk), A.W);
                             }
                             __syncwarp();
                         }
