@@ -81,6 +81,17 @@ __device__ __forceinline__ float finish8(f2x a0, f2x a1, f2x a2, f2x a3) {
 // adds the other half's partials (add2) and finishes the sum (finish8).  The chunk loop
 // stays rolled, which keeps the search kernel's instruction footprint small.
 
+// (x - q) of an fp16 pair against an fp32 pair: one mixed-precision subtract per element
+// (the fp16 operand is widened exactly and the difference rounded once, as a widening
+// followed by an fp32 subtract would); (x - q)^2 == (q - x)^2, rounding being symmetric.
+__device__ __forceinline__ f2x hsub_f2x(uint32_t h, f2x q) {
+    float lo, hi;
+    asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n sub.rn.f32.f16 %0, a, %3;\n sub.rn.f32.f16 %1, b, %4;\n}\n"
+        : "=f"(lo), "=f"(hi)
+        : "r"(h), "f"(lo2(q)), "f"(hi2(q)));
+    return pack2(lo, hi);
+}
+
 // fp16 rows: the query is held as fp32 pairs q2[c*4 .. c*4+3] of chunk c.
 template <int NCH>
 __device__ __forceinline__ void half16(const uint4* srow, const f2x* q2, uint32_t nch_rt, uint32_t half, f2x* p) {
@@ -90,10 +101,10 @@ __device__ __forceinline__ void half16(const uint4* srow, const f2x* q2, uint32_
         const uint4 x = srow[c];
         const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(q2 + c * 4);
         const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(q2 + c * 4 + 2);
-        p[0] = sqacc2(sub2(qa.x, h2_to_f2x(x.x)), p[0]);
-        p[1] = sqacc2(sub2(qa.y, h2_to_f2x(x.y)), p[1]);
-        p[2] = sqacc2(sub2(qb.x, h2_to_f2x(x.z)), p[2]);
-        p[3] = sqacc2(sub2(qb.y, h2_to_f2x(x.w)), p[3]);
+        p[0] = sqacc2(hsub_f2x(x.x, qa.x), p[0]);
+        p[1] = sqacc2(hsub_f2x(x.y, qa.y), p[1]);
+        p[2] = sqacc2(hsub_f2x(x.z, qb.x), p[2]);
+        p[3] = sqacc2(hsub_f2x(x.w, qb.y), p[3]);
     }
 }
 
