@@ -391,6 +391,24 @@ __device__ __forceinline__ key_t warp_sort32_key(key_t k) {
     return k;
 }
 
+// The same network stopped after the runs of `width` lanes (a power of two, warp-uniform):
+// when every lane from `width` on holds kEmptyKey, lanes [0, width) end sorted ascending and
+// the result equals the full sort (later lanes only ever meet lanes of their own run).
+__device__ __forceinline__ key_t warp_sort_key_upto(key_t k, uint32_t width) {
+    const uint32_t lane = lane_id();
+#pragma unroll
+    for (uint32_t s = 2; s <= 32; s <<= 1) {
+        if (s > width) break;
+#pragma unroll
+        for (uint32_t j = s >> 1; j > 0; j >>= 1) {
+            const key_t o = shfl_xor_key(k, j);
+            const bool keep_min = ((lane & j) == 0) == ((lane & s) == 0);
+            k = keep_min ? (o < k ? o : k) : (o > k ? o : k);
+        }
+    }
+    return k;
+}
+
 // Bitonic sort of n (power of two) keys in shared memory, ascending.
 __device__ __forceinline__ void warp_sort_keys(key_t* a, uint32_t n) {
     const uint32_t lane = lane_id();

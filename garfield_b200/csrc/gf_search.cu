@@ -228,7 +228,7 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         if (ns) {
             const key_t k = lane < ns ? B[lane] : kEmptyKey;
             __syncwarp();
-            B[lane] = warp_sort32_key(k);
+            B[lane] = warp_sort_key_upto(k, next_pow2(ns));
             __syncwarp();
         }
         return ns;
