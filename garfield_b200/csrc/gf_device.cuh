@@ -453,7 +453,8 @@ static __device__ __noinline__ uint32_t merge_keys(const key_t* t, key_t* o, uin
                                             key_t* ev, bool recycle) {
     const uint32_t lane = lane_id();
     // entering batch prefix: b[j] enters iff j + #(t < b[j]) < L (increasing in j)
-    uint32_t m = 0;
+    // (first: list entries before b[0]'s insertion point, lane 0's rank in the first pass)
+    uint32_t m = 0, first = 0;
     for (uint32_t j0 = 0; j0 < nb; j0 += 32) {
         const uint32_t j = j0 + lane;
         uint32_t pos = 0xFFFFFFFFu;
@@ -462,13 +463,13 @@ static __device__ __noinline__ uint32_t merge_keys(const key_t* t, key_t* o, uin
             kj = b[j];
             pos = j + keys_below(t, L, kj);
         }
+        if (j0 == 0) first = __shfl_sync(kFull, pos, 0);
         const uint32_t msk = __ballot_sync(kFull, pos < L);
         if (pos < L) o[pos] = kj;
         m += __popc(msk);
         if (__popc(msk) < 32) break;
     }
     if (m == 0) return 0;
-    const uint32_t first = __shfl_sync(kFull, keys_below(t, L, b[0]), 0);
     uint32_t nev = 0;
     for (uint32_t i0 = 0; i0 < L; i0 += 32) {
         const uint32_t i = i0 + lane;
