@@ -218,6 +218,9 @@ gf_status gf_plan_destroy(gf_plan* plan);
  *   queries: device, qnum x dim fp32; lb/rb: device, qnum x n_attr closed bounds.
  *   prefilter: --prefilter (box count / n <= prefilter => exact route); the box count
  *   pass runs only when prefilter > 0.
+ * On a whole index the centroid stage runs on a stream of the plan, forked from `stream`
+ * after the query copy and joined back before the cell ordering with events: all work is
+ * ordered on `stream` when the call returns, and the host never waits.
  * On a shard index (gf_index_desc.shard_cells) only the queries with two or more of the
  * shard's cells get their 4 nearest centroids and an ordered cell list: the others keep
  * their cells in increasing id and top4 = 0xFFFFFFFF.  A shard searches only its own cells,
