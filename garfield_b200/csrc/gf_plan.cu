@@ -409,7 +409,7 @@ gf_status plan_queries(gf_index* idx, gf_plan* plan, const float* queries, const
     GF_CUDA(cudaMemcpyAsync(p.lb, lb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
     GF_CUDA(cudaMemcpyAsync(p.rb, rb, sizeof(float) * qnum * a, cudaMemcpyDeviceToDevice, s));
     GF_CUDA(cudaMemcpyAsync(p.q32, queries, sizeof(float) * qnum * d.dim, cudaMemcpyDeviceToDevice, s));
-    // planner counters, read by gf_plan_stats: scratch[8] tensor-core waits that ran out,
+    // planner counters, read by gf_search_stats_read: scratch[8] tensor-core waits that ran out,
     // [9] queries that fell back to the exact centroid scan, [10] centroids re-ranked exactly
     GF_CUDA(cudaMemsetAsync(p.scratch + 8, 0, 3 * sizeof(uint32_t), s));
     // 4 nearest centroids of rows[0 .. qnum) (with `live`: of the listed rows) into top4
