@@ -204,10 +204,10 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // Closed-box test of one point (merge_top_with_recycle_list's filter, gpu_graph.cu:514-520).
 __device__ __forceinline__ bool in_box(const float* __restrict__ attrs, long long row, uint32_t a,
                                        const float* __restrict__ lb, const float* __restrict__ rb) {
-    bool ok = true;
+    bool ok = true;  // no short-circuit: the attribute loads are independent
     for (uint32_t j = 0; j < a; ++j) {
-        float v = __ldg(attrs + row * a + j);
-        ok = ok && (v >= lb[j]) && (v <= rb[j]);
+        const float v = __ldg(attrs + row * a + j);
+        ok &= (v >= lb[j]) & (v <= rb[j]);
     }
     return ok;
 }
@@ -342,8 +342,10 @@ __device__ __forceinline__ bool hash_contains(const uint32_t* H, uint32_t hs, ui
     return false;
 }
 
+// H is 16-byte aligned and hs a multiple of 4 (a power of two >= 256)
 __device__ __forceinline__ void hash_clear(uint32_t* H, uint32_t hs) {
-    for (uint32_t i = lane_id(); i < hs; i += 32) H[i] = kEmpty;
+    uint4* H4 = reinterpret_cast<uint4*>(H);
+    for (uint32_t i = lane_id(); i < (hs >> 2); i += 32) H4[i] = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
     __syncwarp();
 }
 
