@@ -71,6 +71,8 @@ struct SArgs {
     uint32_t qnum, nch, a, P, R, E, L, K, W, max_iter, n_entry, postfilter, n;
     float prefilter;
     uint32_t hs, hshift, bcap, stage_rows, stage_stride, warp_words;
+    uint32_t stage_shift;           // log2(stage_rows)
+    unsigned long long e_magic;     // ceil(2^32 / E): j / E == (j * e_magic) >> 32 for the hop's pairs
     uint32_t wait_polls, extra_tx;  // staging wait limit; test hook: bytes expected but never sent
     uint32_t graph_bulk;            // neighbour rows are fetched with bulk copies (R * 4 a multiple of 16)
     // word offsets inside a warp's shared-memory slice
@@ -198,7 +200,7 @@ __device__ __noinline__ uint32_t eval_sort(const SArgs& A, uint32_t* base, uint3
         }
         return inr;
     };
-    const uint32_t nst = (nb + SR - 1) / SR;
+    const uint32_t nst = (nb + SR - 1) >> A.stage_shift;
     bool inr_next = nst ? issue(0) : false;
     for (uint32_t s = 0; s < nst; ++s) {
         const bool inr = inr_next;
@@ -472,8 +474,9 @@ __device__ __noinline__ uint32_t cross_hop(const SArgs& A, W& w, uint32_t next, 
         bool ok = false;
         uint32_t pos = kEmpty;
         if (j < pairs) {
-            const uint32_t src = key_pos(T[j / A.E]);
-            pos = __ldg(A.cross + cross_row(A, src, next) + (j % A.E));
+            const uint32_t si = (uint32_t)(((unsigned long long)j * A.e_magic) >> 32);  // j / E
+            const uint32_t src = key_pos(T[si]);
+            pos = __ldg(A.cross + cross_row(A, src, next) + (j - si * A.E));
             if (pos != kEmpty) ok = hash_insert(H, A.hs, A.hshift, pos);
         }
         append(P, nb, ok, pos);
@@ -1173,6 +1176,10 @@ gf_status search(gf_index* idx, gf_plan* plan, const gf_search_params* prm, uint
     uint32_t sr = 16;
     while (sr > 1 && sr * A.stage_stride * 16 > stage_budget) sr >>= 1;
     A.stage_rows = sr;
+    A.stage_shift = 0;
+    while ((1u << A.stage_shift) < sr) ++A.stage_shift;
+    // exact for the hop's j < 64 E, E <= 4 (j * (e_magic * E - 2^32) < 2^32)
+    A.e_magic = A.E ? ((1ull << 32) + A.E - 1) / A.E : 0ull;
     make_layout(A, nch16, bytes);
 
     KernelFn kern = fullgraph ? pick_fullgraph(A.nch, bytes) : pick_kernel(A.nch, bytes);
