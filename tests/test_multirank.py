@@ -128,3 +128,31 @@ def test_two_gloo_ranks_cell_sharded(tmp_path):
     port = 30500 + (os.getpid() % 1000)
     mp.spawn(_shard_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
     assert bool(np.load(tmp_path / "ok.npy")[0])
+
+
+def test_shard_result_depends_only_on_its_own_cell_order(small):
+    """The premise of shard planning (a shard orders the cells of its multi-cell queries
+    only): in the oracle's batched search with a shard as the batch, a query whose cells
+    include fewer than two of the shard's gets the same answer whatever the order of its
+    cells, so those queries may keep their cells in id order."""
+    import oracle
+    from garfield_b200.dist import shard_cells
+    from conftest import mt_entry
+    c = small
+    ent = mt_entry(c.ix.degree, int(np.bincount(c.ix.cell_of, minlength=c.ncells).min()))
+    for sh in shard_cells(c.ix.grid, 2):
+        held = set(int(x) for x in sh)
+        cells = c.cells.copy()
+        changed = 0
+        for q in range(c.counts.shape[0]):
+            o, m = int(c.offsets[q]), int(c.counts[q])
+            if sum(int(x) in held for x in cells[o:o + m]) < 2 and m > 1:
+                cells[o:o + m] = np.sort(cells[o:o + m])
+                changed += int(not np.array_equal(cells[o:o + m], c.cells[o:o + m]))
+        kw = dict(L=32, K=10, batches=[sh])
+        ref = oracle.search(c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts, c.offsets,
+                            c.cells, ent, **kw)
+        got = oracle.search(c.ix, c.ds.vectors, c.ds.attrs, c.ds.queries, c.ds.lo, c.ds.hi, c.counts, c.offsets,
+                            cells, ent, **kw)
+        assert np.array_equal(ref[0], got[0]) and np.array_equal(ref[1], got[1])
+        assert changed > 0  # some queries really had their order dropped
