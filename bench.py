@@ -1140,8 +1140,8 @@ def main():
     ap.add_argument("--cpu-sample", dest="cpu_sample", type=int, default=200)
     ap.add_argument("--ref-sample", dest="ref_sample", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", dest="no_cpu_baseline", action="store_true")
-    ap.add_argument("--cache", default=str(ROOT / ".gf_cache"))  # synthetic indexes, git- and gpurun-ignored
-    ap.add_argument("--out-dir", dest="out_dir", default=str(ROOT / "gpurun_out"))  # logs of --impl reference-cuda
+    ap.add_argument("--cache", default=str(ROOT / ".gf_cache"))  # synthetic indexes, kept out of git
+    ap.add_argument("--out-dir", dest="out_dir", default=str(ROOT / ".gf_cache" / "logs"))  # --impl reference-cuda logs
     ap.add_argument("--alphas", type=float, nargs="+", default=[0.01, 0.005, 0.02])
     ap.add_argument("--ref-timeout", dest="ref_timeout", type=int, default=900)
     ap.add_argument("--mode", default="in-memory",
